@@ -1,0 +1,432 @@
+"""Benchmark of the activation-compression hot path (one JSON line on stdout).
+
+Workload (one B200 per rank, weak scaling): each rank
+holds its own 16384-token shard of a LLaMA-7B-shaped MLP activation
+X (16384 x 4096 bf16, rank-64 signal + 0.05 N(0,1) noise + 16 outlier
+channels x30, seed = rank), compressed with r = 32, k = 16, int4, group 64.
+
+One step = encode X + decode X^ (the channel-group kernels through the C ABI,
+inputs resident in HBM).  ``value`` = algorithmic bytes of all ranks' steps /
+max-over-ranks device time, in GB/s.  Per-component numbers (encode, decode,
+fused SiLU backward on the 16384 x 11008 input, fused dequant-dW GEMM of
+config 4 in TFLOP/s) ride along under "components".
+
+``--impl reference`` times the reference's algorithm on the host cores
+instead (the oracle port in oracle/, all threads, bounded sample).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import subprocess
+import sys
+import time
+
+ROOT = os.path.dirname(os.path.abspath(__file__))
+sys.path.insert(0, os.path.join(ROOT, "triton-kernel-test_b200"))
+
+METRIC = "encode/decode GB/s of bf16 activation vs HBM peak; fused dequant-dW GEMM TFLOPS"
+FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustained": 1400.0}
+
+
+# ---------------------------------------------------------------- algorithmic work
+def packed_bytes_per_row(H, bits, group, rank, k):
+    return H * bits // 8 + (H // group) * 4 + rank + (4 if rank else 0) + 2 * k
+
+
+def basis_bytes(H, rank):
+    return rank * H * 2 + H * rank + rank * 4
+
+
+def encode_bytes(T, H, bits, group, rank, k):
+    """Read X once, write every packed buffer once, read the basis once."""
+    return T * (2 * H + packed_bytes_per_row(H, bits, group, rank, k)) + basis_bytes(H, rank)
+
+
+decode_bytes = encode_bytes  # the same buffers, the other way round
+
+
+def consumer_bytes(T, H, bits, group, rank, k):
+    """Read the packed activation and dY, write dX."""
+    return T * (4 * H + packed_bytes_per_row(H, bits, group, rank, k)) + basis_bytes(H, rank)
+
+
+def peaks():
+    p = os.path.join(ROOT, "MEASURED_PEAKS.json")
+    if os.path.exists(p):
+        d = json.load(open(p))
+        return d, "measured"
+    return dict(FALLBACK_PEAKS), "fallback"
+
+
+# ---------------------------------------------------------------- clocks
+class ClockSampler:
+    """nvidia-smi clocks/throttle reasons sampled every 200 ms while running."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu = gpu_index
+        self.proc = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
+                                          "--format=csv,noheader,nounits", "-lms", "200"],
+                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+        except OSError:
+            self.proc = None
+        return self
+
+    def __exit__(self, *exc):
+        self.lines = []
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                out, _ = self.proc.communicate(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+                out, _ = self.proc.communicate()
+            self.lines = [l for l in out.splitlines() if l.strip()]
+
+    def summary(self):
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for l in getattr(self, "lines", []):
+            f = [x.strip() for x in l.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, f[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- distributed plumbing
+def dist_setup(n_gpus):
+    import torch
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world != n_gpus and world > 1:
+        raise SystemExit(f"--gpus {n_gpus} but WORLD_SIZE={world}")
+    if world > 1:
+        import datetime
+
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    elif torch.cuda.is_available():
+        torch.cuda.set_device(0)
+    return rank, world, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def allreduce_max(x, world):
+    import torch
+
+    if world == 1:
+        return x
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return t.item()
+
+
+# ---------------------------------------------------------------- timing
+def time_steps(fn, steps, warmup, flush, world):
+    """Warm up, then time exactly `steps` calls of fn, each bracketed by CUDA
+    events on the current stream, with an L2 flush (a 256 MB write) between
+    calls outside the events.  Returns per-step ms (mean) as max over ranks."""
+    import torch
+
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    evs = []
+    for _ in range(steps):
+        flush.zero_()
+        a = torch.cuda.Event(enable_timing=True)
+        b = torch.cuda.Event(enable_timing=True)
+        a.record()
+        fn()
+        b.record()
+        evs.append((a, b))
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    ms = sum(a.elapsed_time(b) for a, b in evs) / steps
+    return allreduce_max(ms, world)
+
+
+# ---------------------------------------------------------------- CPU baseline (oracle port)
+def cpu_baseline(T_sample, H, bits, group, rank, k, reps_seconds=10.0, max_reps=5):
+    """The reference's algorithm restated in oracle/ (C, OpenMP over tokens),
+    encode + decode of a T_sample-token slice of the config-2 activation."""
+    import numpy as np
+
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import oracle as O
+    import torch
+
+    from actcomp import synthetic
+
+    x, ch = synthetic.lowrank_activation(T_sample, H, n_outlier=k, seed=0)
+    xb = x.view(torch.int16).numpy().view(np.uint16)
+    rng = np.random.default_rng(0)
+    V = np.linalg.qr(rng.standard_normal((H, rank)))[0].astype(np.float32)
+    prep = O.basis_prepare(V)
+    idx = ch.numpy()
+    times = []
+    t_end = time.perf_counter() + reps_seconds
+    while len(times) < max_reps and (len(times) < 2 or time.perf_counter() < t_end):
+        t0 = time.perf_counter()
+        enc = O.encode(xb, prep, idx, bits, group, False)
+        O.decode(enc["codes"], enc["scales"], enc["lr_codes"], enc["lr_scale"], prep[1], enc["outliers"], idx, H,
+                 bits, group, False)
+        times.append(time.perf_counter() - t0)
+    t = statistics.median(times)
+    work = encode_bytes(T_sample, H, bits, group, rank, k) + decode_bytes(T_sample, H, bits, group, rank, k)
+    return {"value": work / t / 1e9, "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
+            "sample": f"oracle encode+decode of {T_sample} x {H} tokens (config-2 parameters), "
+                      f"median of {len(times)} runs, {t:.3f} s each"}
+
+
+def run_reference(args):
+    rank = int(os.environ.get("RANK", "0"))
+    cfg = {"workload": "config-2 encode+decode, 16384 x 4096 bf16 per rank, r=32 k=16 int4 g64",
+           "tokens_per_rank": 16384, "channels": 4096, "rank": 32, "n_outlier": 16, "bits": 4, "group": 64,
+           "global_batch": 16384 * args.gpus, "parallelism": f"token-shard x{args.gpus}"}
+    if rank != 0:
+        return
+    T_sample = 1024
+    H, bits, group, r, k = 4096, 4, 64, 32, 16
+    sys.path.insert(0, os.path.join(ROOT, "oracle"))
+    import numpy as np
+    import oracle as O
+    import torch
+
+    from actcomp import synthetic
+
+    x, ch = synthetic.lowrank_activation(T_sample, H, n_outlier=k, seed=0)
+    xb = x.view(torch.int16).numpy().view(np.uint16)
+    V = np.linalg.qr(np.random.default_rng(0).standard_normal((H, r)))[0].astype(np.float32)
+    prep = O.basis_prepare(V)
+    idx = ch.numpy()
+
+    def step():
+        enc = O.encode(xb, prep, idx, bits, group, False)
+        O.decode(enc["codes"], enc["scales"], enc["lr_codes"], enc["lr_scale"], prep[1], enc["outliers"], idx, H,
+                 bits, group, False)
+
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        step()
+    dt = (time.perf_counter() - t0) / args.steps
+    work = encode_bytes(T_sample, H, bits, group, r, k) + decode_bytes(T_sample, H, bits, group, r, k)
+    v = work / dt / 1e9
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "GB/s", "n_gpus": args.gpus,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3, "higher_is_better": True,
+            "scaling": "weak", "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "config": cfg,
+            "cpu_baseline": {"value": v, "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
+                             "sample": f"oracle encode+decode of {T_sample} x {H} per step (the reference's "
+                                       "algorithm restated in C, OpenMP over tokens; the reference itself is "
+                                       "Triton/PyTorch and has no CPU path that runs here)"},
+            "e2e": {"value": v, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- GPU arm
+def run_gpu(args):
+    import torch
+
+    import actcomp
+    from actcomp import synthetic
+
+    rank, world, local = dist_setup(args.gpus)
+    dev = torch.device("cuda", torch.cuda.current_device())
+    T, H, H2, N = args.tokens, 4096, 11008, 11008
+    bits, group, r, k = 4, 64, 32, 16
+    pk, peak_kind = peaks()
+
+    # calibration (off the timed path): basis and outlier channels from a seed-0 sample shared by all ranks
+    xcal, ch = synthetic.lowrank_activation(min(T, 4096), H, n_outlier=k, seed=0, device=dev, outlier_seed=0)
+    basis = actcomp.Basis.fit(xcal, r)
+    idx = actcomp.select_outlier_channels(xcal, k)
+    x, _ = synthetic.lowrank_activation(T, H, n_outlier=k, seed=rank, device=dev, outlier_seed=0)
+    del xcal
+    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+
+    state = {}
+
+    def step():
+        c = actcomp.encode(x, basis, idx, bits=bits, group=group)
+        state["xh"] = actcomp.decode(c)
+        state["c"] = c
+
+    def enc_only():
+        state["c"] = actcomp.encode(x, basis, idx, bits=bits, group=group)
+
+    step()
+    c0 = state["c"]
+
+    def dec_only():
+        actcomp.decode(c0, out=state["xh"].view(1, T, H))
+
+    with ClockSampler(physical_gpu(local)) as clk:
+        ms_step = time_steps(step, args.steps, args.warmup, flush, world)
+        ms_enc = time_steps(enc_only, args.steps, 1, flush, world)
+        ms_dec = time_steps(dec_only, args.steps, 1, flush, world)
+    clocks = clk.summary()
+
+    eb = encode_bytes(T, H, bits, group, r, k)
+    db = decode_bytes(T, H, bits, group, r, k)
+    value = world * (eb + db) / (ms_step * 1e-3) / 1e9
+    hbm = pk.get("hbm_gbs", FALLBACK_PEAKS["hbm_gbs"])
+    enc_gbs = eb / (ms_enc * 1e-3) / 1e9
+    dec_gbs = db / (ms_dec * 1e-3) / 1e9
+    dom = ("encode", ms_enc, eb) if ms_enc >= ms_dec else ("decode", ms_dec, db)
+    achieved = dom[2] / (dom[1] * 1e-3) / 1e9
+
+    # error statistics of the reconstruction, all-reduced over ranks (the only collective)
+    stats = actcomp.error_stats(state["xh"], x)
+    if world > 1:
+        import torch.distributed as dist
+
+        s2 = stats[:2].clone()
+        dist.all_reduce(s2)
+        m = stats[2:3].clone()
+        dist.all_reduce(m, op=dist.ReduceOp.MAX)
+        stats = torch.cat([s2, m, stats[3:]])
+    st = stats.cpu().tolist()
+
+    components = {"encode": {"ms": ms_enc, "GB/s": enc_gbs, "frac_of_hbm": enc_gbs / hbm, "bytes": eb},
+                  "decode": {"ms": ms_dec, "GB/s": dec_gbs, "frac_of_hbm": dec_gbs / hbm, "bytes": db}}
+
+    if not args.skip_extra:
+        # fused SiLU backward on the 16384 x 11008 SiLU input (config 2)
+        x2, _ = synthetic.lowrank_activation(T, H2, n_outlier=k, seed=100 + rank, device=dev, outlier_seed=100)
+        b2 = actcomp.Basis.fit(x2[: min(T, 4096)], r)
+        i2 = actcomp.select_outlier_channels(x2, k)
+        c2 = actcomp.encode(x2, b2, i2, bits=bits, group=group)
+        del x2
+        dy2 = synthetic.gradient((T, H2), seed=7 + rank, device=dev)
+        ms_silu = time_steps(lambda: actcomp.silu_backward(c2, dy2), args.steps, 1, flush, world)
+        sb = consumer_bytes(T, H2, bits, group, r, k)
+        components["silu_bwd_fused_16384x11008"] = {"ms": ms_silu, "GB/s": sb / (ms_silu * 1e-3) / 1e9,
+                                                    "frac_of_hbm": sb / (ms_silu * 1e-3) / 1e9 / hbm, "bytes": sb}
+        del c2, dy2
+        # fused dequant + dW GEMM (config 4): dW (4096 x 11008) = Xhat^T dY, K = 16384 tokens
+        dy = synthetic.gradient((T, N), seed=11 + rank, device=dev)
+        ws = torch.empty(actcomp._lib.load().actcomp_cg_dw_workspace(__import__("ctypes").byref(c0.desc()), N),
+                         dtype=torch.uint8, device=dev)
+        ms_dw = time_steps(lambda: actcomp.weight_grad(c0, dy, torch.float32, ws), max(3, args.steps // 2), 1,
+                           flush, world)
+        flops = 2.0 * H * N * T
+        tf = flops / (ms_dw * 1e-3) / 1e12
+        components["dw_gemm_fused_4096x11008_k16384"] = {
+            "ms": ms_dw, "TFLOP/s": tf, "frac_of_bf16_peak": tf / pk.get("bf16_tflops", 1590.0), "flops": flops}
+        del dy, ws
+
+    # end to end through the public API with host buffers: pinned X -> H2D -> encode -> decode -> D2H
+    xh_host = torch.empty((T, H), dtype=torch.bfloat16, pin_memory=True)
+    x_host = x.cpu().pin_memory()
+    x_dev = torch.empty_like(x)
+
+    def e2e_step():
+        x_dev.copy_(x_host, non_blocking=True)
+        c = actcomp.encode(x_dev, basis, idx, bits=bits, group=group)
+        xh_host.copy_(actcomp.decode(c), non_blocking=True)
+
+    ms_e2e = time_steps(e2e_step, max(3, args.steps // 2), 2, flush, world)
+    e2e_val = world * (eb + db) / (ms_e2e * 1e-3) / 1e9
+
+    if rank == 0:
+        traffic = None
+        tp = os.path.join(ROOT, "profiles", "traffic.json")
+        if os.path.exists(tp):
+            traffic = json.load(open(tp)).get(dom[0])
+        line = {
+            "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+            "warmup": args.warmup, "ms_per_step": ms_step, "higher_is_better": True, "scaling": "weak",
+            "vs_baseline": None, "dtype": "bf16", "data": "synthetic (seeded, config-2 generator)",
+            "config": {"workload": "config-2 encode+decode, 16384 x 4096 bf16 per rank, r=32 k=16 int4 g64",
+                       "tokens_per_rank": T, "channels": H, "rank": r, "n_outlier": k, "bits": bits,
+                       "group": group, "global_batch": T * world, "parallelism": f"token-shard x{world}",
+                       "l2": "256 MB write between timed steps (outside the events)"},
+            "roofline": {"bound": "hbm", "kernel": dom[0], "achieved": achieved, "peak": hbm, "unit": "GB/s",
+                         "frac": achieved / hbm, "traffic": traffic, "peak_kind": peak_kind,
+                         "algorithmic_bytes_per_launch": dom[2]},
+            "clocks": clocks,
+            "e2e": {"value": e2e_val, "unit": "GB/s", "h2d_bytes_per_step": T * H * 2,
+                    "d2h_bytes_per_step": T * H * 2},
+            "gpu_launches": args.steps * launches_per_step(),
+            "components": components,
+            "error": {"rel_fro": (st[0] / st[1]) ** 0.5 if st[1] else None, "max_abs": st[2],
+                      "changed_values": st[3]},
+        }
+        if not args.no_cpu_baseline:
+            line["cpu_baseline"] = cpu_baseline(2048, H, bits, group, r, k)
+        print(json.dumps(line), flush=True)
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.destroy_process_group()
+
+
+def physical_gpu(local: int) -> int:
+    vis = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
+    if vis and local < len(vis) and vis[local].strip().isdigit():
+        return int(vis[local])
+    return local
+
+
+def launches_per_step():
+    """Kernels of this library launched by one encode + decode."""
+    return 3  # projection, residual quantisation, decode
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", default="actcomp", choices=["actcomp", "reference"])
+    ap.add_argument("--tokens", type=int, default=16384, help="tokens per rank (profiling runs use fewer)")
+    ap.add_argument("--skip-extra", action="store_true", help="only the encode/decode step")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.warmup < 3 and not args.skip_extra:
+        args.warmup = 3
+    if args.impl == "reference":
+        return run_reference(args)
+    return run_gpu(args)
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,447 @@
+/*
+ * actcomp_oracle.c -- CPU restatement of the activation-compression hot path.
+ *
+ * TEST INFRASTRUCTURE ONLY.  This file is the checker that the CUDA kernels in
+ * triton-kernel-test_b200/csrc are compared against.  Only tests/, the smoke()
+ * entry point and bench.py's CPU-baseline leg may load it; the product path
+ * never calls it and has no CPU fallback.
+ *
+ * Two algorithm families are restated here:
+ *
+ *  (1) Reference-compat ("rc_*"): the reference's own encode/decode,
+ *      low_rank_extraction_fuse_compression_quantization.py:13-115 (Triton
+ *      kernel K2) and :153-171 (PyTorch twin),
+ *      low_rank_extraction_fuse_decompression_dequantization.py:13-113 (kernel
+ *      K3) and :155-165 (twin), low_rank_kernel_accuracy_test.py:6-16 (naive
+ *      end-to-end).  The Triton kernel and the PyTorch twin disagree in five
+ *      places; each is a flag (RC_* below) so the oracle can reproduce either.
+ *      Pinned against the reference's runnable PyTorch functions by the
+ *      fixtures in tests/golden (made by tests/golden/make_golden.py).
+ *
+ *  (2) Channel-group format ("cg_*"): the encode the north star describes --
+ *      rank-r projection onto a basis V, top-k outlier channels kept verbatim,
+ *      optional 128-wide Walsh-Hadamard rotation, int4/int8 codes with
+ *      per-token group-absmax scales.  The reference has no code for this
+ *      variant (its closest relatives are extraction_outlier_channel.py:11-14
+ *      for the channel gather and the encode math of K2), so this part of the
+ *      oracle is "parity unpinned" by the reference; it is pinned by its own
+ *      algebraic properties (tests/test_oracle.py).
+ *
+ * Every floating-point step below is a single IEEE-754 binary32 operation with
+ * round-to-nearest-even, in the order written, so the CUDA kernels can match
+ * it bit for bit.  The only exception is cg_project (a K=H reduction whose
+ * order the tensor cores choose); it is computed in binary64 and the tests
+ * compare the GPU's low-rank codes to it within one code step.
+ *
+ * Build: oracle/Makefile -> oracle/_build/libactcomp_oracle.so
+ */
+#include <math.h>
+#include <stdint.h>
+#include <stdlib.h>
+#include <string.h>
+
+/* ------------------------------------------------------------------ bf16 */
+static inline float bf2f(uint16_t h) {
+    uint32_t u = ((uint32_t)h) << 16;
+    float f;
+    memcpy(&f, &u, 4);
+    return f;
+}
+static inline uint16_t f2bf(float f) {
+    uint32_t u;
+    memcpy(&u, &f, 4);
+    if ((u & 0x7fffffffu) > 0x7f800000u) return 0x7fc0; /* NaN */
+    u += 0x7fffu + ((u >> 16) & 1u);
+    return (uint16_t)(u >> 16);
+}
+static inline float rne_bf(float f) { return bf2f(f2bf(f)); }
+
+/* ============================================================ channel-group
+ * Basis preparation.  V is H x r (column j = basis vector j).
+ *   sV[j]    = max_c |V[c,j]| / 127                     (binary32 division)
+ *   Vq[c,j]  = clamp(rint(V[c,j] / sV[j]), -127, 127)   (0 when sV[j] == 0)
+ *   Vt[j,c]  = bf16_rne(V[c,j])                          (projection basis)
+ */
+void cg_basis_prepare(const float *V, int64_t H, int r, uint16_t *Vt, int8_t *Vq, float *sV) {
+    for (int j = 0; j < r; ++j) {
+        float amax = 0.f;
+        for (int64_t c = 0; c < H; ++c) {
+            float a = fabsf(V[c * r + j]);
+            if (a > amax) amax = a;
+        }
+        float s = amax / 127.0f;
+        sV[j] = s;
+        for (int64_t c = 0; c < H; ++c) {
+            float v = V[c * r + j];
+            int q = 0;
+            if (s > 0.f) {
+                float t = rintf(v / s);
+                if (t > 127.f) t = 127.f;
+                if (t < -127.f) t = -127.f;
+                q = (int)t;
+            }
+            Vq[c * r + j] = (int8_t)q;
+            Vt[(int64_t)j * H + c] = f2bf(v);
+        }
+    }
+}
+
+/* L[t,j] = sum_c X[t,c] * Vt[j,c], accumulated in binary64, rounded once. */
+void cg_project(const void *X, int x_f32, int64_t T, int64_t H, int64_t ldx, const uint16_t *Vt, int r,
+                float *L) {
+#pragma omp parallel for schedule(static)
+    for (int64_t t = 0; t < T; ++t) {
+        for (int j = 0; j < r; ++j) {
+            double acc = 0.0;
+            for (int64_t c = 0; c < H; ++c) {
+                double xv = x_f32 ? (double)((const float *)X)[t * ldx + c]
+                                  : (double)bf2f(((const uint16_t *)X)[t * ldx + c]);
+                acc += xv * (double)bf2f(Vt[(int64_t)j * H + c]);
+            }
+            L[t * r + j] = (float)acc;
+        }
+    }
+}
+
+/* Per-token quantisation of the low-rank coefficients.
+ *   Lt[j]  = L[t,j] * sV[j]
+ *   sL[t]  = max_j |Lt[j]| / 127
+ *   Lq[t,j]= clamp(rint(Lt[j] / sL[t]), -127, 127)      (0 when sL == 0)   */
+void cg_lr_quantize(const float *L, int64_t T, int r, const float *sV, int8_t *Lq, float *sL) {
+#pragma omp parallel for schedule(static)
+    for (int64_t t = 0; t < T; ++t) {
+        float lt[256];
+        float amax = 0.f;
+        for (int j = 0; j < r; ++j) {
+            lt[j] = L[t * r + j] * sV[j];
+            float a = fabsf(lt[j]);
+            if (a > amax) amax = a;
+        }
+        float s = amax / 127.0f;
+        sL[t] = s;
+        for (int j = 0; j < r; ++j) {
+            int q = 0;
+            if (s > 0.f) {
+                float v = rintf(lt[j] / s);
+                if (v > 127.f) v = 127.f;
+                if (v < -127.f) v = -127.f;
+                q = (int)v;
+            }
+            Lq[t * r + j] = (int8_t)q;
+        }
+    }
+}
+
+/* P[t,c] = (float)(sum_j Lq[t,j]*Vq[c,j]) * sL[t]; the integer sum is exact. */
+static inline float lowrank_term(const int8_t *lq, const int8_t *vq, int r, float sl) {
+    int32_t acc = 0;
+    for (int j = 0; j < r; ++j) acc += (int32_t)lq[j] * (int32_t)vq[j];
+    return (float)acc * sl;
+}
+
+/* Unnormalised 128-point Walsh-Hadamard butterflies, stage m = 1,2,...,64:
+ * (x[i], x[i+m]) <- (x[i] + x[i+m], x[i] - x[i+m]) for (i & m) == 0.       */
+static void wht128(float *x) {
+    for (int m = 1; m < 128; m <<= 1)
+        for (int i = 0; i < 128; ++i)
+            if (!(i & m)) {
+                float a = x[i], b = x[i + m];
+                x[i] = a + b;
+                x[i + m] = a - b;
+            }
+}
+
+/* Encode one token row given its low-rank codes (see file header, part 2).
+ * X row -> codes (H*bits/8 bytes), scales (H/group), outliers (k values).
+ *   R[c]   = X[c] - P[c]                       (binary32)
+ *   O[j]   = X[idx[j]] (verbatim);  R[idx[j]] = 0
+ *   W      = wht ? WHT128(R) per 128-block : R
+ *   s      = max_{c in group} |W[c]| / qmax,  qmax = 2^(bits-1) - 1
+ *   q      = clamp(rint(W[c] / s), -qmax, qmax)   (0 when s == 0)
+ *   u      = q + 2^(bits-1); int4 packs channel 2i in the low nibble.      */
+void cg_encode_given_lr(const void *X, int x_f32, int64_t T, int64_t H, int64_t ldx, const int8_t *Lq,
+                        const float *sL, const int8_t *Vq, int r, const int32_t *idx, int k, int bits,
+                        int group, int wht, uint8_t *codes, float *scales, void *outl) {
+    const int qmax = (1 << (bits - 1)) - 1;
+    const int off = 1 << (bits - 1);
+    const int64_t row_bytes = H * bits / 8;
+    const int64_t ngroups = H / group;
+#pragma omp parallel
+    {
+        float *w = (float *)malloc(sizeof(float) * (size_t)H);
+#pragma omp for schedule(static)
+        for (int64_t t = 0; t < T; ++t) {
+            for (int64_t c = 0; c < H; ++c) {
+                float xv = x_f32 ? ((const float *)X)[t * ldx + c] : bf2f(((const uint16_t *)X)[t * ldx + c]);
+                float p = r ? lowrank_term(Lq + t * r, Vq + c * r, r, sL[t]) : 0.f;
+                w[c] = xv - p;
+            }
+            for (int j = 0; j < k; ++j) {
+                int64_t c = idx[j];
+                if (x_f32)
+                    ((float *)outl)[t * k + j] = ((const float *)X)[t * ldx + c];
+                else
+                    ((uint16_t *)outl)[t * k + j] = ((const uint16_t *)X)[t * ldx + c];
+                w[c] = 0.f;
+            }
+            if (wht)
+                for (int64_t b = 0; b < H; b += 128) wht128(w + b);
+            uint8_t *crow = codes + t * row_bytes;
+            if (bits == 4) memset(crow, 0, (size_t)row_bytes);
+            for (int64_t gi = 0; gi < ngroups; ++gi) {
+                float amax = 0.f;
+                for (int c = 0; c < group; ++c) {
+                    float a = fabsf(w[gi * group + c]);
+                    if (a > amax) amax = a;
+                }
+                float s = amax / (float)qmax;
+                scales[t * ngroups + gi] = s;
+                for (int c = 0; c < group; ++c) {
+                    int64_t cc = gi * group + c;
+                    int q = 0;
+                    if (s > 0.f) {
+                        float v = rintf(w[cc] / s);
+                        if (v > (float)qmax) v = (float)qmax;
+                        if (v < -(float)qmax) v = -(float)qmax;
+                        q = (int)v;
+                    }
+                    unsigned u = (unsigned)(q + off);
+                    if (bits == 8)
+                        crow[cc] = (uint8_t)u;
+                    else
+                        crow[cc >> 1] |= (uint8_t)(u << ((cc & 1) * 4));
+                }
+            }
+        }
+        free(w);
+    }
+}
+
+/* Decode (see file header, part 2):
+ *   w  = (float)(u - 2^(bits-1)) * s
+ *   r^ = wht ? WHT128(w) * (1/128) : w
+ *   x^ = out_dtype(r^ + P);  x^[idx[j]] = O[j] verbatim.                     */
+void cg_decode(const uint8_t *codes, const float *scales, const int8_t *Lq, const float *sL, const int8_t *Vq,
+               int r, const void *outl, const int32_t *idx, int k, int64_t T, int64_t H, int bits, int group,
+               int wht, int x_f32, void *Xhat) {
+    const int off = 1 << (bits - 1);
+    const int64_t row_bytes = H * bits / 8;
+    const int64_t ngroups = H / group;
+#pragma omp parallel
+    {
+        float *w = (float *)malloc(sizeof(float) * (size_t)H);
+#pragma omp for schedule(static)
+        for (int64_t t = 0; t < T; ++t) {
+            const uint8_t *crow = codes + t * row_bytes;
+            for (int64_t c = 0; c < H; ++c) {
+                unsigned u = bits == 8 ? crow[c] : ((crow[c >> 1] >> ((c & 1) * 4)) & 0xfu);
+                w[c] = (float)((int)u - off) * scales[t * ngroups + c / group];
+            }
+            if (wht)
+                for (int64_t b = 0; b < H; b += 128) {
+                    wht128(w + b);
+                    for (int i = 0; i < 128; ++i) w[b + i] = w[b + i] * 0.0078125f;
+                }
+            for (int64_t c = 0; c < H; ++c) {
+                float p = r ? lowrank_term(Lq + t * r, Vq + c * r, r, sL[t]) : 0.f;
+                float v = w[c] + p;
+                if (x_f32)
+                    ((float *)Xhat)[t * H + c] = v;
+                else
+                    ((uint16_t *)Xhat)[t * H + c] = f2bf(v);
+            }
+            for (int j = 0; j < k; ++j) {
+                int64_t c = idx[j];
+                if (x_f32)
+                    ((float *)Xhat)[t * H + c] = ((const float *)outl)[t * k + j];
+                else
+                    ((uint16_t *)Xhat)[t * H + c] = ((const uint16_t *)outl)[t * k + j];
+            }
+        }
+        free(w);
+    }
+}
+
+/* Column absmax of X (T x H) -> score[H]; top-k channel selection orders by
+ * score descending, ties by lower index, and returns the chosen indices in
+ * ascending channel order (extraction_outlier_channel.py:11-14 takes such an
+ * index list as its input).                                                 */
+void cg_channel_absmax(const uint16_t *X, int64_t T, int64_t H, int64_t ldx, float *score) {
+    for (int64_t c = 0; c < H; ++c) score[c] = 0.f;
+    for (int64_t t = 0; t < T; ++t)
+        for (int64_t c = 0; c < H; ++c) {
+            float a = fabsf(bf2f(X[t * ldx + c]));
+            if (a > score[c]) score[c] = a;
+        }
+}
+
+void cg_topk_channels(const float *score, int64_t H, int k, int32_t *idx) {
+    char *taken = (char *)calloc((size_t)H, 1);
+    for (int j = 0; j < k; ++j) {
+        int64_t best = -1;
+        for (int64_t c = 0; c < H; ++c) {
+            if (taken[c]) continue;
+            if (best < 0 || score[c] > score[best]) best = c;
+        }
+        if (best < 0) break;
+        taken[best] = 1;
+    }
+    int n = 0;
+    for (int64_t c = 0; c < H; ++c)
+        if (taken[c]) idx[n++] = (int32_t)c;
+    free(taken);
+}
+
+/* ============================================================ consumers
+ * Each takes the decoded bf16 activation and computes in binary32 exactly as
+ * written, rounding the result once to bf16.                                */
+
+/* silu_backward.py:6-8: g * (s * (1 + x * (1 - s))), s = sigmoid(x). */
+void orc_silu_bwd(const uint16_t *x, const uint16_t *g, int64_t n, uint16_t *out) {
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; ++i) {
+        float xv = bf2f(x[i]), gv = bf2f(g[i]);
+        float s = 1.0f / (1.0f + expf(-xv));
+        out[i] = f2bf(gv * (s * (1.0f + xv * (1.0f - s))));
+    }
+}
+
+/* gelu_backward.py:14-21 (tanh approximation). */
+void orc_gelu_bwd(const uint16_t *x, const uint16_t *g, int64_t n, uint16_t *out) {
+    const float gamma = 0.7978845608028654f, kappa = 0.044715f;
+#pragma omp parallel for schedule(static)
+    for (int64_t i = 0; i < n; ++i) {
+        float xv = bf2f(x[i]), gv = bf2f(g[i]);
+        float x2 = xv * xv;
+        float y = gamma * (xv + kappa * (x2 * xv));
+        float th = tanhf(y);
+        float d = 0.5f * ((1.0f + th) + xv * ((1.0f - th * th) * gamma * (1.0f + 3.0f * kappa * x2)));
+        out[i] = f2bf(d * gv);
+    }
+}
+
+/* extraction_fuse_hadamard.py:5 (elementwise product a*b). */
+void orc_mul(const uint16_t *a, const uint16_t *b, int64_t n, uint16_t *out) {
+    for (int64_t i = 0; i < n; ++i) out[i] = f2bf(bf2f(a[i]) * bf2f(b[i]));
+}
+
+/* softmax_backward.py:6: (g - sum_row(g*y)) * y, row sum in binary64. */
+void orc_softmax_bwd(const uint16_t *y, const uint16_t *g, int64_t rows, int64_t n, uint16_t *out) {
+#pragma omp parallel for schedule(static)
+    for (int64_t rr = 0; rr < rows; ++rr) {
+        double acc = 0.0;
+        for (int64_t c = 0; c < n; ++c) acc += (double)bf2f(y[rr * n + c]) * (double)bf2f(g[rr * n + c]);
+        float sum = (float)acc;
+        for (int64_t c = 0; c < n; ++c)
+            out[rr * n + c] = f2bf((bf2f(g[rr * n + c]) - sum) * bf2f(y[rr * n + c]));
+    }
+}
+
+/* C[M,N] = A^T B with A (K x M) and B (K x N) bf16, binary64 accumulation. */
+void orc_gemm_tn(const uint16_t *A, const uint16_t *B, int64_t M, int64_t N, int64_t K, float *C) {
+#pragma omp parallel for schedule(static)
+    for (int64_t m = 0; m < M; ++m) {
+        double *acc = (double *)calloc((size_t)N, sizeof(double));
+        for (int64_t kk = 0; kk < K; ++kk) {
+            double a = bf2f(A[kk * M + m]);
+            if (a == 0.0) continue;
+            const uint16_t *b = B + kk * N;
+            for (int64_t nn = 0; nn < N; ++nn) acc[nn] += a * (double)bf2f(b[nn]);
+        }
+        for (int64_t nn = 0; nn < N; ++nn) C[m * N + nn] = (float)acc[nn];
+        free(acc);
+    }
+}
+
+/* ============================================================ reference-compat
+ * Flags selecting the PyTorch-twin behaviour where it differs from the
+ * Triton kernel (the default, which is what the reference's public
+ * functions run):                                                           */
+#define RC_TWIN_LOWRANK 1  /* x - bf16(l@r) in bf16 (twin :154) vs one rounding of x - l@r (kernel :63-78) */
+#define RC_HALF_EVEN 2     /* torch.round (twin :160) vs libdevice round, half away (kernel :97)          */
+#define RC_SCALE_BATCH 4   /* s[b,:] (twin :159) vs s[0,:] for every batch (kernel :92-95 ignores stride) */
+#define RC_ROW_PACK 8      /* whole-row interleave (twin :165-167) vs 32-column blocks (kernel :103-112) */
+#define RC_OUTLIER_BF16 16 /* |x| > bf16(outlier) (torch scalar promotion) vs |x| > fp32(outlier)           */
+
+/* Column of packed byte and bit shift for element n of a row. */
+static inline void rc_pack_pos(int64_t n, int64_t N, int bits, int flags, int64_t *byte, int *shift) {
+    int epp = 8 / bits;
+    if (flags & RC_ROW_PACK) {
+        int64_t w = N / epp; /* bytes per row */
+        *byte = n % w;
+        *shift = (int)(n / w) * bits;
+    } else {
+        int64_t blk = n / 32, within = n % 32;
+        int64_t w = 32 / epp;
+        *byte = blk * w + within % w;
+        *shift = (int)(within / w) * bits;
+    }
+}
+
+/* dot of l[m,:] and r[:,n] as sequential binary32 FMAs from k = 0. */
+static inline float rc_dot(const uint16_t *l, const uint16_t *r, int64_t m, int64_t n, int K, int64_t N) {
+    float d = 0.f;
+    for (int kk = 0; kk < K; ++kk) d = fmaf(bf2f(l[m * K + kk]), bf2f(r[(int64_t)kk * N + n]), d);
+    return d;
+}
+
+/* low_rank_addition_fuse_compression_quantization (reference
+ * low_rank_extraction_fuse_compression_quantization.py:118-150, kernel
+ * :13-115).  x (B,M,N) with strides (sxb, sxm, 1); l (M,K); r (K,N); s
+ * (s_rows,N).  Writes the dense outlier tensor o (B,M,N), the packed codes q
+ * (B,M,N*bits/8) and, if non-null, the signed codes before the offset.     */
+void rc_encode(const uint16_t *l, const uint16_t *r, const uint16_t *x, int64_t sxb, int64_t sxm, const uint16_t *s,
+               int64_t s_rows, int64_t B, int64_t M, int64_t N, int K, int bits, float outlier, int flags, uint16_t *o,
+               uint8_t *q, int32_t *signed_codes) {
+    const int lo = -(1 << (bits - 1)), hi = (1 << (bits - 1)) - 1, off = 1 << (bits - 1);
+    const int64_t qrow = N * bits / 8;
+    const float thr = (flags & RC_OUTLIER_BF16) ? rne_bf(outlier) : outlier;
+    memset(q, 0, (size_t)(B * M * qrow));
+    for (int64_t b = 0; b < B; ++b)
+        for (int64_t m = 0; m < M; ++m)
+            for (int64_t n = 0; n < N; ++n) {
+                float xv = bf2f(x[b * sxb + m * sxm + n]);
+                float d = rc_dot(l, r, m, n, K, N);
+                float res = (flags & RC_TWIN_LOWRANK) ? rne_bf(xv - rne_bf(d)) : rne_bf(xv - d);
+                float ov = fabsf(res) > thr ? res : 0.f;
+                o[(b * M + m) * N + n] = f2bf(ov);
+                float xr = res - ov; /* exact: res or 0 */
+                int64_t srow = (flags & RC_SCALE_BATCH) ? (s_rows > 1 ? b : 0) : 0;
+                float sv = bf2f(s[srow * N + n]);
+                float t = rne_bf(xr / sv);
+                float rq = (flags & RC_HALF_EVEN) ? rintf(t) : roundf(t);
+                if (rq < (float)lo) rq = (float)lo;
+                if (rq > (float)hi) rq = (float)hi;
+                int code = (int)rq;
+                if (signed_codes) signed_codes[(b * M + m) * N + n] = code;
+                int64_t byte;
+                int shift;
+                rc_pack_pos(n, N, bits, flags, &byte, &shift);
+                q[(b * M + m) * qrow + byte] |= (uint8_t)((unsigned)(code + off) << shift);
+            }
+}
+
+/* low_rank_addition_fuse_decompression_dequantization (reference
+ * low_rank_extraction_fuse_decompression_dequantization.py:116-152, kernel
+ * :13-113).  o may be NULL (the outlier-free variants used by the fused
+ * consumers, extraction_fuse_hadamard.py:220-314).                          */
+void rc_decode(const uint16_t *l, const uint16_t *r, const uint8_t *q, const uint16_t *o, const uint16_t *s,
+               int64_t s_rows, int64_t B, int64_t M, int64_t N, int K, int bits, int flags, uint16_t *x) {
+    const int off = 1 << (bits - 1);
+    const unsigned mask = (1u << bits) - 1u;
+    const int64_t qrow = N * bits / 8;
+    for (int64_t b = 0; b < B; ++b)
+        for (int64_t m = 0; m < M; ++m)
+            for (int64_t n = 0; n < N; ++n) {
+                int64_t byte;
+                int shift;
+                rc_pack_pos(n, N, bits, flags, &byte, &shift);
+                unsigned u = (q[(b * M + m) * qrow + byte] >> shift) & mask;
+                int64_t srow = (flags & RC_SCALE_BATCH) ? (s_rows > 1 ? b : 0) : 0;
+                float w = rne_bf((float)((int)u - off) * bf2f(s[srow * N + n]));
+                float a = o ? rne_bf(w + bf2f(o[(b * M + m) * N + n])) : w;
+                float d = rc_dot(l, r, m, n, K, N);
+                float v = (flags & RC_TWIN_LOWRANK) ? rne_bf(a + rne_bf(d)) : rne_bf(a + d);
+                x[(b * M + m) * N + n] = f2bf(v);
+            }
+}

@@ -1,0 +1,162 @@
+"""GPU parity of the channel-group format against the CPU oracle.
+
+Protocol: the basis quantisation, the residual codes, scales and outliers
+given the kernel's low-rank codes, and every reconstruction are bit-exact.
+The low-rank codes themselves come from a length-H tensor-core reduction
+whose order is the hardware's; they must agree with the oracle's binary64
+projection to within one code step (and almost all exactly)."""
+import numpy as np
+import pytest
+import torch
+
+from conftest import bits, to_bf16
+
+pytestmark = pytest.mark.gpu
+
+
+def make_case(O, T, H, r, k, seed=0):
+    from actcomp import synthetic
+
+    x, ch = synthetic.lowrank_activation(T, H, signal_rank=24, n_outlier=max(k, 1), seed=seed)
+    xb = bits(x)
+    V = np.zeros((H, 0), np.float32)
+    if r:
+        _, _, vt = np.linalg.svd(O.bf16_to_f32(xb).astype(np.float64), full_matrices=False)
+        V = vt[:r].T.astype(np.float32)
+    idx = O.topk_channels(O.channel_absmax(xb), k) if k else np.zeros(0, np.int32)
+    return xb, V, idx
+
+
+def gpu_encode(xb, V, idx, bits_, group, wht):
+    import actcomp
+
+    x = to_bf16(xb)
+    basis = actcomp.Basis.from_vectors(torch.from_numpy(V).cuda()) if V.shape[1] else None
+    oi = torch.from_numpy(idx).cuda() if len(idx) else None
+    c = actcomp.encode(x, basis, oi, bits=bits_, group=group, wht=wht)
+    torch.cuda.synchronize()
+    return c
+
+
+CASES = [
+    # T, H, r, k, bits, group, wht
+    (256, 512, 32, 16, 4, 64, False),   # config-2 style
+    (128, 640, 16, 0, 4, 128, True),    # config-3 style (rotation, no outliers)
+    (96, 384, 16, 8, 8, 128, False),    # config-1 style (int8 g128)
+    (37, 320, 32, 5, 4, 64, False),     # ragged: T not a multiple of anything, H % 128 != 0
+    (64, 256, 0, 0, 4, 32, False),      # no low rank, no outliers
+    (64, 256, 64, 64, 8, 64, False),    # maximum rank and outlier count
+    (50, 1024, 48, 3, 4, 128, True),
+]
+
+
+@pytest.mark.parametrize("T,H,r,k,b,g,wht", CASES)
+def test_encode_decode_parity(O, T, H, r, k, b, g, wht):
+    xb, V, idx = make_case(O, T, H, r, k)
+    c = gpu_encode(xb, V, idx, b, g, wht)
+    if r:
+        Vt, Vq, sV = O.basis_prepare(V)
+        assert np.array_equal(bits(c.basis.basis_t[0]), Vt)
+        assert np.array_equal(c.basis.basis_q[0].cpu().numpy(), Vq)
+        assert np.array_equal(c.basis.basis_scale[0].cpu().numpy(), sV)
+        Lq_o, sL_o = O.lr_quantize(O.project(xb, Vt), sV)
+        Lq = c.lr_codes.cpu().numpy()
+        sL = c.lr_scale.cpu().numpy()
+        assert np.abs(Lq.astype(int) - Lq_o.astype(int)).max() <= 1
+        assert (Lq == Lq_o).mean() > 0.98
+        np.testing.assert_allclose(sL, sL_o, rtol=1e-5)
+    else:
+        Vq = np.zeros((H, 0), np.int8)
+        Lq = sL = None
+    codes, scales, outl = O.encode_given_lr(xb, Lq, sL, Vq, idx, b, g, wht)
+    assert np.array_equal(c.codes.cpu().numpy(), codes), "codes differ"
+    assert np.array_equal(c.scales.cpu().numpy(), scales), "scales differ"
+    if k:
+        assert np.array_equal(bits(c.outliers), outl)
+    # decode of the GPU buffers, bit for bit
+    import actcomp
+
+    xh = bits(actcomp.decode(c))
+    ref = O.decode(codes, scales, Lq, sL, Vq, outl if k else None, idx, H, b, g, wht)
+    assert np.array_equal(xh, ref)
+    # and the reconstruction is close to the input
+    assert O.rel_fro(xh, xb) < (0.06 if b == 4 else 0.01)
+
+
+@pytest.mark.parametrize("op", ["silu", "gelu", "mul"])
+@pytest.mark.parametrize("T,H,r,k,b,g,wht", [CASES[0], CASES[1], CASES[3]])
+def test_fused_consumers(O, op, T, H, r, k, b, g, wht):
+    import actcomp
+
+    xb, V, idx = make_case(O, T, H, r, k, seed=2)
+    c = gpu_encode(xb, V, idx, b, g, wht)
+    dy = (torch.randn(T, H, generator=torch.Generator().manual_seed(5)) * 0.02).to(torch.bfloat16)
+    fn = {"silu": actcomp.silu_backward, "gelu": actcomp.gelu_backward, "mul": actcomp.mul}[op]
+    out = bits(fn(c, dy.cuda()))
+    xh = bits(actcomp.decode(c))
+    ref = {"silu": O.silu_bwd, "gelu": O.gelu_bwd, "mul": O.mul}[op](xh, bits(dy))
+    assert O.rel_fro(out, ref) < 1e-3
+    assert (out == ref).mean() > 0.999
+
+
+@pytest.mark.parametrize("causal", [True, False])
+def test_softmax_backward_on_compressed_probabilities(O, causal):
+    import actcomp
+    from actcomp import synthetic
+
+    B, heads, S = 1, 3, 256
+    p = synthetic.causal_softmax(B, heads, S, seed=4) if causal else \
+        torch.softmax(torch.randn(B, heads, S, S, generator=torch.Generator().manual_seed(4)), -1).to(torch.bfloat16)
+    p3 = p.reshape(-1, S, S)
+    Vs = []
+    for h in range(p3.shape[0]):
+        _, _, vt = np.linalg.svd(p3[h].float().numpy().astype(np.float64), full_matrices=False)
+        Vs.append(vt[:32].T.astype(np.float32))
+    basis = actcomp.Basis.from_vectors(torch.from_numpy(np.stack(Vs)).cuda())
+    c = actcomp.encode(p3.cuda(), basis, None, bits=4, group=64)
+    dp = (torch.randn(p3.shape, generator=torch.Generator().manual_seed(6)) * 0.02).to(torch.bfloat16)
+    ds = bits(actcomp.softmax_backward(c, dp.cuda(), causal=causal))
+    ph = bits(actcomp.decode(c)).reshape(-1, S, S)
+    if causal:
+        ph = np.where(np.tril(np.ones((S, S), bool)), ph, np.uint16(0))
+    ref = O.softmax_bwd(ph, bits(dp))
+    assert O.rel_fro(ds, ref) < 1e-3
+
+
+@pytest.mark.parametrize("T,H,N", [(256, 256, 384), (512, 384, 200)])
+def test_weight_gradient(O, T, H, N):
+    import actcomp
+
+    xb, V, idx = make_case(O, T, H, 32, 8, seed=7)
+    c = gpu_encode(xb, V, idx, 4, 64, False)
+    dy = (torch.randn(T, N, generator=torch.Generator().manual_seed(8)) * 0.02).to(torch.bfloat16)
+    dw = actcomp.weight_grad(c, dy.cuda(), torch.float32).cpu().numpy()
+    xh = bits(actcomp.decode(c))
+    ref = O.gemm_tn(xh, bits(dy))
+    assert O.rel_fro(dw, ref) < 1e-5
+
+
+def test_channel_topk_matches_oracle(O):
+    import actcomp
+
+    xb, _, _ = make_case(O, 200, 768, 0, 0, seed=9)
+    for k in (1, 16, 64):
+        idx = actcomp.select_outlier_channels(to_bf16(xb), k).cpu().numpy()
+        assert list(idx) == list(O.topk_channels(O.channel_absmax(xb), k))
+
+
+def test_batched_slices_are_independent(O):
+    """batch > 1 with a different basis per slice equals per-slice encodes."""
+    import actcomp
+
+    xs, Vs = [], []
+    for s in range(3):
+        xb, V, _ = make_case(O, 64, 256, 16, 0, seed=20 + s)
+        xs.append(xb)
+        Vs.append(V)
+    basis = actcomp.Basis.from_vectors(torch.from_numpy(np.stack(Vs)).cuda())
+    c = actcomp.encode(to_bf16(np.stack(xs)), basis, None, bits=4, group=64)
+    xh = bits(actcomp.decode(c))
+    for s in range(3):
+        cs = gpu_encode(xs[s], Vs[s], np.zeros(0, np.int32), 4, 64, False)
+        assert np.array_equal(xh[s], bits(actcomp.decode(cs)))

@@ -1,0 +1,590 @@
+// cg_simt.cu -- channel-group format: basis preparation, top-k channel
+// selection, and the warp-cooperative encode / decode / consumer kernels.
+//
+// Layout of the work: one warp handles one (token, 128-channel chunk) item;
+// lane l owns the four consecutive channels chunk*128 + 4l .. 4l+3.  A 64- or
+// 128-channel quantisation group is then 16 or 32 lanes (shuffle reductions),
+// and one 128-point Walsh-Hadamard block is the whole warp (two in-register
+// butterfly stages, five shuffle stages).
+//
+// Arithmetic follows oracle/actcomp_oracle.c step for step (single binary32
+// operations, round-to-nearest-even, no contraction), so codes, scales and
+// reconstructions match it bit for bit; the low-rank term is an exact integer
+// dot product (dp4a) times the per-token scale.
+#include "common.cuh"
+
+namespace act {
+
+// ------------------------------------------------------------------ helpers
+struct CgSlice {
+    int64_t T, H;
+    int bits, group, rank, k, wht;
+    uint8_t *codes;
+    float *scales;
+    int8_t *lrq;
+    float *lrs;
+    uint16_t *outl;
+    const int32_t *idx;
+    const uint16_t *basis_t;
+    const int8_t *basis_q;
+    const float *basis_s;
+};
+
+__device__ __forceinline__ CgSlice slice_of(const actcomp_cg_desc &d, int b) {
+    CgSlice s;
+    s.T = d.tokens;
+    s.H = d.channels;
+    s.bits = d.bits;
+    s.group = d.group;
+    s.rank = d.rank;
+    s.k = d.n_outlier;
+    s.wht = d.wht;
+    const int64_t T = d.tokens, H = d.channels;
+    s.codes = d.codes + (int64_t)b * T * (H * d.bits / 8);
+    s.scales = d.scales + (int64_t)b * T * (H / d.group);
+    s.lrq = d.rank ? d.lr_codes + (int64_t)b * T * d.rank : nullptr;
+    s.lrs = d.rank ? d.lr_scale + (int64_t)b * T : nullptr;
+    s.outl = d.n_outlier ? d.outliers + (int64_t)b * T * d.n_outlier : nullptr;
+    s.idx = d.n_outlier ? d.outlier_idx + (int64_t)b * d.n_outlier : nullptr;
+    s.basis_t = d.rank ? d.basis_t + (int64_t)b * d.rank * H : nullptr;
+    s.basis_q = d.rank ? d.basis_q + (int64_t)b * H * d.rank : nullptr;
+    s.basis_s = d.rank ? d.basis_scale + (int64_t)b * d.rank : nullptr;
+    return s;
+}
+
+// exact low-rank integer term for channel c: sum_j lq[j] * Vq[c, j]
+__device__ __forceinline__ int32_t lr_dot(const uint32_t (&lw)[16], const int8_t *vq_row, int rank) {
+    int32_t acc = 0;
+    const uint4 *v = reinterpret_cast<const uint4 *>(vq_row);
+#pragma unroll
+    for (int w4 = 0; w4 < 4; ++w4) {
+        if (w4 * 16 < rank) {
+            uint4 q = __ldg(v + w4);
+            acc = __dp4a((int)lw[w4 * 4 + 0], (int)q.x, acc);
+            acc = __dp4a((int)lw[w4 * 4 + 1], (int)q.y, acc);
+            acc = __dp4a((int)lw[w4 * 4 + 2], (int)q.z, acc);
+            acc = __dp4a((int)lw[w4 * 4 + 3], (int)q.w, acc);
+        }
+    }
+    return acc;
+}
+
+__device__ __forceinline__ void load_lr_row(const CgSlice &s, int64_t t, uint32_t (&lw)[16], float &sl) {
+#pragma unroll
+    for (int i = 0; i < 16; ++i) lw[i] = 0;
+    sl = 0.f;
+    if (s.rank) {
+        const uint4 *p = reinterpret_cast<const uint4 *>(s.lrq + t * s.rank);
+#pragma unroll
+        for (int w4 = 0; w4 < 4; ++w4)
+            if (w4 * 16 < s.rank) {
+                uint4 q = __ldg(p + w4);
+                lw[w4 * 4 + 0] = q.x;
+                lw[w4 * 4 + 1] = q.y;
+                lw[w4 * 4 + 2] = q.z;
+                lw[w4 * 4 + 3] = q.w;
+            }
+        sl = __ldg(s.lrs + t);
+    }
+}
+
+// 128-point unnormalised Walsh-Hadamard over a warp, lane owns v[0..3] =
+// elements 4*lane .. 4*lane+3.  Stage m: pair (i, i+m), i has bit m clear,
+// (a, b) -> (a + b, a - b); stages in increasing m, as in the oracle.
+__device__ __forceinline__ void wht128_warp(float (&v)[4], int lane) {
+    // m = 1: (0,1), (2,3)
+    {
+        float a0 = v[0], b0 = v[1], a1 = v[2], b1 = v[3];
+        v[0] = __fadd_rn(a0, b0);
+        v[1] = __fsub_rn(a0, b0);
+        v[2] = __fadd_rn(a1, b1);
+        v[3] = __fsub_rn(a1, b1);
+    }
+    // m = 2: (0,2), (1,3)
+    {
+        float a0 = v[0], b0 = v[2], a1 = v[1], b1 = v[3];
+        v[0] = __fadd_rn(a0, b0);
+        v[2] = __fsub_rn(a0, b0);
+        v[1] = __fadd_rn(a1, b1);
+        v[3] = __fsub_rn(a1, b1);
+    }
+    // m = 4 .. 64: partner lane = lane ^ (m / 4)
+#pragma unroll
+    for (int lm = 1; lm < 32; lm <<= 1) {
+        const bool upper = (lane & lm) != 0;
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            float other = __shfl_xor_sync(0xffffffffu, v[i], lm);
+            v[i] = upper ? __fsub_rn(other, v[i]) : __fadd_rn(v[i], other);
+        }
+    }
+}
+
+// first index j in [0, k) with idx[j] >= c (idx ascending)
+__device__ __forceinline__ int lower_bound_idx(const int32_t *idx, int k, int64_t c) {
+    int lo = 0, hi = k;
+    while (lo < hi) {
+        int mid = (lo + hi) >> 1;
+        if ((int64_t)idx[mid] < c) lo = mid + 1;
+        else hi = mid;
+    }
+    return lo;
+}
+
+// ------------------------------------------------------------------ basis
+__global__ void basis_prepare_kernel(const float *V, int64_t H, int rank, uint16_t *Vt, int8_t *Vq, float *sV) {
+    const int b = blockIdx.y;
+    const int j = blockIdx.x;  // one block per basis vector
+    const float *v = V + (int64_t)b * H * rank;
+    __shared__ float red[32];
+    float amax = 0.f;
+    for (int64_t c = threadIdx.x; c < H; c += blockDim.x) amax = fmaxf(amax, fabsf(v[c * rank + j]));
+    amax = warp_max(amax);
+    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
+    __syncthreads();
+    if (threadIdx.x < 32) {
+        float m = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
+        m = warp_max(m);
+        if (threadIdx.x == 0) red[0] = m;
+    }
+    __syncthreads();
+    const float s = __fdiv_rn(red[0], 127.0f);
+    if (threadIdx.x == 0) sV[(int64_t)b * rank + j] = s;
+    for (int64_t c = threadIdx.x; c < H; c += blockDim.x) {
+        float x = v[c * rank + j];
+        int q = 0;
+        if (s > 0.f) q = max(-127, min(127, __float2int_rn(__fdiv_rn(x, s))));
+        Vq[(int64_t)b * H * rank + c * rank + j] = (int8_t)q;
+        Vt[(int64_t)b * rank * H + (int64_t)j * H + c] = f2bf(x);
+    }
+}
+
+// ------------------------------------------------------------------ top-k channels
+__global__ void channel_absmax_kernel(const uint16_t *x, int64_t T, int64_t H, int64_t ldx, float *score) {
+    int64_t c = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (c >= H) return;
+    float m = 0.f;
+    for (int64_t t = blockIdx.y; t < T; t += gridDim.y) m = fmaxf(m, fabsf(bf2f(x[t * ldx + c])));
+    // scores are non-negative floats: their bit patterns order like unsigned ints
+    atomicMax(reinterpret_cast<unsigned int *>(score) + c, __float_as_uint(m));
+}
+
+// One block: k rounds of arg-max over H scores (ties -> lower index), then
+// the chosen set is written in ascending channel order.
+__global__ void topk_kernel(float *score, int64_t H, int k, int32_t *idx) {
+    __shared__ unsigned long long best[32];
+    __shared__ int chosen[64];
+    for (int round = 0; round < k; ++round) {
+        // key: score bits high, inverted index low -> max key = max score, min index
+        unsigned long long key = 0;
+        for (int64_t c = threadIdx.x; c < H; c += blockDim.x) {
+            float s = score[c];
+            if (s < 0.f) continue;  // taken
+            unsigned long long kk = ((unsigned long long)__float_as_uint(s) << 32) |
+                                    (unsigned long long)(0xffffffffu - (uint32_t)c);
+            key = kk > key ? kk : key;
+        }
+        for (int o = 16; o > 0; o >>= 1) {
+            unsigned long long other = __shfl_xor_sync(0xffffffffu, key, o);
+            key = other > key ? other : key;
+        }
+        if ((threadIdx.x & 31) == 0) best[threadIdx.x >> 5] = key;
+        __syncthreads();
+        if (threadIdx.x == 0) {
+            unsigned long long m = 0;
+            for (int w = 0; w < (int)(blockDim.x >> 5); ++w) m = best[w] > m ? best[w] : m;
+            int c = (int)(0xffffffffu - (uint32_t)(m & 0xffffffffu));
+            chosen[round] = c;
+            score[c] = -1.f;
+        }
+        __syncthreads();
+    }
+    if (threadIdx.x == 0) {
+        // insertion sort of <= 64 entries
+        for (int i = 1; i < k; ++i) {
+            int v = chosen[i], j = i - 1;
+            while (j >= 0 && chosen[j] > v) {
+                chosen[j + 1] = chosen[j];
+                --j;
+            }
+            chosen[j + 1] = v;
+        }
+        for (int i = 0; i < k; ++i) idx[i] = chosen[i];
+    }
+}
+
+// ------------------------------------------------------------------ encode
+// Projection and low-rank codes: one warp per token.  L = x . V (binary32
+// accumulation in lane-strided order), then the per-token int8 quantisation
+// of L * sV exactly as cg_lr_quantize.
+template <int RANK>
+__global__ void __launch_bounds__(256) cg_project_kernel(actcomp_cg_desc d, const uint16_t *x, int64_t ldx) {
+    const int b = blockIdx.y;
+    const CgSlice s = slice_of(d, b);
+    const int lane = threadIdx.x & 31;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const uint16_t *xs = x + (int64_t)b * s.T * ldx;
+    for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < s.T; t += warps) {
+        float acc[RANK];
+#pragma unroll
+        for (int j = 0; j < RANK; ++j) acc[j] = 0.f;
+        const uint16_t *xr = xs + t * ldx;
+        for (int64_t c = (int64_t)lane * 8; c < s.H; c += 256) {
+            uint4 xv = __ldg(reinterpret_cast<const uint4 *>(xr + c));
+            float xf[8];
+            const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                xf[2 * i] = __uint_as_float(xw[i] << 16);
+                xf[2 * i + 1] = __uint_as_float(xw[i] & 0xffff0000u);
+            }
+#pragma unroll
+            for (int j = 0; j < RANK; ++j) {
+                uint4 vv = __ldg(reinterpret_cast<const uint4 *>(s.basis_t + (int64_t)j * s.H + c));
+                const uint32_t vw[4] = {vv.x, vv.y, vv.z, vv.w};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    acc[j] = __fmaf_rn(xf[2 * i], __uint_as_float(vw[i] << 16), acc[j]);
+                    acc[j] = __fmaf_rn(xf[2 * i + 1], __uint_as_float(vw[i] & 0xffff0000u), acc[j]);
+                }
+            }
+        }
+        // lane j ends up with coefficient j (and j + 32 when RANK == 64)
+        float mine0 = 0.f, mine1 = 0.f;
+#pragma unroll
+        for (int j = 0; j < RANK; ++j) {
+            float v = warp_sum(acc[j]);
+            if (j == lane) mine0 = v;
+            if (j == lane + 32) mine1 = v;
+        }
+        const bool has0 = lane < RANK, has1 = lane + 32 < RANK;
+        float lt0 = has0 ? __fmul_rn(mine0, s.basis_s[lane]) : 0.f;
+        float lt1 = has1 ? __fmul_rn(mine1, s.basis_s[lane + 32]) : 0.f;
+        float amax = warp_max(fmaxf(fabsf(lt0), fabsf(lt1)));
+        float sl = __fdiv_rn(amax, 127.0f);
+        if (has0) {
+            int q = sl > 0.f ? max(-127, min(127, __float2int_rn(__fdiv_rn(lt0, sl)))) : 0;
+            s.lrq[t * RANK + lane] = (int8_t)q;
+        }
+        if (has1) {
+            int q = sl > 0.f ? max(-127, min(127, __float2int_rn(__fdiv_rn(lt1, sl)))) : 0;
+            s.lrq[t * RANK + lane + 32] = (int8_t)q;
+        }
+        if (lane == 0) s.lrs[t] = sl;
+    }
+}
+
+// Residual codes: one warp per (token, 128-channel chunk).
+template <int BITS>
+__global__ void __launch_bounds__(256) cg_quant_kernel(actcomp_cg_desc d, const uint16_t *x, int64_t ldx) {
+    const int b = blockIdx.y;
+    const CgSlice s = slice_of(d, b);
+    const int lane = threadIdx.x & 31;
+    const int64_t nchunk = (s.H + 127) / 128;
+    const int64_t items = s.T * nchunk;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const int qmax = (1 << (BITS - 1)) - 1, off = 1 << (BITS - 1);
+    const int glanes = s.group / 4;  // lanes per quantisation group
+    const int64_t ngroups = s.H / s.group;
+    const uint16_t *xs = x + (int64_t)b * s.T * ldx;
+    for (int64_t it = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); it < items; it += warps) {
+        const int64_t t = it / nchunk, ch = it % nchunk;
+        const int64_t c0 = ch * 128 + lane * 4;
+        const bool valid = c0 < s.H;
+        uint32_t lw[16];
+        float sl;
+        load_lr_row(s, t, lw, sl);
+        float w[4] = {0.f, 0.f, 0.f, 0.f};
+        uint2 xraw = make_uint2(0, 0);
+        if (valid) {
+            xraw = __ldg(reinterpret_cast<const uint2 *>(xs + t * ldx + c0));
+            const uint32_t xw[2] = {xraw.x, xraw.y};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float xv = __uint_as_float(i & 1 ? (xw[i >> 1] & 0xffff0000u) : (xw[i >> 1] << 16));
+                float p = 0.f;
+                if (s.rank) p = __fmul_rn(__int2float_rn(lr_dot(lw, s.basis_q + (c0 + i) * s.rank, s.rank)), sl);
+                w[i] = __fsub_rn(xv, p);
+            }
+        }
+        // outlier channels of this chunk: verbatim copy, residual zeroed
+        if (s.k) {
+            const int64_t cs = ch * 128, ce = cs + 128;
+            int j = lower_bound_idx(s.idx, s.k, cs);
+            for (; j < s.k && s.idx[j] < ce; ++j) {
+                const int64_t c = s.idx[j];
+                if (c >= c0 && c < c0 + 4 && valid) {
+                    const int i = (int)(c - c0);
+                    const uint32_t word = i < 2 ? xraw.x : xraw.y;
+                    s.outl[t * s.k + j] = (uint16_t)(i & 1 ? (word >> 16) : (word & 0xffffu));
+                    w[i] = 0.f;
+                }
+            }
+        }
+        if (s.wht) wht128_warp(w, lane);
+        float amax = fmaxf(fmaxf(fabsf(w[0]), fabsf(w[1])), fmaxf(fabsf(w[2]), fabsf(w[3])));
+        amax = group_max(amax, glanes);
+        const float sc = __fdiv_rn(amax, (float)qmax);
+        if (!valid) continue;
+        if ((lane % glanes) == 0) s.scales[t * ngroups + c0 / s.group] = sc;
+        uint32_t u[4];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            int q = sc > 0.f ? max(-qmax, min(qmax, __float2int_rn(__fdiv_rn(w[i], sc)))) : 0;
+            u[i] = (uint32_t)(q + off);
+        }
+        if constexpr (BITS == 4) {
+            uint16_t packed = (uint16_t)(u[0] | (u[1] << 4) | (u[2] << 8) | (u[3] << 12));
+            *reinterpret_cast<uint16_t *>(s.codes + t * (s.H / 2) + c0 / 2) = packed;
+        } else {
+            uint32_t packed = u[0] | (u[1] << 8) | (u[2] << 16) | (u[3] << 24);
+            *reinterpret_cast<uint32_t *>(s.codes + t * s.H + c0) = packed;
+        }
+    }
+}
+
+// ------------------------------------------------------------------ decode + consumers
+// Reconstruct four channels of one token (bit-exact with cg_decode) into bf16.
+template <int BITS>
+__device__ __forceinline__ void reconstruct4(const CgSlice &s, int64_t t, int64_t ch, int lane, bool valid,
+                                             const uint32_t (&lw)[16], float sl, uint16_t (&xh)[4]) {
+    const int off = 1 << (BITS - 1);
+    const int64_t c0 = ch * 128 + lane * 4;
+    float w[4] = {0.f, 0.f, 0.f, 0.f};
+    if (valid) {
+        uint32_t raw;
+        if constexpr (BITS == 4) raw = *reinterpret_cast<const uint16_t *>(s.codes + t * (s.H / 2) + c0 / 2);
+        else raw = *reinterpret_cast<const uint32_t *>(s.codes + t * s.H + c0);
+        const float sc = s.scales[t * (s.H / s.group) + c0 / s.group];
+#pragma unroll
+        for (int i = 0; i < 4; ++i) {
+            int u = (int)((raw >> (i * BITS)) & ((1u << BITS) - 1u));
+            w[i] = __fmul_rn(__int2float_rn(u - off), sc);
+        }
+    }
+    if (s.wht) {
+        wht128_warp(w, lane);
+#pragma unroll
+        for (int i = 0; i < 4; ++i) w[i] = __fmul_rn(w[i], 0.0078125f);
+    }
+#pragma unroll
+    for (int i = 0; i < 4; ++i) {
+        float p = 0.f;
+        if (s.rank && valid) p = __fmul_rn(__int2float_rn(lr_dot(lw, s.basis_q + (c0 + i) * s.rank, s.rank)), sl);
+        xh[i] = f2bf(__fadd_rn(w[i], p));
+    }
+    if (s.k) {
+        const int64_t cs = ch * 128, ce = cs + 128;
+        int j = lower_bound_idx(s.idx, s.k, cs);
+        for (; j < s.k && s.idx[j] < ce; ++j) {
+            const int64_t c = s.idx[j];
+            if (c >= c0 && c < c0 + 4) xh[c - c0] = s.outl[t * s.k + j];
+        }
+    }
+}
+
+template <int BITS, int OP>
+__global__ void __launch_bounds__(256) cg_consume_kernel(actcomp_cg_desc d, const uint16_t *y, int64_t ldy,
+                                                         uint16_t *out, int64_t ldo) {
+    const int b = blockIdx.y;
+    const CgSlice s = slice_of(d, b);
+    const int lane = threadIdx.x & 31;
+    const int64_t nchunk = (s.H + 127) / 128;
+    const int64_t items = s.T * nchunk;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const uint16_t *ys = OP != ACT_OP_DECODE ? y + (int64_t)b * s.T * ldy : nullptr;
+    uint16_t *os = out + (int64_t)b * s.T * ldo;
+    for (int64_t it = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); it < items; it += warps) {
+        const int64_t t = it / nchunk, ch = it % nchunk;
+        const int64_t c0 = ch * 128 + lane * 4;
+        const bool valid = c0 < s.H;
+        uint32_t lw[16];
+        float sl;
+        load_lr_row(s, t, lw, sl);
+        uint16_t xh[4];
+        reconstruct4<BITS>(s, t, ch, lane, valid, lw, sl, xh);
+        if (!valid) continue;
+        uint16_t o[4];
+        if constexpr (OP == ACT_OP_DECODE) {
+#pragma unroll
+            for (int i = 0; i < 4; ++i) o[i] = xh[i];
+        } else {
+            uint2 yr = __ldg(reinterpret_cast<const uint2 *>(ys + t * ldy + c0));
+            const uint32_t yw[2] = {yr.x, yr.y};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                float yv = __uint_as_float(i & 1 ? (yw[i >> 1] & 0xffff0000u) : (yw[i >> 1] << 16));
+                o[i] = f2bf(apply_op<OP>(bf2f(xh[i]), yv));
+            }
+        }
+        uint2 packed;
+        packed.x = (uint32_t)o[0] | ((uint32_t)o[1] << 16);
+        packed.y = (uint32_t)o[2] | ((uint32_t)o[3] << 16);
+        *reinterpret_cast<uint2 *>(os + t * ldo + c0) = packed;
+    }
+}
+
+// Softmax backward over compressed probabilities: one warp per row, two
+// sweeps (row sum of dP * P^, then the output).
+template <int BITS>
+__global__ void __launch_bounds__(256) cg_softmax_bwd_kernel(actcomp_cg_desc d, const uint16_t *dp, uint16_t *ds,
+                                                             int64_t ld, int causal) {
+    const int b = blockIdx.y;
+    const CgSlice s = slice_of(d, b);
+    const int lane = threadIdx.x & 31;
+    const int64_t nchunk = (s.H + 127) / 128;
+    const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
+    const uint16_t *dps = dp + (int64_t)b * s.T * ld;
+    uint16_t *dss = ds + (int64_t)b * s.T * ld;
+    for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < s.T; t += warps) {
+        uint32_t lw[16];
+        float sl;
+        load_lr_row(s, t, lw, sl);
+        const int64_t last = causal ? t : s.H - 1;  // last column with P != 0
+        const int64_t nch = causal ? (last / 128 + 1) : nchunk;
+        float acc = 0.f;
+        for (int64_t ch = 0; ch < nch; ++ch) {
+            const int64_t c0 = ch * 128 + lane * 4;
+            const bool valid = c0 < s.H;
+            uint16_t xh[4];
+            reconstruct4<BITS>(s, t, ch, lane, valid, lw, sl, xh);
+            if (!valid) continue;
+            uint2 g = __ldg(reinterpret_cast<const uint2 *>(dps + t * ld + c0));
+            const uint32_t gw[2] = {g.x, g.y};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                if (c0 + i > last) continue;
+                float gv = __uint_as_float(i & 1 ? (gw[i >> 1] & 0xffff0000u) : (gw[i >> 1] << 16));
+                acc = __fmaf_rn(bf2f(xh[i]), gv, acc);
+            }
+        }
+        const float sum = warp_sum(acc);
+        for (int64_t ch = 0; ch < nchunk; ++ch) {
+            const int64_t c0 = ch * 128 + lane * 4;
+            const bool valid = c0 < s.H;
+            uint16_t o[4] = {0, 0, 0, 0};
+            if (ch < nch) {
+                uint16_t xh[4];
+                reconstruct4<BITS>(s, t, ch, lane, valid, lw, sl, xh);
+                if (!valid) continue;
+                uint2 g = __ldg(reinterpret_cast<const uint2 *>(dps + t * ld + c0));
+                const uint32_t gw[2] = {g.x, g.y};
+#pragma unroll
+                for (int i = 0; i < 4; ++i) {
+                    if (c0 + i > last) continue;
+                    float gv = __uint_as_float(i & 1 ? (gw[i >> 1] & 0xffff0000u) : (gw[i >> 1] << 16));
+                    o[i] = f2bf(__fmul_rn(__fsub_rn(gv, sum), bf2f(xh[i])));
+                }
+            } else if (!valid) {
+                continue;
+            }
+            uint2 packed;
+            packed.x = (uint32_t)o[0] | ((uint32_t)o[1] << 16);
+            packed.y = (uint32_t)o[2] | ((uint32_t)o[3] << 16);
+            *reinterpret_cast<uint2 *>(dss + t * ld + c0) = packed;
+        }
+    }
+}
+
+// ------------------------------------------------------------------ validation
+int validate_desc(const actcomp_cg_desc *d) {
+    ACT_CHECK(d, ACT_E_INVALID);
+    ACT_CHECK(d->tokens >= 0 && d->channels > 0 && d->batch >= 1, ACT_E_INVALID);
+    ACT_CHECK(d->bits == 4 || d->bits == 8, ACT_E_UNSUPPORTED);
+    ACT_CHECK(d->group == 32 || d->group == 64 || d->group == 128, ACT_E_UNSUPPORTED);
+    ACT_CHECK(d->channels % d->group == 0, ACT_E_INVALID);
+    ACT_CHECK(d->rank >= 0 && d->rank <= 64 && d->rank % 16 == 0, ACT_E_UNSUPPORTED);
+    ACT_CHECK(d->n_outlier >= 0 && d->n_outlier <= 64 && d->n_outlier <= d->channels, ACT_E_UNSUPPORTED);
+    ACT_CHECK(d->wht == 0 || d->wht == 1, ACT_E_INVALID);
+    if (d->wht) ACT_CHECK(d->channels % 128 == 0, ACT_E_UNSUPPORTED);
+    ACT_CHECK(d->codes && d->scales, ACT_E_INVALID);
+    ACT_CHECK(aligned(d->codes, 4) && aligned(d->scales, 4), ACT_E_ALIGN);
+    if (d->rank) {
+        ACT_CHECK(d->lr_codes && d->lr_scale && d->basis_q && d->basis_scale, ACT_E_INVALID);
+        ACT_CHECK(aligned(d->lr_codes, 16) && aligned(d->basis_q, 16), ACT_E_ALIGN);
+    }
+    if (d->n_outlier) ACT_CHECK(d->outliers && d->outlier_idx, ACT_E_INVALID);
+    return ACT_OK;
+}
+
+static int grid_for(int64_t items_per_slice) {
+    int64_t blocks = (items_per_slice + 7) / 8;
+    int64_t cap = (int64_t)num_sms() * 16;
+    if (blocks > cap) blocks = cap;
+    return (int)(blocks < 1 ? 1 : blocks);
+}
+
+}  // namespace act
+
+using namespace act;
+
+extern "C" int actcomp_cg_basis_prepare(const float *V, int64_t H, int32_t rank, int32_t batch, uint16_t *basis_t,
+                                        int8_t *basis_q, float *basis_scale, void *stream) {
+    ACT_CHECK(V && basis_t && basis_q && basis_scale, ACT_E_INVALID);
+    ACT_CHECK(H > 0 && rank > 0 && rank <= 64 && batch >= 1, ACT_E_INVALID);
+    dim3 grid((unsigned)rank, (unsigned)batch);
+    basis_prepare_kernel<<<grid, 256, 0, as_stream(stream)>>>(V, H, rank, basis_t, basis_q, basis_scale);
+    return launch_status();
+}
+
+extern "C" int actcomp_cg_channel_topk(const uint16_t *x, int64_t T, int64_t H, int64_t ldx, int32_t k,
+                                       int32_t *idx, float *score_ws, void *stream) {
+    ACT_CHECK(x && idx && score_ws, ACT_E_INVALID);
+    ACT_CHECK(T > 0 && H > 0 && ldx >= H && k >= 0 && k <= 64 && k <= H, ACT_E_INVALID);
+    if (k == 0) return ACT_OK;
+    cudaStream_t s = as_stream(stream);
+    ACT_CUDA_TRY(cudaMemsetAsync(score_ws, 0, sizeof(float) * H, s));
+    dim3 grid((unsigned)((H + 255) / 256), (unsigned)(T < 64 ? T : 64));
+    channel_absmax_kernel<<<grid, 256, 0, s>>>(x, T, H, ldx, score_ws);
+    topk_kernel<<<1, 1024, 0, s>>>(score_ws, H, k, idx);
+    return launch_status();
+}
+
+// Encode entry point: SIMT path.  (The tensor-core encode in cg_tc.cu takes
+// over for the shapes it supports; see actcomp_cg_encode in capi.cu.)
+int act_cg_encode_simt(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cudaStream_t s) {
+    if (d->tokens == 0) return ACT_OK;
+    if (d->rank) {
+        dim3 grid(grid_for(d->tokens), d->batch);
+        switch (d->rank) {
+            case 16: cg_project_kernel<16><<<grid, 256, 0, s>>>(*d, x, ldx); break;
+            case 32: cg_project_kernel<32><<<grid, 256, 0, s>>>(*d, x, ldx); break;
+            case 48: cg_project_kernel<48><<<grid, 256, 0, s>>>(*d, x, ldx); break;
+            default: cg_project_kernel<64><<<grid, 256, 0, s>>>(*d, x, ldx); break;
+        }
+        ACT_CUDA_TRY(cudaGetLastError());
+    }
+    dim3 grid(grid_for(d->tokens * ((d->channels + 127) / 128)), d->batch);
+    if (d->bits == 4) cg_quant_kernel<4><<<grid, 256, 0, s>>>(*d, x, ldx);
+    else cg_quant_kernel<8><<<grid, 256, 0, s>>>(*d, x, ldx);
+    return launch_status();
+}
+
+int act_cg_consume_simt(const actcomp_cg_desc *d, int op, const uint16_t *y, int64_t ldy, uint16_t *out,
+                        int64_t ldo, cudaStream_t s) {
+    if (d->tokens == 0) return ACT_OK;
+    dim3 grid(grid_for(d->tokens * ((d->channels + 127) / 128)), d->batch);
+#define ACT_LAUNCH_CONSUME(B)                                                                                 \
+    switch (op) {                                                                                             \
+        case ACT_OP_DECODE: cg_consume_kernel<B, ACT_OP_DECODE><<<grid, 256, 0, s>>>(*d, y, ldy, out, ldo); break; \
+        case ACT_OP_MUL: cg_consume_kernel<B, ACT_OP_MUL><<<grid, 256, 0, s>>>(*d, y, ldy, out, ldo); break;       \
+        case ACT_OP_SILU_BWD: cg_consume_kernel<B, ACT_OP_SILU_BWD><<<grid, 256, 0, s>>>(*d, y, ldy, out, ldo); break; \
+        default: cg_consume_kernel<B, ACT_OP_GELU_BWD><<<grid, 256, 0, s>>>(*d, y, ldy, out, ldo); break;         \
+    }
+    if (d->bits == 4) {
+        ACT_LAUNCH_CONSUME(4)
+    } else {
+        ACT_LAUNCH_CONSUME(8)
+    }
+#undef ACT_LAUNCH_CONSUME
+    return launch_status();
+}
+
+int act_cg_softmax_simt(const actcomp_cg_desc *d, const uint16_t *dp, uint16_t *ds, int64_t ld, int causal,
+                        cudaStream_t s) {
+    if (d->tokens == 0) return ACT_OK;
+    dim3 grid(grid_for(d->tokens), d->batch);
+    if (d->bits == 4) cg_softmax_bwd_kernel<4><<<grid, 256, 0, s>>>(*d, dp, ds, ld, causal);
+    else cg_softmax_bwd_kernel<8><<<grid, 256, 0, s>>>(*d, dp, ds, ld, causal);
+    return launch_status();
+}

@@ -1,0 +1,89 @@
+// common.cuh -- shared helpers of libactcomp (sm_100a).
+//
+// The library is compiled with --fmad=false: every a*b+c written in these
+// sources is a multiply and an add, each rounded to nearest-even, exactly as
+// the CPU oracle evaluates it.  Where a fused multiply-add is wanted it is
+// written as __fmaf_rn explicitly.
+#pragma once
+
+#include <cuda_bf16.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "../../include/actcomp.h"
+
+#define ACT_CUDA_TRY(expr)                         \
+    do {                                           \
+        cudaError_t _e = (expr);                   \
+        if (_e != cudaSuccess) return ACT_E_CUDA;  \
+    } while (0)
+
+#define ACT_CHECK(cond, code)     \
+    do {                          \
+        if (!(cond)) return code; \
+    } while (0)
+
+namespace act {
+
+// Error word set by device-side bounded waits that give up (never by a trap).
+extern __device__ uint32_t g_device_error;
+enum : uint32_t { DEV_ERR_MBAR_TIMEOUT = 1u, DEV_ERR_BAD_ARG = 2u };
+
+static inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
+static inline int launch_status() { return cudaGetLastError() == cudaSuccess ? ACT_OK : ACT_E_CUDA; }
+static inline bool aligned(const void *p, size_t a) { return (reinterpret_cast<uintptr_t>(p) % a) == 0; }
+
+int num_sms();  // cached per device
+
+// ---------------------------------------------------------------- bf16 bits
+__device__ __forceinline__ float bf2f(uint16_t h) { return __uint_as_float(((uint32_t)h) << 16); }
+__device__ __forceinline__ uint16_t f2bf(float f) {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(f));
+}
+__device__ __forceinline__ float rne_bf(float f) { return bf2f(f2bf(f)); }
+
+// ---------------------------------------------------------------- warp reductions
+__device__ __forceinline__ float warp_sum(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = __fadd_rn(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+__device__ __forceinline__ float warp_max(float v) {
+#pragma unroll
+    for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+// max over aligned groups of `width` lanes (width a power of two <= 32)
+__device__ __forceinline__ float group_max(float v, int width) {
+    for (int o = width >> 1; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+    return v;
+}
+
+// ---------------------------------------------------------------- consumer ops
+// All evaluate in binary32 in the order the reference twins write them and
+// round once to bf16.
+__device__ __forceinline__ float silu_bwd_f(float x, float g) {
+    // silu_backward.py:6-8
+    float s = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x)));
+    return __fmul_rn(g, __fmul_rn(s, __fadd_rn(1.0f, __fmul_rn(x, __fsub_rn(1.0f, s)))));
+}
+__device__ __forceinline__ float gelu_bwd_f(float x, float g) {
+    // gelu_backward.py:14-21 (tanh approximation)
+    const float gamma = 0.7978845608028654f, kappa = 0.044715f;
+    float x2 = __fmul_rn(x, x);
+    float y = __fmul_rn(gamma, __fadd_rn(x, __fmul_rn(kappa, __fmul_rn(x2, x))));
+    float th = tanhf(y);
+    float inner = __fmul_rn(__fmul_rn(__fsub_rn(1.0f, __fmul_rn(th, th)), gamma),
+                            __fadd_rn(1.0f, __fmul_rn(__fmul_rn(3.0f, kappa), x2)));
+    float d = __fmul_rn(0.5f, __fadd_rn(__fadd_rn(1.0f, th), __fmul_rn(x, inner)));
+    return __fmul_rn(d, g);
+}
+template <int OP>
+__device__ __forceinline__ float apply_op(float xhat, float y) {
+    if constexpr (OP == ACT_OP_MUL) return __fmul_rn(xhat, y);
+    else if constexpr (OP == ACT_OP_SILU_BWD) return silu_bwd_f(xhat, y);
+    else if constexpr (OP == ACT_OP_GELU_BWD) return gelu_bwd_f(xhat, y);
+    else return xhat;
+}
+
+}  // namespace act
