@@ -408,7 +408,7 @@ def physical_gpu(local: int) -> int:
 
 def launches_per_step():
     """Kernels of this library launched by one encode + decode."""
-    return 3  # projection, residual quantisation, decode
+    return 2  # tensor-core encode (one cluster kernel) and decode
 
 
 def main():

@@ -26,6 +26,10 @@ int gemm_launch(const actcomp_gemm_args *g, cudaStream_t stream);
 int act_cg_encode_simt(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cudaStream_t s);
 int act_cg_consume_simt(const actcomp_cg_desc *d, int op, const uint16_t *y, int64_t ldy, uint16_t *out,
                         int64_t ldo, cudaStream_t s);
+int act_cg_consume_tc(const actcomp_cg_desc *d, int op, const uint16_t *y, int64_t ldy, uint16_t *out, int64_t ldo,
+                      cudaStream_t s);
+bool act_cg_encode_tc_supported(const actcomp_cg_desc *d);
+int act_cg_encode_tc(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cudaStream_t s);
 int act_cg_softmax_simt(const actcomp_cg_desc *d, const uint16_t *dp, uint16_t *ds, int64_t ld, int causal,
                         cudaStream_t s);
 
@@ -74,6 +78,7 @@ extern "C" int actcomp_cg_encode(const actcomp_cg_desc *d, const uint16_t *x, in
     if (st) return st;
     if ((st = check_rows(x, ldx, d->channels))) return st;
     if (d->rank) ACT_CHECK(d->basis_t && aligned(d->basis_t, 16), ACT_E_ALIGN);
+    if (act_cg_encode_tc_supported(d)) return act_cg_encode_tc(d, x, ldx, as_stream(stream));
     return act_cg_encode_simt(d, x, ldx, as_stream(stream));
 }
 
@@ -81,7 +86,7 @@ extern "C" int actcomp_cg_decode(const actcomp_cg_desc *d, uint16_t *xhat, int64
     int st = validate_desc(d);
     if (st) return st;
     if ((st = check_rows(xhat, ldo, d->channels))) return st;
-    return act_cg_consume_simt(d, ACT_OP_DECODE, nullptr, 0, xhat, ldo, as_stream(stream));
+    return act_cg_consume_tc(d, ACT_OP_DECODE, nullptr, 0, xhat, ldo, as_stream(stream));
 }
 
 extern "C" int actcomp_cg_consume(const actcomp_cg_desc *d, int32_t op, const uint16_t *y, int64_t ldy,
@@ -91,7 +96,7 @@ extern "C" int actcomp_cg_consume(const actcomp_cg_desc *d, int32_t op, const ui
     ACT_CHECK(op >= ACT_OP_DECODE && op <= ACT_OP_GELU_BWD, ACT_E_INVALID);
     if ((st = check_rows(out, ldo, d->channels))) return st;
     if (op != ACT_OP_DECODE && (st = check_rows(y, ldy, d->channels))) return st;
-    return act_cg_consume_simt(d, op, y, ldy, out, ldo, as_stream(stream));
+    return act_cg_consume_tc(d, op, y, ldy, out, ldo, as_stream(stream));
 }
 
 extern "C" int actcomp_cg_softmax_bwd(const actcomp_cg_desc *d, const uint16_t *dp, uint16_t *ds, int64_t ld,
@@ -123,7 +128,7 @@ extern "C" int actcomp_cg_dw(const actcomp_cg_desc *d, const uint16_t *dy, int64
     ACT_CHECK(aligned(workspace, 256), ACT_E_ALIGN);
     cudaStream_t s = as_stream(stream);
     uint16_t *xhat = static_cast<uint16_t *>(workspace);
-    if ((st = act_cg_consume_simt(d, ACT_OP_DECODE, nullptr, 0, xhat, d->channels, s))) return st;
+    if ((st = act_cg_consume_tc(d, ACT_OP_DECODE, nullptr, 0, xhat, d->channels, s))) return st;
     actcomp_gemm_args g{};
     g.M = d->channels;
     g.N = N;

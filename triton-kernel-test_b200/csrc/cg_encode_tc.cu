@@ -1,0 +1,586 @@
+// cg_encode_tc.cu -- channel-group encode on the tcgen05 tensor cores.
+//
+// A cluster of C CTAs owns one block of 128 tokens at a time; CTA c of the
+// cluster owns a contiguous, group-aligned slice of the channels.  Per block:
+//   phase 1  (warps 0, 1) TMA streams X[128 x slice] (64-channel steps) and
+//            V^T[r x 64]; tcgen05.mma kind::f16 (M=128, N=r) accumulates the
+//            partial projection L_c = X_slice . V_slice in TMEM;
+//   exchange the epilogue writes L_c to shared memory; the CTAs signal each
+//            other with remote mbarrier arrivals and read every partial over
+//            DSMEM, summing them in rank order -- every CTA gets the same L,
+//            from which it forms the per-token int8 low-rank codes Lq and
+//            their scale sL (rank 0 stores them);
+//   phase 2  (warps 2, 3, after phase 1 of the block completed) per
+//            128-channel chunk: TMA re-reads the X chunk (the slice was read
+//            moments ago and is still in L2) and the quantised basis
+//            rows; tcgen05.mma kind::i8 gives the exact I = Lq . Vq^T; the
+//            epilogue (one token row per thread) forms the residual
+//            x - I * sL, copies the outlier channels verbatim, optionally
+//            rotates 128-channel blocks (Walsh-Hadamard), and writes int4/int8
+//            codes with per-token group-absmax scales.
+// The two phases run on separate rings and issuers, so phase 1 of the next
+// block streams from HBM while phase 2 of this block is quantised.
+// X is read from HBM once; every other byte is written once.  Arithmetic
+// matches oracle/actcomp_oracle.c (cg_encode_given_lr) bit for bit given L.
+#include <cudaTypedefs.h>
+
+#include "tc_ptx.cuh"
+
+namespace act {
+namespace cgenc {
+
+constexpr int ROWS = 128;  // tokens per block (MMA M)
+constexpr int KC = 64;     // channels per projection step
+constexpr int CH = 128;    // channels per quantisation chunk (MMA N)
+constexpr int NA = 3, SLOT_A = 24 * 1024;  // projection ring: X 128x64 (16 KB) + V^T r x 64 (<= 8 KB)
+constexpr int NB = 2, SLOT_B = 40 * 1024;  // residual ring: X 128x128 (32 KB) + Vq 128 x r (<= 8 KB)
+constexpr int PART_PITCH = 68;   // floats per row of the partial-projection buffer
+
+struct EncParams {
+    int64_t T, H;
+    int rank, k, group, batch;
+    const float *basis_scale;
+    uint8_t *codes;
+    float *scales;
+    int8_t *lrq;
+    float *lrs;
+    uint16_t *outl;
+    const int32_t *idx;
+    int C;         // CTAs per cluster
+    int unit;      // channels per split unit (multiple of 64 and of the group)
+    int nunits;
+    int ntb;       // token blocks per slice
+    int64_t nblocks;
+    int nclusters;
+};
+
+template <int BITS, bool WHT, int RB, int EW>
+struct EncLayout {
+    static constexpr int RING = NA * SLOT_A + NB * SLOT_B;
+    static constexpr int PART = ROWS * PART_PITCH * 4;
+    static constexpr int LQT = ROWS * RB;
+    static constexpr int BAR_OFF = RING + PART + LQT;
+    static constexpr int TOTAL = BAR_OFF + 512 + 1024;
+    static constexpr int THREADS = 128 + 32 * EW;  // 2 producers, 2 MMA issuers, epilogue
+};
+
+template <int PITCH>
+__device__ __forceinline__ int swz(int r, int c) {
+    if constexpr (PITCH == 128) return r * 128 + ((c ^ (r & 7)) << 4);
+    else if constexpr (PITCH == 64) return r * 64 + ((c ^ ((r >> 1) & 3)) << 4);
+    else return r * 32 + ((c ^ ((r >> 2) & 1)) << 4);
+}
+
+__device__ __forceinline__ void wht128_reg(float (&v)[128]) {
+#pragma unroll
+    for (int m = 1; m < 128; m <<= 1) {
+#pragma unroll
+        for (int i = 0; i < 128; ++i) {
+            if (!(i & m)) {
+                float a = v[i], b = v[i + m];
+                v[i] = __fadd_rn(a, b);
+                v[i + m] = __fsub_rn(a, b);
+            }
+        }
+    }
+}
+
+// rint(w / s) clamped to +-qmax, with the quotient correctly rounded first (as
+// the oracle): a reciprocal product decides every case that is not within
+// 2^-11 of a rounding tie; those few take the exact division.
+__device__ __forceinline__ int quant_code(float w, float s, float rcp, int qmax) {
+    if (!(s > 0.f)) return 0;
+    const float y = __fmul_rn(w, rcp);
+    const float ry = rintf(y);
+    int q;
+    if (fabsf(__fsub_rn(y, ry)) < 0.4995f) q = (int)ry;
+    else q = __float2int_rn(__fdiv_rn(w, s));
+    return max(-qmax, min(qmax, q));
+}
+
+template <int BITS, bool WHT, int RB, int EW>
+__global__ void __launch_bounds__(EncLayout<BITS, WHT, RB, EW>::THREADS, 1)
+    cg_encode_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_vt,
+                        const __grid_constant__ CUtensorMap tm_vq, EncParams p) {
+    using L = EncLayout<BITS, WHT, RB, EW>;
+    constexpr int qmax = (1 << (BITS - 1)) - 1, off = 1 << (BITS - 1);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    float *part = reinterpret_cast<float *>(smem + L::RING);
+    uint8_t *lqt = smem + L::RING + L::PART;
+    uint64_t *fullA = reinterpret_cast<uint64_t *>(smem + L::BAR_OFF);
+    uint64_t *emptyA = fullA + NA;
+    uint64_t *fullB = emptyA + NA;
+    uint64_t *emptyB = fullB + NB;
+    uint64_t *tfull = emptyB + NB;  // [2]
+    uint64_t *tempty = tfull + 2;   // [2]
+    uint64_t *lfull = tempty + 2;
+    uint64_t *lempty = lfull + 1;
+    uint64_t *lqready = lempty + 1;
+    uint64_t *pready = lqready + 1;
+    uint64_t *pdone = pready + 1;
+    uint64_t *lseen = pdone + 1;  // phase-2 producer has observed lfull of the block
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(lseen + 1);
+    volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    uint8_t *ringA = smem, *ringB = smem + NA * SLOT_A;
+
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int C = p.C;
+    const uint32_t crank = C > 1 ? tc::cluster_rank() : 0;
+    const int cluster = blockIdx.x / C;
+    // my channel slice [c_lo, c_hi)
+    const int u_lo = (int)((int64_t)crank * p.nunits / C), u_hi = (int)((int64_t)(crank + 1) * p.nunits / C);
+    const int64_t c_lo = (int64_t)u_lo * p.unit, c_hi = (int64_t)u_hi * p.unit;
+    const int nk1 = (int)((c_hi - c_lo) / KC);
+    const int nk2 = (int)((c_hi - c_lo + CH - 1) / CH);
+    const int r = p.rank;
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < NA; ++s) {
+            tc::mbar_init(&fullA[s], 1);
+            tc::mbar_init(&emptyA[s], 1);
+        }
+        for (int s = 0; s < NB; ++s) {
+            tc::mbar_init(&fullB[s], 1);
+            tc::mbar_init(&emptyB[s], 1 + EW);
+        }
+        for (int b = 0; b < 2; ++b) {
+            tc::mbar_init(&tfull[b], 1);
+            tc::mbar_init(&tempty[b], EW);
+        }
+        tc::mbar_init(lfull, 1);
+        tc::mbar_init(lempty, EW);
+        tc::mbar_init(lqready, EW);
+        tc::mbar_init(pready, C > 1 ? C - 1 : 1);
+        tc::mbar_init(pdone, C > 1 ? C - 1 : 1);
+        tc::mbar_init(lseen, 1);
+        *abort = 0;
+        tc::fence_mbar_init();
+    }
+    if (warp == 1) {
+        tc::tmem_alloc(tmem_slot, 512);
+        tc::tmem_relinquish();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (C > 1) tc::cluster_sync();  // peers' barriers are initialised before any remote arrive
+    tc::tc_fence_after();
+    const uint32_t tmem = *tmem_slot;
+    const uint32_t tm_l = tmem;        // projection accumulator, columns [0, 64)
+    const uint32_t tm_p = tmem + 128;  // residual-term accumulators, [128, 384)
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ phase-1 producer
+        if (lane == 0) {
+            tc::prefetch_tmap(&tm_x);
+            tc::prefetch_tmap(&tm_vt);
+            int i = 0;
+            bool ok = true;
+            for (int64_t blk = cluster; blk < p.nblocks && ok; blk += p.nclusters) {
+                const int b = (int)(blk / p.ntb), tb = (int)(blk % p.ntb);
+                for (int ks = 0; ks < nk1; ++ks, ++i) {
+                    const int s = i % NA;
+                    if (!(ok = tc::mbar_wait(&emptyA[s], ((i / NA) & 1) ^ 1, abort))) break;
+                    uint8_t *st = ringA + s * SLOT_A;
+                    tc::mbar_arrive_expect_tx(&fullA[s], ROWS * 128 + r * 128);
+                    const int x = (int)(c_lo + ks * KC);
+                    tc::tma_load_3d(st, &tm_x, &fullA[s], x, tb * ROWS, b);
+                    tc::tma_load_3d(st + 16 * 1024, &tm_vt, &fullA[s], x, 0, b);
+                }
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ projection MMA
+        if (lane == 0) {
+            const uint32_t id_proj = tc::idesc_f16(ROWS, r, true, false, false);
+            int i = 0, nb = 0;
+            bool ok = true;
+            for (int64_t blk = cluster; blk < p.nblocks && ok; blk += p.nclusters, ++nb) {
+                // the epilogue has read the previous block's projection
+                if (!(ok = tc::mbar_wait(lempty, (nb & 1) ^ 1, abort))) break;
+                tc::tc_fence_after();
+                for (int ks = 0; ks < nk1; ++ks, ++i) {
+                    const int s = i % NA;
+                    if (!(ok = tc::mbar_wait(&fullA[s], (i / NA) & 1, abort))) break;
+                    tc::tc_fence_after();
+                    uint8_t *st = ringA + s * SLOT_A;
+#pragma unroll
+                    for (int kk = 0; kk < KC / 16; ++kk) {
+                        const uint64_t ad = tc::smem_desc(st + kk * 32, 16, 1024, tc::SW_128B);
+                        const uint64_t bd = tc::smem_desc(st + 16 * 1024 + kk * 32, 16, 1024, tc::SW_128B);
+                        tc::mma_f16(tm_l, ad, bd, id_proj, (ks | kk) != 0);
+                    }
+                    tc::mma_commit(&emptyA[s]);
+                }
+                // lfull must not run two phases ahead of the phase-2 producer's parity wait
+                if (ok && nb > 0) ok = tc::mbar_wait(lseen, (nb - 1) & 1, abort);
+                if (ok) tc::mma_commit(lfull);
+            }
+        }
+    } else if (warp == 2) {
+        // ------------------------------------------------------------ phase-2 producer
+        if (lane == 0) {
+            tc::prefetch_tmap(&tm_vq);
+            int i = 0, nb = 0;
+            bool ok = true;
+            for (int64_t blk = cluster; blk < p.nblocks && ok; blk += p.nclusters, ++nb) {
+                const int b = (int)(blk / p.ntb), tb = (int)(blk % p.ntb);
+                // re-read X only after phase 1 of this block has streamed it into L2
+                if (!(ok = tc::mbar_wait(lfull, nb & 1, abort))) break;
+                tc::mbar_arrive(lseen);
+                for (int ck = 0; ck < nk2; ++ck, ++i) {
+                    const int s = i % NB;
+                    if (!(ok = tc::mbar_wait(&emptyB[s], ((i / NB) & 1) ^ 1, abort))) break;
+                    uint8_t *st = ringB + s * SLOT_B;
+                    tc::mbar_arrive_expect_tx(&fullB[s], 2 * ROWS * 128 + CH * RB);
+                    const int x = (int)(c_lo + ck * CH);
+                    tc::tma_load_3d(st, &tm_x, &fullB[s], x, tb * ROWS, b);
+                    tc::tma_load_3d(st + ROWS * 128, &tm_x, &fullB[s], x + 64, tb * ROWS, b);
+                    tc::tma_load_3d(st + 32 * 1024, &tm_vq, &fullB[s], 0, x, b);
+                }
+            }
+        }
+    } else if (warp == 3) {
+        // ------------------------------------------------------------ residual-term MMA
+        if (lane == 0) {
+            constexpr uint32_t id_i8 = tc::idesc_i8(ROWS, CH);
+            constexpr tc::Swizzle SWQ = RB == 32 ? tc::SW_32B : tc::SW_64B;
+            int i = 0, nb = 0;
+            bool ok = true;
+            for (int64_t blk = cluster; blk < p.nblocks && ok; blk += p.nclusters, ++nb) {
+                // low-rank codes of this block are in shared memory
+                if (!(ok = tc::mbar_wait(lqready, nb & 1, abort))) break;
+                tc::tc_fence_after();
+                for (int ck = 0; ck < nk2; ++ck, ++i) {
+                    const int s = i % NB, tb2 = i & 1;
+                    if (!(ok = tc::mbar_wait(&fullB[s], (i / NB) & 1, abort))) break;
+                    if (!(ok = tc::mbar_wait(&tempty[tb2], ((i >> 1) & 1) ^ 1, abort))) break;
+                    tc::tc_fence_after();
+                    uint8_t *st = ringB + s * SLOT_B;
+#pragma unroll
+                    for (int kk = 0; kk < RB / 32; ++kk) {
+                        const uint64_t ad = tc::smem_desc(lqt + kk * 32, 16, 8 * RB, SWQ);
+                        const uint64_t bd = tc::smem_desc(st + 32 * 1024 + kk * 32, 16, 8 * RB, SWQ);
+                        tc::mma_i8(tm_p + tb2 * CH, ad, bd, id_i8, kk > 0);
+                    }
+                    tc::mma_commit(&tfull[tb2]);
+                    tc::mma_commit(&emptyB[s]);
+                }
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const int ew = warp - 4;
+        const int q = warp & 3;
+        const int h = (EW == 8) ? (ew >> 2) : 0;
+        constexpr int NC = EW == 8 ? 64 : 128;
+        const int row = q * 32 + lane;
+        const int ngr = (int)(p.H / p.group);
+        const int64_t rowb = p.H * BITS / 8;
+        int j = 0, nb = 0;
+        bool ok = true;
+        for (int64_t blk = cluster; blk < p.nblocks && ok; blk += p.nclusters, ++nb) {
+            const int b = (int)(blk / p.ntb), tb = (int)(blk % p.ntb);
+            const int64_t t = (int64_t)tb * ROWS + row;
+            const bool rv = t < p.T;
+            const int64_t trow = (int64_t)b * p.T + t;
+            // ---- partial projection -> shared memory
+            if (!(ok = tc::mbar_wait(lfull, nb & 1, abort))) break;
+            tc::tc_fence_after();
+            float Lr[RB];
+            {
+                uint32_t v[32];
+#pragma unroll
+                for (int jj = 0; jj < RB / 32; ++jj) {
+                    tc::tmem_ld32(tm_l + ((uint32_t)(q * 32) << 16) + 32 * jj, v);
+                    tc::tmem_ld_wait();
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) Lr[32 * jj + e] = __uint_as_float(v[e]);
+                }
+            }
+            tc::tc_fence_before();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(lempty);
+            if (C > 1) {
+                // our partial buffer may be overwritten once every peer has read the previous one
+                if (nb > 0 && !(ok = tc::mbar_wait_cluster(pdone, (nb - 1) & 1, abort))) break;
+                if (h == 0) {
+                    float4 *dst = reinterpret_cast<float4 *>(part + row * PART_PITCH);
+#pragma unroll
+                    for (int e = 0; e < RB / 4; ++e)
+                        if (4 * e < r) dst[e] = make_float4(Lr[4 * e], Lr[4 * e + 1], Lr[4 * e + 2], Lr[4 * e + 3]);
+                }
+                tc::named_bar(1, 32 * EW);
+                if (ew == 0 && lane < C && lane != (int)crank) {
+                    tc::fence_acq_rel_cluster();
+                    tc::mbar_arrive_remote(tc::map_cluster(pready, lane));
+                }
+                if (!(ok = tc::mbar_wait_cluster(pready, nb & 1, abort))) break;
+                // L = sum of the partials in rank order (identical in every CTA)
+                for (int pr = 0; pr < C; ++pr) {
+                    const uint32_t base = tc::map_cluster(part + row * PART_PITCH, pr);
+#pragma unroll
+                    for (int e = 0; e < RB / 4; ++e) {
+                        if (4 * e < r) {
+                            const float4 v = tc::ld_cluster_f4(base + 16 * e);
+                            Lr[4 * e] = pr ? __fadd_rn(Lr[4 * e], v.x) : v.x;
+                            Lr[4 * e + 1] = pr ? __fadd_rn(Lr[4 * e + 1], v.y) : v.y;
+                            Lr[4 * e + 2] = pr ? __fadd_rn(Lr[4 * e + 2], v.z) : v.z;
+                            Lr[4 * e + 3] = pr ? __fadd_rn(Lr[4 * e + 3], v.w) : v.w;
+                        }
+                    }
+                }
+                // tell every peer we are done reading its partial
+                tc::named_bar(1, 32 * EW);
+                if (ew == 0 && lane < C && lane != (int)crank) {
+                    tc::fence_acq_rel_cluster();
+                    tc::mbar_arrive_remote(tc::map_cluster(pdone, lane));
+                }
+            }
+            // ---- per-token low-rank codes
+            float amax = 0.f;
+#pragma unroll
+            for (int e = 0; e < RB; ++e) {
+                if (e < r) {
+                    Lr[e] = __fmul_rn(Lr[e], __ldg(p.basis_scale + (int64_t)b * r + e));
+                    amax = fmaxf(amax, fabsf(Lr[e]));
+                }
+            }
+            const float sl = __fdiv_rn(amax, 127.0f);
+            uint32_t lw[RB / 4];
+#pragma unroll
+            for (int e = 0; e < RB / 4; ++e) lw[e] = 0;
+#pragma unroll
+            for (int e = 0; e < RB; ++e) {
+                if (e < r) {
+                    const int qv = sl > 0.f ? max(-127, min(127, __float2int_rn(__fdiv_rn(Lr[e], sl)))) : 0;
+                    lw[e >> 2] |= (uint32_t)(qv & 0xff) << ((e & 3) * 8);
+                }
+            }
+            if (h == 0) {
+#pragma unroll
+                for (int c16 = 0; c16 < RB / 16; ++c16)
+                    *reinterpret_cast<uint4 *>(lqt + swz<RB>(row, c16)) =
+                        make_uint4(lw[4 * c16], lw[4 * c16 + 1], lw[4 * c16 + 2], lw[4 * c16 + 3]);
+                if (crank == 0 && rv) {
+                    uint32_t *dst = reinterpret_cast<uint32_t *>(p.lrq + trow * r);
+#pragma unroll
+                    for (int e = 0; e < RB / 4; ++e)
+                        if (4 * e < r) dst[e] = lw[e];
+                    p.lrs[trow] = sl;
+                }
+            }
+            tc::fence_proxy_async();
+            __syncwarp();
+            if (lane == 0) tc::mbar_arrive(lqready);
+
+            // ---- residual codes, chunk by chunk
+            const int32_t *idx = p.k ? p.idx + (int64_t)b * p.k : nullptr;
+            for (int ck = 0; ck < nk2 && ok; ++ck, ++j) {
+                const int s = j % NB, tb2 = j & 1;
+                if (!(ok = tc::mbar_wait(&fullB[s], (j / NB) & 1, abort))) break;
+                if (!(ok = tc::mbar_wait(&tfull[tb2], (j >> 1) & 1, abort))) break;
+                tc::tc_fence_after();
+                const int64_t c0 = c_lo + (int64_t)ck * CH + h * 64;  // first channel of my columns
+                const bool cv = c0 < c_hi;                            // warp-uniform
+                const uint8_t *xt = ringB + s * SLOT_B;
+                float w[NC];
+                if (cv) {
+#pragma unroll
+                    for (int jj = 0; jj < NC / 32; ++jj) {
+                        uint32_t I[32];
+                        tc::tmem_ld32(tm_p + tb2 * CH + ((uint32_t)(q * 32) << 16) + h * 64 + 32 * jj, I);
+                        tc::tmem_ld_wait();
+                        const uint8_t *box = xt + (h + (jj >> 1)) * ROWS * 128;
+#pragma unroll
+                        for (int c16 = 0; c16 < 4; ++c16) {
+                            const uint4 v = *reinterpret_cast<const uint4 *>(box + swz<128>(row, (jj & 1) * 4 + c16));
+                            const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
+#pragma unroll
+                            for (int e = 0; e < 8; ++e) {
+                                const float xv = __uint_as_float(e & 1 ? (wd[e >> 1] & 0xffff0000u) : (wd[e >> 1] << 16));
+                                const int col = 32 * jj + 8 * c16 + e;
+                                w[col] = __fsub_rn(xv, __fmul_rn(__int2float_rn((int)I[8 * c16 + e]), sl));
+                            }
+                        }
+                    }
+                }
+                tc::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&tempty[tb2]);
+                // outlier channels of my columns: verbatim copy, residual zeroed
+                if (cv && p.k) {
+#pragma unroll
+                    for (int g = 0; g < NC / 64; ++g) {
+                        const int64_t lo_c = c0 + 64 * g, hi_c = lo_c + 64;
+                        int lo = 0, hi = p.k;
+                        while (lo < hi) {
+                            const int mid = (lo + hi) >> 1;
+                            if (__ldg(idx + mid) < lo_c) lo = mid + 1;
+                            else hi = mid;
+                        }
+                        uint64_t om = 0;
+                        for (int jj = lo; jj < p.k; ++jj) {
+                            const int64_t c = __ldg(idx + jj);
+                            if (c >= hi_c) break;
+                            om |= 1ull << (c - lo_c);
+                        }
+                        if (om) {
+                            const uint8_t *box = xt + (h + g) * ROWS * 128;
+#pragma unroll
+                            for (int e = 0; e < 64; ++e) {
+                                if ((om >> e) & 1ull) {
+                                    const int slot = lo + __popcll(om & ((1ull << e) - 1ull));
+                                    const uint16_t bits =
+                                        *reinterpret_cast<const uint16_t *>(box + swz<128>(row, e >> 3) + 2 * (e & 7));
+                                    if (rv) p.outl[trow * p.k + slot] = bits;
+                                    w[g * 64 + e] = 0.f;
+                                }
+                            }
+                        }
+                    }
+                }
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&emptyB[s]);  // X and basis tile no longer needed
+                if (!cv) continue;
+                if constexpr (WHT) wht128_reg(*reinterpret_cast<float(*)[128]>(&w[0]));
+                // group absmax, scale, codes
+                uint32_t packed[NC * BITS / 32];
+#pragma unroll
+                for (int e = 0; e < NC * BITS / 32; ++e) packed[e] = 0;
+                // absmax of each 32-column piece, combined over the pieces of a group
+                float am[NC / 32];
+#pragma unroll
+                for (int pc = 0; pc < NC / 32; ++pc) {
+                    float m = 0.f;
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) m = fmaxf(m, fabsf(w[32 * pc + e]));
+                    am[pc] = m;
+                }
+                const int G = p.group;
+#pragma unroll
+                for (int pc = 0; pc < NC / 32; ++pc) {
+                    float gam = am[pc];
+                    if (G >= 64) gam = fmaxf(gam, am[pc ^ 1]);
+                    if constexpr (NC == 128) {
+                        if (G >= 128) gam = fmaxf(gam, fmaxf(am[pc ^ 2], am[pc ^ 3]));
+                    }
+                    const float sc = __fdiv_rn(gam, (float)qmax);
+                    const float rcp = __frcp_rn(sc);
+                    if (((32 * pc) % G) == 0 && rv) p.scales[trow * ngr + (c0 + 32 * pc) / G] = sc;
+#pragma unroll
+                    for (int e = 0; e < 32; ++e) {
+                        const uint32_t u = (uint32_t)(quant_code(w[32 * pc + e], sc, rcp, qmax) + off);
+                        const int col = 32 * pc + e;
+                        packed[col * BITS / 32] |= u << ((col * BITS) % 32);
+                    }
+                }
+                if (rv) {
+                    uint4 *dst = reinterpret_cast<uint4 *>(p.codes + trow * rowb + c0 * BITS / 8);
+#pragma unroll
+                    for (int e = 0; e < NC * BITS / 128; ++e)
+                        dst[e] = make_uint4(packed[4 * e], packed[4 * e + 1], packed[4 * e + 2], packed[4 * e + 3]);
+                }
+            }
+        }
+        // do not exit while a peer may still read our partial buffer
+        if (C > 1 && ok && nb > 0) tc::mbar_wait_cluster(pdone, (nb - 1) & 1, abort);
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (warp == 1) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, 512);
+    }
+    // no CTA leaves while a peer may still read its shared memory
+    if (C > 1) tc::cluster_sync();
+}
+
+template <int BITS, bool WHT, int RB, int EW>
+int launch_encode(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cudaStream_t stream) {
+    using L = EncLayout<BITS, WHT, RB, EW>;
+    const int64_t T = d->tokens, H = d->channels, B = d->batch;
+    const int r = d->rank;
+    CUtensorMap m_x{}, m_vt{}, m_vq{};
+    int st;
+    if ((st = make_map_3d(&m_x, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, H, T, B, ldx, T * ldx, 64, ROWS,
+                          CU_TENSOR_MAP_SWIZZLE_128B)))
+        return st;
+    if ((st = make_map_3d(&m_vt, d->basis_t, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, H, r, B, H, (int64_t)r * H, 64, r,
+                          CU_TENSOR_MAP_SWIZZLE_128B)))
+        return st;
+    if ((st = make_map_3d(&m_vq, d->basis_q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, r, H, B, r, H * r, RB, CH,
+                          RB == 32 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B)))
+        return st;
+    EncParams p{};
+    p.T = T;
+    p.H = H;
+    p.rank = r;
+    p.k = d->n_outlier;
+    p.group = d->group;
+    p.batch = d->batch;
+    p.basis_scale = d->basis_scale;
+    p.codes = d->codes;
+    p.scales = d->scales;
+    p.lrq = d->lr_codes;
+    p.lrs = d->lr_scale;
+    p.outl = d->outliers;
+    p.idx = d->outlier_idx;
+    p.unit = (d->wht || d->group == 128) ? 128 : 64;
+    p.nunits = (int)(H / p.unit);
+    // smallest cluster whose per-CTA slice keeps the second sweep's L2 window small
+    int C = 1;
+    while (C < 8 && (H / C > 1536) && p.nunits / (C * 2) >= 1) C *= 2;
+    if (C > p.nunits) C = p.nunits;
+    p.C = C;
+    p.ntb = (int)((T + ROWS - 1) / ROWS);
+    p.nblocks = (int64_t)p.ntb * B;
+    int maxc = num_sms() / C;
+    p.nclusters = (int)(p.nblocks < maxc ? p.nblocks : maxc);
+    auto kern = cg_encode_tc_kernel<BITS, WHT, RB, EW>;
+    ACT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
+    cudaLaunchConfig_t cfg{};
+    cfg.gridDim = dim3((unsigned)(p.nclusters * C), 1, 1);
+    cfg.blockDim = dim3(L::THREADS, 1, 1);
+    cfg.dynamicSmemBytes = L::TOTAL;
+    cfg.stream = stream;
+    cudaLaunchAttribute attr[1];
+    attr[0].id = cudaLaunchAttributeClusterDimension;
+    attr[0].val.clusterDim.x = C;
+    attr[0].val.clusterDim.y = 1;
+    attr[0].val.clusterDim.z = 1;
+    cfg.attrs = attr;
+    cfg.numAttrs = 1;
+    ACT_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, m_x, m_vt, m_vq, p));
+    return ACT_OK;
+}
+
+}  // namespace cgenc
+}  // namespace act
+
+// Tensor-core encode: needs a low-rank basis (rank 16..64), H a multiple of 64
+// (of 128 with the rotation or group 128).  Other shapes use the SIMT encode.
+bool act_cg_encode_tc_supported(const actcomp_cg_desc *d) {
+    if (d->rank < 16 || d->rank > 64) return false;
+    const int unit = (d->wht || d->group == 128) ? 128 : 64;
+    return d->channels % unit == 0;
+}
+
+int act_cg_encode_tc(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cudaStream_t s) {
+    using namespace act::cgenc;
+    if (d->tokens == 0) return ACT_OK;
+    const bool wide = d->wht || d->group == 128;  // a group or rotation block spans 128 channels
+    const int rb = d->rank <= 32 ? 32 : 64;
+#define ACT_ENC(B, W, R, E) return launch_encode<B, W, R, E>(d, x, ldx, s)
+    if (d->bits == 4) {
+        if (d->wht) { if (rb == 32) ACT_ENC(4, true, 32, 4); ACT_ENC(4, true, 64, 4); }
+        if (wide) { if (rb == 32) ACT_ENC(4, false, 32, 4); ACT_ENC(4, false, 64, 4); }
+        if (rb == 32) ACT_ENC(4, false, 32, 8);
+        ACT_ENC(4, false, 64, 8);
+    }
+    if (d->wht) { if (rb == 32) ACT_ENC(8, true, 32, 4); ACT_ENC(8, true, 64, 4); }
+    if (wide) { if (rb == 32) ACT_ENC(8, false, 32, 4); ACT_ENC(8, false, 64, 4); }
+    if (rb == 32) ACT_ENC(8, false, 32, 8);
+    ACT_ENC(8, false, 64, 8);
+#undef ACT_ENC
+}
