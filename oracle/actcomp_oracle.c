@@ -57,11 +57,25 @@ static inline uint16_t f2bf(float f) {
 static inline float rne_bf(float f) { return bf2f(f2bf(f)); }
 
 /* ============================================================ channel-group
+ * Quantisation rule used throughout this format: for a set of values with
+ * absmax a and code range qmax,
+ *   scale  s  = a / qmax        (binary32 division; stored, used to decode)
+ *   rscale rs = qmax / a        (binary32 division; 0 when a == 0)
+ *   code   q  = clamp(rint(v * rs), -qmax, qmax)   (binary32 product, ties to even)
+ * i.e. codes multiply by a correctly rounded reciprocal instead of dividing.
+ *
  * Basis preparation.  V is H x r (column j = basis vector j).
- *   sV[j]    = max_c |V[c,j]| / 127                     (binary32 division)
- *   Vq[c,j]  = clamp(rint(V[c,j] / sV[j]), -127, 127)   (0 when sV[j] == 0)
+ *   sV[j]    = max_c |V[c,j]| / 127
+ *   Vq[c,j]  = clamp(rint(V[c,j] * (127 / max_c |V[c,j]|)), -127, 127)
  *   Vt[j,c]  = bf16_rne(V[c,j])                          (projection basis)
  */
+static inline float rscale_of(float amax, float qmax) { return amax > 0.f ? qmax / amax : 0.f; }
+static inline int code_of(float v, float rs, int qmax) {
+    float t = rintf(v * rs);
+    if (t > (float)qmax) t = (float)qmax;
+    if (t < -(float)qmax) t = -(float)qmax;
+    return (int)t;
+}
 void cg_basis_prepare(const float *V, int64_t H, int r, uint16_t *Vt, int8_t *Vq, float *sV) {
     for (int j = 0; j < r; ++j) {
         float amax = 0.f;
@@ -69,18 +83,11 @@ void cg_basis_prepare(const float *V, int64_t H, int r, uint16_t *Vt, int8_t *Vq
             float a = fabsf(V[c * r + j]);
             if (a > amax) amax = a;
         }
-        float s = amax / 127.0f;
-        sV[j] = s;
+        sV[j] = amax / 127.0f;
+        const float rs = rscale_of(amax, 127.0f);
         for (int64_t c = 0; c < H; ++c) {
             float v = V[c * r + j];
-            int q = 0;
-            if (s > 0.f) {
-                float t = rintf(v / s);
-                if (t > 127.f) t = 127.f;
-                if (t < -127.f) t = -127.f;
-                q = (int)t;
-            }
-            Vq[c * r + j] = (int8_t)q;
+            Vq[c * r + j] = (int8_t)code_of(v, rs, 127);
             Vt[(int64_t)j * H + c] = f2bf(v);
         }
     }
@@ -106,7 +113,7 @@ void cg_project(const void *X, int x_f32, int64_t T, int64_t H, int64_t ldx, con
 /* Per-token quantisation of the low-rank coefficients.
  *   Lt[j]  = L[t,j] * sV[j]
  *   sL[t]  = max_j |Lt[j]| / 127
- *   Lq[t,j]= clamp(rint(Lt[j] / sL[t]), -127, 127)      (0 when sL == 0)   */
+ *   Lq[t,j]= clamp(rint(Lt[j] * (127 / max_j |Lt[j]|)), -127, 127)          */
 void cg_lr_quantize(const float *L, int64_t T, int r, const float *sV, int8_t *Lq, float *sL) {
 #pragma omp parallel for schedule(static)
     for (int64_t t = 0; t < T; ++t) {
@@ -117,26 +124,19 @@ void cg_lr_quantize(const float *L, int64_t T, int r, const float *sV, int8_t *L
             float a = fabsf(lt[j]);
             if (a > amax) amax = a;
         }
-        float s = amax / 127.0f;
-        sL[t] = s;
-        for (int j = 0; j < r; ++j) {
-            int q = 0;
-            if (s > 0.f) {
-                float v = rintf(lt[j] / s);
-                if (v > 127.f) v = 127.f;
-                if (v < -127.f) v = -127.f;
-                q = (int)v;
-            }
-            Lq[t * r + j] = (int8_t)q;
-        }
+        sL[t] = amax / 127.0f;
+        const float rs = rscale_of(amax, 127.0f);
+        for (int j = 0; j < r; ++j) Lq[t * r + j] = (int8_t)code_of(lt[j], rs, 127);
     }
 }
 
-/* P[t,c] = (float)(sum_j Lq[t,j]*Vq[c,j]) * sL[t]; the integer sum is exact. */
-static inline float lowrank_term(const int8_t *lq, const int8_t *vq, int r, float sl) {
+/* I[t,c] = sum_j Lq[t,j]*Vq[c,j], an exact integer (|I| < 2^21 for r <= 64);
+ * the low-rank term enters the arithmetic only as fma(+-I, sL[t], .), one
+ * rounding. */
+static inline float lowrank_int(const int8_t *lq, const int8_t *vq, int r) {
     int32_t acc = 0;
     for (int j = 0; j < r; ++j) acc += (int32_t)lq[j] * (int32_t)vq[j];
-    return (float)acc * sl;
+    return (float)acc;
 }
 
 /* Unnormalised 128-point Walsh-Hadamard butterflies, stage m = 1,2,...,64:
@@ -153,11 +153,11 @@ static void wht128(float *x) {
 
 /* Encode one token row given its low-rank codes (see file header, part 2).
  * X row -> codes (H*bits/8 bytes), scales (H/group), outliers (k values).
- *   R[c]   = X[c] - P[c]                       (binary32)
+ *   R[c]   = fma(-I[t,c], sL[t], X[c])         (binary32, one rounding)
  *   O[j]   = X[idx[j]] (verbatim);  R[idx[j]] = 0
  *   W      = wht ? WHT128(R) per 128-block : R
  *   s      = max_{c in group} |W[c]| / qmax,  qmax = 2^(bits-1) - 1
- *   q      = clamp(rint(W[c] / s), -qmax, qmax)   (0 when s == 0)
+ *   q      = clamp(rint(W[c] * (qmax / max_{c in group} |W[c]|)), -qmax, qmax)
  *   u      = q + 2^(bits-1); int4 packs channel 2i in the low nibble.      */
 void cg_encode_given_lr(const void *X, int x_f32, int64_t T, int64_t H, int64_t ldx, const int8_t *Lq,
                         const float *sL, const int8_t *Vq, int r, const int32_t *idx, int k, int bits,
@@ -173,8 +173,7 @@ void cg_encode_given_lr(const void *X, int x_f32, int64_t T, int64_t H, int64_t 
         for (int64_t t = 0; t < T; ++t) {
             for (int64_t c = 0; c < H; ++c) {
                 float xv = x_f32 ? ((const float *)X)[t * ldx + c] : bf2f(((const uint16_t *)X)[t * ldx + c]);
-                float p = r ? lowrank_term(Lq + t * r, Vq + c * r, r, sL[t]) : 0.f;
-                w[c] = xv - p;
+                w[c] = r ? fmaf(-lowrank_int(Lq + t * r, Vq + c * r, r), sL[t], xv) : xv;
             }
             for (int j = 0; j < k; ++j) {
                 int64_t c = idx[j];
@@ -194,18 +193,11 @@ void cg_encode_given_lr(const void *X, int x_f32, int64_t T, int64_t H, int64_t 
                     float a = fabsf(w[gi * group + c]);
                     if (a > amax) amax = a;
                 }
-                float s = amax / (float)qmax;
-                scales[t * ngroups + gi] = s;
+                scales[t * ngroups + gi] = amax / (float)qmax;
+                const float rs = rscale_of(amax, (float)qmax);
                 for (int c = 0; c < group; ++c) {
                     int64_t cc = gi * group + c;
-                    int q = 0;
-                    if (s > 0.f) {
-                        float v = rintf(w[cc] / s);
-                        if (v > (float)qmax) v = (float)qmax;
-                        if (v < -(float)qmax) v = -(float)qmax;
-                        q = (int)v;
-                    }
-                    unsigned u = (unsigned)(q + off);
+                    unsigned u = (unsigned)(code_of(w[cc], rs, qmax) + off);
                     if (bits == 8)
                         crow[cc] = (uint8_t)u;
                     else
@@ -220,7 +212,7 @@ void cg_encode_given_lr(const void *X, int x_f32, int64_t T, int64_t H, int64_t 
 /* Decode (see file header, part 2):
  *   w  = (float)(u - 2^(bits-1)) * s
  *   r^ = wht ? WHT128(w) * (1/128) : w
- *   x^ = out_dtype(r^ + P);  x^[idx[j]] = O[j] verbatim.                     */
+ *   x^ = out_dtype(fma(I[t,c], sL[t], r^));  x^[idx[j]] = O[j] verbatim.     */
 void cg_decode(const uint8_t *codes, const float *scales, const int8_t *Lq, const float *sL, const int8_t *Vq,
                int r, const void *outl, const int32_t *idx, int k, int64_t T, int64_t H, int bits, int group,
                int wht, int x_f32, void *Xhat) {
@@ -243,8 +235,7 @@ void cg_decode(const uint8_t *codes, const float *scales, const int8_t *Lq, cons
                     for (int i = 0; i < 128; ++i) w[b + i] = w[b + i] * 0.0078125f;
                 }
             for (int64_t c = 0; c < H; ++c) {
-                float p = r ? lowrank_term(Lq + t * r, Vq + c * r, r, sL[t]) : 0.f;
-                float v = w[c] + p;
+                float v = r ? fmaf(lowrank_int(Lq + t * r, Vq + c * r, r), sL[t], w[c]) : w[c];
                 if (x_f32)
                     ((float *)Xhat)[t * H + c] = v;
                 else

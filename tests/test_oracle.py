@@ -128,6 +128,7 @@ def test_cg_lowrank_term_is_exact_integer(O):
     Lq, sL = O.lr_quantize(L, prep[2])
     zero_codes = np.full((16, 64), 0x88, np.uint8)
     xh = O.decode(zero_codes, np.zeros((16, 2), np.float32), Lq, sL, prep[1], None, None, 128, 4, 64, False)
+    # decode of an all-zero residual is bf16(fma(I, sL, 0)) = bf16(I * sL), I exact
     ref = (Lq.astype(np.int64) @ prep[1].astype(np.int64).T).astype(np.float32) * sL[:, None]
     assert np.array_equal(xh, O.f32_to_bf16(ref))
 

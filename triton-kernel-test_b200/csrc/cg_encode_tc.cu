@@ -60,7 +60,7 @@ struct EncLayout {
     static constexpr int PART = ROWS * PART_PITCH * 4;
     static constexpr int LQT = ROWS * RB;
     static constexpr int BAR_OFF = RING + PART + LQT;
-    static constexpr int TOTAL = BAR_OFF + 512 + 1024;
+    static constexpr int TOTAL = BAR_OFF + 768 + 1024;
     static constexpr int THREADS = 128 + 32 * EW;  // 2 producers, 2 MMA issuers, epilogue
 };
 
@@ -85,18 +85,11 @@ __device__ __forceinline__ void wht128_reg(float (&v)[128]) {
     }
 }
 
-// rint(w / s) clamped to +-qmax, with the quotient correctly rounded first (as
-// the oracle): a reciprocal product decides every case that is not within
-// 2^-11 of a rounding tie; those few take the exact division.
-__device__ __forceinline__ int quant_code(float w, float s, float rcp, int qmax) {
-    if (!(s > 0.f)) return 0;
-    const float y = __fmul_rn(w, rcp);
-    const float ry = rintf(y);
-    int q;
-    if (fabsf(__fsub_rn(y, ry)) < 0.4995f) q = (int)ry;
-    else q = __float2int_rn(__fdiv_rn(w, s));
-    return max(-qmax, min(qmax, q));
-}
+// Codes: q = clamp(rint(w * rs), -qmax, qmax) with rs = qmax / absmax (one
+// correctly rounded division per group, as the oracle).  Adding
+// MAGIC = 1.5 * 2^23 + 2^(b-1) to y = w * rs rounds it to the nearest integer
+// (ties to even) and leaves q + 2^(b-1) in the low mantissa bits.  Since
+// |w| <= absmax, |y| <= qmax (1 + 2^-23) < qmax + 1/2: the clamp never acts.
 
 template <int BITS, bool WHT, int RB, int EW>
 __global__ void __launch_bounds__(EncLayout<BITS, WHT, RB, EW>::THREADS, 1)
@@ -274,6 +267,9 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RB, EW>::THREADS, 1)
         const int q = warp & 3;
         const int h = (EW == 8) ? (ew >> 2) : 0;
         constexpr int NC = EW == 8 ? 64 : 128;
+        constexpr int NP = NC / 32;
+        int32_t *sidx = reinterpret_cast<int32_t *>(tmem_slot + 8);  // outlier channels of the current slice
+        int cur_slice = -1;
         const int row = q * 32 + lane;
         const int ngr = (int)(p.H / p.group);
         const int64_t rowb = p.H * BITS / 8;
@@ -347,13 +343,14 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RB, EW>::THREADS, 1)
                 }
             }
             const float sl = __fdiv_rn(amax, 127.0f);
+            const float rsl = amax > 0.f ? __fdiv_rn(127.0f, amax) : 0.f;
             uint32_t lw[RB / 4];
 #pragma unroll
             for (int e = 0; e < RB / 4; ++e) lw[e] = 0;
 #pragma unroll
             for (int e = 0; e < RB; ++e) {
                 if (e < r) {
-                    const int qv = sl > 0.f ? max(-127, min(127, __float2int_rn(__fdiv_rn(Lr[e], sl)))) : 0;
+                    const int qv = max(-127, min(127, __float2int_rn(__fmul_rn(Lr[e], rsl))));
                     lw[e >> 2] |= (uint32_t)(qv & 0xff) << ((e & 3) * 8);
                 }
             }
@@ -375,7 +372,13 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RB, EW>::THREADS, 1)
             if (lane == 0) tc::mbar_arrive(lqready);
 
             // ---- residual codes, chunk by chunk
-            const int32_t *idx = p.k ? p.idx + (int64_t)b * p.k : nullptr;
+            const float nsl = -sl;
+            if (p.k && b != cur_slice) {
+                tc::named_bar(2, 32 * EW);
+                for (int jx = ew * 32 + lane; jx < p.k; jx += 32 * EW) sidx[jx] = __ldg(p.idx + (int64_t)b * p.k + jx);
+                tc::named_bar(2, 32 * EW);
+                cur_slice = b;
+            }
             for (int ck = 0; ck < nk2 && ok; ++ck, ++j) {
                 const int s = j % NB, tb2 = j & 1;
                 if (!(ok = tc::mbar_wait(&fullB[s], (j / NB) & 1, abort))) break;
@@ -385,12 +388,24 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RB, EW>::THREADS, 1)
                 const bool cv = c0 < c_hi;                            // warp-uniform
                 const uint8_t *xt = ringB + s * SLOT_B;
                 float w[NC];
+                float am[NP];
                 if (cv) {
+                    // with 64 columns both TMEM reads go out before the first wait
+                    constexpr int IN = NP <= 2 ? NP : 1;
+                    uint32_t I[IN][32];
+                    const uint32_t tbase = tm_p + tb2 * CH + ((uint32_t)(q * 32) << 16) + h * 64;
+                    if constexpr (NP <= 2) {
 #pragma unroll
-                    for (int jj = 0; jj < NC / 32; ++jj) {
-                        uint32_t I[32];
-                        tc::tmem_ld32(tm_p + tb2 * CH + ((uint32_t)(q * 32) << 16) + h * 64 + 32 * jj, I);
+                        for (int jj = 0; jj < NP; ++jj) tc::tmem_ld32(tbase + 32 * jj, I[jj]);
                         tc::tmem_ld_wait();
+                    }
+#pragma unroll
+                    for (int jj = 0; jj < NP; ++jj) {
+                        uint32_t (&Ij)[32] = I[NP <= 2 ? jj : 0];
+                        if constexpr (NP > 2) {
+                            tc::tmem_ld32(tbase + 32 * jj, Ij);
+                            tc::tmem_ld_wait();
+                        }
                         const uint8_t *box = xt + (h + (jj >> 1)) * ROWS * 128;
 #pragma unroll
                         for (int c16 = 0; c16 < 4; ++c16) {
@@ -399,8 +414,7 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RB, EW>::THREADS, 1)
 #pragma unroll
                             for (int e = 0; e < 8; ++e) {
                                 const float xv = __uint_as_float(e & 1 ? (wd[e >> 1] & 0xffff0000u) : (wd[e >> 1] << 16));
-                                const int col = 32 * jj + 8 * c16 + e;
-                                w[col] = __fsub_rn(xv, __fmul_rn(__int2float_rn((int)I[8 * c16 + e]), sl));
+                                w[32 * jj + 8 * c16 + e] = __fmaf_rn(i2f_exact((int)Ij[8 * c16 + e]), nsl, xv);
                             }
                         }
                     }
@@ -408,29 +422,29 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RB, EW>::THREADS, 1)
                 tc::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(&tempty[tb2]);
-                // outlier channels of my columns: verbatim copy, residual zeroed
+                // outlier channels of my columns: verbatim copy, residual zeroed.
+                // The mask comes from the shared copy of the indices by two ballots.
                 if (cv && p.k) {
 #pragma unroll
                     for (int g = 0; g < NC / 64; ++g) {
-                        const int64_t lo_c = c0 + 64 * g, hi_c = lo_c + 64;
-                        int lo = 0, hi = p.k;
-                        while (lo < hi) {
-                            const int mid = (lo + hi) >> 1;
-                            if (__ldg(idx + mid) < lo_c) lo = mid + 1;
-                            else hi = mid;
-                        }
+                        const int64_t lo_c = c0 + 64 * g;
                         uint64_t om = 0;
-                        for (int jj = lo; jj < p.k; ++jj) {
-                            const int64_t c = __ldg(idx + jj);
-                            if (c >= hi_c) break;
-                            om |= 1ull << (c - lo_c);
+                        int below = 0;
+#pragma unroll
+                        for (int half = 0; half < 2; ++half) {
+                            const int jx = lane + 32 * half;
+                            const int64_t c = jx < p.k ? (int64_t)sidx[jx] : INT64_MAX;
+                            below += __popc(__ballot_sync(0xffffffffu, c < lo_c));
+                            if (c >= lo_c && c < lo_c + 64) om |= 1ull << (c - lo_c);
                         }
+#pragma unroll
+                        for (int o = 16; o > 0; o >>= 1) om |= __shfl_xor_sync(0xffffffffu, om, o);
                         if (om) {
                             const uint8_t *box = xt + (h + g) * ROWS * 128;
 #pragma unroll
                             for (int e = 0; e < 64; ++e) {
                                 if ((om >> e) & 1ull) {
-                                    const int slot = lo + __popcll(om & ((1ull << e) - 1ull));
+                                    const int slot = below + __popcll(om & ((1ull << e) - 1ull));
                                     const uint16_t bits =
                                         *reinterpret_cast<const uint16_t *>(box + swz<128>(row, e >> 3) + 2 * (e & 7));
                                     if (rv) p.outl[trow * p.k + slot] = bits;
@@ -444,35 +458,37 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RB, EW>::THREADS, 1)
                 if (lane == 0) tc::mbar_arrive(&emptyB[s]);  // X and basis tile no longer needed
                 if (!cv) continue;
                 if constexpr (WHT) wht128_reg(*reinterpret_cast<float(*)[128]>(&w[0]));
-                // group absmax, scale, codes
-                uint32_t packed[NC * BITS / 32];
-#pragma unroll
-                for (int e = 0; e < NC * BITS / 32; ++e) packed[e] = 0;
                 // absmax of each 32-column piece, combined over the pieces of a group
-                float am[NC / 32];
 #pragma unroll
-                for (int pc = 0; pc < NC / 32; ++pc) {
+                for (int pc = 0; pc < NP; ++pc) {
                     float m = 0.f;
 #pragma unroll
                     for (int e = 0; e < 32; ++e) m = fmaxf(m, fabsf(w[32 * pc + e]));
                     am[pc] = m;
                 }
                 const int G = p.group;
+                uint32_t packed[NC * BITS / 32];
+                constexpr float MAGIC = 12582912.0f + (float)off;
+                constexpr uint32_t UMASK = (1u << BITS) - 1u;
 #pragma unroll
-                for (int pc = 0; pc < NC / 32; ++pc) {
+                for (int pc = 0; pc < NP; ++pc) {
                     float gam = am[pc];
                     if (G >= 64) gam = fmaxf(gam, am[pc ^ 1]);
                     if constexpr (NC == 128) {
                         if (G >= 128) gam = fmaxf(gam, fmaxf(am[pc ^ 2], am[pc ^ 3]));
                     }
                     const float sc = __fdiv_rn(gam, (float)qmax);
-                    const float rcp = __frcp_rn(sc);
+                    const float rs = gam > 0.f ? __fdiv_rn((float)qmax, gam) : 0.f;
                     if (((32 * pc) % G) == 0 && rv) p.scales[trow * ngr + (c0 + 32 * pc) / G] = sc;
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) {
-                        const uint32_t u = (uint32_t)(quant_code(w[32 * pc + e], sc, rcp, qmax) + off);
-                        const int col = 32 * pc + e;
-                        packed[col * BITS / 32] |= u << ((col * BITS) % 32);
+                    for (int wd = 0; wd < BITS; ++wd) {  // BITS words of codes per 32-column piece
+                        uint32_t acc = 0;
+#pragma unroll
+                        for (int e = 0; e < 32 / BITS; ++e) {
+                            const float t = __fadd_rn(__fmul_rn(w[32 * pc + wd * (32 / BITS) + e], rs), MAGIC);
+                            acc |= (__float_as_uint(t) & UMASK) << (e * BITS);
+                        }
+                        packed[pc * BITS + wd] = acc;
                     }
                 }
                 if (rv) {

@@ -10,7 +10,7 @@
 // Arithmetic follows oracle/actcomp_oracle.c step for step (single binary32
 // operations, round-to-nearest-even, no contraction), so codes, scales and
 // reconstructions match it bit for bit; the low-rank term is an exact integer
-// dot product (dp4a) times the per-token scale.
+// dot product (dp4a) entering one fused multiply-add with the per-token scale.
 #include "common.cuh"
 
 namespace act {
@@ -149,11 +149,11 @@ __global__ void basis_prepare_kernel(const float *V, int64_t H, int rank, uint16
     }
     __syncthreads();
     const float s = __fdiv_rn(red[0], 127.0f);
+    const float rs = red[0] > 0.f ? __fdiv_rn(127.0f, red[0]) : 0.f;
     if (threadIdx.x == 0) sV[(int64_t)b * rank + j] = s;
     for (int64_t c = threadIdx.x; c < H; c += blockDim.x) {
         float x = v[c * rank + j];
-        int q = 0;
-        if (s > 0.f) q = max(-127, min(127, __float2int_rn(__fdiv_rn(x, s))));
+        const int q = max(-127, min(127, __float2int_rn(__fmul_rn(x, rs))));
         Vq[(int64_t)b * H * rank + c * rank + j] = (int8_t)q;
         Vt[(int64_t)b * rank * H + (int64_t)j * H + c] = f2bf(x);
     }
@@ -262,14 +262,9 @@ __global__ void __launch_bounds__(256) cg_project_kernel(actcomp_cg_desc d, cons
         float lt1 = has1 ? __fmul_rn(mine1, s.basis_s[lane + 32]) : 0.f;
         float amax = warp_max(fmaxf(fabsf(lt0), fabsf(lt1)));
         float sl = __fdiv_rn(amax, 127.0f);
-        if (has0) {
-            int q = sl > 0.f ? max(-127, min(127, __float2int_rn(__fdiv_rn(lt0, sl)))) : 0;
-            s.lrq[t * RANK + lane] = (int8_t)q;
-        }
-        if (has1) {
-            int q = sl > 0.f ? max(-127, min(127, __float2int_rn(__fdiv_rn(lt1, sl)))) : 0;
-            s.lrq[t * RANK + lane + 32] = (int8_t)q;
-        }
+        const float rs = amax > 0.f ? __fdiv_rn(127.0f, amax) : 0.f;
+        if (has0) s.lrq[t * RANK + lane] = (int8_t)max(-127, min(127, __float2int_rn(__fmul_rn(lt0, rs))));
+        if (has1) s.lrq[t * RANK + lane + 32] = (int8_t)max(-127, min(127, __float2int_rn(__fmul_rn(lt1, rs))));
         if (lane == 0) s.lrs[t] = sl;
     }
 }
@@ -302,9 +297,8 @@ __global__ void __launch_bounds__(256) cg_quant_kernel(actcomp_cg_desc d, const 
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 float xv = __uint_as_float(i & 1 ? (xw[i >> 1] & 0xffff0000u) : (xw[i >> 1] << 16));
-                float p = 0.f;
-                if (s.rank) p = __fmul_rn(__int2float_rn(lr_dot(lw, s.basis_q + (c0 + i) * s.rank, s.rank)), sl);
-                w[i] = __fsub_rn(xv, p);
+                w[i] = s.rank ? __fmaf_rn(-__int2float_rn(lr_dot(lw, s.basis_q + (c0 + i) * s.rank, s.rank)), sl, xv)
+                              : xv;
             }
         }
         // outlier channels of this chunk: verbatim copy, residual zeroed
@@ -325,14 +319,12 @@ __global__ void __launch_bounds__(256) cg_quant_kernel(actcomp_cg_desc d, const 
         float amax = fmaxf(fmaxf(fabsf(w[0]), fabsf(w[1])), fmaxf(fabsf(w[2]), fabsf(w[3])));
         amax = group_max(amax, glanes);
         const float sc = __fdiv_rn(amax, (float)qmax);
+        const float rs = amax > 0.f ? __fdiv_rn((float)qmax, amax) : 0.f;
         if (!valid) continue;
         if ((lane % glanes) == 0) s.scales[t * ngroups + c0 / s.group] = sc;
         uint32_t u[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) {
-            int q = sc > 0.f ? max(-qmax, min(qmax, __float2int_rn(__fdiv_rn(w[i], sc)))) : 0;
-            u[i] = (uint32_t)(q + off);
-        }
+        for (int i = 0; i < 4; ++i) u[i] = (uint32_t)(max(-qmax, min(qmax, __float2int_rn(__fmul_rn(w[i], rs)))) + off);
         if constexpr (BITS == 4) {
             uint16_t packed = (uint16_t)(u[0] | (u[1] << 4) | (u[2] << 8) | (u[3] << 12));
             *reinterpret_cast<uint16_t *>(s.codes + t * (s.H / 2) + c0 / 2) = packed;
@@ -369,9 +361,10 @@ __device__ __forceinline__ void reconstruct4(const CgSlice &s, int64_t t, int64_
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        float p = 0.f;
-        if (s.rank && valid) p = __fmul_rn(__int2float_rn(lr_dot(lw, s.basis_q + (c0 + i) * s.rank, s.rank)), sl);
-        xh[i] = f2bf(__fadd_rn(w[i], p));
+        const float v = (s.rank && valid)
+                            ? __fmaf_rn(__int2float_rn(lr_dot(lw, s.basis_q + (c0 + i) * s.rank, s.rank)), sl, w[i])
+                            : w[i];
+        xh[i] = f2bf(v);
     }
     if (s.k) {
         const int64_t cs = ch * 128, ce = cs + 128;

@@ -48,7 +48,7 @@ struct DecLayout {
     static constexpr int EW = WHT ? 4 : 8;  // epilogue warps
     static constexpr int THREADS = 64 + 32 * EW;
     static constexpr int BAR_OFF = S * STAGE + 2 * OUT;
-    static constexpr int TOTAL = BAR_OFF + 256 + 1024;
+    static constexpr int TOTAL = BAR_OFF + 512 + 1024;
     static constexpr int CODE_ROW = CH * BITS / 8;  // bytes of one token's codes in the tile
 };
 
@@ -181,9 +181,35 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
         const int q = warp & 3;              // TMEM lane quadrant of this warp
         const int h = WHT ? 0 : ew >> 2;     // column half (64 columns) when 8 warps
         constexpr int NC = WHT ? 128 : 64;   // columns per thread
+        constexpr int NP = NC / 32;          // 32-column pieces per thread
         const int r = q * 32 + lane;         // row of the tile
         const int ngr = (int)(p.H / p.group);
         const bool leader = (ew == 0 && lane == 0);
+        int32_t *sidx = reinterpret_cast<int32_t *>(tmem_slot + 8);  // outlier channels of the current slice
+        int cur_slice = -1;
+
+        // per-row scalars of a tile, loaded one tile ahead so their latency hides
+        float nsc[NP], nsl = 0.f;
+        auto prefetch = [&](int64_t tile) {
+#pragma unroll
+            for (int j = 0; j < NP; ++j) nsc[j] = 0.f;
+            nsl = 0.f;
+            if (tile >= p.ntiles) return;
+            const int cc = (int)(tile % p.ncc);
+            const int64_t bt = tile / p.ncc;
+            const int tb = (int)(bt % p.ntb), sb = (int)(bt / p.ntb);
+            const int64_t t = (int64_t)tb * ROWS + r;
+            if (t >= p.T) return;
+            const int64_t trow = (int64_t)sb * p.T + t;
+#pragma unroll
+            for (int j = 0; j < NP; ++j) {
+                const int64_t c = (int64_t)cc * CH + h * 64 + 32 * j;
+                if (c < p.H) nsc[j] = __ldg(p.scales + trow * ngr + c / p.group);
+            }
+            if (RB) nsl = __ldg(p.lr_scale + trow);
+        };
+        prefetch(blockIdx.x);
+
         int i = 0;
         for (int64_t tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x, ++i) {
             const int s = i % L::S, b = i & 1, ob = i & 1;
@@ -191,29 +217,42 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
             const int cc = (int)(tile % p.ncc);
             const int64_t bt = tile / p.ncc;
             const int tb = (int)(bt % p.ntb), sl_b = (int)(bt / p.ntb);
+            float sc[NP];
+#pragma unroll
+            for (int j = 0; j < NP; ++j) sc[j] = nsc[j];
+            const float sl = nsl;
+            prefetch(tile + gridDim.x);
+
+            // outlier channels of this slice, in shared memory
+            if (p.k && sl_b != cur_slice) {
+                tc::named_bar(2, 32 * L::EW);
+                for (int j = ew * 32 + lane; j < p.k; j += 32 * L::EW) sidx[j] = __ldg(p.idx + (int64_t)sl_b * p.k + j);
+                tc::named_bar(2, 32 * L::EW);
+                cur_slice = sl_b;
+            }
             bool ok = tc::mbar_wait(&full[s], ph, abort);
             if (RB) ok = ok && tc::mbar_wait(&tfull[b], bph, abort);
             if (!ok) break;
             tc::tc_fence_after();
             const int64_t t = (int64_t)tb * ROWS + r;
             const bool rv = t < p.T;
-            const int64_t trow = (int64_t)sl_b * p.T + t;  // token row across slices
+            const int64_t trow = (int64_t)sl_b * p.T + t;
             const int64_t c_first = (int64_t)cc * CH + h * 64;
 
-            const float sl = (RB && rv) ? p.lr_scale[trow] : 0.f;
-            // low-rank term I for my columns: read up front without the rotation
-            // (latency overlaps the residual), chunk by chunk after it (registers)
+            // low-rank term I: read up front without the rotation (its latency
+            // overlaps the residual), piece by piece after it (registers)
             uint32_t I[WHT ? 32 : NC];
             const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + b * CH + h * 64;
             if constexpr (RB > 0 && !WHT) {
 #pragma unroll
-                for (int j = 0; j < NC / 32; ++j)
+                for (int j = 0; j < NP; ++j)
                     tc::tmem_ld32(taddr + 32 * j, *reinterpret_cast<uint32_t(*)[32]>(&I[32 * j]));
             }
 
-            // residual: codes of my row and columns
+            // residual: w = (u - 2^(b-1)) * s
             const uint8_t *ct = smem + s * L::STAGE + L::LQ + L::VQ;
             float w[NC];
+            constexpr float UOFF = 8388608.0f + (float)off;
 #pragma unroll
             for (int c16 = 0; c16 < NC * BITS / 128; ++c16) {  // 16-byte code chunks
                 const int chunk = (h * 64 * BITS / 8) / 16 + c16;
@@ -223,77 +262,73 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
                 for (int e = 0; e < 128 / BITS; ++e) {
                     const int col = c16 * (128 / BITS) + e;
                     const uint32_t u = (wd[e / (32 / BITS)] >> ((e % (32 / BITS)) * BITS)) & ((1u << BITS) - 1u);
-                    w[col] = __int2float_rn((int)u - off);
+                    w[col] = __fmul_rn(u2f_minus(u, UOFF), sc[col / 32]);
                 }
-            }
-            // scales: one per group; the group size is a multiple of 32
-#pragma unroll
-            for (int j = 0; j < NC; j += 32) {
-                const int64_t c = c_first + j;
-                float sc = 0.f;
-                if (rv && c < p.H) sc = __ldg(p.scales + trow * ngr + c / p.group);
-#pragma unroll
-                for (int e = 0; e < 32; ++e) w[j + e] = __fmul_rn(w[j + e], sc);
             }
             if constexpr (WHT) {
                 wht128_reg(w);
 #pragma unroll
                 for (int j = 0; j < NC; ++j) w[j] = __fmul_rn(w[j], 0.0078125f);
             }
-            // xhat = bf16(w + I * sL), in place
+            // xhat = fma(I, sL, w), in place
             if constexpr (RB > 0) {
                 if constexpr (WHT) {
 #pragma unroll
-                    for (int j = 0; j < NC / 32; ++j) {
+                    for (int j = 0; j < NP; ++j) {
                         tc::tmem_ld32(taddr + 32 * j, *reinterpret_cast<uint32_t(*)[32]>(&I[0]));
                         tc::tmem_ld_wait();
 #pragma unroll
-                        for (int e = 0; e < 32; ++e)
-                            w[32 * j + e] = __fadd_rn(w[32 * j + e], __fmul_rn(__int2float_rn((int)I[e]), sl));
+                        for (int e = 0; e < 32; ++e) w[32 * j + e] = __fmaf_rn(i2f_exact((int)I[e]), sl, w[32 * j + e]);
                     }
                 } else {
                     tc::tmem_ld_wait();
 #pragma unroll
-                    for (int j = 0; j < NC; ++j) w[j] = __fadd_rn(w[j], __fmul_rn(__int2float_rn((int)I[j]), sl));
+                    for (int j = 0; j < NC; ++j) w[j] = __fmaf_rn(i2f_exact((int)I[j]), sl, w[j]);
                 }
                 tc::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(&tempty[b]);
             }
-            // outlier channels inside my columns: mask of their positions (uniform over the warp)
+            // outlier channels inside my columns (uniform over the warp): a mask
+            // built from the shared copy of the slice's indices with two ballots
             uint64_t om[NC / 64];
             int olo[NC / 64];
 #pragma unroll
             for (int g = 0; g < NC / 64; ++g) {
                 om[g] = 0;
                 olo[g] = 0;
-            }
-            if (p.k) {
-                const int32_t *idx = p.idx + (int64_t)sl_b * p.k;
+                if (p.k) {
+                    const int64_t lo_c = c_first + 64 * g;
+                    uint64_t bits = 0;
+                    int below = 0;
 #pragma unroll
-                for (int g = 0; g < NC / 64; ++g) {
-                    const int64_t lo_c = c_first + 64 * g, hi_c = lo_c + 64;
-                    int lo = 0, hi = p.k;
-                    while (lo < hi) {
-                        int mid = (lo + hi) >> 1;
-                        if (__ldg(idx + mid) < lo_c) lo = mid + 1;
-                        else hi = mid;
+                    for (int half = 0; half < 2; ++half) {
+                        const int j = lane + 32 * half;
+                        const int64_t c = j < p.k ? (int64_t)sidx[j] : INT64_MAX;
+                        below += __popc(__ballot_sync(0xffffffffu, c < lo_c));
+                        if (c >= lo_c && c < lo_c + 64) bits |= 1ull << (c - lo_c);
                     }
-                    olo[g] = lo;
-                    for (int j = lo; j < p.k; ++j) {
-                        const int64_t c = __ldg(idx + j);
-                        if (c >= hi_c) break;
-                        om[g] |= 1ull << (c - lo_c);
-                    }
+#pragma unroll
+                    for (int o = 16; o > 0; o >>= 1) bits |= __shfl_xor_sync(0xffffffffu, bits, o);
+                    om[g] = bits;
+                    olo[g] = below;
                 }
             }
-            float (&xh)[NC] = w;
+            // bf16 reconstruction (the consumer ops take it as their input)
+            if constexpr (OP != ACT_OP_DECODE) {
 #pragma unroll
-            for (int j = 0; j < NC; ++j) {
-                xh[j] = rne_bf(xh[j]);
-                if ((om[j / 64] >> (j % 64)) & 1ull) {
-                    const int slot = olo[j / 64] + __popcll(om[j / 64] & ((1ull << (j % 64)) - 1ull));
-                    xh[j] = rv ? bf2f(p.outliers[trow * p.k + slot]) : 0.f;
+                for (int j = 0; j < NC; ++j) w[j] = rne_bf(w[j]);
+            }
+#pragma unroll
+            for (int g = 0; g < NC / 64; ++g) {
+                if (om[g]) {
+#pragma unroll
+                    for (int e = 0; e < 64; ++e) {
+                        if ((om[g] >> e) & 1ull) {
+                            const int slot = olo[g] + __popcll(om[g] & ((1ull << e) - 1ull));
+                            w[g * 64 + e] = rv ? bf2f(p.outliers[trow * p.k + slot]) : 0.f;
+                        }
+                    }
                 }
             }
             // second operand and consumer op
@@ -309,8 +344,8 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
 #pragma unroll
                         for (int e = 0; e < 4; ++e) {
                             const int j = g * 64 + c16 * 8 + 2 * e;
-                            xh[j] = apply_op<OP>(xh[j], lo_bf(wd[e]));
-                            xh[j + 1] = apply_op<OP>(xh[j + 1], hi_bf(wd[e]));
+                            w[j] = apply_op<OP>(w[j], lo_bf(wd[e]));
+                            w[j + 1] = apply_op<OP>(w[j + 1], hi_bf(wd[e]));
                         }
                     }
                 }
@@ -330,10 +365,10 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
                 for (int c16 = 0; c16 < 8; ++c16) {
                     const int j = g * 64 + c16 * 8;
                     uint4 v;
-                    v.x = pack_bf(xh[j], xh[j + 1]);
-                    v.y = pack_bf(xh[j + 2], xh[j + 3]);
-                    v.z = pack_bf(xh[j + 4], xh[j + 5]);
-                    v.w = pack_bf(xh[j + 6], xh[j + 7]);
+                    v.x = pack_bf16x2(w[j], w[j + 1]);
+                    v.y = pack_bf16x2(w[j + 2], w[j + 3]);
+                    v.z = pack_bf16x2(w[j + 4], w[j + 5]);
+                    v.w = pack_bf16x2(w[j + 6], w[j + 7]);
                     *reinterpret_cast<uint4 *>(box + swz<128>(r, c16)) = v;
                 }
             }

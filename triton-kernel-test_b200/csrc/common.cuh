@@ -59,23 +59,52 @@ __device__ __forceinline__ float group_max(float v, int width) {
     return v;
 }
 
+// ---------------------------------------------------------------- exact int <-> float
+// For |v| < 2^22, v + 1.5 * 2^23 is a float whose mantissa holds v exactly, so
+// one integer add and one float subtract convert without the quarter-rate
+// conversion pipe.
+__device__ __forceinline__ float i2f_exact(int v) {
+    return __fsub_rn(__int_as_float(v + 0x4B400000), 12582912.0f);
+}
+// (float)u for 0 <= u < 2^23, minus a constant folded into the subtraction.
+__device__ __forceinline__ float u2f_minus(uint32_t u, float c_plus_2p23) {
+    return __fsub_rn(__uint_as_float(0x4B000000u | u), c_plus_2p23);
+}
+__device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
+    __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
+    return *reinterpret_cast<uint32_t *>(&v);
+}
+
 // ---------------------------------------------------------------- consumer ops
-// All evaluate in binary32 in the order the reference twins write them and
-// round once to bf16.
+// The derivative formulas of the reference twins, evaluated in binary32 in the
+// order they are written there and rounded once to bf16.  exp and the
+// reciprocal use the hardware approximations (ex2.approx, rcp.approx: a few
+// ulp), so outputs agree with the libm-based oracle except where a bf16
+// rounding boundary falls inside that error.
+__device__ __forceinline__ float hw_exp(float x) {
+    float y;
+    asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(__fmul_rn(x, 1.4426950408889634f)));
+    return y;
+}
+__device__ __forceinline__ float hw_rcp(float x) {
+    float y;
+    asm("rcp.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+    return y;
+}
 __device__ __forceinline__ float silu_bwd_f(float x, float g) {
     // silu_backward.py:6-8
-    float s = __fdiv_rn(1.0f, __fadd_rn(1.0f, expf(-x)));
+    const float s = hw_rcp(__fadd_rn(1.0f, hw_exp(-x)));
     return __fmul_rn(g, __fmul_rn(s, __fadd_rn(1.0f, __fmul_rn(x, __fsub_rn(1.0f, s)))));
 }
 __device__ __forceinline__ float gelu_bwd_f(float x, float g) {
-    // gelu_backward.py:14-21 (tanh approximation)
+    // gelu_backward.py:14-21 (tanh approximation); tanh(y) = 1 - 2 / (e^{2y} + 1)
     const float gamma = 0.7978845608028654f, kappa = 0.044715f;
-    float x2 = __fmul_rn(x, x);
-    float y = __fmul_rn(gamma, __fadd_rn(x, __fmul_rn(kappa, __fmul_rn(x2, x))));
-    float th = tanhf(y);
-    float inner = __fmul_rn(__fmul_rn(__fsub_rn(1.0f, __fmul_rn(th, th)), gamma),
-                            __fadd_rn(1.0f, __fmul_rn(__fmul_rn(3.0f, kappa), x2)));
-    float d = __fmul_rn(0.5f, __fadd_rn(__fadd_rn(1.0f, th), __fmul_rn(x, inner)));
+    const float x2 = __fmul_rn(x, x);
+    const float y = __fmul_rn(gamma, __fadd_rn(x, __fmul_rn(kappa, __fmul_rn(x2, x))));
+    const float th = __fsub_rn(1.0f, __fmul_rn(2.0f, hw_rcp(__fadd_rn(hw_exp(__fmul_rn(2.0f, y)), 1.0f))));
+    const float inner = __fmul_rn(__fmul_rn(__fsub_rn(1.0f, __fmul_rn(th, th)), gamma),
+                                  __fadd_rn(1.0f, __fmul_rn(__fmul_rn(3.0f, kappa), x2)));
+    const float d = __fmul_rn(0.5f, __fadd_rn(__fadd_rn(1.0f, th), __fmul_rn(x, inner)));
     return __fmul_rn(d, g);
 }
 template <int OP>
