@@ -34,7 +34,6 @@ constexpr int KC = 64;     // channels per projection step
 constexpr int CH = 128;    // channels per quantisation chunk (MMA N)
 constexpr int NA = 3, SLOT_A = 24 * 1024;  // projection ring: X 128x64 (16 KB) + V^T r x 64 (<= 8 KB)
 constexpr int NB = 2, SLOT_B = 40 * 1024;  // residual ring: X 128x128 (32 KB) + Vq 128 x r (<= 8 KB)
-constexpr int PART_PITCH = 68;   // floats per row of the partial-projection buffer
 
 struct EncParams {
     int64_t T, H;
@@ -54,15 +53,26 @@ struct EncParams {
     int nclusters;
 };
 
+// Shared memory: the two rings, the low-rank code tile, barriers, then the
+// projection exchange buffers (send + C-1 receive slots, 128 x r floats each),
+// whose size depends on C and r and is added at launch.
 template <int BITS, bool WHT, int RB, int EW>
 struct EncLayout {
     static constexpr int RING = NA * SLOT_A + NB * SLOT_B;
-    static constexpr int PART = ROWS * PART_PITCH * 4;
     static constexpr int LQT = ROWS * RB;
-    static constexpr int BAR_OFF = RING + PART + LQT;
-    static constexpr int TOTAL = BAR_OFF + 768 + 1024;
+    static constexpr int BAR_OFF = RING + LQT;
+    static constexpr int XCH_OFF = BAR_OFF + 1024;
     static constexpr int THREADS = 128 + 32 * EW;  // 2 producers, 2 MMA issuers, epilogue
+    static int total(int C, int r) { return XCH_OFF + (C > 1 ? C * ROWS * r * 4 : 0) + 1024; }
 };
+// byte offset of float4 chunk c (0 .. r/4-1) of row `row` in an exchange
+// buffer: rows of r floats, chunks XOR-swizzled by the row (within aligned
+// groups of 8 chunks, or of 4 when r/4 is not a multiple of 8) so that 32
+// threads writing their rows' chunk c spread over the banks
+__device__ __forceinline__ int xch_off(int row, int c, int r) {
+    const int m = ((r / 4) % 8 == 0) ? 7 : 3;
+    return row * r * 4 + ((c ^ (row & m)) << 4);
+}
 
 template <int PITCH>
 __device__ __forceinline__ int swz(int r, int c) {
@@ -99,8 +109,9 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RB, EW>::THREADS, 1)
     constexpr int qmax = (1 << (BITS - 1)) - 1, off = 1 << (BITS - 1);
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    float *part = reinterpret_cast<float *>(smem + L::RING);
-    uint8_t *lqt = smem + L::RING + L::PART;
+    uint8_t *lqt = smem + L::RING;
+    uint8_t *xsend = smem + L::XCH_OFF;  // this CTA's partial projection
+    uint8_t *xrecv = xsend;              // + (slot + 1) * ROWS * r * 4: peers' partials
     uint64_t *fullA = reinterpret_cast<uint64_t *>(smem + L::BAR_OFF);
     uint64_t *emptyA = fullA + NA;
     uint64_t *fullB = emptyA + NA;
@@ -110,8 +121,8 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RB, EW>::THREADS, 1)
     uint64_t *lfull = tempty + 2;
     uint64_t *lempty = lfull + 1;
     uint64_t *lqready = lempty + 1;
-    uint64_t *pready = lqready + 1;
-    uint64_t *pdone = pready + 1;
+    uint64_t *pready = lqready + 1;  // peers' partials have landed (transaction bytes)
+    uint64_t *pdone = pready + 1;    // peers have consumed our previous partial
     uint64_t *lseen = pdone + 1;  // phase-2 producer has observed lfull of the block
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(lseen + 1);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
@@ -144,7 +155,7 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RB, EW>::THREADS, 1)
         tc::mbar_init(lfull, 1);
         tc::mbar_init(lempty, EW);
         tc::mbar_init(lqready, EW);
-        tc::mbar_init(pready, C > 1 ? C - 1 : 1);
+        tc::mbar_init(pready, 1);
         tc::mbar_init(pdone, C > 1 ? C - 1 : 1);
         tc::mbar_init(lseen, 1);
         *abort = 0;
@@ -298,27 +309,40 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RB, EW>::THREADS, 1)
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(lempty);
             if (C > 1) {
-                // our partial buffer may be overwritten once every peer has read the previous one
+                // Exchange: every CTA pushes its 128 x r partial to each peer with one
+                // bulk copy (completing on the peer's pready), then sums all partials
+                // in rank order from local shared memory.
+                const int PB = ROWS * r * 4;
+                // our send buffer and the peers' receive slots are free again once
+                // every peer has consumed the previous block
                 if (nb > 0 && !(ok = tc::mbar_wait_cluster(pdone, (nb - 1) & 1, abort))) break;
                 if (h == 0) {
-                    float4 *dst = reinterpret_cast<float4 *>(part + row * PART_PITCH);
 #pragma unroll
                     for (int e = 0; e < RB / 4; ++e)
-                        if (4 * e < r) dst[e] = make_float4(Lr[4 * e], Lr[4 * e + 1], Lr[4 * e + 2], Lr[4 * e + 3]);
+                        if (4 * e < r)
+                            *reinterpret_cast<float4 *>(xsend + xch_off(row, e, r)) =
+                                make_float4(Lr[4 * e], Lr[4 * e + 1], Lr[4 * e + 2], Lr[4 * e + 3]);
                 }
+                tc::fence_proxy_async();
                 tc::named_bar(1, 32 * EW);
-                if (ew == 0 && lane < C && lane != (int)crank) {
-                    tc::fence_acq_rel_cluster();
-                    tc::mbar_arrive_remote(tc::map_cluster(pready, lane));
+                if (ew == 0 && lane == 0) {
+                    tc::mbar_arrive_expect_tx(pready, (uint32_t)((C - 1) * PB));
+                    for (int q2 = 0; q2 < C; ++q2) {
+                        if (q2 == (int)crank) continue;
+                        const int slot = (int)crank < q2 ? (int)crank : (int)crank - 1;  // our slot at q2
+                        tc::bulk_copy_to_peer(tc::map_cluster(xrecv + (slot + 1) * PB, q2), xsend, (uint32_t)PB,
+                                              tc::map_cluster(pready, q2));
+                    }
                 }
-                if (!(ok = tc::mbar_wait_cluster(pready, nb & 1, abort))) break;
+                if (!(ok = tc::mbar_wait(pready, nb & 1, abort))) break;
                 // L = sum of the partials in rank order (identical in every CTA)
                 for (int pr = 0; pr < C; ++pr) {
-                    const uint32_t base = tc::map_cluster(part + row * PART_PITCH, pr);
+                    const uint8_t *src =
+                        pr == (int)crank ? xsend : xrecv + ((pr < (int)crank ? pr : pr - 1) + 1) * PB;
 #pragma unroll
                     for (int e = 0; e < RB / 4; ++e) {
                         if (4 * e < r) {
-                            const float4 v = tc::ld_cluster_f4(base + 16 * e);
+                            const float4 v = *reinterpret_cast<const float4 *>(src + xch_off(row, e, r));
                             Lr[4 * e] = pr ? __fadd_rn(Lr[4 * e], v.x) : v.x;
                             Lr[4 * e + 1] = pr ? __fadd_rn(Lr[4 * e + 1], v.y) : v.y;
                             Lr[4 * e + 2] = pr ? __fadd_rn(Lr[4 * e + 2], v.z) : v.z;
@@ -326,12 +350,9 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RB, EW>::THREADS, 1)
                         }
                     }
                 }
-                // tell every peer we are done reading its partial
+                // tell every peer we have consumed its partial (the values are in registers)
                 tc::named_bar(1, 32 * EW);
-                if (ew == 0 && lane < C && lane != (int)crank) {
-                    tc::fence_acq_rel_cluster();
-                    tc::mbar_arrive_remote(tc::map_cluster(pdone, lane));
-                }
+                if (ew == 0 && lane < C && lane != (int)crank) tc::mbar_arrive_remote(tc::map_cluster(pdone, lane));
             }
             // ---- per-token low-rank codes
             float amax = 0.f;
@@ -545,8 +566,10 @@ int launch_encode(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cuda
     p.unit = (d->wht || d->group == 128) ? 128 : 64;
     p.nunits = (int)(H / p.unit);
     // smallest cluster whose per-CTA slice keeps the second sweep's L2 window small
+    // smallest cluster whose per-CTA slice keeps the second sweep's L2 window
+    // small, within 64 KB of exchange buffers (C * 128 * r * 4 bytes)
     int C = 1;
-    while (C < 8 && (H / C > 1536) && p.nunits / (C * 2) >= 1) C *= 2;
+    while (C < 8 && (H / C > 1536) && p.nunits / (C * 2) >= 1 && (2 * C) * ROWS * r * 4 <= 64 * 1024) C *= 2;
     if (C > p.nunits) C = p.nunits;
     p.C = C;
     p.ntb = (int)((T + ROWS - 1) / ROWS);
@@ -554,11 +577,12 @@ int launch_encode(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cuda
     int maxc = num_sms() / C;
     p.nclusters = (int)(p.nblocks < maxc ? p.nblocks : maxc);
     auto kern = cg_encode_tc_kernel<BITS, WHT, RB, EW>;
-    ACT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
+    const int smem = L::total(C, r);
+    ACT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)(p.nclusters * C), 1, 1);
     cfg.blockDim = dim3(L::THREADS, 1, 1);
-    cfg.dynamicSmemBytes = L::TOTAL;
+    cfg.dynamicSmemBytes = smem;
     cfg.stream = stream;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;

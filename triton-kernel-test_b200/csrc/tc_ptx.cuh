@@ -111,12 +111,13 @@ __device__ __forceinline__ uint32_t map_cluster(const void *p, uint32_t rank) {
     asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(out) : "r"(smem_u32(p)), "r"(rank));
     return out;
 }
+// Volatile (kept in program order after the barrier wait that publishes the
+// data) but without a memory clobber, so consecutive loads issue back to back.
 __device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
     float4 v;
     asm volatile("ld.shared::cluster.v4.f32 {%0, %1, %2, %3}, [%4];"
                  : "=f"(v.x), "=f"(v.y), "=f"(v.z), "=f"(v.w)
-                 : "r"(addr)
-                 : "memory");
+                 : "r"(addr));
     return v;
 }
 
@@ -124,10 +125,13 @@ __device__ __forceinline__ float4 ld_cluster_f4(uint32_t addr) {
 __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
     asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
+// Non-suspending test: a thread suspended in try_wait on a barrier that only
+// other CTAs arrive on was observed to sleep out its whole suspend interval,
+// so cluster-scope waits poll with test_wait instead.
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t parity) {
     uint32_t ok;
     asm volatile(
-        "{\n .reg .pred p;\n mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
+        "{\n .reg .pred p;\n mbarrier.test_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n"
         " selp.u32 %0, 1, 0, p;\n}\n"
         : "=r"(ok)
         : "r"(smem_u32(bar)), "r"(parity)
@@ -136,7 +140,7 @@ __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t *bar, uint32_t pa
 }
 // bounded wait with cluster-scope acquire (for arrivals made by other CTAs)
 __device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity, volatile int *abort) {
-    for (uint32_t i = 0; i < (1u << 24); ++i) {
+    for (uint32_t i = 0; i < (1u << 28); ++i) {
         if (mbar_try_wait_cluster(bar, parity)) return true;
         if (*abort) return false;
     }
@@ -145,6 +149,19 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity
     return false;
 }
 __device__ __forceinline__ void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
+
+// Bulk copy of `bytes` (multiple of 16) from this CTA's shared memory into
+// another CTA's shared memory (both cluster addresses from map_cluster),
+// completing `bytes` of transaction count on the destination's mbarrier.
+// A point-to-point copy, no multicast.
+__device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst_cluster, const void *src, uint32_t bytes,
+                                                  uint32_t mbar_cluster) {
+    asm volatile(
+        "cp.async.bulk.shared::cluster.shared::cta.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+            dst_cluster),
+        "r"(smem_u32(src)), "r"(bytes), "r"(mbar_cluster)
+        : "memory");
+}
 
 // Make generic-proxy shared-memory writes visible to the async proxy
 // (tensor-core operand reads).
