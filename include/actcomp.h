@@ -66,6 +66,9 @@ int actcomp_clear_device_error(void *stream);
  *   basis_t     bf16    rank x H         V^T for the projection
  *   basis_q     int8    H x rank         quantised basis for the reconstruction
  *   basis_scale float   rank             per basis vector scale of basis_q
+ *   basis_qb    bf16    H x rank         basis_q as (exact) bf16 integers, the
+ *                                        tensor-core encode's operand (may be NULL:
+ *                                        the encode then runs on CUDA cores)
  * bits in {4, 8}; group in {32, 64, 128} dividing H; rank in {0, 16, 32, 48, 64};
  * 0 <= n_outlier <= 64; wht requires H % 128 == 0 and group <= 128.          */
 typedef struct actcomp_cg_desc {
@@ -86,13 +89,15 @@ typedef struct actcomp_cg_desc {
     const uint16_t *basis_t;
     const int8_t *basis_q;
     const float *basis_scale;
+    const uint16_t *basis_qb;
 } actcomp_cg_desc;
 
 /* Quantise a basis V (batch x H x rank, float32 row-major) into basis_t,
- * basis_q, basis_scale (layouts above).  No reference counterpart (the
- * reference takes l, r as given, low_rank_extraction_fuse_compression_quantization.py:118). */
+ * basis_q, basis_scale and (if non-NULL) basis_qb (layouts above).  No
+ * reference counterpart (the reference takes l, r as given,
+ * low_rank_extraction_fuse_compression_quantization.py:118). */
 int actcomp_cg_basis_prepare(const float *V, int64_t H, int32_t rank, int32_t batch, uint16_t *basis_t,
-                             int8_t *basis_q, float *basis_scale, void *stream);
+                             int8_t *basis_q, float *basis_scale, uint16_t *basis_qb, void *stream);
 
 /* Encode x (batch x T x H bf16, row stride ldx elements, slice stride T*ldx)
  * into the buffers of d.  Replaces low_rank_addition_fuse_compression_quantization

@@ -61,17 +61,21 @@ static inline float rne_bf(float f) { return bf2f(f2bf(f)); }
  * absmax a and code range qmax,
  *   scale  s  = a / qmax        (binary32 division; stored, used to decode)
  *   rscale rs = qmax / a        (binary32 division; 0 when a == 0)
- *   code   q  = clamp(rint(v * rs), -qmax, qmax)   (binary32 product, ties to even)
- * i.e. codes multiply by a correctly rounded reciprocal instead of dividing.
+ *   code   q  = clamp(nearest(v * rs), -qmax, qmax)
+ * where nearest() rounds the EXACT product v * rs to an integer, ties to even,
+ * with one rounding: q = fma(v, rs, 1.5 * 2^23) - 1.5 * 2^23 (exact because
+ * |v * rs| <= qmax + 1/2 < 2^22).  Codes multiply by a correctly rounded
+ * reciprocal instead of dividing, and the single fused rounding is what a GPU
+ * computes with one fma whatever the compiler contracts.
  *
  * Basis preparation.  V is H x r (column j = basis vector j).
  *   sV[j]    = max_c |V[c,j]| / 127
- *   Vq[c,j]  = clamp(rint(V[c,j] * (127 / max_c |V[c,j]|)), -127, 127)
+ *   Vq[c,j]  = clamp(nearest(V[c,j] * (127 / max_c |V[c,j]|)), -127, 127)
  *   Vt[j,c]  = bf16_rne(V[c,j])                          (projection basis)
  */
 static inline float rscale_of(float amax, float qmax) { return amax > 0.f ? qmax / amax : 0.f; }
 static inline int code_of(float v, float rs, int qmax) {
-    float t = rintf(v * rs);
+    float t = fmaf(v, rs, 12582912.0f) - 12582912.0f;
     if (t > (float)qmax) t = (float)qmax;
     if (t < -(float)qmax) t = -(float)qmax;
     return (int)t;
@@ -113,7 +117,7 @@ void cg_project(const void *X, int x_f32, int64_t T, int64_t H, int64_t ldx, con
 /* Per-token quantisation of the low-rank coefficients.
  *   Lt[j]  = L[t,j] * sV[j]
  *   sL[t]  = max_j |Lt[j]| / 127
- *   Lq[t,j]= clamp(rint(Lt[j] * (127 / max_j |Lt[j]|)), -127, 127)          */
+ *   Lq[t,j]= clamp(nearest(Lt[j] * (127 / max_j |Lt[j]|)), -127, 127)          */
 void cg_lr_quantize(const float *L, int64_t T, int r, const float *sV, int8_t *Lq, float *sL) {
 #pragma omp parallel for schedule(static)
     for (int64_t t = 0; t < T; ++t) {
@@ -157,7 +161,7 @@ static void wht128(float *x) {
  *   O[j]   = X[idx[j]] (verbatim);  R[idx[j]] = 0
  *   W      = wht ? WHT128(R) per 128-block : R
  *   s      = max_{c in group} |W[c]| / qmax,  qmax = 2^(bits-1) - 1
- *   q      = clamp(rint(W[c] * (qmax / max_{c in group} |W[c]|)), -qmax, qmax)
+ *   q      = clamp(nearest(W[c] * (qmax / max_{c in group} |W[c]|)), -qmax, qmax)
  *   u      = q + 2^(bits-1); int4 packs channel 2i in the low nibble.      */
 void cg_encode_given_lr(const void *X, int x_f32, int64_t T, int64_t H, int64_t ldx, const int8_t *Lq,
                         const float *sL, const int8_t *Vq, int r, const int32_t *idx, int k, int bits,

@@ -70,7 +70,9 @@ def test_encode_decode_parity(O, T, H, r, k, b, g, wht):
         sL = c.lr_scale.cpu().numpy()
         assert np.abs(Lq.astype(int) - Lq_o.astype(int)).max() <= 1
         assert (Lq == Lq_o).mean() > 0.98
-        np.testing.assert_allclose(sL, sL_o, rtol=1e-5)
+        # sL = max|L * sV| / 127 with L an fp32 tensor-core sum of H products in
+        # the hardware's order: relative error vs binary64 well under H * 2^-24
+        np.testing.assert_allclose(sL, sL_o, rtol=1e-4)
     else:
         Vq = np.zeros((H, 0), np.int8)
         Lq = sL = None

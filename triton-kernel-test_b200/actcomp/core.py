@@ -40,11 +40,13 @@ class Basis:
 
     ``basis_t`` (batch, r, H) bf16 is V^T for the projection; ``basis_q``
     (batch, H, r) int8 with ``basis_scale`` (batch, r) is the quantised basis of
-    the reconstruction, whose integer products the kernels sum exactly."""
+    the reconstruction, whose integer products the kernels sum exactly;
+    ``basis_qb`` holds the same integers as bf16 (the tensor-core encode's operand)."""
 
     basis_t: torch.Tensor
     basis_q: torch.Tensor
     basis_scale: torch.Tensor
+    basis_qb: Optional[torch.Tensor] = None
 
     @property
     def rank(self) -> int:
@@ -69,9 +71,10 @@ class Basis:
         bt = torch.empty((b, r, H), dtype=BF16, device=V.device)
         bq = torch.empty((b, H, r), dtype=torch.int8, device=V.device)
         bs = torch.empty((b, r), dtype=torch.float32, device=V.device)
+        bqb = torch.empty((b, H, r), dtype=BF16, device=V.device)
         call("actcomp_cg_basis_prepare", V.data_ptr(), H, r, b, bt.data_ptr(), bq.data_ptr(), bs.data_ptr(),
-             _stream(V))
-        return Basis(bt, bq, bs)
+             bqb.data_ptr(), _stream(V))
+        return Basis(bt, bq, bs, bqb)
 
     @staticmethod
     def fit(x: torch.Tensor, rank: int) -> "Basis":
@@ -147,6 +150,7 @@ class Compressed:
         if self.basis is not None:
             d.basis_t, d.basis_q, d.basis_scale = (self.basis.basis_t.data_ptr(), self.basis.basis_q.data_ptr(),
                                                     self.basis.basis_scale.data_ptr())
+            d.basis_qb = _ptr(self.basis.basis_qb)
         return d
 
     def with_buffers(self, **bufs) -> "Compressed":

@@ -55,17 +55,18 @@ def _(l, r, x):
 
 
 # ---------------------------------------------------------------- channel-group format
-def _basis(basis_t, basis_q, basis_scale):
+def _basis(basis_t, basis_q, basis_scale, for_encode=False):
     if basis_q is None or basis_q.numel() == 0:
         return None
-    return core.Basis(basis_t, basis_q, basis_scale)
+    # the tensor-core encode reads the quantised basis as bf16 integers
+    return core.Basis(basis_t, basis_q, basis_scale, basis_q.to(_BF) if for_encode else None)
 
 
 @torch.library.custom_op("actcomp::cg_encode", mutates_args=())
 def cg_encode(x: torch.Tensor, basis_t: Optional[torch.Tensor], basis_q: Optional[torch.Tensor],
               basis_scale: Optional[torch.Tensor], outlier_idx: Optional[torch.Tensor], bits: int, group: int,
               wht: bool) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
-    c = core.encode(x, _basis(basis_t, basis_q, basis_scale), outlier_idx, bits=bits, group=group, wht=wht)
+    c = core.encode(x, _basis(basis_t, basis_q, basis_scale, True), outlier_idx, bits=bits, group=group, wht=wht)
     e = x.new_empty((0,))
     return (c.codes, c.scales, c.lr_codes if c.rank else e.to(_I8), c.lr_scale if c.rank else e.to(_F32),
             c.outliers if c.n_outlier else e)

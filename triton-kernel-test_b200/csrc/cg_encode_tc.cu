@@ -5,17 +5,19 @@
 //   phase 1  (warps 0, 1) TMA streams X[128 x slice] (64-channel steps) and
 //            V^T[r x 64]; tcgen05.mma kind::f16 (M=128, N=r) accumulates the
 //            partial projection L_c = X_slice . V_slice in TMEM;
-//   exchange the epilogue writes L_c to shared memory; the CTAs signal each
-//            other with remote mbarrier arrivals and read every partial over
-//            DSMEM, summing them in rank order -- every CTA gets the same L,
-//            from which it forms the per-token int8 low-rank codes Lq and
-//            their scale sL (rank 0 stores them);
+//   exchange the epilogue pushes L_c to every peer with one bulk shared-to-
+//            shared copy each (completing on the peer's mbarrier) and sums
+//            all partials in rank order from local shared memory -- every CTA
+//            gets the same L, from which it forms the per-token int8 low-rank
+//            codes Lq and their scale sL (rank 0 stores them);
 //   phase 2  (warps 2, 3, after phase 1 of the block completed) per
 //            128-channel chunk: TMA re-reads the X chunk (the slice was read
-//            moments ago and is still in L2) and the quantised basis
-//            rows; tcgen05.mma kind::i8 gives the exact I = Lq . Vq^T; the
-//            epilogue (one token row per thread) forms the residual
-//            x - I * sL, copies the outlier channels verbatim, optionally
+//            moments ago and is still in L2) and the quantised basis rows as
+//            bf16 integers; tcgen05.mma kind::f16 with those integer-valued
+//            operands gives I = Lq . Vq^T exactly in fp32 (every product and
+//            partial sum is an integer below 2^24); the epilogue (one token
+//            row per thread, packed f32x2 arithmetic) forms the residual
+//            fma(-I, sL, x), copies the outlier channels verbatim, optionally
 //            rotates 128-channel blocks (Walsh-Hadamard), and writes int4/int8
 //            codes with per-token group-absmax scales.
 // The two phases run on separate rings and issuers, so phase 1 of the next
@@ -33,7 +35,7 @@ constexpr int ROWS = 128;  // tokens per block (MMA M)
 constexpr int KC = 64;     // channels per projection step
 constexpr int CH = 128;    // channels per quantisation chunk (MMA N)
 constexpr int NA = 3, SLOT_A = 24 * 1024;  // projection ring: X 128x64 (16 KB) + V^T r x 64 (<= 8 KB)
-constexpr int NB = 2, SLOT_B = 40 * 1024;  // residual ring: X 128x128 (32 KB) + Vq 128 x r (<= 8 KB)
+constexpr int NB = 2;                      // residual ring: X 128x128 (32 KB) + Vq 128 x r bf16
 
 struct EncParams {
     int64_t T, H;
@@ -53,18 +55,38 @@ struct EncParams {
     int nclusters;
 };
 
+// RK: rank rounded up to 16, 32 or 64; LB = bytes of one bf16 row of Lq / Vq.
 // Shared memory: the two rings, the low-rank code tile, barriers, then the
 // projection exchange buffers (send + C-1 receive slots, 128 x r floats each),
 // whose size depends on C and r and is added at launch.
-template <int BITS, bool WHT, int RB, int EW>
+template <int BITS, bool WHT, int RK, int EW>
 struct EncLayout {
+    static constexpr int LB = 2 * RK;
+    static constexpr int SLOT_B = 32 * 1024 + CH * LB;
     static constexpr int RING = NA * SLOT_A + NB * SLOT_B;
-    static constexpr int LQT = ROWS * RB;
+    static constexpr int LQT = ROWS * LB;
     static constexpr int BAR_OFF = RING + LQT;
     static constexpr int XCH_OFF = BAR_OFF + 1024;
     static constexpr int THREADS = 128 + 32 * EW;  // 2 producers, 2 MMA issuers, epilogue
     static int total(int C, int r) { return XCH_OFF + (C > 1 ? C * ROWS * r * 4 : 0) + 1024; }
 };
+
+template <int PITCH>
+__device__ __forceinline__ int swz(int r, int c) {
+    if constexpr (PITCH == 128) return r * 128 + ((c ^ (r & 7)) << 4);
+    else if constexpr (PITCH == 64) return r * 64 + ((c ^ ((r >> 1) & 3)) << 4);
+    else return r * 32 + ((c ^ ((r >> 2) & 1)) << 4);
+}
+template <int PITCH>
+constexpr tc::Swizzle swz_mode() {
+    return PITCH == 128 ? tc::SW_128B : (PITCH == 64 ? tc::SW_64B : tc::SW_32B);
+}
+template <int PITCH>
+constexpr CUtensorMapSwizzle tma_swz() {
+    return PITCH == 128 ? CU_TENSOR_MAP_SWIZZLE_128B
+                        : (PITCH == 64 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+}
+
 // byte offset of float4 chunk c (0 .. r/4-1) of row `row` in an exchange
 // buffer: rows of r floats, chunks XOR-swizzled by the row (within aligned
 // groups of 8 chunks, or of 4 when r/4 is not a multiple of 8) so that 32
@@ -74,38 +96,82 @@ __device__ __forceinline__ int xch_off(int row, int c, int r) {
     return row * r * 4 + ((c ^ (row & m)) << 4);
 }
 
-template <int PITCH>
-__device__ __forceinline__ int swz(int r, int c) {
-    if constexpr (PITCH == 128) return r * 128 + ((c ^ (r & 7)) << 4);
-    else if constexpr (PITCH == 64) return r * 64 + ((c ^ ((r >> 1) & 3)) << 4);
-    else return r * 32 + ((c ^ ((r >> 2) & 1)) << 4);
+// ------------------------------------------------------------------ packed fp32 pairs
+__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
+    float2 d;
+    asm("{.reg .b64 ra, rb, rc, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n mov.b64 rc, {%6, %7};\n"
+        " fma.rn.f32x2 rd, ra, rb, rc;\n mov.b64 {%0, %1}, rd;}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
+    return d;
+}
+__device__ __forceinline__ float2 add2(float2 a, float2 b) {
+    float2 d;
+    asm("{.reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n add.rn.f32x2 rd, ra, rb;\n"
+        " mov.b64 {%0, %1}, rd;}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
+}
+__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
+    float2 d;
+    asm("{.reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n sub.rn.f32x2 rd, ra, rb;\n"
+        " mov.b64 {%0, %1}, rd;}"
+        : "=f"(d.x), "=f"(d.y)
+        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
+    return d;
 }
 
-__device__ __forceinline__ void wht128_reg(float (&v)[128]) {
+// 128-point unnormalised Walsh-Hadamard on 64 register pairs, stages m = 1..64
+// in order, (a, b) -> (a + b, a - b) as the oracle; stages m >= 2 pair whole
+// float2 elements and run as packed adds.
+__device__ __forceinline__ void wht128_pairs(float2 (&v)[64]) {
 #pragma unroll
-    for (int m = 1; m < 128; m <<= 1) {
+    for (int i = 0; i < 64; ++i) {
+        const float a = v[i].x, b = v[i].y;
+        v[i] = make_float2(__fadd_rn(a, b), __fsub_rn(a, b));
+    }
 #pragma unroll
-        for (int i = 0; i < 128; ++i) {
-            if (!(i & m)) {
-                float a = v[i], b = v[i + m];
-                v[i] = __fadd_rn(a, b);
-                v[i + m] = __fsub_rn(a, b);
+    for (int m2 = 1; m2 < 64; m2 <<= 1) {  // m = 2 * m2
+#pragma unroll
+        for (int i = 0; i < 64; ++i) {
+            if (!(i & m2)) {
+                const float2 a = v[i], b = v[i + m2];
+                v[i] = add2(a, b);
+                v[i + m2] = sub2(a, b);
             }
         }
     }
 }
 
-// Codes: q = clamp(rint(w * rs), -qmax, qmax) with rs = qmax / absmax (one
-// correctly rounded division per group, as the oracle).  Adding
-// MAGIC = 1.5 * 2^23 + 2^(b-1) to y = w * rs rounds it to the nearest integer
-// (ties to even) and leaves q + 2^(b-1) in the low mantissa bits.  Since
-// |w| <= absmax, |y| <= qmax (1 + 2^-23) < qmax + 1/2: the clamp never acts.
+// Codes: q = the exact product w * rs rounded to the nearest integer (ties to
+// even) with rs = qmax / absmax (one correctly rounded division per group, as
+// the oracle).  fma(w, rs, MAGIC) with MAGIC = 1.5 * 2^23 + 2^(b-1) does that
+// rounding once and leaves q + 2^(b-1) in the low mantissa bits, with zeros up
+// to bit 21.  Since |w| <= absmax, |w * rs| <= qmax (1 + 2^-24) < qmax + 1/2:
+// the clamp never acts.  Packs 8 int4 codes (4 pairs) or 4 int8 codes (2 pairs)
+// into one word, channel order low to high.
+template <int BITS>
+__device__ __forceinline__ uint32_t pack_codes(float2 t0, float2 t1, float2 t2, float2 t3) {
+    const uint32_t a0 = __float_as_uint(t0.x), a1 = __float_as_uint(t0.y), a2 = __float_as_uint(t1.x),
+                   a3 = __float_as_uint(t1.y);
+    if constexpr (BITS == 4) {
+        const uint32_t a4 = __float_as_uint(t2.x), a5 = __float_as_uint(t2.y), a6 = __float_as_uint(t3.x),
+                       a7 = __float_as_uint(t3.y);
+        // byte = u0 + 16 u1 (bits 4..21 of a0 are zero, so nothing carries into the low byte)
+        const uint32_t b0 = a1 * 16u + a0, b1 = a3 * 16u + a2, b2 = a5 * 16u + a4, b3 = a7 * 16u + a6;
+        return __byte_perm(__byte_perm(b0, b1, 0x0040), __byte_perm(b2, b3, 0x0040), 0x5410);
+    } else {
+        return __byte_perm(__byte_perm(a0, a1, 0x0040), __byte_perm(a2, a3, 0x0040), 0x5410);
+    }
+}
 
-template <int BITS, bool WHT, int RB, int EW>
-__global__ void __launch_bounds__(EncLayout<BITS, WHT, RB, EW>::THREADS, 1)
+template <int BITS, bool WHT, int RK, int EW>
+__global__ void __launch_bounds__(EncLayout<BITS, WHT, RK, EW>::THREADS, 1)
     cg_encode_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_vt,
                         const __grid_constant__ CUtensorMap tm_vq, EncParams p) {
-    using L = EncLayout<BITS, WHT, RB, EW>;
+    using L = EncLayout<BITS, WHT, RK, EW>;
+    constexpr int LB = L::LB;
     constexpr int qmax = (1 << (BITS - 1)) - 1, off = 1 << (BITS - 1);
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -123,7 +189,7 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RB, EW>::THREADS, 1)
     uint64_t *lqready = lempty + 1;
     uint64_t *pready = lqready + 1;  // peers' partials have landed (transaction bytes)
     uint64_t *pdone = pready + 1;    // peers have consumed our previous partial
-    uint64_t *lseen = pdone + 1;  // phase-2 producer has observed lfull of the block
+    uint64_t *lseen = pdone + 1;     // phase-2 producer has observed lfull of the block
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(lseen + 1);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
     uint8_t *ringA = smem, *ringB = smem + NA * SLOT_A;
@@ -235,8 +301,8 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RB, EW>::THREADS, 1)
                 for (int ck = 0; ck < nk2; ++ck, ++i) {
                     const int s = i % NB;
                     if (!(ok = tc::mbar_wait(&emptyB[s], ((i / NB) & 1) ^ 1, abort))) break;
-                    uint8_t *st = ringB + s * SLOT_B;
-                    tc::mbar_arrive_expect_tx(&fullB[s], 2 * ROWS * 128 + CH * RB);
+                    uint8_t *st = ringB + s * L::SLOT_B;
+                    tc::mbar_arrive_expect_tx(&fullB[s], 2 * ROWS * 128 + CH * LB);
                     const int x = (int)(c_lo + ck * CH);
                     tc::tma_load_3d(st, &tm_x, &fullB[s], x, tb * ROWS, b);
                     tc::tma_load_3d(st + ROWS * 128, &tm_x, &fullB[s], x + 64, tb * ROWS, b);
@@ -247,8 +313,9 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RB, EW>::THREADS, 1)
     } else if (warp == 3) {
         // ------------------------------------------------------------ residual-term MMA
         if (lane == 0) {
-            constexpr uint32_t id_i8 = tc::idesc_i8(ROWS, CH);
-            constexpr tc::Swizzle SWQ = RB == 32 ? tc::SW_32B : tc::SW_64B;
+            constexpr uint32_t id_q = tc::idesc_f16(ROWS, CH, true, false, false);
+            constexpr tc::Swizzle SWQ = swz_mode<LB>();
+            const int nkq = (r + 15) / 16;
             int i = 0, nb = 0;
             bool ok = true;
             for (int64_t blk = cluster; blk < p.nblocks && ok; blk += p.nclusters, ++nb) {
@@ -260,12 +327,11 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RB, EW>::THREADS, 1)
                     if (!(ok = tc::mbar_wait(&fullB[s], (i / NB) & 1, abort))) break;
                     if (!(ok = tc::mbar_wait(&tempty[tb2], ((i >> 1) & 1) ^ 1, abort))) break;
                     tc::tc_fence_after();
-                    uint8_t *st = ringB + s * SLOT_B;
-#pragma unroll
-                    for (int kk = 0; kk < RB / 32; ++kk) {
-                        const uint64_t ad = tc::smem_desc(lqt + kk * 32, 16, 8 * RB, SWQ);
-                        const uint64_t bd = tc::smem_desc(st + 32 * 1024 + kk * 32, 16, 8 * RB, SWQ);
-                        tc::mma_i8(tm_p + tb2 * CH, ad, bd, id_i8, kk > 0);
+                    uint8_t *st = ringB + s * L::SLOT_B;
+                    for (int kk = 0; kk < nkq; ++kk) {
+                        const uint64_t ad = tc::smem_desc(lqt + kk * 32, 16, 8 * LB, SWQ);
+                        const uint64_t bd = tc::smem_desc(st + 32 * 1024 + kk * 32, 16, 8 * LB, SWQ);
+                        tc::mma_f16(tm_p + tb2 * CH, ad, bd, id_q, kk > 0);
                     }
                     tc::mma_commit(&tfull[tb2]);
                     tc::mma_commit(&emptyB[s]);
@@ -294,15 +360,16 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RB, EW>::THREADS, 1)
             // ---- partial projection -> shared memory
             if (!(ok = tc::mbar_wait(lfull, nb & 1, abort))) break;
             tc::tc_fence_after();
-            float Lr[RB];
+            float Lr[RK];
             {
                 uint32_t v[32];
 #pragma unroll
-                for (int jj = 0; jj < RB / 32; ++jj) {
+                for (int jj = 0; jj < (RK + 31) / 32; ++jj) {
                     tc::tmem_ld32(tm_l + ((uint32_t)(q * 32) << 16) + 32 * jj, v);
                     tc::tmem_ld_wait();
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) Lr[32 * jj + e] = __uint_as_float(v[e]);
+                    for (int e = 0; e < 32; ++e)
+                        if (32 * jj + e < RK) Lr[32 * jj + e] = __uint_as_float(v[e]);
                 }
             }
             tc::tc_fence_before();
@@ -318,7 +385,7 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RB, EW>::THREADS, 1)
                 if (nb > 0 && !(ok = tc::mbar_wait_cluster(pdone, (nb - 1) & 1, abort))) break;
                 if (h == 0) {
 #pragma unroll
-                    for (int e = 0; e < RB / 4; ++e)
+                    for (int e = 0; e < RK / 4; ++e)
                         if (4 * e < r)
                             *reinterpret_cast<float4 *>(xsend + xch_off(row, e, r)) =
                                 make_float4(Lr[4 * e], Lr[4 * e + 1], Lr[4 * e + 2], Lr[4 * e + 3]);
@@ -340,7 +407,7 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RB, EW>::THREADS, 1)
                     const uint8_t *src =
                         pr == (int)crank ? xsend : xrecv + ((pr < (int)crank ? pr : pr - 1) + 1) * PB;
 #pragma unroll
-                    for (int e = 0; e < RB / 4; ++e) {
+                    for (int e = 0; e < RK / 4; ++e) {
                         if (4 * e < r) {
                             const float4 v = *reinterpret_cast<const float4 *>(src + xch_off(row, e, r));
                             Lr[4 * e] = pr ? __fadd_rn(Lr[4 * e], v.x) : v.x;
@@ -354,10 +421,10 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RB, EW>::THREADS, 1)
                 tc::named_bar(1, 32 * EW);
                 if (ew == 0 && lane < C && lane != (int)crank) tc::mbar_arrive_remote(tc::map_cluster(pdone, lane));
             }
-            // ---- per-token low-rank codes
+            // ---- per-token low-rank codes: Lq = nearest(L * sV * 127 / max|L * sV|), one fma
             float amax = 0.f;
 #pragma unroll
-            for (int e = 0; e < RB; ++e) {
+            for (int e = 0; e < RK; ++e) {
                 if (e < r) {
                     Lr[e] = __fmul_rn(Lr[e], __ldg(p.basis_scale + (int64_t)b * r + e));
                     amax = fmaxf(amax, fabsf(Lr[e]));
@@ -365,25 +432,33 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RB, EW>::THREADS, 1)
             }
             const float sl = __fdiv_rn(amax, 127.0f);
             const float rsl = amax > 0.f ? __fdiv_rn(127.0f, amax) : 0.f;
-            uint32_t lw[RB / 4];
+            constexpr float MAGIC_L = 12582912.0f + 128.0f;
+            uint32_t lw[RK / 4];  // int8 codes, four per word
+            uint32_t lb[RK / 2];  // the same codes as bf16 pairs (exact integers)
 #pragma unroll
-            for (int e = 0; e < RB / 4; ++e) lw[e] = 0;
+            for (int e = 0; e < RK / 4; ++e) lw[e] = 0;
 #pragma unroll
-            for (int e = 0; e < RB; ++e) {
+            for (int e = 0; e < RK; e += 2) {
+                float f0 = 0.f, f1 = 0.f;
                 if (e < r) {
-                    const int qv = max(-127, min(127, __float2int_rn(__fmul_rn(Lr[e], rsl))));
-                    lw[e >> 2] |= (uint32_t)(qv & 0xff) << ((e & 3) * 8);
+                    const float t0 = __fmaf_rn(Lr[e], rsl, MAGIC_L);
+                    const float t1 = __fmaf_rn(Lr[e + 1], rsl, MAGIC_L);
+                    const uint32_t u0 = __float_as_uint(t0) & 0xffu, u1 = __float_as_uint(t1) & 0xffu;  // q + 128
+                    lw[e >> 2] |= ((u0 ^ 0x80u) << ((e & 3) * 8)) | ((u1 ^ 0x80u) << (((e + 1) & 3) * 8));
+                    f0 = __fsub_rn(t0, MAGIC_L);
+                    f1 = __fsub_rn(t1, MAGIC_L);
                 }
+                lb[e >> 1] = pack_bf16x2(f0, f1);
             }
             if (h == 0) {
 #pragma unroll
-                for (int c16 = 0; c16 < RB / 16; ++c16)
-                    *reinterpret_cast<uint4 *>(lqt + swz<RB>(row, c16)) =
-                        make_uint4(lw[4 * c16], lw[4 * c16 + 1], lw[4 * c16 + 2], lw[4 * c16 + 3]);
+                for (int c16 = 0; c16 < LB / 16; ++c16)
+                    *reinterpret_cast<uint4 *>(lqt + swz<LB>(row, c16)) =
+                        make_uint4(lb[4 * c16], lb[4 * c16 + 1], lb[4 * c16 + 2], lb[4 * c16 + 3]);
                 if (crank == 0 && rv) {
                     uint32_t *dst = reinterpret_cast<uint32_t *>(p.lrq + trow * r);
 #pragma unroll
-                    for (int e = 0; e < RB / 4; ++e)
+                    for (int e = 0; e < RK / 4; ++e)
                         if (4 * e < r) dst[e] = lw[e];
                     p.lrs[trow] = sl;
                 }
@@ -393,7 +468,7 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RB, EW>::THREADS, 1)
             if (lane == 0) tc::mbar_arrive(lqready);
 
             // ---- residual codes, chunk by chunk
-            const float nsl = -sl;
+            const float2 nsl2 = make_float2(-sl, -sl);
             if (p.k && b != cur_slice) {
                 tc::named_bar(2, 32 * EW);
                 for (int jx = ew * 32 + lane; jx < p.k; jx += 32 * EW) sidx[jx] = __ldg(p.idx + (int64_t)b * p.k + jx);
@@ -407,9 +482,8 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RB, EW>::THREADS, 1)
                 tc::tc_fence_after();
                 const int64_t c0 = c_lo + (int64_t)ck * CH + h * 64;  // first channel of my columns
                 const bool cv = c0 < c_hi;                            // warp-uniform
-                const uint8_t *xt = ringB + s * SLOT_B;
-                float w[NC];
-                float am[NP];
+                const uint8_t *xt = ringB + s * L::SLOT_B;
+                float2 w[NC / 2];
                 if (cv) {
                     // with 64 columns both TMEM reads go out before the first wait
                     constexpr int IN = NP <= 2 ? NP : 1;
@@ -433,9 +507,12 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RB, EW>::THREADS, 1)
                             const uint4 v = *reinterpret_cast<const uint4 *>(box + swz<128>(row, (jj & 1) * 4 + c16));
                             const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-                            for (int e = 0; e < 8; ++e) {
-                                const float xv = __uint_as_float(e & 1 ? (wd[e >> 1] & 0xffff0000u) : (wd[e >> 1] << 16));
-                                w[32 * jj + 8 * c16 + e] = __fmaf_rn(i2f_exact((int)Ij[8 * c16 + e]), nsl, xv);
+                            for (int e = 0; e < 4; ++e) {
+                                const float2 xv = make_float2(__uint_as_float(wd[e] << 16),
+                                                              __uint_as_float(wd[e] & 0xffff0000u));
+                                const float2 iv = make_float2(__uint_as_float(Ij[8 * c16 + 2 * e]),
+                                                              __uint_as_float(Ij[8 * c16 + 2 * e + 1]));
+                                w[16 * jj + 4 * c16 + e] = fma2(iv, nsl2, xv);  // x - I * sL, one rounding
                             }
                         }
                     }
@@ -469,7 +546,8 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RB, EW>::THREADS, 1)
                                     const uint16_t bits =
                                         *reinterpret_cast<const uint16_t *>(box + swz<128>(row, e >> 3) + 2 * (e & 7));
                                     if (rv) p.outl[trow * p.k + slot] = bits;
-                                    w[g * 64 + e] = 0.f;
+                                    if (e & 1) w[g * 32 + e / 2].y = 0.f;
+                                    else w[g * 32 + e / 2].x = 0.f;
                                 }
                             }
                         }
@@ -478,19 +556,20 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RB, EW>::THREADS, 1)
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(&emptyB[s]);  // X and basis tile no longer needed
                 if (!cv) continue;
-                if constexpr (WHT) wht128_reg(*reinterpret_cast<float(*)[128]>(&w[0]));
+                if constexpr (WHT) wht128_pairs(*reinterpret_cast<float2(*)[64]>(&w[0]));
                 // absmax of each 32-column piece, combined over the pieces of a group
+                float am[NP];
 #pragma unroll
                 for (int pc = 0; pc < NP; ++pc) {
                     float m = 0.f;
 #pragma unroll
-                    for (int e = 0; e < 32; ++e) m = fmaxf(m, fabsf(w[32 * pc + e]));
+                    for (int e = 0; e < 16; ++e) m = fmaxf(m, fmaxf(fabsf(w[16 * pc + e].x), fabsf(w[16 * pc + e].y)));
                     am[pc] = m;
                 }
                 const int G = p.group;
                 uint32_t packed[NC * BITS / 32];
                 constexpr float MAGIC = 12582912.0f + (float)off;
-                constexpr uint32_t UMASK = (1u << BITS) - 1u;
+                const float2 magic2 = make_float2(MAGIC, MAGIC);
 #pragma unroll
                 for (int pc = 0; pc < NP; ++pc) {
                     float gam = am[pc];
@@ -500,16 +579,21 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RB, EW>::THREADS, 1)
                     }
                     const float sc = __fdiv_rn(gam, (float)qmax);
                     const float rs = gam > 0.f ? __fdiv_rn((float)qmax, gam) : 0.f;
+                    const float2 rs2 = make_float2(rs, rs);
                     if (((32 * pc) % G) == 0 && rv) p.scales[trow * ngr + (c0 + 32 * pc) / G] = sc;
 #pragma unroll
                     for (int wd = 0; wd < BITS; ++wd) {  // BITS words of codes per 32-column piece
-                        uint32_t acc = 0;
-#pragma unroll
-                        for (int e = 0; e < 32 / BITS; ++e) {
-                            const float t = __fadd_rn(__fmul_rn(w[32 * pc + wd * (32 / BITS) + e], rs), MAGIC);
-                            acc |= (__float_as_uint(t) & UMASK) << (e * BITS);
+                        if constexpr (BITS == 4) {
+                            const int pp = 16 * pc + 4 * wd;  // 8 columns = 4 pairs per word
+                            packed[pc * 4 + wd] = pack_codes<4>(
+                                fma2(w[pp], rs2, magic2), fma2(w[pp + 1], rs2, magic2), fma2(w[pp + 2], rs2, magic2),
+                                fma2(w[pp + 3], rs2, magic2));
+                        } else {
+                            const int pp = 16 * pc + 2 * wd;  // 4 columns = 2 pairs per word
+                            const float2 z = make_float2(0.f, 0.f);
+                            packed[pc * 8 + wd] =
+                                pack_codes<8>(fma2(w[pp], rs2, magic2), fma2(w[pp + 1], rs2, magic2), z, z);
                         }
-                        packed[pc * BITS + wd] = acc;
                     }
                 }
                 if (rv) {
@@ -533,9 +617,9 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RB, EW>::THREADS, 1)
     if (C > 1) tc::cluster_sync();
 }
 
-template <int BITS, bool WHT, int RB, int EW>
+template <int BITS, bool WHT, int RK, int EW>
 int launch_encode(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cudaStream_t stream) {
-    using L = EncLayout<BITS, WHT, RB, EW>;
+    using L = EncLayout<BITS, WHT, RK, EW>;
     const int64_t T = d->tokens, H = d->channels, B = d->batch;
     const int r = d->rank;
     CUtensorMap m_x{}, m_vt{}, m_vq{};
@@ -546,8 +630,8 @@ int launch_encode(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cuda
     if ((st = make_map_3d(&m_vt, d->basis_t, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, H, r, B, H, (int64_t)r * H, 64, r,
                           CU_TENSOR_MAP_SWIZZLE_128B)))
         return st;
-    if ((st = make_map_3d(&m_vq, d->basis_q, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, r, H, B, r, H * r, RB, CH,
-                          RB == 32 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B)))
+    if ((st = make_map_3d(&m_vq, d->basis_qb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, r, H, B, r, H * r, L::LB / 2, CH,
+                          tma_swz<L::LB>())))
         return st;
     EncParams p{};
     p.T = T;
@@ -565,18 +649,20 @@ int launch_encode(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cuda
     p.idx = d->outlier_idx;
     p.unit = (d->wht || d->group == 128) ? 128 : 64;
     p.nunits = (int)(H / p.unit);
-    // smallest cluster whose per-CTA slice keeps the second sweep's L2 window small
     // smallest cluster whose per-CTA slice keeps the second sweep's L2 window
-    // small, within 64 KB of exchange buffers (C * 128 * r * 4 bytes)
+    // small, within 64 KB of exchange buffers (C * 128 * r * 4 bytes) and the
+    // 227 KB of shared memory a CTA may have
     int C = 1;
-    while (C < 8 && (H / C > 1536) && p.nunits / (C * 2) >= 1 && (2 * C) * ROWS * r * 4 <= 64 * 1024) C *= 2;
+    while (C < 8 && (H / C > 1536) && p.nunits / (C * 2) >= 1 && (2 * C) * ROWS * r * 4 <= 64 * 1024 &&
+           L::total(2 * C, r) <= 227 * 1024)
+        C *= 2;
     if (C > p.nunits) C = p.nunits;
     p.C = C;
     p.ntb = (int)((T + ROWS - 1) / ROWS);
     p.nblocks = (int64_t)p.ntb * B;
     int maxc = num_sms() / C;
     p.nclusters = (int)(p.nblocks < maxc ? p.nblocks : maxc);
-    auto kern = cg_encode_tc_kernel<BITS, WHT, RB, EW>;
+    auto kern = cg_encode_tc_kernel<BITS, WHT, RK, EW>;
     const int smem = L::total(C, r);
     ACT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     cudaLaunchConfig_t cfg{};
@@ -598,10 +684,12 @@ int launch_encode(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cuda
 }  // namespace cgenc
 }  // namespace act
 
-// Tensor-core encode: needs a low-rank basis (rank 16..64), H a multiple of 64
-// (of 128 with the rotation or group 128).  Other shapes use the SIMT encode.
+// Tensor-core encode: needs a low-rank basis (rank 16..64, a multiple of 8, so
+// that bf16 basis rows are 16-byte strided for TMA) with its bf16 copy,
+// and H a multiple of 64 (of 128 with the rotation or group 128).  Other
+// shapes use the SIMT encode.
 bool act_cg_encode_tc_supported(const actcomp_cg_desc *d) {
-    if (d->rank < 16 || d->rank > 64) return false;
+    if (d->rank < 16 || d->rank > 64 || d->rank % 8 || !d->basis_qb) return false;
     const int unit = (d->wht || d->group == 128) ? 128 : 64;
     return d->channels % unit == 0;
 }
@@ -610,17 +698,20 @@ int act_cg_encode_tc(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, c
     using namespace act::cgenc;
     if (d->tokens == 0) return ACT_OK;
     const bool wide = d->wht || d->group == 128;  // a group or rotation block spans 128 channels
-    const int rb = d->rank <= 32 ? 32 : 64;
-#define ACT_ENC(B, W, R, E) return launch_encode<B, W, R, E>(d, x, ldx, s)
+    const int rk = d->rank <= 16 ? 16 : (d->rank <= 32 ? 32 : 64);
+#define ACT_ENC_RK(B, W, E)                                            \
+    do {                                                               \
+        if (rk == 16) return launch_encode<B, W, 16, E>(d, x, ldx, s); \
+        if (rk == 32) return launch_encode<B, W, 32, E>(d, x, ldx, s); \
+        return launch_encode<B, W, 64, E>(d, x, ldx, s);               \
+    } while (0)
     if (d->bits == 4) {
-        if (d->wht) { if (rb == 32) ACT_ENC(4, true, 32, 4); ACT_ENC(4, true, 64, 4); }
-        if (wide) { if (rb == 32) ACT_ENC(4, false, 32, 4); ACT_ENC(4, false, 64, 4); }
-        if (rb == 32) ACT_ENC(4, false, 32, 8);
-        ACT_ENC(4, false, 64, 8);
+        if (d->wht) ACT_ENC_RK(4, true, 4);
+        if (wide) ACT_ENC_RK(4, false, 4);
+        ACT_ENC_RK(4, false, 8);
     }
-    if (d->wht) { if (rb == 32) ACT_ENC(8, true, 32, 4); ACT_ENC(8, true, 64, 4); }
-    if (wide) { if (rb == 32) ACT_ENC(8, false, 32, 4); ACT_ENC(8, false, 64, 4); }
-    if (rb == 32) ACT_ENC(8, false, 32, 8);
-    ACT_ENC(8, false, 64, 8);
-#undef ACT_ENC
+    if (d->wht) ACT_ENC_RK(8, true, 4);
+    if (wide) ACT_ENC_RK(8, false, 4);
+    ACT_ENC_RK(8, false, 8);
+#undef ACT_ENC_RK
 }

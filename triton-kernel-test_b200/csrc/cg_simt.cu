@@ -132,7 +132,8 @@ __device__ __forceinline__ int lower_bound_idx(const int32_t *idx, int k, int64_
 }
 
 // ------------------------------------------------------------------ basis
-__global__ void basis_prepare_kernel(const float *V, int64_t H, int rank, uint16_t *Vt, int8_t *Vq, float *sV) {
+__global__ void basis_prepare_kernel(const float *V, int64_t H, int rank, uint16_t *Vt, int8_t *Vq, float *sV,
+                                     uint16_t *Vqb) {
     const int b = blockIdx.y;
     const int j = blockIdx.x;  // one block per basis vector
     const float *v = V + (int64_t)b * H * rank;
@@ -153,8 +154,9 @@ __global__ void basis_prepare_kernel(const float *V, int64_t H, int rank, uint16
     if (threadIdx.x == 0) sV[(int64_t)b * rank + j] = s;
     for (int64_t c = threadIdx.x; c < H; c += blockDim.x) {
         float x = v[c * rank + j];
-        const int q = max(-127, min(127, __float2int_rn(__fmul_rn(x, rs))));
+        const int q = nearest_code(x, rs, 127);
         Vq[(int64_t)b * H * rank + c * rank + j] = (int8_t)q;
+        if (Vqb) Vqb[(int64_t)b * H * rank + c * rank + j] = f2bf((float)q);  // exact: |q| <= 127
         Vt[(int64_t)b * rank * H + (int64_t)j * H + c] = f2bf(x);
     }
 }
@@ -263,8 +265,8 @@ __global__ void __launch_bounds__(256) cg_project_kernel(actcomp_cg_desc d, cons
         float amax = warp_max(fmaxf(fabsf(lt0), fabsf(lt1)));
         float sl = __fdiv_rn(amax, 127.0f);
         const float rs = amax > 0.f ? __fdiv_rn(127.0f, amax) : 0.f;
-        if (has0) s.lrq[t * RANK + lane] = (int8_t)max(-127, min(127, __float2int_rn(__fmul_rn(lt0, rs))));
-        if (has1) s.lrq[t * RANK + lane + 32] = (int8_t)max(-127, min(127, __float2int_rn(__fmul_rn(lt1, rs))));
+        if (has0) s.lrq[t * RANK + lane] = (int8_t)nearest_code(lt0, rs, 127);
+        if (has1) s.lrq[t * RANK + lane + 32] = (int8_t)nearest_code(lt1, rs, 127);
         if (lane == 0) s.lrs[t] = sl;
     }
 }
@@ -324,7 +326,7 @@ __global__ void __launch_bounds__(256) cg_quant_kernel(actcomp_cg_desc d, const 
         if ((lane % glanes) == 0) s.scales[t * ngroups + c0 / s.group] = sc;
         uint32_t u[4];
 #pragma unroll
-        for (int i = 0; i < 4; ++i) u[i] = (uint32_t)(max(-qmax, min(qmax, __float2int_rn(__fmul_rn(w[i], rs)))) + off);
+        for (int i = 0; i < 4; ++i) u[i] = (uint32_t)(nearest_code(w[i], rs, qmax) + off);
         if constexpr (BITS == 4) {
             uint16_t packed = (uint16_t)(u[0] | (u[1] << 4) | (u[2] << 8) | (u[3] << 12));
             *reinterpret_cast<uint16_t *>(s.codes + t * (s.H / 2) + c0 / 2) = packed;
@@ -512,11 +514,11 @@ static int grid_for(int64_t items_per_slice) {
 using namespace act;
 
 extern "C" int actcomp_cg_basis_prepare(const float *V, int64_t H, int32_t rank, int32_t batch, uint16_t *basis_t,
-                                        int8_t *basis_q, float *basis_scale, void *stream) {
+                                        int8_t *basis_q, float *basis_scale, uint16_t *basis_qb, void *stream) {
     ACT_CHECK(V && basis_t && basis_q && basis_scale, ACT_E_INVALID);
     ACT_CHECK(H > 0 && rank > 0 && rank <= 64 && batch >= 1, ACT_E_INVALID);
     dim3 grid((unsigned)rank, (unsigned)batch);
-    basis_prepare_kernel<<<grid, 256, 0, as_stream(stream)>>>(V, H, rank, basis_t, basis_q, basis_scale);
+    basis_prepare_kernel<<<grid, 256, 0, as_stream(stream)>>>(V, H, rank, basis_t, basis_q, basis_scale, basis_qb);
     return launch_status();
 }
 

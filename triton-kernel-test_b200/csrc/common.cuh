@@ -66,6 +66,14 @@ __device__ __forceinline__ float group_max(float v, int width) {
 __device__ __forceinline__ float i2f_exact(int v) {
     return __fsub_rn(__int_as_float(v + 0x4B400000), 12582912.0f);
 }
+// Quantisation code of v with reciprocal scale rs: the exact product v * rs
+// rounded to the nearest integer (ties to even) by ONE fma against 1.5 * 2^23,
+// whose bit pattern then holds 0x4B400000 + q; |v * rs| <= qmax + 1/2 < 2^22.
+// A single explicit fma gives the same code whatever the compiler contracts.
+__device__ __forceinline__ int nearest_code(float v, float rs, int qmax) {
+    const int q = __float_as_int(__fmaf_rn(v, rs, 12582912.0f)) - 0x4B400000;
+    return max(-qmax, min(qmax, q));
+}
 // (float)u for 0 <= u < 2^23, minus a constant folded into the subtraction.
 __device__ __forceinline__ float u2f_minus(uint32_t u, float c_plus_2p23) {
     return __fsub_rn(__uint_as_float(0x4B000000u | u), c_plus_2p23);
