@@ -18,8 +18,11 @@
 //            partial sum is an integer below 2^24); the epilogue (one token
 //            row per thread, packed f32x2 arithmetic) forms the residual
 //            fma(-I, sL, x), copies the outlier channels verbatim, optionally
-//            rotates 128-channel blocks (Walsh-Hadamard), and writes int4/int8
-//            codes with per-token group-absmax scales.
+//            rotates 128-channel blocks (Walsh-Hadamard), and forms int4/int8
+//            codes with per-token group-absmax scales.  Codes go through a
+//            shared-memory staging tile and leave with one TMA store per chunk;
+//            scales and outlier values are staged and written with coalesced
+//            stores (per FL chunks, per block), never one token row per thread.
 // The two phases run on separate rings and issuers, so phase 1 of the next
 // block streams from HBM while phase 2 of this block is quantised.
 // X is read from HBM once; every other byte is written once.  Arithmetic
@@ -34,8 +37,6 @@ namespace cgenc {
 constexpr int ROWS = 128;  // tokens per block (MMA M)
 constexpr int KC = 64;     // channels per projection step
 constexpr int CH = 128;    // channels per quantisation chunk (MMA N)
-constexpr int NA = 3, SLOT_A = 24 * 1024;  // projection ring: X 128x64 (16 KB) + V^T r x 64 (<= 8 KB)
-constexpr int NB = 2;                      // residual ring: X 128x128 (32 KB) + Vq 128 x r bf16
 
 struct EncParams {
     int64_t T, H;
@@ -48,27 +49,55 @@ struct EncParams {
     uint16_t *outl;
     const int32_t *idx;
     int C;         // CTAs per cluster
-    int unit;      // channels per split unit (multiple of 64 and of the group)
-    int nunits;
+    int nunits;    // 128-channel chunks in H (the split unit)
     int ntb;       // token blocks per slice
     int64_t nblocks;
     int nclusters;
+    int na;        // projection ring stages
+    int ngs;       // 64-channel groups in the widest slice (outlier table entries)
+    int ostage;    // outliers staged in shared memory and flushed per block
+    // shared-memory offsets (bytes from the 1024-aligned base)
+    int off_ringB, off_lqt, off_bar, off_cst, off_xch, off_ot, off_sst, off_ost;
 };
 
+constexpr int NB = 2;      // residual ring: X 128x128 (32 KB) + Vq 128 x r bf16
+constexpr int MAXNA = 6;   // projection ring: X 128x64 (16 KB) + V^T r x 64
+constexpr int FL = 4;      // chunks per scale flush
+
 // RK: rank rounded up to 16, 32 or 64; LB = bytes of one bf16 row of Lq / Vq.
-// Shared memory: the two rings, the low-rank code tile, barriers, then the
-// projection exchange buffers (send + C-1 receive slots, 128 x r floats each),
-// whose size depends on C and r and is added at launch.
 template <int BITS, bool WHT, int RK, int EW>
 struct EncLayout {
     static constexpr int LB = 2 * RK;
+    static constexpr int SLOT_A = 16 * 1024 + RK * 128;
     static constexpr int SLOT_B = 32 * 1024 + CH * LB;
-    static constexpr int RING = NA * SLOT_A + NB * SLOT_B;
     static constexpr int LQT = ROWS * LB;
-    static constexpr int BAR_OFF = RING + LQT;
-    static constexpr int XCH_OFF = BAR_OFF + 1024;
+    static constexpr int CROW = CH * BITS / 8;  // code bytes of one token row of a chunk
+    static constexpr int CST = ROWS * CROW;     // one code staging buffer
     static constexpr int THREADS = 128 + 32 * EW;  // 2 producers, 2 MMA issuers, epilogue
-    static int total(int C, int r) { return XCH_OFF + (C > 1 ? C * ROWS * r * 4 : 0) + 1024; }
+    // Shared memory: projection ring, residual ring, low-rank code tile,
+    // barriers, two code staging buffers (TMA-stored per chunk), then the sizes
+    // that depend on the launch: projection exchange buffers (send + C-1
+    // receive slots, 128 x r floats each), the outlier table of the current
+    // slice (per 64-channel group: a mask of its outlier channels and the
+    // number of outliers below it), the scale staging rows (FL chunks of
+    // scales per token row, flushed with coalesced stores) and the outlier
+    // staging rows (k values per token row, flushed per block).
+    static int plan(EncParams &p, int na, int C, int r, int ngs, int group, int k, int ostage) {
+        p.na = na;
+        p.C = C;
+        p.ngs = ngs;
+        p.ostage = ostage;
+        p.off_ringB = na * SLOT_A;
+        p.off_lqt = p.off_ringB + NB * SLOT_B;
+        p.off_bar = p.off_lqt + LQT;
+        p.off_cst = p.off_bar + 1024;
+        p.off_xch = p.off_cst + 2 * CST;
+        p.off_ot = p.off_xch + (C > 1 ? C * ROWS * r * 4 : 0);
+        p.off_sst = p.off_ot + ((ngs * 12 + 15) & ~15);
+        const int spp = FL * (CH / group) + 4;
+        p.off_ost = p.off_sst + ROWS * spp * 4;
+        return p.off_ost + (ostage ? ((ROWS * k * 2 + 15) & ~15) : 0) + 1024;
+    }
 };
 
 template <int PITCH>
@@ -169,18 +198,21 @@ __device__ __forceinline__ uint32_t pack_codes(float2 t0, float2 t1, float2 t2, 
 template <int BITS, bool WHT, int RK, int EW>
 __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK, EW>::THREADS, 1)
     cg_encode_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_vt,
-                        const __grid_constant__ CUtensorMap tm_vq, EncParams p) {
+                        const __grid_constant__ CUtensorMap tm_vq, const __grid_constant__ CUtensorMap tm_c,
+                        EncParams p) {
     using L = EncLayout<BITS, WHT, RK, EW>;
     constexpr int LB = L::LB;
     constexpr int qmax = (1 << (BITS - 1)) - 1, off = 1 << (BITS - 1);
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint8_t *lqt = smem + L::RING;
-    uint8_t *xsend = smem + L::XCH_OFF;  // this CTA's partial projection
-    uint8_t *xrecv = xsend;              // + (slot + 1) * ROWS * r * 4: peers' partials
-    uint64_t *fullA = reinterpret_cast<uint64_t *>(smem + L::BAR_OFF);
-    uint64_t *emptyA = fullA + NA;
-    uint64_t *fullB = emptyA + NA;
+    const int NA = p.na;
+    uint8_t *ringA = smem, *ringB = smem + p.off_ringB;
+    uint8_t *lqt = smem + p.off_lqt;
+    uint8_t *xsend = smem + p.off_xch;  // this CTA's partial projection
+    uint8_t *xrecv = xsend;             // + (slot + 1) * ROWS * r * 4: peers' partials
+    uint64_t *fullA = reinterpret_cast<uint64_t *>(smem + p.off_bar);
+    uint64_t *emptyA = fullA + MAXNA;
+    uint64_t *fullB = emptyA + MAXNA;
     uint64_t *emptyB = fullB + NB;
     uint64_t *tfull = emptyB + NB;  // [2]
     uint64_t *tempty = tfull + 2;   // [2]
@@ -192,17 +224,16 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK, EW>::THREADS, 1)
     uint64_t *lseen = pdone + 1;     // phase-2 producer has observed lfull of the block
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(lseen + 1);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
-    uint8_t *ringA = smem, *ringB = smem + NA * SLOT_A;
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int C = p.C;
     const uint32_t crank = C > 1 ? tc::cluster_rank() : 0;
     const int cluster = blockIdx.x / C;
-    // my channel slice [c_lo, c_hi)
+    // my channel slice [c_lo, c_hi): a whole number of 128-channel chunks
     const int u_lo = (int)((int64_t)crank * p.nunits / C), u_hi = (int)((int64_t)(crank + 1) * p.nunits / C);
-    const int64_t c_lo = (int64_t)u_lo * p.unit, c_hi = (int64_t)u_hi * p.unit;
+    const int64_t c_lo = (int64_t)u_lo * CH, c_hi = (int64_t)u_hi * CH;
     const int nk1 = (int)((c_hi - c_lo) / KC);
-    const int nk2 = (int)((c_hi - c_lo + CH - 1) / CH);
+    const int nk2 = u_hi - u_lo;
     const int r = p.rank;
 
     if (threadIdx.x == 0) {
@@ -251,7 +282,7 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK, EW>::THREADS, 1)
                 for (int ks = 0; ks < nk1; ++ks, ++i) {
                     const int s = i % NA;
                     if (!(ok = tc::mbar_wait(&emptyA[s], ((i / NA) & 1) ^ 1, abort))) break;
-                    uint8_t *st = ringA + s * SLOT_A;
+                    uint8_t *st = ringA + s * L::SLOT_A;
                     tc::mbar_arrive_expect_tx(&fullA[s], ROWS * 128 + r * 128);
                     const int x = (int)(c_lo + ks * KC);
                     tc::tma_load_3d(st, &tm_x, &fullA[s], x, tb * ROWS, b);
@@ -273,7 +304,7 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK, EW>::THREADS, 1)
                     const int s = i % NA;
                     if (!(ok = tc::mbar_wait(&fullA[s], (i / NA) & 1, abort))) break;
                     tc::tc_fence_after();
-                    uint8_t *st = ringA + s * SLOT_A;
+                    uint8_t *st = ringA + s * L::SLOT_A;
 #pragma unroll
                     for (int kk = 0; kk < KC / 16; ++kk) {
                         const uint64_t ad = tc::smem_desc(st + kk * 32, 16, 1024, tc::SW_128B);
@@ -341,15 +372,27 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK, EW>::THREADS, 1)
     } else {
         // ------------------------------------------------------------ epilogue
         const int ew = warp - 4;
+        const int etid = threadIdx.x - 128;
+        constexpr int ETH = 32 * EW;
         const int q = warp & 3;
         const int h = (EW == 8) ? (ew >> 2) : 0;
-        constexpr int NC = EW == 8 ? 64 : 128;
+        constexpr int NC = EW == 8 ? 64 : 128;  // channels of a chunk per thread
         constexpr int NP = NC / 32;
-        int32_t *sidx = reinterpret_cast<int32_t *>(tmem_slot + 8);  // outlier channels of the current slice
+        constexpr int CROW = L::CROW;
+        uint64_t *omask = reinterpret_cast<uint64_t *>(smem + p.off_ot);
+        int32_t *obelow = reinterpret_cast<int32_t *>(omask + p.ngs);
+        float *sst = reinterpret_cast<float *>(smem + p.off_sst);
+        uint16_t *ost = reinterpret_cast<uint16_t *>(smem + p.off_ost);
+        uint8_t *cst = smem + p.off_cst;
+        const int ngs_mine = (int)((c_hi - c_lo) / 64);
         int cur_slice = -1;
         const int row = q * 32 + lane;
-        const int ngr = (int)(p.H / p.group);
-        const int64_t rowb = p.H * BITS / 8;
+        const int G = p.group;
+        const int ppg = G >> 5;        // 32-column pieces per group
+        const int gpc = CH / G;        // groups per chunk
+        const int spp = FL * gpc + 4;  // staged scales per token row (padded)
+        const int ngr = (int)(p.H / G);
+        const bool issuer = etid == 0;
         int j = 0, nb = 0;
         bool ok = true;
         for (int64_t blk = cluster; blk < p.nblocks && ok; blk += p.nclusters, ++nb) {
@@ -357,6 +400,7 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK, EW>::THREADS, 1)
             const int64_t t = (int64_t)tb * ROWS + row;
             const bool rv = t < p.T;
             const int64_t trow = (int64_t)b * p.T + t;
+            const int nrows = (int)((p.T - (int64_t)tb * ROWS) < ROWS ? (p.T - (int64_t)tb * ROWS) : ROWS);
             // ---- partial projection -> shared memory
             if (!(ok = tc::mbar_wait(lfull, nb & 1, abort))) break;
             tc::tc_fence_after();
@@ -378,11 +422,17 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK, EW>::THREADS, 1)
             if (C > 1) {
                 // Exchange: every CTA pushes its 128 x r partial to each peer with one
                 // bulk copy (completing on the peer's pready), then sums all partials
-                // in rank order from local shared memory.
+                // in rank order from local shared memory.  Lane 0 of each warp polls
+                // the cluster-scope barriers; the warp follows it.
                 const int PB = ROWS * r * 4;
                 // our send buffer and the peers' receive slots are free again once
                 // every peer has consumed the previous block
-                if (nb > 0 && !(ok = tc::mbar_wait_cluster(pdone, (nb - 1) & 1, abort))) break;
+                if (nb > 0) {
+                    int okw = 1;
+                    if (lane == 0) okw = tc::mbar_wait_cluster(pdone, (nb - 1) & 1, abort);
+                    ok = __shfl_sync(0xffffffffu, okw, 0) != 0;
+                    if (!ok) break;
+                }
                 if (h == 0) {
 #pragma unroll
                     for (int e = 0; e < RK / 4; ++e)
@@ -391,8 +441,8 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK, EW>::THREADS, 1)
                                 make_float4(Lr[4 * e], Lr[4 * e + 1], Lr[4 * e + 2], Lr[4 * e + 3]);
                 }
                 tc::fence_proxy_async();
-                tc::named_bar(1, 32 * EW);
-                if (ew == 0 && lane == 0) {
+                tc::named_bar(1, ETH);
+                if (issuer) {
                     tc::mbar_arrive_expect_tx(pready, (uint32_t)((C - 1) * PB));
                     for (int q2 = 0; q2 < C; ++q2) {
                         if (q2 == (int)crank) continue;
@@ -401,7 +451,14 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK, EW>::THREADS, 1)
                                               tc::map_cluster(pready, q2));
                     }
                 }
-                if (!(ok = tc::mbar_wait(pready, nb & 1, abort))) break;
+                {
+                    // a suspended try_wait on a barrier that only other CTAs complete
+                    // sleeps out its whole interval: poll
+                    int okw = 1;
+                    if (lane == 0) okw = tc::mbar_wait_cluster(pready, nb & 1, abort);
+                    ok = __shfl_sync(0xffffffffu, okw, 0) != 0;
+                    if (!ok) break;
+                }
                 // L = sum of the partials in rank order (identical in every CTA)
                 for (int pr = 0; pr < C; ++pr) {
                     const uint8_t *src =
@@ -418,7 +475,7 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK, EW>::THREADS, 1)
                     }
                 }
                 // tell every peer we have consumed its partial (the values are in registers)
-                tc::named_bar(1, 32 * EW);
+                tc::named_bar(1, ETH);
                 if (ew == 0 && lane < C && lane != (int)crank) tc::mbar_arrive_remote(tc::map_cluster(pdone, lane));
             }
             // ---- per-token low-rank codes: Lq = nearest(L * sV * 127 / max|L * sV|), one fma
@@ -467,24 +524,37 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK, EW>::THREADS, 1)
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(lqready);
 
-            // ---- residual codes, chunk by chunk
-            const float2 nsl2 = make_float2(-sl, -sl);
+            // ---- outlier table of slice b (indices ascending); the first barrier
+            // keeps the old table until every epilogue warp has left the previous slice
             if (p.k && b != cur_slice) {
-                tc::named_bar(2, 32 * EW);
-                for (int jx = ew * 32 + lane; jx < p.k; jx += 32 * EW) sidx[jx] = __ldg(p.idx + (int64_t)b * p.k + jx);
-                tc::named_bar(2, 32 * EW);
+                tc::named_bar(2, ETH);
+                for (int gi = etid; gi < ngs_mine; gi += ETH) {
+                    const int64_t lo = c_lo + 64 * (int64_t)gi;
+                    uint64_t m = 0;
+                    int below = 0;
+                    for (int jx = 0; jx < p.k; ++jx) {
+                        const int64_t c = __ldg(p.idx + (int64_t)b * p.k + jx);
+                        below += c < lo;
+                        if (c >= lo && c < lo + 64) m |= 1ull << (c - lo);
+                    }
+                    omask[gi] = m;
+                    obelow[gi] = below;
+                }
+                tc::named_bar(2, ETH);
                 cur_slice = b;
             }
+
+            // ---- residual codes, chunk by chunk
+            const float2 nsl2 = make_float2(-sl, -sl);
             for (int ck = 0; ck < nk2 && ok; ++ck, ++j) {
                 const int s = j % NB, tb2 = j & 1;
                 if (!(ok = tc::mbar_wait(&fullB[s], (j / NB) & 1, abort))) break;
                 if (!(ok = tc::mbar_wait(&tfull[tb2], (j >> 1) & 1, abort))) break;
                 tc::tc_fence_after();
                 const int64_t c0 = c_lo + (int64_t)ck * CH + h * 64;  // first channel of my columns
-                const bool cv = c0 < c_hi;                            // warp-uniform
                 const uint8_t *xt = ringB + s * L::SLOT_B;
                 float2 w[NC / 2];
-                if (cv) {
+                {
                     // with 64 columns both TMEM reads go out before the first wait
                     constexpr int IN = NP <= 2 ? NP : 1;
                     uint32_t I[IN][32];
@@ -521,33 +591,31 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK, EW>::THREADS, 1)
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(&tempty[tb2]);
                 // outlier channels of my columns: verbatim copy, residual zeroed.
-                // The mask comes from the shared copy of the indices by two ballots.
-                if (cv && p.k) {
+                // Mask and slot base come from the slice's table (warp-uniform).
+                if (p.k) {
 #pragma unroll
                     for (int g = 0; g < NC / 64; ++g) {
-                        const int64_t lo_c = c0 + 64 * g;
-                        uint64_t om = 0;
-                        int below = 0;
-#pragma unroll
-                        for (int half = 0; half < 2; ++half) {
-                            const int jx = lane + 32 * half;
-                            const int64_t c = jx < p.k ? (int64_t)sidx[jx] : INT64_MAX;
-                            below += __popc(__ballot_sync(0xffffffffu, c < lo_c));
-                            if (c >= lo_c && c < lo_c + 64) om |= 1ull << (c - lo_c);
-                        }
-#pragma unroll
-                        for (int o = 16; o > 0; o >>= 1) om |= __shfl_xor_sync(0xffffffffu, om, o);
+                        const int gi = (int)((c0 - c_lo) >> 6) + g;
+                        const uint64_t om = omask[gi];
                         if (om) {
+                            const int below = obelow[gi];
                             const uint8_t *box = xt + (h + g) * ROWS * 128;
 #pragma unroll
-                            for (int e = 0; e < 64; ++e) {
-                                if ((om >> e) & 1ull) {
-                                    const int slot = below + __popcll(om & ((1ull << e) - 1ull));
-                                    const uint16_t bits =
-                                        *reinterpret_cast<const uint16_t *>(box + swz<128>(row, e >> 3) + 2 * (e & 7));
-                                    if (rv) p.outl[trow * p.k + slot] = bits;
-                                    if (e & 1) w[g * 32 + e / 2].y = 0.f;
-                                    else w[g * 32 + e / 2].x = 0.f;
+                            for (int c8 = 0; c8 < 8; ++c8) {
+                                const uint32_t m8 = (uint32_t)(om >> (8 * c8)) & 0xffu;
+                                if (!m8) continue;
+#pragma unroll
+                                for (int e8 = 0; e8 < 8; ++e8) {
+                                    if ((m8 >> e8) & 1u) {
+                                        const int e = 8 * c8 + e8;
+                                        const int slot = below + __popcll(om & ((1ull << e) - 1ull));
+                                        const uint16_t bits =
+                                            *reinterpret_cast<const uint16_t *>(box + swz<128>(row, c8) + 2 * e8);
+                                        if (p.ostage) ost[row * p.k + slot] = bits;
+                                        else if (rv) p.outl[trow * p.k + slot] = bits;
+                                        if (e & 1) w[g * 32 + e / 2].y = 0.f;
+                                        else w[g * 32 + e / 2].x = 0.f;
+                                    }
                                 }
                             }
                         }
@@ -555,32 +623,37 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK, EW>::THREADS, 1)
                 }
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(&emptyB[s]);  // X and basis tile no longer needed
-                if (!cv) continue;
                 if constexpr (WHT) wht128_pairs(*reinterpret_cast<float2(*)[64]>(&w[0]));
                 // absmax of each 32-column piece, combined over the pieces of a group
                 float am[NP];
 #pragma unroll
                 for (int pc = 0; pc < NP; ++pc) {
-                    float m = 0.f;
+                    float a[16];  // balanced tree: four levels instead of a 32-long chain
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) m = fmaxf(m, fmaxf(fabsf(w[16 * pc + e].x), fabsf(w[16 * pc + e].y)));
-                    am[pc] = m;
+                    for (int e = 0; e < 16; ++e) a[e] = fmaxf(fabsf(w[16 * pc + e].x), fabsf(w[16 * pc + e].y));
+#pragma unroll
+                    for (int st = 8; st > 0; st >>= 1)
+#pragma unroll
+                        for (int e = 0; e < st; ++e) a[e] = fmaxf(a[e], a[e + st]);
+                    am[pc] = a[0];
                 }
-                const int G = p.group;
                 uint32_t packed[NC * BITS / 32];
+                float scv[NP];
                 constexpr float MAGIC = 12582912.0f + (float)off;
                 const float2 magic2 = make_float2(MAGIC, MAGIC);
+                float rs = 0.f;
 #pragma unroll
                 for (int pc = 0; pc < NP; ++pc) {
-                    float gam = am[pc];
-                    if (G >= 64) gam = fmaxf(gam, am[pc ^ 1]);
-                    if constexpr (NC == 128) {
-                        if (G >= 128) gam = fmaxf(gam, fmaxf(am[pc ^ 2], am[pc ^ 3]));
+                    if (pc % ppg == 0) {  // first piece of a group: its scale and reciprocal
+                        float gam = am[pc];
+                        if (G >= 64) gam = fmaxf(gam, am[pc ^ 1]);
+                        if constexpr (NC == 128) {
+                            if (G >= 128) gam = fmaxf(gam, fmaxf(am[pc ^ 2], am[pc ^ 3]));
+                        }
+                        scv[pc] = __fdiv_rn(gam, (float)qmax);
+                        rs = gam > 0.f ? __fdiv_rn((float)qmax, gam) : 0.f;
                     }
-                    const float sc = __fdiv_rn(gam, (float)qmax);
-                    const float rs = gam > 0.f ? __fdiv_rn((float)qmax, gam) : 0.f;
                     const float2 rs2 = make_float2(rs, rs);
-                    if (((32 * pc) % G) == 0 && rv) p.scales[trow * ngr + (c0 + 32 * pc) / G] = sc;
 #pragma unroll
                     for (int wd = 0; wd < BITS; ++wd) {  // BITS words of codes per 32-column piece
                         if constexpr (BITS == 4) {
@@ -596,16 +669,59 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK, EW>::THREADS, 1)
                         }
                     }
                 }
-                if (rv) {
-                    uint4 *dst = reinterpret_cast<uint4 *>(p.codes + trow * rowb + c0 * BITS / 8);
+                // ---- staging: codes (TMA-stored per chunk) and scales (flushed every FL chunks).
+                // Staging buffer j & 1 was last read by the store of chunk j - 2.
+                if (issuer) tc::bulk_wait_read<1>();
+                tc::named_bar(3, ETH);
+                {
+                    uint8_t *cb = cst + (j & 1) * L::CST;
 #pragma unroll
-                    for (int e = 0; e < NC * BITS / 128; ++e)
-                        dst[e] = make_uint4(packed[4 * e], packed[4 * e + 1], packed[4 * e + 2], packed[4 * e + 3]);
+                    for (int e = 0; e < NC * BITS / 128; ++e) {
+                        const int c16 = h * (NC * BITS / 128) + e;  // 16-byte chunk of the row
+                        *reinterpret_cast<uint4 *>(cb + swz<CROW>(row, c16)) =
+                            make_uint4(packed[4 * e], packed[4 * e + 1], packed[4 * e + 2], packed[4 * e + 3]);
+                    }
+                    float *srow = sst + row * spp + (ck % FL) * gpc;
+#pragma unroll
+                    for (int pc = 0; pc < NP; ++pc)
+                        if (pc % ppg == 0) srow[(h * 64 + 32 * pc) / G] = scv[pc];
+                }
+                tc::fence_proxy_async();
+                tc::named_bar(3, ETH);
+                if (issuer) {
+                    tc::tma_store_3d(&tm_c, cst + (j & 1) * L::CST, (int)((c_lo + (int64_t)ck * CH) * BITS / 8),
+                                     tb * ROWS, b);
+                    tc::bulk_commit();
+                }
+                if ((ck % FL) == FL - 1 || ck == nk2 - 1) {
+                    // the staged scales of chunks ck - ck % FL .. ck: consecutive threads
+                    // take consecutive scales of a token row
+                    const int n = (ck % FL + 1) * gpc;
+                    const int64_t g0 = (c_lo + (int64_t)(ck - ck % FL) * CH) / G;
+                    for (int i = etid; i < nrows * n; i += ETH) {
+                        const int rr = i / n, e = i - rr * n;
+                        p.scales[((int64_t)b * p.T + (int64_t)tb * ROWS + rr) * ngr + g0 + e] = sst[rr * spp + e];
+                    }
                 }
             }
+            if (ok && p.k && p.ostage) {
+                // the block's outliers of this slice: slots [s_lo, s_lo + s_n) of each row
+                const int s_lo = obelow[0];
+                const int s_n = obelow[ngs_mine - 1] + __popcll(omask[ngs_mine - 1]) - s_lo;
+                if (s_n > 0)
+                    for (int i = etid; i < nrows * s_n; i += ETH) {
+                        const int rr = i / s_n, sl = s_lo + (i - rr * s_n);
+                        p.outl[((int64_t)b * p.T + (int64_t)tb * ROWS + rr) * p.k + sl] = ost[rr * p.k + sl];
+                    }
+                tc::named_bar(3, ETH);  // read out before the next block stages its outliers
+            }
         }
+        if (issuer) tc::bulk_wait<0>();  // code stores complete before the CTA exits
         // do not exit while a peer may still read our partial buffer
-        if (C > 1 && ok && nb > 0) tc::mbar_wait_cluster(pdone, (nb - 1) & 1, abort);
+        if (C > 1 && ok && nb > 0) {
+            if (lane == 0) tc::mbar_wait_cluster(pdone, (nb - 1) & 1, abort);
+            __syncwarp();
+        }
     }
     tc::tc_fence_before();
     __syncthreads();
@@ -622,7 +738,8 @@ int launch_encode(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cuda
     using L = EncLayout<BITS, WHT, RK, EW>;
     const int64_t T = d->tokens, H = d->channels, B = d->batch;
     const int r = d->rank;
-    CUtensorMap m_x{}, m_vt{}, m_vq{};
+    const int64_t rowb = H * BITS / 8;
+    CUtensorMap m_x{}, m_vt{}, m_vq{}, m_c{};
     int st;
     if ((st = make_map_3d(&m_x, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, H, T, B, ldx, T * ldx, 64, ROWS,
                           CU_TENSOR_MAP_SWIZZLE_128B)))
@@ -632,6 +749,9 @@ int launch_encode(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cuda
         return st;
     if ((st = make_map_3d(&m_vq, d->basis_qb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, r, H, B, r, H * r, L::LB / 2, CH,
                           tma_swz<L::LB>())))
+        return st;
+    if ((st = make_map_3d(&m_c, d->codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rowb, T, B, rowb, T * rowb, L::CROW, ROWS,
+                          tma_swz<L::CROW>())))
         return st;
     EncParams p{};
     p.T = T;
@@ -647,23 +767,35 @@ int launch_encode(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cuda
     p.lrs = d->lr_scale;
     p.outl = d->outliers;
     p.idx = d->outlier_idx;
-    p.unit = (d->wht || d->group == 128) ? 128 : 64;
-    p.nunits = (int)(H / p.unit);
+    p.nunits = (int)(H / CH);
+    const int k = d->n_outlier;
+    constexpr int SMEM_MAX = 227 * 1024;
+    // widest slice of a C-way split (ceil(nunits / C) chunks) in 64-channel groups
+    auto ngs_of = [&](int c) { return (int)(((p.nunits + c - 1) / c) * (int64_t)CH / 64); };
+    // the deepest projection ring (and outlier staging) that fits beside the rest
+    auto fits = [&](int c) {
+        EncParams t = p;
+        return L::plan(t, 2, c, r, ngs_of(c), d->group, k, 0) <= SMEM_MAX;
+    };
     // smallest cluster whose per-CTA slice keeps the second sweep's L2 window
-    // small, within 64 KB of exchange buffers (C * 128 * r * 4 bytes) and the
-    // 227 KB of shared memory a CTA may have
+    // small, within 64 KB of exchange buffers (C * 128 * r * 4 bytes)
     int C = 1;
-    while (C < 8 && (H / C > 1536) && p.nunits / (C * 2) >= 1 && (2 * C) * ROWS * r * 4 <= 64 * 1024 &&
-           L::total(2 * C, r) <= 227 * 1024)
+    while (C < 8 && (H / C > 1536) && p.nunits / (C * 2) >= 1 && (2 * C) * ROWS * r * 4 <= 64 * 1024 && fits(2 * C))
         C *= 2;
     if (C > p.nunits) C = p.nunits;
-    p.C = C;
+    int na = 4, ostage = k > 0;
+    while (L::plan(p, na, C, r, ngs_of(C), d->group, k, ostage) > SMEM_MAX) {
+        if (na > 3) --na;
+        else if (ostage) ostage = 0;
+        else if (na > 2) --na;
+        else return ACT_E_UNSUPPORTED;
+    }
+    const int smem = L::plan(p, na, C, r, ngs_of(C), d->group, k, ostage);
     p.ntb = (int)((T + ROWS - 1) / ROWS);
     p.nblocks = (int64_t)p.ntb * B;
     int maxc = num_sms() / C;
     p.nclusters = (int)(p.nblocks < maxc ? p.nblocks : maxc);
     auto kern = cg_encode_tc_kernel<BITS, WHT, RK, EW>;
-    const int smem = L::total(C, r);
     ACT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)(p.nclusters * C), 1, 1);
@@ -677,7 +809,7 @@ int launch_encode(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cuda
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    ACT_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, m_x, m_vt, m_vq, p));
+    ACT_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, m_x, m_vt, m_vq, m_c, p));
     return ACT_OK;
 }
 
@@ -686,12 +818,11 @@ int launch_encode(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cuda
 
 // Tensor-core encode: needs a low-rank basis (rank 16..64, a multiple of 8, so
 // that bf16 basis rows are 16-byte strided for TMA) with its bf16 copy,
-// and H a multiple of 64 (of 128 with the rotation or group 128).  Other
-// shapes use the SIMT encode.
+// and H a multiple of 128 (the chunk the CTAs split H by).  Other shapes use
+// the SIMT encode.
 bool act_cg_encode_tc_supported(const actcomp_cg_desc *d) {
     if (d->rank < 16 || d->rank > 64 || d->rank % 8 || !d->basis_qb) return false;
-    const int unit = (d->wht || d->group == 128) ? 128 : 64;
-    return d->channels % unit == 0;
+    return d->channels % act::cgenc::CH == 0;
 }
 
 int act_cg_encode_tc(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cudaStream_t s) {
