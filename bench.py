@@ -17,6 +17,7 @@ instead (the oracle port in oracle/, all threads, bounded sample).
 from __future__ import annotations
 
 import argparse
+import contextlib
 import json
 import os
 import statistics
@@ -63,54 +64,77 @@ def peaks():
 
 # ---------------------------------------------------------------- clocks
 class ClockSampler:
-    """nvidia-smi clocks/throttle reasons sampled every 200 ms while running."""
+    """SM clocks and clock-event (throttle) reasons sampled every 10 ms by a
+    thread while the timed regions run.  Read-only NVML queries (nvidia-ml-py);
+    the device is matched to the CUDA device by UUID.  Falls back to
+    ``nvidia-smi -lms`` when NVML is not importable."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    NAMES = {"hw_slowdown": 0x8, "hw_thermal_slowdown": 0x40, "sw_thermal_slowdown": 0x20,
+             "sw_power_cap": 0x4, "hw_power_brake_slowdown": 0x80}
 
-    def __init__(self, gpu_index: int):
-        self.gpu = gpu_index
-        self.proc = None
+    def __init__(self, device_index: int):
+        self.device_index = device_index
+        self.samples = []  # (sm_mhz, reasons bitmask)
+        self.max_mhz = None
+        self._stop = None
+        self._thread = None
+        self._active = 0
 
     def __enter__(self):
+        import threading
+
         try:
-            self.proc = subprocess.Popen(["nvidia-smi", f"--id={self.gpu}", f"--query-gpu={self.Q}",
-                                          "--format=csv,noheader,nounits", "-lms", "200"],
-                                         stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-        except OSError:
-            self.proc = None
+            import pynvml
+            import torch
+
+            pynvml.nvmlInit()
+            uuid = "GPU-" + str(torch.cuda.get_device_properties(self.device_index).uuid)
+            h = pynvml.nvmlDeviceGetHandleByUUID(uuid)
+            self.max_mhz = pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM)
+            get_reasons = getattr(pynvml, "nvmlDeviceGetCurrentClocksEventReasons",
+                                  getattr(pynvml, "nvmlDeviceGetCurrentClocksThrottleReasons", None))
+        except Exception:  # no NVML: nothing to sample with
+            return self
+        self._stop = threading.Event()
+
+        def run():
+            while not self._stop.is_set():
+                if self._active:
+                    try:
+                        self.samples.append((pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM),
+                                             int(get_reasons(h)) if get_reasons else 0))
+                    except Exception:
+                        pass
+                self._stop.wait(0.01)
+
+        self._thread = threading.Thread(target=run, daemon=True)
+        self._thread.start()
         return self
 
+    def timed(self):
+        """Context manager marking a timed region (samples are kept only inside)."""
+        sampler = self
+
+        class _T:
+            def __enter__(self_):
+                sampler._active += 1
+
+            def __exit__(self_, *exc):
+                sampler._active -= 1
+
+        return _T()
+
     def __exit__(self, *exc):
-        self.lines = []
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                out, _ = self.proc.communicate(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
-                out, _ = self.proc.communicate()
-            self.lines = [l for l in out.splitlines() if l.strip()]
+        if self._stop is not None:
+            self._stop.set()
+            self._thread.join(timeout=2)
 
     def summary(self):
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for l in getattr(self, "lines", []):
-            f = [x.strip() for x in l.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for n, v in zip(names, f[5:9]):
-                if v.lower() == "active":
-                    reasons.add(n)
-        if not sm:
-            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": ["unavailable"], "samples": 0}
-        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": mx, "reasons": sorted(reasons), "samples": len(sm)}
+        if not self.samples:
+            return {"sm_mhz": None, "sm_max_mhz": self.max_mhz, "reasons": ["unavailable"], "samples": 0}
+        reasons = sorted(n for n, bit in self.NAMES.items() if any(r & bit for _, r in self.samples))
+        return {"sm_mhz": statistics.median(m for m, _ in self.samples), "sm_max_mhz": self.max_mhz,
+                "reasons": reasons, "samples": len(self.samples)}
 
 
 # ---------------------------------------------------------------- distributed plumbing
@@ -155,7 +179,7 @@ def allreduce_max(x, world):
 
 
 # ---------------------------------------------------------------- timing
-def time_steps(fn, steps, warmup, flush, world):
+def time_steps(fn, steps, warmup, flush, world, clk=None):
     """Warm up, then time exactly `steps` calls of fn, each bracketed by CUDA
     events on the current stream, with an L2 flush (a 256 MB write) between
     calls outside the events.  Returns per-step ms (mean) as max over ranks."""
@@ -167,15 +191,16 @@ def time_steps(fn, steps, warmup, flush, world):
     barrier(world)
     torch.cuda.synchronize()
     evs = []
-    for _ in range(steps):
-        flush.zero_()
-        a = torch.cuda.Event(enable_timing=True)
-        b = torch.cuda.Event(enable_timing=True)
-        a.record()
-        fn()
-        b.record()
-        evs.append((a, b))
-    torch.cuda.synchronize()
+    with (clk.timed() if clk is not None else contextlib.nullcontext()):
+        for _ in range(steps):
+            flush.zero_()
+            a = torch.cuda.Event(enable_timing=True)
+            b = torch.cuda.Event(enable_timing=True)
+            a.record()
+            fn()
+            b.record()
+            evs.append((a, b))
+        torch.cuda.synchronize()
     barrier(world)
     torch.cuda.synchronize()
     ms = sum(a.elapsed_time(b) for a, b in evs) / steps
@@ -183,7 +208,7 @@ def time_steps(fn, steps, warmup, flush, world):
 
 
 # ---------------------------------------------------------------- CPU baseline (oracle port)
-def cpu_baseline(T_sample, H, bits, group, rank, k, reps_seconds=10.0, max_reps=5):
+def cpu_baseline(T_sample, H, bits, group, rank, k, reps_seconds=10.0, max_reps=40):
     """The reference's algorithm restated in oracle/ (C, OpenMP over tokens),
     encode + decode of a T_sample-token slice of the config-2 activation."""
     import numpy as np
@@ -212,7 +237,7 @@ def cpu_baseline(T_sample, H, bits, group, rank, k, reps_seconds=10.0, max_reps=
     work = encode_bytes(T_sample, H, bits, group, rank, k) + decode_bytes(T_sample, H, bits, group, rank, k)
     return {"value": work / t / 1e9, "unit": "GB/s", "cores": os.cpu_count(), "kind": "port",
             "sample": f"oracle encode+decode of {T_sample} x {H} tokens (config-2 parameters), "
-                      f"median of {len(times)} runs, {t:.3f} s each"}
+                      f"median of {len(times)} runs ({sum(times):.1f} s of CPU work), {t:.3f} s each"}
 
 
 def run_reference(args):
@@ -222,7 +247,7 @@ def run_reference(args):
            "global_batch": 16384 * args.gpus, "parallelism": f"token-shard x{args.gpus}"}
     if rank != 0:
         return
-    T_sample = 1024
+    T_sample = 4096  # a quarter of the config-2 activation per step keeps K + W steps within a few minutes
     H, bits, group, r, k = 4096, 4, 64, 32, 16
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import numpy as np
@@ -298,11 +323,10 @@ def run_gpu(args):
     def dec_only():
         actcomp.decode(c0, out=state["xh"].view(1, T, H))
 
-    with ClockSampler(physical_gpu(local)) as clk:
-        ms_step = time_steps(step, args.steps, args.warmup, flush, world)
-        ms_enc = time_steps(enc_only, args.steps, 1, flush, world)
-        ms_dec = time_steps(dec_only, args.steps, 1, flush, world)
-    clocks = clk.summary()
+    clk = ClockSampler(torch.cuda.current_device()).__enter__()
+    ms_step = time_steps(step, args.steps, args.warmup, flush, world, clk)
+    ms_enc = time_steps(enc_only, args.steps, 1, flush, world, clk)
+    ms_dec = time_steps(dec_only, args.steps, 1, flush, world, clk)
 
     eb = encode_bytes(T, H, bits, group, r, k)
     db = decode_bytes(T, H, bits, group, r, k)
@@ -314,15 +338,7 @@ def run_gpu(args):
     achieved = dom[2] / (dom[1] * 1e-3) / 1e9
 
     # error statistics of the reconstruction, all-reduced over ranks (the only collective)
-    stats = actcomp.error_stats(state["xh"], x)
-    if world > 1:
-        import torch.distributed as dist
-
-        s2 = stats[:2].clone()
-        dist.all_reduce(s2)
-        m = stats[2:3].clone()
-        dist.all_reduce(m, op=dist.ReduceOp.MAX)
-        stats = torch.cat([s2, m, stats[3:]])
+    stats = actcomp.dist.reduce_error_stats(actcomp.error_stats(state["xh"], x))
     st = stats.cpu().tolist()
 
     components = {"encode": {"ms": ms_enc, "GB/s": enc_gbs, "frac_of_hbm": enc_gbs / hbm, "bytes": eb},
@@ -336,7 +352,7 @@ def run_gpu(args):
         c2 = actcomp.encode(x2, b2, i2, bits=bits, group=group)
         del x2
         dy2 = synthetic.gradient((T, H2), seed=7 + rank, device=dev)
-        ms_silu = time_steps(lambda: actcomp.silu_backward(c2, dy2), args.steps, 1, flush, world)
+        ms_silu = time_steps(lambda: actcomp.silu_backward(c2, dy2), args.steps, 1, flush, world, clk)
         sb = consumer_bytes(T, H2, bits, group, r, k)
         components["silu_bwd_fused_16384x11008"] = {"ms": ms_silu, "GB/s": sb / (ms_silu * 1e-3) / 1e9,
                                                     "frac_of_hbm": sb / (ms_silu * 1e-3) / 1e9 / hbm, "bytes": sb}
@@ -346,12 +362,46 @@ def run_gpu(args):
         ws = torch.empty(actcomp._lib.load().actcomp_cg_dw_workspace(__import__("ctypes").byref(c0.desc()), N),
                          dtype=torch.uint8, device=dev)
         ms_dw = time_steps(lambda: actcomp.weight_grad(c0, dy, torch.float32, ws), max(3, args.steps // 2), 1,
-                           flush, world)
+                           flush, world, clk)
         flops = 2.0 * H * N * T
         tf = flops / (ms_dw * 1e-3) / 1e12
         components["dw_gemm_fused_4096x11008_k16384"] = {
             "ms": ms_dw, "TFLOP/s": tf, "frac_of_bf16_peak": tf / pk.get("bf16_tflops", 1590.0), "flops": flops}
         del dy, ws
+
+    # offload of the packed activation to pinned host memory and back (side stream, events)
+    off = actcomp.Offloader(dev)
+
+    def time_copy(fn, reps, release):
+        ts = []
+        for i in range(reps + 2):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            h = fn()
+            h.wait()
+            e1.record()
+            torch.cuda.synchronize()
+            if i >= 2:
+                ts.append(e0.elapsed_time(e1))
+            if release:
+                off.release(h)
+        return float(statistics.median(ts))
+
+    nb_packed = c0.nbytes()
+    ms_off = time_copy(lambda: off.offload(c0), max(3, args.steps // 2), True)
+    h_keep = off.offload(c0)
+    h_keep.wait()
+
+    def reload_once():
+        state["back"] = off.reload(h_keep)
+        return h_keep
+
+    ms_rel = time_copy(reload_once, max(3, args.steps // 2), False)
+    torch.cuda.synchronize()
+    assert torch.equal(state["back"].codes, c0.codes)
+    components["offload_d2h"] = {"ms": ms_off, "GB/s": nb_packed / (ms_off * 1e-3) / 1e9, "bytes": nb_packed}
+    components["reload_h2d"] = {"ms": ms_rel, "GB/s": nb_packed / (ms_rel * 1e-3) / 1e9, "bytes": nb_packed}
+    del state["back"]
 
     # end to end through the public API with host buffers: pinned X -> H2D -> encode -> decode -> D2H
     xh_host = torch.empty((T, H), dtype=torch.bfloat16, pin_memory=True)
@@ -363,7 +413,9 @@ def run_gpu(args):
         c = actcomp.encode(x_dev, basis, idx, bits=bits, group=group)
         xh_host.copy_(actcomp.decode(c), non_blocking=True)
 
-    ms_e2e = time_steps(e2e_step, max(3, args.steps // 2), 2, flush, world)
+    ms_e2e = time_steps(e2e_step, max(3, args.steps // 2), 2, flush, world, clk)
+    clk.__exit__(None, None, None)
+    clocks = clk.summary()
     e2e_val = world * (eb + db) / (ms_e2e * 1e-3) / 1e9
 
     if rank == 0:
@@ -391,19 +443,12 @@ def run_gpu(args):
                       "changed_values": st[3]},
         }
         if not args.no_cpu_baseline:
-            line["cpu_baseline"] = cpu_baseline(2048, H, bits, group, r, k)
+            line["cpu_baseline"] = cpu_baseline(T, H, bits, group, r, k)
         print(json.dumps(line), flush=True)
     if world > 1:
         import torch.distributed as dist
 
         dist.destroy_process_group()
-
-
-def physical_gpu(local: int) -> int:
-    vis = [v for v in os.environ.get("CUDA_VISIBLE_DEVICES", "").split(",") if v.strip()]
-    if vis and local < len(vis) and vis[local].strip().isdigit():
-        return int(vis[local])
-    return local
 
 
 def launches_per_step():
