@@ -120,7 +120,7 @@ def load() -> ctypes.CDLL:
                 build.build()
             else:
                 raise ImportError(
-                    f"{LIB_PATH} is missing: build it with `python -m actcomp.build` "
+                    f"{LIB_PATH} is missing: build it with `python triton-kernel-test_b200/actcomp/build.py` "
                     "(nvcc, sm_100a). actcomp has no CPU fallback.")
         lib = ctypes.CDLL(LIB_PATH)
         for name, (res, args) in SIGNATURES.items():

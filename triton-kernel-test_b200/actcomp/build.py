@@ -1,6 +1,7 @@
 """In-tree build of libactcomp.so (sm_100a) with nvcc.
 
-``python -m actcomp.build`` (or ``actcomp.build.build()``) compiles every
+``python triton-kernel-test_b200/actcomp/build.py`` (this file run on its own:
+importing the ``actcomp`` package loads the library it builds) compiles every
 ``csrc/*.cu`` into ``actcomp/libactcomp.so`` next to this file.  The library
 links the CUDA runtime statically and takes the driver's tensor-map encoder
 through ``cudaGetDriverEntryPoint``, so it loads on a machine without a GPU
