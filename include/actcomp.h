@@ -136,6 +136,29 @@ size_t actcomp_cg_dw_workspace(const actcomp_cg_desc *d, int64_t N);
 int actcomp_cg_dw(const actcomp_cg_desc *d, const uint16_t *dy, int64_t N, int64_t lddy, void *dw, int32_t dw_dtype,
                   int64_t lddw, void *workspace, size_t workspace_bytes, void *stream);
 
+/* Allocation-free variant of actcomp_cg_dw.  No reference counterpart: the
+ * reference allocates its outputs with torch.empty and has no such entry point.
+ * The decoded activation goes to a device array of
+ * ACTCOMP_DW_STATIC_SCRATCH_BYTES (32 MiB) that the library reserves per device
+ * when its kernels load, instead of a caller workspace.  For callers that cannot
+ * allocate device memory on the call path: plain C / ctypes callers without an
+ * allocator of their own, and code that must not call cudaMalloc / cudaFree
+ * (both can synchronise the device).
+ *   Limit: actcomp_cg_dw_workspace(d, N) -- T * H * 2 bytes rounded up to 256,
+ *   e.g. 4096 tokens x 4096 channels -- must not exceed
+ *   ACTCOMP_DW_STATIC_SCRATCH_BYTES; larger calls return ACT_E_WORKSPACE and
+ *   launch nothing (use actcomp_cg_dw with a workspace).
+ *   Nothing in the scratch has to start at zero: the decode writes all of it
+ *   before the GEMM reads it.
+ *   The scratch is shared by every call on a device: calls that overlap in time
+ *   (on other streams or host threads) race on it -- serialise them.
+ *   The first call on each device, with that device current, looks up the
+ *   scratch's address (cudaGetSymbolAddress); make that first call before any
+ *   stream capture. */
+#define ACTCOMP_DW_STATIC_SCRATCH_BYTES ((size_t)32 << 20)
+int actcomp_cg_dw_static(const actcomp_cg_desc *d, const uint16_t *dy, int64_t N, int64_t lddy, void *dw,
+                         int32_t dw_dtype, int64_t lddw, void *stream);
+
 /* Column absmax of x (T x H, row stride ldx) and the k largest channels
  * (score descending, ties to the lower index), returned ascending in idx.
  * score_ws: H floats of device scratch.  Selection rule for the outlier
