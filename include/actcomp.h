@@ -66,9 +66,20 @@ int actcomp_clear_device_error(void *stream);
  *   basis_t     bf16    rank x H         V^T for the projection
  *   basis_q     int8    H x rank         quantised basis for the reconstruction
  *   basis_scale float   rank             per basis vector scale of basis_q
- *   basis_qb    bf16    H x rank         basis_q as (exact) bf16 integers, the
- *                                        tensor-core encode's operand (may be NULL:
- *                                        the encode then runs on CUDA cores)
+ *   basis_qb    bf16    tile operand     basis_q as (exact) bf16 integers in the
+ *                                        tensor-core encode's shared-memory layout
+ *                                        (may be NULL: the encode then runs on CUDA cores)
+ *   basis_qs    int8    tile operand     basis_q in the tensor-core decode's
+ *                                        shared-memory layout (may be NULL: the decode
+ *                                        then gathers basis_q tiles itself)
+ * Tile operands: per slice ceil(H/128) tiles of 128 channels; tile t row `row`
+ * (channel 128 t + row) holds the row's rank values in W bytes -- basis_qb:
+ * W = 2 * RK, RK = rank rounded up to 16, 32 or 64, value j at byte 2 j;
+ * basis_qs: W = 32 (rank <= 32) or 64, value j at byte j -- with the 16-byte
+ * chunk c of the row stored at chunk c ^ s(row), s = (row >> 2) & 1 for W = 32,
+ * (row >> 1) & 3 for W = 64, row & 7 for W = 128 (the swizzled K-major layout
+ * tcgen05.mma reads), zero beyond the rank and beyond H.  Sizes: batch *
+ * ceil(H/128) * 128 * W bytes.  actcomp_cg_basis_prepare writes both.
  * bits in {4, 8}; group in {32, 64, 128} dividing H; rank in {0, 16, 32, 48, 64};
  * 0 <= n_outlier <= 64; wht requires H % 128 == 0 and group <= 128.          */
 typedef struct actcomp_cg_desc {
@@ -90,14 +101,17 @@ typedef struct actcomp_cg_desc {
     const int8_t *basis_q;
     const float *basis_scale;
     const uint16_t *basis_qb;
+    const int8_t *basis_qs;
 } actcomp_cg_desc;
 
 /* Quantise a basis V (batch x H x rank, float32 row-major) into basis_t,
- * basis_q, basis_scale and (if non-NULL) basis_qb (layouts above).  No
+ * basis_q, basis_scale and (if non-NULL) the tile operands basis_qb and
+ * basis_qs (layouts above; both are fully written, padding included).  No
  * reference counterpart (the reference takes l, r as given,
  * low_rank_extraction_fuse_compression_quantization.py:118). */
 int actcomp_cg_basis_prepare(const float *V, int64_t H, int32_t rank, int32_t batch, uint16_t *basis_t,
-                             int8_t *basis_q, float *basis_scale, uint16_t *basis_qb, void *stream);
+                             int8_t *basis_q, float *basis_scale, uint16_t *basis_qb, int8_t *basis_qs,
+                             void *stream);
 
 /* Encode x (batch x T x H bf16, row stride ldx elements, slice stride T*ldx)
  * into the buffers of d.  Replaces low_rank_addition_fuse_compression_quantization

@@ -44,6 +44,7 @@ class CgDesc(ctypes.Structure):
         ("bits", c_i32), ("group", c_i32), ("rank", c_i32), ("n_outlier", c_i32), ("wht", c_i32), ("batch", c_i32),
         ("codes", c_vp), ("scales", c_vp), ("lr_codes", c_vp), ("lr_scale", c_vp), ("outliers", c_vp),
         ("outlier_idx", c_vp), ("basis_t", c_vp), ("basis_q", c_vp), ("basis_scale", c_vp), ("basis_qb", c_vp),
+        ("basis_qs", c_vp),
     ]
 
 
@@ -83,7 +84,7 @@ SIGNATURES = {
     "actcomp_abi_version": (ctypes.c_int, []),
     "actcomp_last_device_error": (ctypes.c_int, [c_vp, ctypes.POINTER(ctypes.c_uint32)]),
     "actcomp_clear_device_error": (ctypes.c_int, [c_vp]),
-    "actcomp_cg_basis_prepare": (ctypes.c_int, [c_vp, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "actcomp_cg_basis_prepare": (ctypes.c_int, [c_vp, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
     "actcomp_cg_encode": (ctypes.c_int, [ctypes.POINTER(CgDesc), c_vp, c_i64, c_vp]),
     "actcomp_cg_decode": (ctypes.c_int, [ctypes.POINTER(CgDesc), c_vp, c_i64, c_vp]),
     "actcomp_cg_consume": (ctypes.c_int, [ctypes.POINTER(CgDesc), c_i32, c_vp, c_i64, c_vp, c_i64, c_vp]),

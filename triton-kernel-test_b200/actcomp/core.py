@@ -41,12 +41,15 @@ class Basis:
     ``basis_t`` (batch, r, H) bf16 is V^T for the projection; ``basis_q``
     (batch, H, r) int8 with ``basis_scale`` (batch, r) is the quantised basis of
     the reconstruction, whose integer products the kernels sum exactly;
-    ``basis_qb`` holds the same integers as bf16 (the tensor-core encode's operand)."""
+    ``basis_qb`` (bf16) and ``basis_qs`` (int8) hold the same integers in the
+    tensor-core encode's and decode's shared-memory tile layouts (see
+    include/actcomp.h); without them those kernels fall back to slower paths."""
 
     basis_t: torch.Tensor
     basis_q: torch.Tensor
     basis_scale: torch.Tensor
     basis_qb: Optional[torch.Tensor] = None
+    basis_qs: Optional[torch.Tensor] = None
 
     @property
     def rank(self) -> int:
@@ -71,10 +74,13 @@ class Basis:
         bt = torch.empty((b, r, H), dtype=BF16, device=V.device)
         bq = torch.empty((b, H, r), dtype=torch.int8, device=V.device)
         bs = torch.empty((b, r), dtype=torch.float32, device=V.device)
-        bqb = torch.empty((b, H, r), dtype=BF16, device=V.device)
+        rows = b * ((H + 127) // 128) * 128
+        rk = 16 if r <= 16 else (32 if r <= 32 else 64)
+        bqb = torch.empty((rows * rk,), dtype=BF16, device=V.device)  # tile operands (layout in actcomp.h)
+        bqs = torch.empty((rows * (32 if r <= 32 else 64),), dtype=torch.int8, device=V.device)
         call("actcomp_cg_basis_prepare", V.data_ptr(), H, r, b, bt.data_ptr(), bq.data_ptr(), bs.data_ptr(),
-             bqb.data_ptr(), _stream(V))
-        return Basis(bt, bq, bs, bqb)
+             bqb.data_ptr(), bqs.data_ptr(), _stream(V))
+        return Basis(bt, bq, bs, bqb, bqs)
 
     @staticmethod
     def fit(x: torch.Tensor, rank: int) -> "Basis":
@@ -151,6 +157,7 @@ class Compressed:
             d.basis_t, d.basis_q, d.basis_scale = (self.basis.basis_t.data_ptr(), self.basis.basis_q.data_ptr(),
                                                     self.basis.basis_scale.data_ptr())
             d.basis_qb = _ptr(self.basis.basis_qb)
+            d.basis_qs = _ptr(self.basis.basis_qs)
         return d
 
     def with_buffers(self, **bufs) -> "Compressed":

@@ -55,25 +55,25 @@ def _(l, r, x):
 
 
 # ---------------------------------------------------------------- channel-group format
-def _basis(basis_t, basis_q, basis_scale, for_encode=False):
+def _basis(basis_t, basis_q, basis_scale, basis_qb=None, basis_qs=None):
     if basis_q is None or basis_q.numel() == 0:
         return None
-    # the tensor-core encode reads the quantised basis as bf16 integers
-    return core.Basis(basis_t, basis_q, basis_scale, basis_q.to(_BF) if for_encode else None)
+    return core.Basis(basis_t, basis_q, basis_scale, basis_qb, basis_qs)
 
 
 @torch.library.custom_op("actcomp::cg_encode", mutates_args=())
 def cg_encode(x: torch.Tensor, basis_t: Optional[torch.Tensor], basis_q: Optional[torch.Tensor],
-              basis_scale: Optional[torch.Tensor], outlier_idx: Optional[torch.Tensor], bits: int, group: int,
+              basis_scale: Optional[torch.Tensor], basis_qb: Optional[torch.Tensor],
+              outlier_idx: Optional[torch.Tensor], bits: int, group: int,
               wht: bool) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
-    c = core.encode(x, _basis(basis_t, basis_q, basis_scale, True), outlier_idx, bits=bits, group=group, wht=wht)
+    c = core.encode(x, _basis(basis_t, basis_q, basis_scale, basis_qb), outlier_idx, bits=bits, group=group, wht=wht)
     e = x.new_empty((0,))
     return (c.codes, c.scales, c.lr_codes if c.rank else e.to(_I8), c.lr_scale if c.rank else e.to(_F32),
             c.outliers if c.n_outlier else e)
 
 
 @cg_encode.register_fake
-def _(x, basis_t, basis_q, basis_scale, outlier_idx, bits, group, wht):
+def _(x, basis_t, basis_q, basis_scale, basis_qb, outlier_idx, bits, group, wht):
     T = x.numel() // x.shape[-1]
     H = x.shape[-1]
     r = 0 if basis_q is None else basis_q.shape[-1]
@@ -83,10 +83,10 @@ def _(x, basis_t, basis_q, basis_scale, outlier_idx, bits, group, wht):
 
 
 def _compressed(shape, codes, scales, lr_codes, lr_scale, outliers, outlier_idx, basis_t, basis_q, basis_scale,
-                bits, group, wht):
+                basis_qs, bits, group, wht):
     batch = shape[0] if len(shape) == 3 else 1
     T, H = shape[-2], shape[-1]
-    basis = _basis(basis_t, basis_q, basis_scale)
+    basis = _basis(basis_t, basis_q, basis_scale, None, basis_qs)
     k = 0 if outlier_idx is None else outlier_idx.shape[-1]
     return core.Compressed(T, H, bits, group, wht, batch, codes, scales, lr_codes if basis else None,
                            lr_scale if basis else None, outliers if k else None,
@@ -97,17 +97,18 @@ def _compressed(shape, codes, scales, lr_codes, lr_scale, outliers, outlier_idx,
 def cg_consume(shape: list[int], codes: torch.Tensor, scales: torch.Tensor, lr_codes: torch.Tensor,
                lr_scale: torch.Tensor, outliers: torch.Tensor, outlier_idx: Optional[torch.Tensor],
                basis_t: Optional[torch.Tensor], basis_q: Optional[torch.Tensor], basis_scale: Optional[torch.Tensor],
-               bits: int, group: int, wht: bool, op: int, y: Optional[torch.Tensor]) -> torch.Tensor:
+               basis_qs: Optional[torch.Tensor], bits: int, group: int, wht: bool, op: int,
+               y: Optional[torch.Tensor]) -> torch.Tensor:
     c = _compressed(shape, codes, scales, lr_codes, lr_scale, outliers, outlier_idx, basis_t, basis_q, basis_scale,
-                    bits, group, wht)
+                    basis_qs, bits, group, wht)
     if op == 0:
         return core.decode(c).reshape(shape)
     return core._consume(c, op, y.reshape(shape)).reshape(shape)
 
 
 @cg_consume.register_fake
-def _(shape, codes, scales, lr_codes, lr_scale, outliers, outlier_idx, basis_t, basis_q, basis_scale, bits, group,
-      wht, op, y):
+def _(shape, codes, scales, lr_codes, lr_scale, outliers, outlier_idx, basis_t, basis_q, basis_scale, basis_qs, bits,
+      group, wht, op, y):
     return _empty(tuple(shape), _BF, codes)
 
 

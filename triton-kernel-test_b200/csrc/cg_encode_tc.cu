@@ -48,6 +48,7 @@ struct EncParams {
     float *lrs;
     uint16_t *outl;
     const int32_t *idx;
+    const uint16_t *vqb;  // basis_qb: bf16 tile operand (layout in include/actcomp.h)
     int C;         // CTAs per cluster
     int nunits;    // 128-channel chunks in H (the split unit)
     int ntb;       // token blocks per slice
@@ -125,32 +126,6 @@ __device__ __forceinline__ int xch_off(int row, int c, int r) {
     return row * r * 4 + ((c ^ (row & m)) << 4);
 }
 
-// ------------------------------------------------------------------ packed fp32 pairs
-__device__ __forceinline__ float2 fma2(float2 a, float2 b, float2 c) {
-    float2 d;
-    asm("{.reg .b64 ra, rb, rc, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n mov.b64 rc, {%6, %7};\n"
-        " fma.rn.f32x2 rd, ra, rb, rc;\n mov.b64 {%0, %1}, rd;}"
-        : "=f"(d.x), "=f"(d.y)
-        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y), "f"(c.x), "f"(c.y));
-    return d;
-}
-__device__ __forceinline__ float2 add2(float2 a, float2 b) {
-    float2 d;
-    asm("{.reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n add.rn.f32x2 rd, ra, rb;\n"
-        " mov.b64 {%0, %1}, rd;}"
-        : "=f"(d.x), "=f"(d.y)
-        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-    return d;
-}
-__device__ __forceinline__ float2 sub2(float2 a, float2 b) {
-    float2 d;
-    asm("{.reg .b64 ra, rb, rd;\n mov.b64 ra, {%2, %3};\n mov.b64 rb, {%4, %5};\n sub.rn.f32x2 rd, ra, rb;\n"
-        " mov.b64 {%0, %1}, rd;}"
-        : "=f"(d.x), "=f"(d.y)
-        : "f"(a.x), "f"(a.y), "f"(b.x), "f"(b.y));
-    return d;
-}
-
 // 128-point unnormalised Walsh-Hadamard on 64 register pairs, stages m = 1..64
 // in order, (a, b) -> (a + b, a - b) as the oracle; stages m >= 2 pair whole
 // float2 elements and run as packed adds.
@@ -198,8 +173,7 @@ __device__ __forceinline__ uint32_t pack_codes(float2 t0, float2 t1, float2 t2, 
 template <int BITS, bool WHT, int RK, int EW>
 __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK, EW>::THREADS, 1)
     cg_encode_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_vt,
-                        const __grid_constant__ CUtensorMap tm_vq, const __grid_constant__ CUtensorMap tm_c,
-                        EncParams p) {
+                        const __grid_constant__ CUtensorMap tm_c, EncParams p) {
     using L = EncLayout<BITS, WHT, RK, EW>;
     constexpr int LB = L::LB;
     constexpr int qmax = (1 << (BITS - 1)) - 1, off = 1 << (BITS - 1);
@@ -321,7 +295,7 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK, EW>::THREADS, 1)
     } else if (warp == 2) {
         // ------------------------------------------------------------ phase-2 producer
         if (lane == 0) {
-            tc::prefetch_tmap(&tm_vq);
+            const int64_t ntile = p.H / CH;
             int i = 0, nb = 0;
             bool ok = true;
             for (int64_t blk = cluster; blk < p.nblocks && ok; blk += p.nclusters, ++nb) {
@@ -337,7 +311,9 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK, EW>::THREADS, 1)
                     const int x = (int)(c_lo + ck * CH);
                     tc::tma_load_3d(st, &tm_x, &fullB[s], x, tb * ROWS, b);
                     tc::tma_load_3d(st + ROWS * 128, &tm_x, &fullB[s], x + 64, tb * ROWS, b);
-                    tc::tma_load_3d(st + 32 * 1024, &tm_vq, &fullB[s], 0, x, b);
+                    // the chunk's basis rows: one contiguous tile of the prepared operand
+                    tc::bulk_load(st + 32 * 1024, p.vqb + ((int64_t)b * ntile + x / CH) * (CH * LB / 2), CH * LB,
+                                  &fullB[s]);
                 }
             }
         }
@@ -739,16 +715,13 @@ int launch_encode(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cuda
     const int64_t T = d->tokens, H = d->channels, B = d->batch;
     const int r = d->rank;
     const int64_t rowb = H * BITS / 8;
-    CUtensorMap m_x{}, m_vt{}, m_vq{}, m_c{};
+    CUtensorMap m_x{}, m_vt{}, m_c{};
     int st;
     if ((st = make_map_3d(&m_x, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, H, T, B, ldx, T * ldx, 64, ROWS,
                           CU_TENSOR_MAP_SWIZZLE_128B)))
         return st;
     if ((st = make_map_3d(&m_vt, d->basis_t, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, H, r, B, H, (int64_t)r * H, 64, r,
                           CU_TENSOR_MAP_SWIZZLE_128B)))
-        return st;
-    if ((st = make_map_3d(&m_vq, d->basis_qb, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, r, H, B, r, H * r, L::LB / 2, CH,
-                          tma_swz<L::LB>())))
         return st;
     if ((st = make_map_3d(&m_c, d->codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rowb, T, B, rowb, T * rowb, L::CROW, ROWS,
                           tma_swz<L::CROW>())))
@@ -767,6 +740,7 @@ int launch_encode(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cuda
     p.lrs = d->lr_scale;
     p.outl = d->outliers;
     p.idx = d->outlier_idx;
+    p.vqb = d->basis_qb;
     p.nunits = (int)(H / CH);
     const int k = d->n_outlier;
     constexpr int SMEM_MAX = 227 * 1024;
@@ -809,7 +783,7 @@ int launch_encode(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cuda
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    ACT_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, m_x, m_vt, m_vq, m_c, p));
+    ACT_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, m_x, m_vt, m_c, p));
     return ACT_OK;
 }
 

@@ -132,8 +132,19 @@ __device__ __forceinline__ int lower_bound_idx(const int32_t *idx, int k, int64_
 }
 
 // ------------------------------------------------------------------ basis
+// byte offset of value j (of `vbytes` bytes) of row `row` in a tile operand
+// with W-byte rows (swizzled K-major layout, see include/actcomp.h)
+__device__ __forceinline__ int64_t tile_operand_off(int64_t c, int j, int vbytes, int W) {
+    const int row = (int)(c & 127);
+    const int64_t tile = c >> 7;
+    const int byte = j * vbytes;
+    const int chunk = byte >> 4;
+    const int s = W == 32 ? ((row >> 2) & 1) : (W == 64 ? ((row >> 1) & 3) : (row & 7));
+    return (tile * 128 + row) * W + ((chunk ^ s) << 4) + (byte & 15);
+}
+
 __global__ void basis_prepare_kernel(const float *V, int64_t H, int rank, uint16_t *Vt, int8_t *Vq, float *sV,
-                                     uint16_t *Vqb) {
+                                     uint16_t *Vqb, int8_t *Vqs) {
     const int b = blockIdx.y;
     const int j = blockIdx.x;  // one block per basis vector
     const float *v = V + (int64_t)b * H * rank;
@@ -152,11 +163,15 @@ __global__ void basis_prepare_kernel(const float *V, int64_t H, int rank, uint16
     const float s = __fdiv_rn(red[0], 127.0f);
     const float rs = red[0] > 0.f ? __fdiv_rn(127.0f, red[0]) : 0.f;
     if (threadIdx.x == 0) sV[(int64_t)b * rank + j] = s;
+    const int rk = rank <= 16 ? 16 : (rank <= 32 ? 32 : 64);  // encode operand: 2 * rk bytes per row
+    const int rb = rank <= 32 ? 32 : 64;                       // decode operand: rb bytes per row
+    const int64_t ntile = (H + 127) / 128;
     for (int64_t c = threadIdx.x; c < H; c += blockDim.x) {
         float x = v[c * rank + j];
         const int q = nearest_code(x, rs, 127);
         Vq[(int64_t)b * H * rank + c * rank + j] = (int8_t)q;
-        if (Vqb) Vqb[(int64_t)b * H * rank + c * rank + j] = f2bf((float)q);  // exact: |q| <= 127
+        if (Vqb) Vqb[((int64_t)b * ntile * 128 * 2 * rk + tile_operand_off(c, j, 2, 2 * rk)) / 2] = f2bf((float)q);
+        if (Vqs) Vqs[(int64_t)b * ntile * 128 * rb + tile_operand_off(c, j, 1, rb)] = (int8_t)q;
         Vt[(int64_t)b * rank * H + (int64_t)j * H + c] = f2bf(x);
     }
 }
@@ -514,11 +529,18 @@ static int grid_for(int64_t items_per_slice) {
 using namespace act;
 
 extern "C" int actcomp_cg_basis_prepare(const float *V, int64_t H, int32_t rank, int32_t batch, uint16_t *basis_t,
-                                        int8_t *basis_q, float *basis_scale, uint16_t *basis_qb, void *stream) {
+                                        int8_t *basis_q, float *basis_scale, uint16_t *basis_qb, int8_t *basis_qs,
+                                        void *stream) {
     ACT_CHECK(V && basis_t && basis_q && basis_scale, ACT_E_INVALID);
     ACT_CHECK(H > 0 && rank > 0 && rank <= 64 && batch >= 1, ACT_E_INVALID);
+    cudaStream_t s = as_stream(stream);
+    const int64_t rows = batch * ((H + 127) / 128) * 128;
+    const int rk = rank <= 16 ? 16 : (rank <= 32 ? 32 : 64), rb = rank <= 32 ? 32 : 64;
+    // padding (values past the rank, channels past H) reads as zero
+    if (basis_qb) ACT_CUDA_TRY(cudaMemsetAsync(basis_qb, 0, (size_t)(rows * 2 * rk), s));
+    if (basis_qs) ACT_CUDA_TRY(cudaMemsetAsync(basis_qs, 0, (size_t)(rows * rb), s));
     dim3 grid((unsigned)rank, (unsigned)batch);
-    basis_prepare_kernel<<<grid, 256, 0, as_stream(stream)>>>(V, H, rank, basis_t, basis_q, basis_scale, basis_qb);
+    basis_prepare_kernel<<<grid, 256, 0, s>>>(V, H, rank, basis_t, basis_q, basis_scale, basis_qb, basis_qs);
     return launch_status();
 }
 

@@ -5,12 +5,13 @@
 //   TMA warp   loads the low-rank codes of the 128 tokens (128 x r int8), the
 //              quantised basis rows of the 128 channels (128 x r int8), the
 //              residual codes (128 x 64 B for int4) and, for a consumer, the
-//              second operand (128 x 128 bf16) into a 2-3 stage ring;
+//              second operand (128 x 128 bf16) into a 2-4 stage ring;
 //   MMA warp   issues one tcgen05.mma kind::i8 (M=128, N=128, K=32) per 32
 //              basis vectors: I = Lq . Vq^T, an exact int32 accumulator in TMEM
 //              (double-buffered, 2 x 128 columns);
-//   epilogue   (8 warps, or 4 with the Walsh-Hadamard rotation; one token row
-//              per thread) reads I with tcgen05.ld, forms
+//   epilogue   (16 warps: 4 row quarters x 4 column quarters, one token row
+//              and 32 channels per thread; the rotation exchanges quarters
+//              through shared memory) reads I with tcgen05.ld, forms
 //              xhat = bf16((u - 2^(b-1)) * s + I * sL) exactly as the oracle,
 //              puts the outlier channels back, applies the consumer op, writes
 //              the tile to a 128B-swizzled staging buffer and stores it by TMA.
@@ -34,21 +35,32 @@ struct DecParams {
     const int32_t *idx;
     int ntb, ncc;
     int64_t ntiles;
+    int n32;      // 32-channel groups of H (outlier table entries)
+    int off_ot;   // shared-memory offset of the outlier table
+    int tq, trem;              // tiles per CTA: tq, and one more for the first trem CTAs
+    const int8_t *vqs;         // basis_qs tile operand (layout in include/actcomp.h), or null
 };
 
 template <int BITS, int OP, bool WHT, int RB>
 struct DecLayout {
-    static constexpr int LQ = RB ? ROWS * RB : 0;
+    static constexpr int LQ = RB ? ROWS * RB : 0;  // low-rank codes of a token block (2 slots, outside the ring)
     static constexpr int VQ = RB ? CH * RB : 0;
     static constexpr int CODES = ROWS * CH * BITS / 8;
     static constexpr int Y = OP == ACT_OP_DECODE ? 0 : ROWS * CH * 2;
-    static constexpr int STAGE = LQ + VQ + CODES + Y;
+    static constexpr int STAGE = VQ + CODES + Y;
     static constexpr int OUT = ROWS * CH * 2;
-    static constexpr int S = (3 * STAGE + 2 * OUT <= 200 * 1024) ? 3 : 2;
-    static constexpr int EW = WHT ? 4 : 8;  // epilogue warps
+    static constexpr int WX = WHT ? 4 * ROWS * 32 * 4 : 0;  // rotation exchange: 32 floats per thread
+    static constexpr int FIXED = 2 * OUT + WX + 2 * LQ + 1024;  // + barriers
+    static constexpr int S = (6 * STAGE + FIXED <= 200 * 1024) ? 6 : (4 * STAGE + FIXED <= 200 * 1024) ? 4
+                                                                  : ((3 * STAGE + FIXED <= 214 * 1024) ? 3 : 2);
+    static constexpr int EW = 16;  // epilogue warps: 4 row quarters x 4 column quarters
     static constexpr int THREADS = 64 + 32 * EW;
-    static constexpr int BAR_OFF = S * STAGE + 2 * OUT;
-    static constexpr int TOTAL = BAR_OFF + 512 + 1024;
+    static constexpr int OUT_OFF = S * STAGE;
+    static constexpr int WX_OFF = OUT_OFF + 2 * OUT;
+    static constexpr int LQ_OFF = WX_OFF + WX;
+    static constexpr int BAR_OFF = LQ_OFF + 2 * LQ;
+    static constexpr int OT_OFF = BAR_OFF + 1024;
+    static int total(int n32) { return OT_OFF + ((n32 * 8 + 15) & ~15) + 1024; }
     static constexpr int CODE_ROW = CH * BITS / 8;  // bytes of one token's codes in the tile
 };
 
@@ -61,27 +73,43 @@ __device__ __forceinline__ int swz(int r, int c) {
     else return r * 32 + ((c ^ ((r >> 2) & 1)) << 4);
 }
 
-__device__ __forceinline__ float lo_bf(uint32_t w) { return __uint_as_float(w << 16); }
-__device__ __forceinline__ float hi_bf(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
-__device__ __forceinline__ uint32_t pack_bf(float a, float b) {
-    return (uint32_t)f2bf(a) | ((uint32_t)f2bf(b) << 16);
-}
-
-// 128-point unnormalised Walsh-Hadamard on registers (stages m = 1..64 as the oracle).
-__device__ __forceinline__ void wht128_reg(float (&v)[128]) {
-#pragma unroll
-    for (int m = 1; m < 128; m <<= 1) {
-#pragma unroll
-        for (int i = 0; i < 128; ++i) {
-            if (!(i & m)) {
-                float a = v[i], b = v[i + m];
-                v[i] = __fadd_rn(a, b);
-                v[i + m] = __fsub_rn(a, b);
+// Coordinates (channel chunk cc, token block tb, slice b) of consecutive
+// tiles in cc-fastest order, advanced without divisions.  Each CTA walks one
+// contiguous range of tiles, so consecutive tiles share their token block (and
+// its low-rank codes) and read neighbouring code columns.
+struct TileWalk {
+    int cc, tb, b;
+    int ncc, ntb;
+    __device__ TileWalk(int64_t first, int ncc_, int ntb_) : ncc(ncc_), ntb(ntb_) {
+        cc = (int)(first % ncc);
+        const int64_t bt = first / ncc;
+        tb = (int)(bt % ntb);
+        b = (int)(bt / ntb);
+    }
+    __device__ __forceinline__ void next() {
+        if (++cc == ncc) {
+            cc = 0;
+            if (++tb == ntb) {
+                tb = 0;
+                ++b;
             }
         }
     }
+};
+__device__ __forceinline__ void tile_range(const DecParams &p, int64_t &lo, int64_t &hi) {
+    const int i = blockIdx.x;
+    lo = (int64_t)i * p.tq + (i < p.trem ? i : p.trem);
+    hi = lo + p.tq + (i < p.trem ? 1 : 0);
 }
 
+__device__ __forceinline__ float lo_bf(uint32_t w) { return __uint_as_float(w << 16); }
+__device__ __forceinline__ float hi_bf(uint32_t w) { return __uint_as_float(w & 0xffff0000u); }
+
+// Epilogue geometry: 16 warps; warp w (2..17) reads TMEM lanes 32 (w % 4) ..
+// (its row quarter q) and handles 32 channels [32 h, 32 h + 32) of the tile,
+// h = (w - 2) / 4, one token row per thread: per tile a thread owns 32
+// consecutive channels of one row, i.e. one int4 group of 32, half of a group
+// of 64, a quarter of a group of 128 or of a rotation block.
 template <int BITS, int OP, bool WHT, int RB>
 __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
     cg_decode_tc_kernel(const __grid_constant__ CUtensorMap tm_lq, const __grid_constant__ CUtensorMap tm_vq,
@@ -95,9 +123,14 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
     uint64_t *empty = full + L::S;
     uint64_t *tfull = empty + L::S;
     uint64_t *tempty = tfull + 2;
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(tempty + 2);
+    uint64_t *lqfull = tempty + 2;   // [2] low-rank code slots loaded
+    uint64_t *lqempty = lqfull + 2;  // [2] ... and no longer read by the tensor cores
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(lqempty + 2);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    uint8_t *lqbuf = smem + L::LQ_OFF;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    int64_t t_lo, t_hi;
+    tile_range(p, t_lo, t_hi);
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < L::S; ++s) {
@@ -107,6 +140,8 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
         for (int b = 0; b < 2; ++b) {
             tc::mbar_init(&tfull[b], 1);
             tc::mbar_init(&tempty[b], L::EW);
+            tc::mbar_init(&lqfull[b], 1);
+            tc::mbar_init(&lqempty[b], 1);
         }
         *abort = 0;
         tc::fence_mbar_init();
@@ -125,26 +160,35 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
         if (lane == 0) {
             if (RB) {
                 tc::prefetch_tmap(&tm_lq);
-                tc::prefetch_tmap(&tm_vq);
+                if (!p.vqs) tc::prefetch_tmap(&tm_vq);
             }
             tc::prefetch_tmap(&tm_codes);
-            int i = 0;
-            for (int64_t tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x, ++i) {
+            int i = 0, nlq = 0;
+            TileWalk tw(t_lo, p.ncc, p.ntb);
+            for (int64_t tile = t_lo; tile < t_hi; ++tile, ++i, tw.next()) {
                 const int s = i % L::S;
                 const uint32_t ph = (i / L::S) & 1;
+                const int cc = tw.cc, tb = tw.tb, b = tw.b;
+                if (RB && (tile == t_lo || cc == 0)) {
+                    // a new token block: its low-rank codes into the free slot
+                    const int ls = nlq & 1;
+                    if (!tc::mbar_wait(&lqempty[ls], ((nlq >> 1) & 1) ^ 1, abort)) break;
+                    tc::mbar_arrive_expect_tx(&lqfull[ls], L::LQ);
+                    tc::tma_load_3d(lqbuf + ls * L::LQ, &tm_lq, &lqfull[ls], 0, tb * ROWS, b);
+                    ++nlq;
+                }
                 if (!tc::mbar_wait(&empty[s], ph ^ 1, abort)) break;
-                const int cc = (int)(tile % p.ncc);
-                const int64_t bt = tile / p.ncc;
-                const int tb = (int)(bt % p.ntb), b = (int)(bt / p.ntb);
                 uint8_t *st = smem + s * L::STAGE;
                 tc::mbar_arrive_expect_tx(&full[s], L::STAGE);
                 if constexpr (RB > 0) {
-                    tc::tma_load_3d(st, &tm_lq, &full[s], 0, tb * ROWS, b);
-                    tc::tma_load_3d(st + L::LQ, &tm_vq, &full[s], 0, cc * CH, b);
+                    if (p.vqs)  // one contiguous tile of the prepared operand
+                        tc::bulk_load(st, p.vqs + ((int64_t)b * p.ncc + cc) * L::VQ, L::VQ, &full[s]);
+                    else
+                        tc::tma_load_3d(st, &tm_vq, &full[s], 0, cc * CH, b);
                 }
-                tc::tma_load_3d(st + L::LQ + L::VQ, &tm_codes, &full[s], cc * L::CODE_ROW, tb * ROWS, b);
+                tc::tma_load_3d(st + L::VQ, &tm_codes, &full[s], cc * L::CODE_ROW, tb * ROWS, b);
                 if constexpr (OP != ACT_OP_DECODE) {
-                    uint8_t *y = st + L::LQ + L::VQ + L::CODES;
+                    uint8_t *y = st + L::VQ + L::CODES;
                     tc::tma_load_3d(y, &tm_y, &full[s], cc * CH, tb * ROWS, b);
                     tc::tma_load_3d(y + ROWS * 128, &tm_y, &full[s], cc * CH + 64, tb * ROWS, b);
                 }
@@ -156,78 +200,92 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
             if (lane == 0) {
                 constexpr uint32_t idesc = tc::idesc_i8(ROWS, CH);
                 constexpr tc::Swizzle SW = RB == 32 ? tc::SW_32B : tc::SW_64B;
-                int i = 0;
-                for (int64_t tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x, ++i) {
+                int i = 0, mlq = 0;
+                TileWalk tw(t_lo, p.ncc, p.ntb);
+                for (int64_t tile = t_lo; tile < t_hi; ++tile, ++i, tw.next()) {
                     const int s = i % L::S, b = i & 1;
                     const uint32_t ph = (i / L::S) & 1, bph = (i >> 1) & 1;
+                    if (tile == t_lo || tw.cc == 0) {  // a new token block: its low-rank codes have landed
+                        if (!tc::mbar_wait(&lqfull[mlq & 1], (mlq >> 1) & 1, abort)) break;
+                        ++mlq;
+                    }
+                    const int lslot = (mlq - 1) & 1;
                     if (!tc::mbar_wait(&full[s], ph, abort)) break;
                     if (!tc::mbar_wait(&tempty[b], bph ^ 1, abort)) break;
                     tc::tc_fence_after();
                     uint8_t *st = smem + s * L::STAGE;
+                    const uint8_t *lq = lqbuf + lslot * L::LQ;
 #pragma unroll
                     for (int kk = 0; kk < RB / 32; ++kk) {
-                        const uint64_t ad = tc::smem_desc(st + kk * 32, 16, 8 * RB, SW);
-                        const uint64_t bd = tc::smem_desc(st + L::LQ + kk * 32, 16, 8 * RB, SW);
+                        const uint64_t ad = tc::smem_desc(lq + kk * 32, 16, 8 * RB, SW);
+                        const uint64_t bd = tc::smem_desc(st + kk * 32, 16, 8 * RB, SW);
                         tc::mma_i8(tmem + b * CH, ad, bd, idesc, kk > 0);
                     }
                     tc::mma_commit(&tfull[b]);
                     tc::mma_commit(&empty[s]);
+                    // last tile of this token block in my range: the slot frees once these MMAs complete
+                    if (tw.cc == p.ncc - 1 || tile == t_hi - 1) tc::mma_commit(&lqempty[lslot]);
                 }
             }
         }
     } else {
         // ------------------------------------------------------------ epilogue
         const int ew = warp - 2;
-        const int q = warp & 3;              // TMEM lane quadrant of this warp
-        const int h = WHT ? 0 : ew >> 2;     // column half (64 columns) when 8 warps
-        constexpr int NC = WHT ? 128 : 64;   // columns per thread
-        constexpr int NP = NC / 32;          // 32-column pieces per thread
-        const int r = q * 32 + lane;         // row of the tile
+        const int etid = threadIdx.x - 64;
+        constexpr int ETH = 32 * L::EW;
+        const int q = warp & 3;  // TMEM lane quadrant of this warp
+        const int h = ew >> 2;   // 32-channel quarter of the tile
+        const int r = q * 32 + lane;
         const int ngr = (int)(p.H / p.group);
-        const bool leader = (ew == 0 && lane == 0);
-        int32_t *sidx = reinterpret_cast<int32_t *>(tmem_slot + 8);  // outlier channels of the current slice
+        const bool leader = etid == 0;
+        uint32_t *omask = reinterpret_cast<uint32_t *>(smem + p.off_ot);  // per 32-channel group of H
+        int32_t *obelow = reinterpret_cast<int32_t *>(omask + p.n32);
+        float *wx = reinterpret_cast<float *>(smem + L::WX_OFF);
         int cur_slice = -1;
 
         // per-row scalars of a tile, loaded one tile ahead so their latency hides
-        float nsc[NP], nsl = 0.f;
-        auto prefetch = [&](int64_t tile) {
-#pragma unroll
-            for (int j = 0; j < NP; ++j) nsc[j] = 0.f;
+        float nsc = 0.f, nsl = 0.f;
+        TileWalk tw(t_lo, p.ncc, p.ntb), nw = tw;  // this tile, the next one
+        auto prefetch = [&](int64_t tile, const TileWalk &at) {
+            nsc = 0.f;
             nsl = 0.f;
             if (tile >= p.ntiles) return;
-            const int cc = (int)(tile % p.ncc);
-            const int64_t bt = tile / p.ncc;
-            const int tb = (int)(bt % p.ntb), sb = (int)(bt / p.ntb);
+            const int cc = at.cc, tb = at.tb, sb = at.b;
             const int64_t t = (int64_t)tb * ROWS + r;
             if (t >= p.T) return;
             const int64_t trow = (int64_t)sb * p.T + t;
-#pragma unroll
-            for (int j = 0; j < NP; ++j) {
-                const int64_t c = (int64_t)cc * CH + h * 64 + 32 * j;
-                if (c < p.H) nsc[j] = __ldg(p.scales + trow * ngr + c / p.group);
-            }
+            const int64_t c = (int64_t)cc * CH + 32 * h;
+            if (c < p.H) nsc = __ldg(p.scales + trow * ngr + c / p.group);
             if (RB) nsl = __ldg(p.lr_scale + trow);
         };
-        prefetch(blockIdx.x);
+        prefetch(t_lo < t_hi ? t_lo : p.ntiles, nw);
 
         int i = 0;
-        for (int64_t tile = blockIdx.x; tile < p.ntiles; tile += gridDim.x, ++i) {
+        for (int64_t tile = t_lo; tile < t_hi; ++tile, ++i, tw.next()) {
             const int s = i % L::S, b = i & 1, ob = i & 1;
             const uint32_t ph = (i / L::S) & 1, bph = (i >> 1) & 1;
-            const int cc = (int)(tile % p.ncc);
-            const int64_t bt = tile / p.ncc;
-            const int tb = (int)(bt % p.ntb), sl_b = (int)(bt / p.ntb);
-            float sc[NP];
-#pragma unroll
-            for (int j = 0; j < NP; ++j) sc[j] = nsc[j];
-            const float sl = nsl;
-            prefetch(tile + gridDim.x);
+            const int cc = tw.cc, tb = tw.tb, sl_b = tw.b;
+            const float sc = nsc, sl = nsl;
+            nw.next();
+            prefetch(tile + 1 < t_hi ? tile + 1 : p.ntiles, nw);
 
-            // outlier channels of this slice, in shared memory
+            // outlier table of the slice: per 32-channel group a mask and the
+            // number of outlier channels below it (indices ascending)
             if (p.k && sl_b != cur_slice) {
-                tc::named_bar(2, 32 * L::EW);
-                for (int j = ew * 32 + lane; j < p.k; j += 32 * L::EW) sidx[j] = __ldg(p.idx + (int64_t)sl_b * p.k + j);
-                tc::named_bar(2, 32 * L::EW);
+                tc::named_bar(2, ETH);
+                for (int g = etid; g < p.n32; g += ETH) {
+                    const int64_t lo = 32 * (int64_t)g;
+                    uint32_t m = 0;
+                    int below = 0;
+                    for (int j = 0; j < p.k; ++j) {
+                        const int64_t c = __ldg(p.idx + (int64_t)sl_b * p.k + j);
+                        below += c < lo;
+                        if (c >= lo && c < lo + 32) m |= 1u << (c - lo);
+                    }
+                    omask[g] = m;
+                    obelow[g] = below;
+                }
+                tc::named_bar(2, ETH);
                 cur_slice = sl_b;
             }
             bool ok = tc::mbar_wait(&full[s], ph, abort);
@@ -237,116 +295,138 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
             const int64_t t = (int64_t)tb * ROWS + r;
             const bool rv = t < p.T;
             const int64_t trow = (int64_t)sl_b * p.T + t;
-            const int64_t c_first = (int64_t)cc * CH + h * 64;
+            const int64_t c_first = (int64_t)cc * CH + 32 * h;
 
-            // low-rank term I: read up front without the rotation (its latency
-            // overlaps the residual), piece by piece after it (registers)
-            uint32_t I[WHT ? 32 : NC];
-            const uint32_t taddr = tmem + ((uint32_t)(q * 32) << 16) + b * CH + h * 64;
-            if constexpr (RB > 0 && !WHT) {
-#pragma unroll
-                for (int j = 0; j < NP; ++j)
-                    tc::tmem_ld32(taddr + 32 * j, *reinterpret_cast<uint32_t(*)[32]>(&I[32 * j]));
-            }
+            // low-rank term I (int32) for my 32 channels: issued first, waited for late
+            uint32_t I[32];
+            if constexpr (RB > 0) tc::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + b * CH + 32 * h, I);
 
-            // residual: w = (u - 2^(b-1)) * s
-            const uint8_t *ct = smem + s * L::STAGE + L::LQ + L::VQ;
-            float w[NC];
-            constexpr float UOFF = 8388608.0f + (float)off;
+            // residual: w = (u - 2^(b-1)) * s, exact conversion of the code
+            const uint8_t *ct = smem + s * L::STAGE + L::VQ;
+            float2 w[16];
+            {
+                const float2 sc2 = make_float2(sc, sc);
+                constexpr float UOFF = 8388608.0f + (float)off;
+                const float2 uoff2 = make_float2(UOFF, UOFF);
+                uint32_t wd[BITS];  // BITS words hold my 32 codes
+                if constexpr (BITS == 4) {
+                    const uint4 v = *reinterpret_cast<const uint4 *>(ct + swz<64>(r, h));
+                    wd[0] = v.x; wd[1] = v.y; wd[2] = v.z; wd[3] = v.w;
+                } else {
+                    const uint4 v0 = *reinterpret_cast<const uint4 *>(ct + swz<128>(r, 2 * h));
+                    const uint4 v1 = *reinterpret_cast<const uint4 *>(ct + swz<128>(r, 2 * h + 1));
+                    wd[0] = v0.x; wd[1] = v0.y; wd[2] = v0.z; wd[3] = v0.w;
+                    wd[4] = v1.x; wd[5] = v1.y; wd[6] = v1.z; wd[7] = v1.w;
+                }
 #pragma unroll
-            for (int c16 = 0; c16 < NC * BITS / 128; ++c16) {  // 16-byte code chunks
-                const int chunk = (h * 64 * BITS / 8) / 16 + c16;
-                const uint4 v = *reinterpret_cast<const uint4 *>(ct + swz<L::CODE_ROW>(r, chunk));
-                const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                for (int e = 0; e < 128 / BITS; ++e) {
-                    const int col = c16 * (128 / BITS) + e;
-                    const uint32_t u = (wd[e / (32 / BITS)] >> ((e % (32 / BITS)) * BITS)) & ((1u << BITS) - 1u);
-                    w[col] = __fmul_rn(u2f_minus(u, UOFF), sc[col / 32]);
+                for (int e = 0; e < 16; ++e) {  // channel pair (2e, 2e + 1)
+                    constexpr int PW = 32 / BITS;  // codes per word
+                    const int c0 = 2 * e, c1 = 2 * e + 1;
+                    const uint32_t u0 = (wd[c0 / PW] >> ((c0 % PW) * BITS)) & ((1u << BITS) - 1u);
+                    const uint32_t u1 = (wd[c1 / PW] >> ((c1 % PW) * BITS)) & ((1u << BITS) - 1u);
+                    const float2 f = make_float2(__uint_as_float(0x4B000000u | u0), __uint_as_float(0x4B000000u | u1));
+                    w[e] = mul2(sub2(f, uoff2), sc2);
                 }
             }
             if constexpr (WHT) {
-                wht128_reg(w);
+                // 128-point rotation over the 4 column quarters of a row: stages
+                // m = 1..16 inside my 32 channels, m = 32 and 64 across quarters
+                // through shared memory (oracle stage order), then * 1/128
+                float (&v)[32] = *reinterpret_cast<float(*)[32]>(&w[0]);
 #pragma unroll
-                for (int j = 0; j < NC; ++j) w[j] = __fmul_rn(w[j], 0.0078125f);
-            }
-            // xhat = fma(I, sL, w), in place
-            if constexpr (RB > 0) {
-                if constexpr (WHT) {
+                for (int m = 1; m < 32; m <<= 1) {
 #pragma unroll
-                    for (int j = 0; j < NP; ++j) {
-                        tc::tmem_ld32(taddr + 32 * j, *reinterpret_cast<uint32_t(*)[32]>(&I[0]));
-                        tc::tmem_ld_wait();
-#pragma unroll
-                        for (int e = 0; e < 32; ++e) w[32 * j + e] = __fmaf_rn(i2f_exact((int)I[e]), sl, w[32 * j + e]);
+                    for (int e = 0; e < 32; ++e) {
+                        if (!(e & m)) {
+                            const float a = v[e], c = v[e + m];
+                            v[e] = __fadd_rn(a, c);
+                            v[e + m] = __fsub_rn(a, c);
+                        }
                     }
-                } else {
-                    tc::tmem_ld_wait();
+                }
+                tc::named_bar(4 + q, 128);  // the previous tile's exchange has been read
+                float *mine = wx + (h * ROWS + r) * 32;
 #pragma unroll
-                    for (int j = 0; j < NC; ++j) w[j] = __fmaf_rn(i2f_exact((int)I[j]), sl, w[j]);
+                for (int c4 = 0; c4 < 8; ++c4)
+                    *reinterpret_cast<float4 *>(mine + ((c4 ^ (r & 7)) << 2)) =
+                        make_float4(v[4 * c4], v[4 * c4 + 1], v[4 * c4 + 2], v[4 * c4 + 3]);
+                tc::named_bar(4 + q, 128);
+#pragma unroll
+                for (int c4 = 0; c4 < 8; ++c4) {  // four channels of each quarter at a time
+                    float4 x4[4];
+#pragma unroll
+                    for (int hh = 0; hh < 4; ++hh)
+                        x4[hh] = *reinterpret_cast<const float4 *>(wx + (hh * ROWS + r) * 32 + ((c4 ^ (r & 7)) << 2));
+                    const float *a0 = &x4[0].x, *a1 = &x4[1].x, *a2 = &x4[2].x, *a3 = &x4[3].x;
+#pragma unroll
+                    for (int j = 0; j < 4; ++j) {
+                        // stage 32 pairs quarters (0, 1) and (2, 3); stage 64 pairs (0', 2') and (1', 3')
+                        const float s01 = __fadd_rn(a0[j], a1[j]), d01 = __fsub_rn(a0[j], a1[j]);
+                        const float s23 = __fadd_rn(a2[j], a3[j]), d23 = __fsub_rn(a2[j], a3[j]);
+                        float o;
+                        if (h == 0) o = __fadd_rn(s01, s23);
+                        else if (h == 1) o = __fadd_rn(d01, d23);
+                        else if (h == 2) o = __fsub_rn(s01, s23);
+                        else o = __fsub_rn(d01, d23);
+                        v[4 * c4 + j] = __fmul_rn(o, 0.0078125f);
+                    }
+                }
+            }
+            // xhat = fma(I, sL, w), I converted exactly (magic-number add)
+            if constexpr (RB > 0) {
+                tc::tmem_ld_wait();
+                const float2 sl2 = make_float2(sl, sl);
+                const float2 m2 = make_float2(12582912.0f, 12582912.0f);
+#pragma unroll
+                for (int e = 0; e < 16; ++e) {
+                    const float2 iv = sub2(make_float2(__int_as_float((int)I[2 * e] + 0x4B400000),
+                                                       __int_as_float((int)I[2 * e + 1] + 0x4B400000)),
+                                           m2);
+                    w[e] = fma2(iv, sl2, w[e]);
                 }
                 tc::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(&tempty[b]);
             }
-            // outlier channels inside my columns (uniform over the warp): a mask
-            // built from the shared copy of the slice's indices with two ballots
-            uint64_t om[NC / 64];
-            int olo[NC / 64];
-#pragma unroll
-            for (int g = 0; g < NC / 64; ++g) {
-                om[g] = 0;
-                olo[g] = 0;
-                if (p.k) {
-                    const int64_t lo_c = c_first + 64 * g;
-                    uint64_t bits = 0;
-                    int below = 0;
-#pragma unroll
-                    for (int half = 0; half < 2; ++half) {
-                        const int j = lane + 32 * half;
-                        const int64_t c = j < p.k ? (int64_t)sidx[j] : INT64_MAX;
-                        below += __popc(__ballot_sync(0xffffffffu, c < lo_c));
-                        if (c >= lo_c && c < lo_c + 64) bits |= 1ull << (c - lo_c);
-                    }
-#pragma unroll
-                    for (int o = 16; o > 0; o >>= 1) bits |= __shfl_xor_sync(0xffffffffu, bits, o);
-                    om[g] = bits;
-                    olo[g] = below;
-                }
-            }
             // bf16 reconstruction (the consumer ops take it as their input)
             if constexpr (OP != ACT_OP_DECODE) {
 #pragma unroll
-                for (int j = 0; j < NC; ++j) w[j] = rne_bf(w[j]);
+                for (int e = 0; e < 16; ++e) w[e] = make_float2(rne_bf(w[e].x), rne_bf(w[e].y));
             }
+            // outlier channels of my 32 (warp-uniform mask): verbatim values
+            if (p.k && c_first < p.H) {
+                const int g32 = (int)(c_first >> 5);
+                const uint32_t om = omask[g32];
+                if (om) {
+                    const int below = obelow[g32];
 #pragma unroll
-            for (int g = 0; g < NC / 64; ++g) {
-                if (om[g]) {
+                    for (int c8 = 0; c8 < 4; ++c8) {
+                        const uint32_t m8 = (om >> (8 * c8)) & 0xffu;
+                        if (!m8) continue;
 #pragma unroll
-                    for (int e = 0; e < 64; ++e) {
-                        if ((om[g] >> e) & 1ull) {
-                            const int slot = olo[g] + __popcll(om[g] & ((1ull << e) - 1ull));
-                            w[g * 64 + e] = rv ? bf2f(p.outliers[trow * p.k + slot]) : 0.f;
+                        for (int e8 = 0; e8 < 8; ++e8) {
+                            if ((m8 >> e8) & 1u) {
+                                const int e = 8 * c8 + e8;
+                                const int slot = below + __popc(om & ((1u << e) - 1u));
+                                const float v = rv ? bf2f(p.outliers[trow * p.k + slot]) : 0.f;
+                                if (e & 1) w[e >> 1].y = v;
+                                else w[e >> 1].x = v;
+                            }
                         }
                     }
                 }
             }
             // second operand and consumer op
             if constexpr (OP != ACT_OP_DECODE) {
-                const uint8_t *yt = smem + s * L::STAGE + L::LQ + L::VQ + L::CODES;
+                const uint8_t *box = smem + s * L::STAGE + L::VQ + L::CODES + (h >> 1) * ROWS * 128;
 #pragma unroll
-                for (int g = 0; g < NC / 64; ++g) {
-                    const uint8_t *box = yt + (h + g) * ROWS * 128;
+                for (int c16 = 0; c16 < 4; ++c16) {
+                    const uint4 v = *reinterpret_cast<const uint4 *>(box + swz<128>(r, (h & 1) * 4 + c16));
+                    const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
 #pragma unroll
-                    for (int c16 = 0; c16 < 8; ++c16) {
-                        const uint4 v = *reinterpret_cast<const uint4 *>(box + swz<128>(r, c16));
-                        const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                        for (int e = 0; e < 4; ++e) {
-                            const int j = g * 64 + c16 * 8 + 2 * e;
-                            w[j] = apply_op<OP>(w[j], lo_bf(wd[e]));
-                            w[j + 1] = apply_op<OP>(w[j + 1], hi_bf(wd[e]));
-                        }
+                    for (int e = 0; e < 4; ++e) {
+                        float2 &x2 = w[4 * c16 + e];
+                        x2 = make_float2(apply_op<OP>(x2.x, lo_bf(wd[e])), apply_op<OP>(x2.y, hi_bf(wd[e])));
                     }
                 }
             }
@@ -355,25 +435,24 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
             if (lane == 0) tc::mbar_arrive(&empty[s]);
 
             // staging buffer ob: free once the store issued two tiles ago has read it
-            uint8_t *stg = smem + L::S * L::STAGE + ob * L::OUT;
+            uint8_t *stg = smem + L::OUT_OFF + ob * L::OUT;
             if (leader) tc::bulk_wait_read<1>();
-            tc::named_bar(1, 32 * L::EW);
+            tc::named_bar(1, ETH);
+            {
+                uint8_t *box = stg + (h >> 1) * ROWS * 128;
 #pragma unroll
-            for (int g = 0; g < NC / 64; ++g) {
-                uint8_t *box = stg + (h + g) * ROWS * 128;
-#pragma unroll
-                for (int c16 = 0; c16 < 8; ++c16) {
-                    const int j = g * 64 + c16 * 8;
+                for (int c16 = 0; c16 < 4; ++c16) {
+                    const int e = 4 * c16;
                     uint4 v;
-                    v.x = pack_bf16x2(w[j], w[j + 1]);
-                    v.y = pack_bf16x2(w[j + 2], w[j + 3]);
-                    v.z = pack_bf16x2(w[j + 4], w[j + 5]);
-                    v.w = pack_bf16x2(w[j + 6], w[j + 7]);
-                    *reinterpret_cast<uint4 *>(box + swz<128>(r, c16)) = v;
+                    v.x = pack_bf16x2(w[e].x, w[e].y);
+                    v.y = pack_bf16x2(w[e + 1].x, w[e + 1].y);
+                    v.z = pack_bf16x2(w[e + 2].x, w[e + 2].y);
+                    v.w = pack_bf16x2(w[e + 3].x, w[e + 3].y);
+                    *reinterpret_cast<uint4 *>(box + swz<128>(r, (h & 1) * 4 + c16)) = v;
                 }
             }
             tc::fence_proxy_async();
-            tc::named_bar(1, 32 * L::EW);
+            tc::named_bar(1, ETH);
             if (leader) {
                 tc::tma_store_3d(&tm_out, stg, cc * CH, tb * ROWS, sl_b);
                 tc::tma_store_3d(&tm_out, stg + ROWS * 128, cc * CH + 64, tb * ROWS, sl_b);
@@ -427,10 +506,17 @@ int launch_decode(const actcomp_cg_desc *d, const uint16_t *y, int64_t ldy, uint
     p.ntb = (int)((T + ROWS - 1) / ROWS);
     p.ncc = (int)((H + CH - 1) / CH);
     p.ntiles = (int64_t)p.ntb * p.ncc * B;
+    p.n32 = (int)((H + 31) / 32);
+    p.off_ot = L::OT_OFF;
+    p.vqs = d->basis_qs;
+    const int smem = L::total(p.n32);
+    if (smem > 227 * 1024) return ACT_E_UNSUPPORTED;
     auto kern = cg_decode_tc_kernel<BITS, OP, WHT, RB>;
-    ACT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, L::TOTAL));
+    ACT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     const int grid = (int)(p.ntiles < num_sms() ? p.ntiles : num_sms());
-    kern<<<grid, L::THREADS, L::TOTAL, stream>>>(m_lq, m_vq, m_codes, m_y, m_out, p);
+    p.tq = (int)(p.ntiles / grid);
+    p.trem = (int)(p.ntiles % grid);
+    kern<<<grid, L::THREADS, smem, stream>>>(m_lq, m_vq, m_codes, m_y, m_out, p);
     return launch_status();
 }
 

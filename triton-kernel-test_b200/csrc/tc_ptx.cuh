@@ -163,6 +163,16 @@ __device__ __forceinline__ void bulk_copy_to_peer(uint32_t dst_cluster, const vo
         : "memory");
 }
 
+// Bulk copy of `bytes` (multiple of 16; both addresses 16-byte aligned) from
+// global memory into this CTA's shared memory, completing on `bar`.  One
+// contiguous transfer, no tensor map, no multicast.
+__device__ __forceinline__ void bulk_load(void *dst, const void *src, uint32_t bytes, uint64_t *bar) {
+    asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                     smem_u32(dst)),
+                 "l"(src), "r"(bytes), "r"(smem_u32(bar))
+                 : "memory");
+}
+
 // Make generic-proxy shared-memory writes visible to the async proxy
 // (tensor-core operand reads).
 __device__ __forceinline__ void fence_proxy_async() { asm volatile("fence.proxy.async.shared::cta;" ::: "memory"); }
