@@ -64,6 +64,8 @@ struct EncParams {
 constexpr int NB = 2;      // residual ring: X 128x128 (32 KB) + Vq 128 x r bf16
 constexpr int MAXNA = 6;   // projection ring: X 128x64 (16 KB) + V^T r x 64
 constexpr int FL = 4;      // chunks per scale flush
+constexpr int NT = 3;      // residual-term accumulators in TMEM (3 x 128 columns after the projection's 128):
+                           // the MMA runs up to NT chunks ahead of the epilogue
 
 // RK: rank rounded up to 16, 32 or 64; LB = bytes of one bf16 row of Lq / Vq.
 template <int BITS, bool WHT, int RK, int EW>
@@ -188,9 +190,9 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK, EW>::THREADS, 1)
     uint64_t *emptyA = fullA + MAXNA;
     uint64_t *fullB = emptyA + MAXNA;
     uint64_t *emptyB = fullB + NB;
-    uint64_t *tfull = emptyB + NB;  // [2]
-    uint64_t *tempty = tfull + 2;   // [2]
-    uint64_t *lfull = tempty + 2;
+    uint64_t *tfull = emptyB + NB;  // [NT]
+    uint64_t *tempty = tfull + NT;  // [NT]
+    uint64_t *lfull = tempty + NT;
     uint64_t *lempty = lfull + 1;
     uint64_t *lqready = lempty + 1;
     uint64_t *pready = lqready + 1;  // peers' partials have landed (transaction bytes)
@@ -219,7 +221,7 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK, EW>::THREADS, 1)
             tc::mbar_init(&fullB[s], 1);
             tc::mbar_init(&emptyB[s], 1 + EW);
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < NT; ++b) {
             tc::mbar_init(&tfull[b], 1);
             tc::mbar_init(&tempty[b], EW);
         }
@@ -242,7 +244,7 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK, EW>::THREADS, 1)
     tc::tc_fence_after();
     const uint32_t tmem = *tmem_slot;
     const uint32_t tm_l = tmem;        // projection accumulator, columns [0, 64)
-    const uint32_t tm_p = tmem + 128;  // residual-term accumulators, [128, 384)
+    const uint32_t tm_p = tmem + 128;  // NT residual-term accumulators, [128, 512)
 
     if (warp == 0) {
         // ------------------------------------------------------------ phase-1 producer
@@ -330,9 +332,9 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK, EW>::THREADS, 1)
                 if (!(ok = tc::mbar_wait(lqready, nb & 1, abort))) break;
                 tc::tc_fence_after();
                 for (int ck = 0; ck < nk2; ++ck, ++i) {
-                    const int s = i % NB, tb2 = i & 1;
+                    const int s = i % NB, tb2 = i % NT;
                     if (!(ok = tc::mbar_wait(&fullB[s], (i / NB) & 1, abort))) break;
-                    if (!(ok = tc::mbar_wait(&tempty[tb2], ((i >> 1) & 1) ^ 1, abort))) break;
+                    if (!(ok = tc::mbar_wait(&tempty[tb2], ((i / NT) & 1) ^ 1, abort))) break;
                     tc::tc_fence_after();
                     uint8_t *st = ringB + s * L::SLOT_B;
                     for (int kk = 0; kk < nkq; ++kk) {
@@ -523,9 +525,9 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK, EW>::THREADS, 1)
             // ---- residual codes, chunk by chunk
             const float2 nsl2 = make_float2(-sl, -sl);
             for (int ck = 0; ck < nk2 && ok; ++ck, ++j) {
-                const int s = j % NB, tb2 = j & 1;
+                const int s = j % NB, tb2 = j % NT;
                 if (!(ok = tc::mbar_wait(&fullB[s], (j / NB) & 1, abort))) break;
-                if (!(ok = tc::mbar_wait(&tfull[tb2], (j >> 1) & 1, abort))) break;
+                if (!(ok = tc::mbar_wait(&tfull[tb2], (j / NT) & 1, abort))) break;
                 tc::tc_fence_after();
                 const int64_t c0 = c_lo + (int64_t)ck * CH + h * 64;  // first channel of my columns
                 const uint8_t *xt = ringB + s * L::SLOT_B;

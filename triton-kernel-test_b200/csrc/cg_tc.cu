@@ -8,7 +8,7 @@
 //              second operand (128 x 128 bf16) into a 2-4 stage ring;
 //   MMA warp   issues one tcgen05.mma kind::i8 (M=128, N=128, K=32) per 32
 //              basis vectors: I = Lq . Vq^T, an exact int32 accumulator in TMEM
-//              (double-buffered, 2 x 128 columns);
+//              (4 accumulators of 128 columns, so the MMA runs ahead);
 //   epilogue   (16 warps: 4 row quarters x 4 column quarters, one token row
 //              and 32 channels per thread; the rotation exchanges quarters
 //              through shared memory) reads I with tcgen05.ld, forms
@@ -25,6 +25,7 @@ namespace cgtc {
 
 constexpr int CH = 128;    // channels per tile (MMA N)
 constexpr int ROWS = 128;  // tokens per tile (MMA M)
+constexpr int NT = 4;      // TMEM accumulators (4 x 128 columns): the MMA runs up to NT tiles ahead
 
 struct DecParams {
     int64_t T, H;
@@ -38,6 +39,7 @@ struct DecParams {
     int n32;      // 32-channel groups of H (outlier table entries)
     int off_ot;   // shared-memory offset of the outlier table
     int tq, trem;              // tiles per CTA: tq, and one more for the first trem CTAs
+    int off_ost, ostb;         // outlier staging: 2 slots of ostb bytes (128 rows x k bf16) at off_ost
     const int8_t *vqs;         // basis_qs tile operand (layout in include/actcomp.h), or null
 };
 
@@ -60,7 +62,8 @@ struct DecLayout {
     static constexpr int LQ_OFF = WX_OFF + WX;
     static constexpr int BAR_OFF = LQ_OFF + 2 * LQ;
     static constexpr int OT_OFF = BAR_OFF + 1024;
-    static int total(int n32) { return OT_OFF + ((n32 * 8 + 15) & ~15) + 1024; }
+    static int ost_off(int n32) { return OT_OFF + ((n32 * 8 + 15) & ~15); }
+    static int total(int n32, int k) { return ost_off(n32) + 2 * ((ROWS * k * 2 + 15) & ~15) + 1024; }
     static constexpr int CODE_ROW = CH * BITS / 8;  // bytes of one token's codes in the tile
 };
 
@@ -96,6 +99,18 @@ struct TileWalk {
         }
     }
 };
+// The outlier values of token block (tb, b) are rows tb*128 .. of the T x k
+// outlier matrix: one contiguous run, copied whole when its size and start
+// are 16-byte multiples (always, except possibly for the last, partial block
+// of a slice, whose values are then read from global memory).
+__device__ __forceinline__ uint32_t ost_bytes(const DecParams &p, int tb, int b, const uint16_t *&src) {
+    if (!p.k) return 0;
+    const int64_t rows = (p.T - (int64_t)tb * ROWS) < ROWS ? (p.T - (int64_t)tb * ROWS) : ROWS;
+    const int64_t bytes = rows * p.k * 2;
+    src = p.outliers + ((int64_t)b * p.T + (int64_t)tb * ROWS) * p.k;
+    if ((bytes & 15) || (reinterpret_cast<uintptr_t>(src) & 15)) return 0;
+    return (uint32_t)bytes;
+}
 __device__ __forceinline__ void tile_range(const DecParams &p, int64_t &lo, int64_t &hi) {
     const int i = blockIdx.x;
     lo = (int64_t)i * p.tq + (i < p.trem ? i : p.trem);
@@ -122,12 +137,14 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + L::BAR_OFF);
     uint64_t *empty = full + L::S;
     uint64_t *tfull = empty + L::S;
-    uint64_t *tempty = tfull + 2;
-    uint64_t *lqfull = tempty + 2;   // [2] low-rank code slots loaded
-    uint64_t *lqempty = lqfull + 2;  // [2] ... and no longer read by the tensor cores
+    uint64_t *tempty = tfull + NT;
+    uint64_t *lqfull = tempty + NT;   // [2] token-block slots (low-rank codes, outlier values) loaded
+    uint64_t *lqempty = lqfull + 2;  // [2] ... and no longer read
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(lqempty + 2);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
     uint8_t *lqbuf = smem + L::LQ_OFF;
+    uint8_t *ostbuf = smem + p.off_ost;
+    const bool blockbuf = RB > 0 || p.k > 0;  // per-token-block slots in use
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int64_t t_lo, t_hi;
     tile_range(p, t_lo, t_hi);
@@ -137,17 +154,19 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
             tc::mbar_init(&full[s], 1);
             tc::mbar_init(&empty[s], L::EW + (RB ? 1 : 0));
         }
-        for (int b = 0; b < 2; ++b) {
+        for (int b = 0; b < NT; ++b) {
             tc::mbar_init(&tfull[b], 1);
             tc::mbar_init(&tempty[b], L::EW);
+        }
+        for (int b = 0; b < 2; ++b) {
             tc::mbar_init(&lqfull[b], 1);
-            tc::mbar_init(&lqempty[b], 1);
+            tc::mbar_init(&lqempty[b], (RB ? 1 : 0) + (p.k ? L::EW : 0));
         }
         *abort = 0;
         tc::fence_mbar_init();
     }
     if (RB && warp == 1) {
-        tc::tmem_alloc(tmem_slot, 2 * CH);
+        tc::tmem_alloc(tmem_slot, NT * CH);
         tc::tmem_relinquish();
     }
     tc::tc_fence_before();
@@ -169,12 +188,15 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
                 const int s = i % L::S;
                 const uint32_t ph = (i / L::S) & 1;
                 const int cc = tw.cc, tb = tw.tb, b = tw.b;
-                if (RB && (tile == t_lo || cc == 0)) {
-                    // a new token block: its low-rank codes into the free slot
+                if (blockbuf && (tile == t_lo || cc == 0)) {
+                    // a new token block: its low-rank codes and outlier values into the free slot
                     const int ls = nlq & 1;
                     if (!tc::mbar_wait(&lqempty[ls], ((nlq >> 1) & 1) ^ 1, abort)) break;
-                    tc::mbar_arrive_expect_tx(&lqfull[ls], L::LQ);
-                    tc::tma_load_3d(lqbuf + ls * L::LQ, &tm_lq, &lqfull[ls], 0, tb * ROWS, b);
+                    const uint16_t *osrc = nullptr;
+                    const uint32_t obytes = ost_bytes(p, tb, b, osrc);
+                    tc::mbar_arrive_expect_tx(&lqfull[ls], (RB ? L::LQ : 0) + obytes);
+                    if (RB) tc::tma_load_3d(lqbuf + ls * L::LQ, &tm_lq, &lqfull[ls], 0, tb * ROWS, b);
+                    if (obytes) tc::bulk_load(ostbuf + ls * p.ostb, osrc, obytes, &lqfull[ls]);
                     ++nlq;
                 }
                 if (!tc::mbar_wait(&empty[s], ph ^ 1, abort)) break;
@@ -203,8 +225,8 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
                 int i = 0, mlq = 0;
                 TileWalk tw(t_lo, p.ncc, p.ntb);
                 for (int64_t tile = t_lo; tile < t_hi; ++tile, ++i, tw.next()) {
-                    const int s = i % L::S, b = i & 1;
-                    const uint32_t ph = (i / L::S) & 1, bph = (i >> 1) & 1;
+                    const int s = i % L::S, b = i % NT;
+                    const uint32_t ph = (i / L::S) & 1, bph = (i / NT) & 1;
                     if (tile == t_lo || tw.cc == 0) {  // a new token block: its low-rank codes have landed
                         if (!tc::mbar_wait(&lqfull[mlq & 1], (mlq >> 1) & 1, abort)) break;
                         ++mlq;
@@ -260,10 +282,11 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
         };
         prefetch(t_lo < t_hi ? t_lo : p.ntiles, nw);
 
-        int i = 0;
+        int i = 0, elq = 0;
+        const uint16_t *ovals = nullptr;  // this token block's outlier values (shared or global)
         for (int64_t tile = t_lo; tile < t_hi; ++tile, ++i, tw.next()) {
-            const int s = i % L::S, b = i & 1, ob = i & 1;
-            const uint32_t ph = (i / L::S) & 1, bph = (i >> 1) & 1;
+            const int s = i % L::S, b = i % NT, ob = i & 1;
+            const uint32_t ph = (i / L::S) & 1, bph = (i / NT) & 1;
             const int cc = tw.cc, tb = tw.tb, sl_b = tw.b;
             const float sc = nsc, sl = nsl;
             nw.next();
@@ -287,6 +310,13 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
                 }
                 tc::named_bar(2, ETH);
                 cur_slice = sl_b;
+            }
+            if (p.k && (tile == t_lo || tw.cc == 0)) {  // a new token block: its outlier values
+                if (!tc::mbar_wait(&lqfull[elq & 1], (elq >> 1) & 1, abort)) break;
+                const uint16_t *osrc = nullptr;
+                ovals = ost_bytes(p, tb, sl_b, osrc) ? reinterpret_cast<const uint16_t *>(ostbuf + (elq & 1) * p.ostb)
+                                                     : osrc;
+                ++elq;
             }
             bool ok = tc::mbar_wait(&full[s], ph, abort);
             if (RB) ok = ok && tc::mbar_wait(&tfull[b], bph, abort);
@@ -408,7 +438,7 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
                             if ((m8 >> e8) & 1u) {
                                 const int e = 8 * c8 + e8;
                                 const int slot = below + __popc(om & ((1u << e) - 1u));
-                                const float v = rv ? bf2f(p.outliers[trow * p.k + slot]) : 0.f;
+                                const float v = rv ? bf2f(ovals[r * p.k + slot]) : 0.f;
                                 if (e & 1) w[e >> 1].y = v;
                                 else w[e >> 1].x = v;
                             }
@@ -432,7 +462,11 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
             }
             // this stage is no longer read by the epilogue
             __syncwarp();
-            if (lane == 0) tc::mbar_arrive(&empty[s]);
+            if (lane == 0) {
+                tc::mbar_arrive(&empty[s]);
+                // last tile of this token block in my range: its outlier slot is free
+                if (p.k && (tw.cc == p.ncc - 1 || tile == t_hi - 1)) tc::mbar_arrive(&lqempty[(elq - 1) & 1]);
+            }
 
             // staging buffer ob: free once the store issued two tiles ago has read it
             uint8_t *stg = smem + L::OUT_OFF + ob * L::OUT;
@@ -465,7 +499,7 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
     __syncthreads();
     if (RB && warp == 1) {
         tc::tc_fence_after();
-        tc::tmem_dealloc(tmem, 2 * CH);
+        tc::tmem_dealloc(tmem, NT * CH);
     }
 }
 
@@ -509,7 +543,9 @@ int launch_decode(const actcomp_cg_desc *d, const uint16_t *y, int64_t ldy, uint
     p.n32 = (int)((H + 31) / 32);
     p.off_ot = L::OT_OFF;
     p.vqs = d->basis_qs;
-    const int smem = L::total(p.n32);
+    p.off_ost = L::ost_off(p.n32);
+    p.ostb = (ROWS * p.k * 2 + 15) & ~15;
+    const int smem = L::total(p.n32, p.k);
     if (smem > 227 * 1024) return ACT_E_UNSUPPORTED;
     auto kern = cg_decode_tc_kernel<BITS, OP, WHT, RB>;
     ACT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
