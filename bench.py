@@ -368,6 +368,37 @@ def run_gpu(args):
         components["dw_gemm_fused_4096x11008_k16384"] = {
             "ms": ms_dw, "TFLOP/s": tf, "frac_of_bf16_peak": tf / pk.get("bf16_tflops", 1590.0), "flops": flops}
         del dy, ws
+        # config 5: GELU backward on a compressed 65536 x 5120 activation
+        T5, H5 = 4 * T, 5120
+        x5, _ = synthetic.lowrank_activation(T5, H5, n_outlier=k, seed=200 + rank, device=dev, outlier_seed=200)
+        c5 = actcomp.encode(x5, actcomp.Basis.fit(x5[:4096], r), actcomp.select_outlier_channels(x5, k), bits=bits,
+                            group=group)
+        del x5
+        dy5 = synthetic.gradient((T5, H5), seed=13 + rank, device=dev)
+        ms_gelu = time_steps(lambda: actcomp.gelu_backward(c5, dy5), max(3, args.steps // 2), 1, flush, world, clk)
+        gb = consumer_bytes(T5, H5, bits, group, r, k)
+        components[f"gelu_bwd_fused_{T5}x{H5}"] = {"ms": ms_gelu, "GB/s": gb / (ms_gelu * 1e-3) / 1e9,
+                                                  "frac_of_hbm": gb / (ms_gelu * 1e-3) / 1e9 / hbm, "bytes": gb}
+        del c5, dy5
+        # config 5: softmax backward on compressed causal probabilities P (8, 32, 2048, 2048), one basis for all heads
+        Bh, NH, S = 8, 32, 2048
+        P = torch.empty((Bh * NH, S, S), dtype=torch.bfloat16, device=dev)
+        for bi in range(Bh):
+            P[bi * NH:(bi + 1) * NH] = synthetic.causal_softmax(1, NH, S, seed=300 + bi, device=dev)[0]
+        pf = P[0].to(torch.float32)
+        V = torch.linalg.eigh(pf.T @ pf)[1][:, -r:].flip(-1)
+        del pf
+        bP = actcomp.Basis.from_vectors(V.unsqueeze(0).expand(Bh * NH, S, r).contiguous())
+        cP = actcomp.encode(P, bP, None, bits=bits, group=group)
+        del P
+        dP = synthetic.gradient((Bh * NH, S, S), seed=17 + rank, device=dev)
+        ms_smax = time_steps(lambda: actcomp.softmax_backward(cP, dP, causal=True), max(3, args.steps // 4), 1, flush,
+                             world, clk)
+        sbytes = Bh * NH * (consumer_bytes(S, S, bits, group, r, 0))
+        components["softmax_bwd_fused_8x32x2048x2048_causal"] = {
+            "ms": ms_smax, "GB/s": sbytes / (ms_smax * 1e-3) / 1e9, "frac_of_hbm": sbytes / (ms_smax * 1e-3) / 1e9 / hbm,
+            "bytes": sbytes}
+        del cP, dP, bP
 
     # offload of the packed activation to pinned host memory and back (side stream, events)
     off = actcomp.Offloader(dev)

@@ -265,22 +265,29 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
         float *wx = reinterpret_cast<float *>(smem + L::WX_OFF);
         int cur_slice = -1;
 
-        // per-row scalars of a tile, loaded one tile ahead so their latency hides
-        float nsc = 0.f, nsl = 0.f;
-        TileWalk tw(t_lo, p.ncc, p.ntb), nw = tw;  // this tile, the next one
-        auto prefetch = [&](int64_t tile, const TileWalk &at) {
-            nsc = 0.f;
-            nsl = 0.f;
-            if (tile >= p.ntiles) return;
-            const int cc = at.cc, tb = at.tb, sb = at.b;
-            const int64_t t = (int64_t)tb * ROWS + r;
+        // per-row scalars of a tile (group scale, low-rank scale), loaded PD tiles
+        // ahead into a register queue so the global-load latency (~1-2 us under
+        // load) hides behind PD tiles of work
+        constexpr int PD = 4;
+        float qsc[PD], qsl[PD];
+        TileWalk tw(t_lo, p.ncc, p.ntb), nw = tw;  // this tile, the one PD ahead
+        const int gshift = 31 - __clz(p.group);
+        auto load_scalars = [&](int64_t tile, const TileWalk &at, float &vsc, float &vsl) {
+            vsc = 0.f;
+            vsl = 0.f;
+            if (tile >= t_hi) return;
+            const int64_t t = (int64_t)at.tb * ROWS + r;
             if (t >= p.T) return;
-            const int64_t trow = (int64_t)sb * p.T + t;
-            const int64_t c = (int64_t)cc * CH + 32 * h;
-            if (c < p.H) nsc = __ldg(p.scales + trow * ngr + c / p.group);
-            if (RB) nsl = __ldg(p.lr_scale + trow);
+            const int64_t trow = (int64_t)at.b * p.T + t;
+            const int64_t c = (int64_t)at.cc * CH + 32 * h;
+            if (c < p.H) vsc = __ldg(p.scales + trow * ngr + (c >> gshift));
+            if (RB) vsl = __ldg(p.lr_scale + trow);
         };
-        prefetch(t_lo < t_hi ? t_lo : p.ntiles, nw);
+#pragma unroll
+        for (int d = 0; d < PD; ++d) {
+            load_scalars(t_lo + d, nw, qsc[d], qsl[d]);
+            nw.next();
+        }
 
         int i = 0, elq = 0;
         const uint16_t *ovals = nullptr;  // this token block's outlier values (shared or global)
@@ -288,9 +295,14 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
             const int s = i % L::S, b = i % NT, ob = i & 1;
             const uint32_t ph = (i / L::S) & 1, bph = (i / NT) & 1;
             const int cc = tw.cc, tb = tw.tb, sl_b = tw.b;
-            const float sc = nsc, sl = nsl;
+            const float sc = qsc[0], sl = qsl[0];
+#pragma unroll
+            for (int d = 0; d + 1 < PD; ++d) {
+                qsc[d] = qsc[d + 1];
+                qsl[d] = qsl[d + 1];
+            }
+            load_scalars(tile + PD, nw, qsc[PD - 1], qsl[PD - 1]);
             nw.next();
-            prefetch(tile + 1 < t_hi ? tile + 1 : p.ntiles, nw);
 
             // outlier table of the slice: per 32-channel group a mask and the
             // number of outlier channels below it (indices ascending)
