@@ -26,6 +26,7 @@ namespace cgtc {
 constexpr int CH = 128;    // channels per tile (MMA N)
 constexpr int ROWS = 128;  // tokens per tile (MMA M)
 constexpr int NT = 4;      // TMEM accumulators (4 x 128 columns): the MMA runs up to NT tiles ahead
+constexpr int WST = 32 * 64;  // one warp's output staging buffer: 32 rows x 32 bf16
 
 struct DecParams {
     int64_t T, H;
@@ -259,7 +260,6 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
         const int h = ew >> 2;   // 32-channel quarter of the tile
         const int r = q * 32 + lane;
         const int ngr = (int)(p.H / p.group);
-        const bool leader = etid == 0;
         uint32_t *omask = reinterpret_cast<uint32_t *>(smem + p.off_ot);  // per 32-channel group of H
         int32_t *obelow = reinterpret_cast<int32_t *>(omask + p.n32);
         float *wx = reinterpret_cast<float *>(smem + L::WX_OFF);
@@ -360,14 +360,28 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
                     wd[0] = v0.x; wd[1] = v0.y; wd[2] = v0.z; wd[3] = v0.w;
                     wd[4] = v1.x; wd[5] = v1.y; wd[6] = v1.z; wd[7] = v1.w;
                 }
+                // code u -> float 2^23 + u by one byte permute against 0x4B000000:
+                // result bytes (code byte, 0, 0, 0x4B); int4 codes are first split
+                // into even (low nibble) and odd channels, one byte per code
+                constexpr uint32_t K4B = 0x4B000000u;
 #pragma unroll
-                for (int e = 0; e < 16; ++e) {  // channel pair (2e, 2e + 1)
-                    constexpr int PW = 32 / BITS;  // codes per word
-                    const int c0 = 2 * e, c1 = 2 * e + 1;
-                    const uint32_t u0 = (wd[c0 / PW] >> ((c0 % PW) * BITS)) & ((1u << BITS) - 1u);
-                    const uint32_t u1 = (wd[c1 / PW] >> ((c1 % PW) * BITS)) & ((1u << BITS) - 1u);
-                    const float2 f = make_float2(__uint_as_float(0x4B000000u | u0), __uint_as_float(0x4B000000u | u1));
-                    w[e] = mul2(sub2(f, uoff2), sc2);
+                for (int wi = 0; wi < BITS; ++wi) {
+                    if constexpr (BITS == 4) {
+                        const uint32_t ev = wd[wi] & 0x0F0F0F0Fu, od = (wd[wi] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+                        for (int m = 0; m < 4; ++m) {  // channels 8 wi + 2 m, 8 wi + 2 m + 1
+                            const float2 f = make_float2(__uint_as_float(__byte_perm(ev, K4B, 0x7540u | m)),
+                                                         __uint_as_float(__byte_perm(od, K4B, 0x7540u | m)));
+                            w[4 * wi + m] = mul2(sub2(f, uoff2), sc2);
+                        }
+                    } else {
+#pragma unroll
+                        for (int m = 0; m < 2; ++m) {  // channels 4 wi + 2 m, 4 wi + 2 m + 1
+                            const float2 f = make_float2(__uint_as_float(__byte_perm(wd[wi], K4B, 0x7540u | (2 * m))),
+                                                         __uint_as_float(__byte_perm(wd[wi], K4B, 0x7541u + 2 * m)));
+                            w[2 * wi + m] = mul2(sub2(f, uoff2), sc2);
+                        }
+                    }
                 }
             }
             if constexpr (WHT) {
@@ -480,32 +494,29 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
                 if (p.k && (tw.cc == p.ncc - 1 || tile == t_hi - 1)) tc::mbar_arrive(&lqempty[(elq - 1) & 1]);
             }
 
-            // staging buffer ob: free once the store issued two tiles ago has read it
-            uint8_t *stg = smem + L::OUT_OFF + ob * L::OUT;
-            if (leader) tc::bulk_wait_read<1>();
-            tc::named_bar(1, ETH);
-            {
-                uint8_t *box = stg + (h >> 1) * ROWS * 128;
+            // each warp stores its own 32 x 32 sub-tile: staging buffer ob of the
+            // warp is free once the warp's store issued two tiles ago has read it
+            uint8_t *stg = smem + L::OUT_OFF + ew * (2 * WST) + ob * WST;
+            if (lane == 0) tc::bulk_wait_read<1>();
+            __syncwarp();
 #pragma unroll
-                for (int c16 = 0; c16 < 4; ++c16) {
-                    const int e = 4 * c16;
-                    uint4 v;
-                    v.x = pack_bf16x2(w[e].x, w[e].y);
-                    v.y = pack_bf16x2(w[e + 1].x, w[e + 1].y);
-                    v.z = pack_bf16x2(w[e + 2].x, w[e + 2].y);
-                    v.w = pack_bf16x2(w[e + 3].x, w[e + 3].y);
-                    *reinterpret_cast<uint4 *>(box + swz<128>(r, (h & 1) * 4 + c16)) = v;
-                }
+            for (int c16 = 0; c16 < 4; ++c16) {
+                const int e = 4 * c16;
+                uint4 v;
+                v.x = pack_bf16x2(w[e].x, w[e].y);
+                v.y = pack_bf16x2(w[e + 1].x, w[e + 1].y);
+                v.z = pack_bf16x2(w[e + 2].x, w[e + 2].y);
+                v.w = pack_bf16x2(w[e + 3].x, w[e + 3].y);
+                *reinterpret_cast<uint4 *>(stg + swz<64>(lane, c16)) = v;
             }
             tc::fence_proxy_async();
-            tc::named_bar(1, ETH);
-            if (leader) {
-                tc::tma_store_3d(&tm_out, stg, cc * CH, tb * ROWS, sl_b);
-                tc::tma_store_3d(&tm_out, stg + ROWS * 128, cc * CH + 64, tb * ROWS, sl_b);
+            __syncwarp();
+            if (lane == 0) {
+                tc::tma_store_3d(&tm_out, stg, cc * CH + 32 * h, tb * ROWS + 32 * q, sl_b);
                 tc::bulk_commit();
             }
         }
-        if (leader) tc::bulk_wait<0>();
+        if (lane == 0) tc::bulk_wait<0>();
     }
     tc::tc_fence_before();
     __syncthreads();
@@ -537,7 +548,8 @@ int launch_decode(const actcomp_cg_desc *d, const uint16_t *y, int64_t ldy, uint
     if (OP != ACT_OP_DECODE &&
         (st = make_map_3d(&m_y, y, BF, 2, H, T, B, ldy, T * ldy, 64, ROWS, CU_TENSOR_MAP_SWIZZLE_128B)))
         return st;
-    if ((st = make_map_3d(&m_out, out, BF, 2, H, T, B, ldo, T * ldo, 64, ROWS, CU_TENSOR_MAP_SWIZZLE_128B))) return st;
+    // per-warp output boxes: 32 tokens x 32 channels (64-byte rows)
+    if ((st = make_map_3d(&m_out, out, BF, 2, H, T, B, ldo, T * ldo, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))) return st;
     DecParams p{};
     p.T = T;
     p.H = H;
