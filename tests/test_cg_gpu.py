@@ -47,11 +47,11 @@ CASES = [
     (64, 256, 0, 0, 4, 32, False),      # no low rank, no outliers
     (64, 256, 64, 64, 8, 64, False),    # maximum rank and outlier count
     (50, 1024, 48, 3, 4, 128, True),
-    # wide activations: the tensor-core encode splits channels over a cluster of 2, 4, 8 CTAs
+    # wide activations (the tensor-core encode splits channels wider than 8192 over a cluster of CTAs)
     (200, 2048, 32, 16, 4, 64, False),
     (130, 4096, 32, 16, 4, 64, False),
     (96, 5120, 16, 0, 4, 128, True),    # config-3 width
-    (64, 11008, 32, 16, 4, 64, False),  # config-2 SiLU-input width (uneven split, 172 groups over 8 CTAs)
+    (64, 11008, 32, 16, 4, 64, False),  # config-2 SiLU-input width: 86 chunks split unevenly over 4 CTAs
     (72, 4096, 64, 7, 8, 32, False),
 ]
 

@@ -78,7 +78,13 @@ extern "C" int actcomp_cg_encode(const actcomp_cg_desc *d, const uint16_t *x, in
     if (st) return st;
     if ((st = check_rows(x, ldx, d->channels))) return st;
     if (d->rank) ACT_CHECK(d->basis_t && aligned(d->basis_t, 16), ACT_E_ALIGN);
-    if (act_cg_encode_tc_supported(d)) return act_cg_encode_tc(d, x, ldx, as_stream(stream));
+    if (act_cg_encode_tc_supported(d)) {
+        // the tensor-core kernel declines (ACT_E_UNSUPPORTED, before launching)
+        // shapes whose buffers do not fit its shared memory; the CUDA-core
+        // encode computes the same codes
+        st = act_cg_encode_tc(d, x, ldx, as_stream(stream));
+        if (st != ACT_E_UNSUPPORTED) return st;
+    }
     return act_cg_encode_simt(d, x, ldx, as_stream(stream));
 }
 

@@ -58,7 +58,7 @@ struct EncParams {
     int ngs;       // 64-channel groups in the widest slice (outlier table entries)
     int ostage;    // outliers staged in shared memory and flushed per block
     // shared-memory offsets (bytes from the 1024-aligned base)
-    int off_ringB, off_lqt, off_bar, off_cst, off_xch, off_ot, off_sst, off_ost;
+    int off_ringB, off_lqt, off_bar, off_cst, off_xch, off_ot, off_sst, off_ost, off_amx, off_wx, off_slr;
 };
 
 constexpr int NB = 2;      // residual ring: X 128x128 (32 KB) + Vq 128 x r bf16
@@ -67,18 +67,23 @@ constexpr int FL = 4;      // chunks per scale flush
 constexpr int NT = 3;      // residual-term accumulators in TMEM (3 x 128 columns after the projection's 128):
                            // the MMA runs up to NT chunks ahead of the epilogue
 
+constexpr int EW = 16;     // epilogue warps: 4 row quarters x 4 column quarters of a chunk
+
 // RK: rank rounded up to 16, 32 or 64; LB = bytes of one bf16 row of Lq / Vq.
-template <int BITS, bool WHT, int RK, int EW>
+template <int BITS, bool WHT, int RK>
 struct EncLayout {
     static constexpr int LB = 2 * RK;
     static constexpr int SLOT_A = 16 * 1024 + RK * 128;
     static constexpr int SLOT_B = 32 * 1024 + CH * LB;
     static constexpr int LQT = ROWS * LB;
     static constexpr int CROW = CH * BITS / 8;  // code bytes of one token row of a chunk
-    static constexpr int CST = ROWS * CROW;     // one code staging buffer
+    static constexpr int QST = 32 * CROW;       // one row quarter's code staging buffer
+    static constexpr int CST = 4 * 2 * QST;     // all quarters, double-buffered
     static constexpr int THREADS = 128 + 32 * EW;  // 2 producers, 2 MMA issuers, epilogue
     // Shared memory: projection ring, residual ring, low-rank code tile,
-    // barriers, two code staging buffers (TMA-stored per chunk), then the sizes
+    // barriers, code staging (per row quarter, double-buffered, TMA-stored per
+    // chunk), group-absmax exchange, per-row low-rank scales, the rotation
+    // exchange (with WHT), then the sizes
     // that depend on the launch: projection exchange buffers (send + C-1
     // receive slots, 128 x r floats each), the outlier table of the current
     // slice (per 64-channel group: a mask of its outlier channels and the
@@ -94,7 +99,10 @@ struct EncLayout {
         p.off_lqt = p.off_ringB + NB * SLOT_B;
         p.off_bar = p.off_lqt + LQT;
         p.off_cst = p.off_bar + 1024;
-        p.off_xch = p.off_cst + 2 * CST;
+        p.off_amx = p.off_cst + CST;                     // [2][4][128] floats
+        p.off_slr = p.off_amx + 2 * 4 * ROWS * 4;        // [2][128] floats
+        p.off_wx = p.off_slr + 2 * ROWS * 4;             // [4][128][32] floats with WHT
+        p.off_xch = p.off_wx + (WHT ? 4 * ROWS * 32 * 4 : 0);
         p.off_ot = p.off_xch + (C > 1 ? C * ROWS * r * 4 : 0);
         p.off_sst = p.off_ot + ((ngs * 12 + 15) & ~15);
         const int spp = FL * (CH / group) + 4;
@@ -172,11 +180,11 @@ __device__ __forceinline__ uint32_t pack_codes(float2 t0, float2 t1, float2 t2, 
     }
 }
 
-template <int BITS, bool WHT, int RK, int EW>
-__global__ void __launch_bounds__(EncLayout<BITS, WHT, RK, EW>::THREADS, 1)
+template <int BITS, bool WHT, int RK>
+__global__ void __launch_bounds__(EncLayout<BITS, WHT, RK>::THREADS, 1)
     cg_encode_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_vt,
                         const __grid_constant__ CUtensorMap tm_c, EncParams p) {
-    using L = EncLayout<BITS, WHT, RK, EW>;
+    using L = EncLayout<BITS, WHT, RK>;
     constexpr int LB = L::LB;
     constexpr int qmax = (1 << (BITS - 1)) - 1, off = 1 << (BITS - 1);
     extern __shared__ uint8_t smem_raw[];
@@ -226,8 +234,8 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK, EW>::THREADS, 1)
             tc::mbar_init(&tempty[b], EW);
         }
         tc::mbar_init(lfull, 1);
-        tc::mbar_init(lempty, EW);
-        tc::mbar_init(lqready, EW);
+        tc::mbar_init(lempty, 4);   // the 4 warps that read the projection (column quarter 0)
+        tc::mbar_init(lqready, 4);
         tc::mbar_init(pready, 1);
         tc::mbar_init(pdone, C > 1 ? C - 1 : 1);
         tc::mbar_init(lseen, 1);
@@ -349,28 +357,38 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK, EW>::THREADS, 1)
         }
     } else {
         // ------------------------------------------------------------ epilogue
+        // 16 warps: warp w (4..19) reads TMEM lanes 32 (w % 4).. (row quarter q)
+        // and owns channels [32 h, 32 h + 32) of each 128-channel chunk,
+        // h = (w - 4) / 4; one token row per thread.  The 4 warps of a row
+        // quarter (a "q-group", 128 threads, named barrier 4 + q) share the
+        // group absmax of groups wider than 32 channels, the rotation, the
+        // code staging buffer and its TMA store.  Column quarter 0 (4 warps, one
+        // thread per token row) also reads the projection and forms the
+        // low-rank codes.
         const int ew = warp - 4;
         const int etid = threadIdx.x - 128;
         constexpr int ETH = 32 * EW;
         const int q = warp & 3;
-        const int h = (EW == 8) ? (ew >> 2) : 0;
-        constexpr int NC = EW == 8 ? 64 : 128;  // channels of a chunk per thread
-        constexpr int NP = NC / 32;
+        const int h = ew >> 2;
+        const int qid = 4 + q;  // the q-group's named barrier
         constexpr int CROW = L::CROW;
-        uint64_t *omask = reinterpret_cast<uint64_t *>(smem + p.off_ot);
+        uint64_t *omask = reinterpret_cast<uint64_t *>(smem + p.off_ot);  // outlier table
         int32_t *obelow = reinterpret_cast<int32_t *>(omask + p.ngs);
         float *sst = reinterpret_cast<float *>(smem + p.off_sst);
         uint16_t *ost = reinterpret_cast<uint16_t *>(smem + p.off_ost);
+        float *amx = reinterpret_cast<float *>(smem + p.off_amx);
+        float *slr = reinterpret_cast<float *>(smem + p.off_slr);
+        float *wx = reinterpret_cast<float *>(smem + p.off_wx);
         uint8_t *cst = smem + p.off_cst;
         const int ngs_mine = (int)((c_hi - c_lo) / 64);
         int cur_slice = -1;
         const int row = q * 32 + lane;
         const int G = p.group;
-        const int ppg = G >> 5;        // 32-column pieces per group
+        const int ppg = G >> 5;        // 32-column pieces (threads) per group
         const int gpc = CH / G;        // groups per chunk
         const int spp = FL * gpc + 4;  // staged scales per token row (padded)
         const int ngr = (int)(p.H / G);
-        const bool issuer = etid == 0;
+        const bool qleader = (h == 0 && lane == 0);  // issues the q-group's code stores
         int j = 0, nb = 0;
         bool ok = true;
         for (int64_t blk = cluster; blk < p.nblocks && ok; blk += p.nclusters, ++nb) {
@@ -379,113 +397,109 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK, EW>::THREADS, 1)
             const bool rv = t < p.T;
             const int64_t trow = (int64_t)b * p.T + t;
             const int nrows = (int)((p.T - (int64_t)tb * ROWS) < ROWS ? (p.T - (int64_t)tb * ROWS) : ROWS);
-            // ---- partial projection -> shared memory
-            if (!(ok = tc::mbar_wait(lfull, nb & 1, abort))) break;
-            tc::tc_fence_after();
-            float Lr[RK];
-            {
-                uint32_t v[32];
+            if (h == 0) do {  // (a do-while so that a failed wait leaves this section, not the block loop)
+                // ---- partial projection -> registers (column quarter 0 only)
+                if (!(ok = tc::mbar_wait(lfull, nb & 1, abort))) break;
+                tc::tc_fence_after();
+                float Lr[RK];
+                {
+                    uint32_t v[32];
 #pragma unroll
-                for (int jj = 0; jj < (RK + 31) / 32; ++jj) {
-                    tc::tmem_ld32(tm_l + ((uint32_t)(q * 32) << 16) + 32 * jj, v);
-                    tc::tmem_ld_wait();
+                    for (int jj = 0; jj < (RK + 31) / 32; ++jj) {
+                        tc::tmem_ld32(tm_l + ((uint32_t)(q * 32) << 16) + 32 * jj, v);
+                        tc::tmem_ld_wait();
 #pragma unroll
-                    for (int e = 0; e < 32; ++e)
-                        if (32 * jj + e < RK) Lr[32 * jj + e] = __uint_as_float(v[e]);
+                        for (int e = 0; e < 32; ++e)
+                            if (32 * jj + e < RK) Lr[32 * jj + e] = __uint_as_float(v[e]);
+                    }
                 }
-            }
-            tc::tc_fence_before();
-            __syncwarp();
-            if (lane == 0) tc::mbar_arrive(lempty);
-            if (C > 1) {
-                // Exchange: every CTA pushes its 128 x r partial to each peer with one
-                // bulk copy (completing on the peer's pready), then sums all partials
-                // in rank order from local shared memory.  Lane 0 of each warp polls
-                // the cluster-scope barriers; the warp follows it.
-                const int PB = ROWS * r * 4;
-                // our send buffer and the peers' receive slots are free again once
-                // every peer has consumed the previous block
-                if (nb > 0) {
-                    int okw = 1;
-                    if (lane == 0) okw = tc::mbar_wait_cluster(pdone, (nb - 1) & 1, abort);
-                    ok = __shfl_sync(0xffffffffu, okw, 0) != 0;
-                    if (!ok) break;
-                }
-                if (h == 0) {
+                tc::tc_fence_before();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(lempty);
+                if (C > 1) {
+                    // Exchange: every CTA pushes its 128 x r partial to each peer with one
+                    // bulk copy (completing on the peer's pready), then sums all partials
+                    // in rank order from local shared memory.  Lane 0 of each warp polls
+                    // the cluster-scope barriers; the warp follows it.
+                    const int PB = ROWS * r * 4;
+                    if (nb > 0) {  // our buffers are free once every peer consumed the previous block
+                        int okw = 1;
+                        if (lane == 0) okw = tc::mbar_wait_cluster(pdone, (nb - 1) & 1, abort);
+                        ok = __shfl_sync(0xffffffffu, okw, 0) != 0;
+                        if (!ok) break;
+                    }
 #pragma unroll
                     for (int e = 0; e < RK / 4; ++e)
                         if (4 * e < r)
                             *reinterpret_cast<float4 *>(xsend + xch_off(row, e, r)) =
                                 make_float4(Lr[4 * e], Lr[4 * e + 1], Lr[4 * e + 2], Lr[4 * e + 3]);
-                }
-                tc::fence_proxy_async();
-                tc::named_bar(1, ETH);
-                if (issuer) {
-                    tc::mbar_arrive_expect_tx(pready, (uint32_t)((C - 1) * PB));
-                    for (int q2 = 0; q2 < C; ++q2) {
-                        if (q2 == (int)crank) continue;
-                        const int slot = (int)crank < q2 ? (int)crank : (int)crank - 1;  // our slot at q2
-                        tc::bulk_copy_to_peer(tc::map_cluster(xrecv + (slot + 1) * PB, q2), xsend, (uint32_t)PB,
-                                              tc::map_cluster(pready, q2));
-                    }
-                }
-                {
-                    // a suspended try_wait on a barrier that only other CTAs complete
-                    // sleeps out its whole interval: poll
-                    int okw = 1;
-                    if (lane == 0) okw = tc::mbar_wait_cluster(pready, nb & 1, abort);
-                    ok = __shfl_sync(0xffffffffu, okw, 0) != 0;
-                    if (!ok) break;
-                }
-                // L = sum of the partials in rank order (identical in every CTA)
-                for (int pr = 0; pr < C; ++pr) {
-                    const uint8_t *src =
-                        pr == (int)crank ? xsend : xrecv + ((pr < (int)crank ? pr : pr - 1) + 1) * PB;
-#pragma unroll
-                    for (int e = 0; e < RK / 4; ++e) {
-                        if (4 * e < r) {
-                            const float4 v = *reinterpret_cast<const float4 *>(src + xch_off(row, e, r));
-                            Lr[4 * e] = pr ? __fadd_rn(Lr[4 * e], v.x) : v.x;
-                            Lr[4 * e + 1] = pr ? __fadd_rn(Lr[4 * e + 1], v.y) : v.y;
-                            Lr[4 * e + 2] = pr ? __fadd_rn(Lr[4 * e + 2], v.z) : v.z;
-                            Lr[4 * e + 3] = pr ? __fadd_rn(Lr[4 * e + 3], v.w) : v.w;
+                    tc::fence_proxy_async();
+                    tc::named_bar(1, 128);
+                    if (ew == 0 && lane == 0) {
+                        tc::mbar_arrive_expect_tx(pready, (uint32_t)((C - 1) * PB));
+                        for (int q2 = 0; q2 < C; ++q2) {
+                            if (q2 == (int)crank) continue;
+                            const int slot = (int)crank < q2 ? (int)crank : (int)crank - 1;  // our slot at q2
+                            tc::bulk_copy_to_peer(tc::map_cluster(xrecv + (slot + 1) * PB, q2), xsend, (uint32_t)PB,
+                                                  tc::map_cluster(pready, q2));
                         }
                     }
-                }
-                // tell every peer we have consumed its partial (the values are in registers)
-                tc::named_bar(1, ETH);
-                if (ew == 0 && lane < C && lane != (int)crank) tc::mbar_arrive_remote(tc::map_cluster(pdone, lane));
-            }
-            // ---- per-token low-rank codes: Lq = nearest(L * sV * 127 / max|L * sV|), one fma
-            float amax = 0.f;
+                    {
+                        // a suspended try_wait on a barrier that only other CTAs complete
+                        // sleeps out its whole interval: poll
+                        int okw = 1;
+                        if (lane == 0) okw = tc::mbar_wait_cluster(pready, nb & 1, abort);
+                        ok = __shfl_sync(0xffffffffu, okw, 0) != 0;
+                        if (!ok) break;
+                    }
+                    // L = sum of the partials in rank order (identical in every CTA)
+                    for (int pr = 0; pr < C; ++pr) {
+                        const uint8_t *src =
+                            pr == (int)crank ? xsend : xrecv + ((pr < (int)crank ? pr : pr - 1) + 1) * PB;
 #pragma unroll
-            for (int e = 0; e < RK; ++e) {
-                if (e < r) {
-                    Lr[e] = __fmul_rn(Lr[e], __ldg(p.basis_scale + (int64_t)b * r + e));
-                    amax = fmaxf(amax, fabsf(Lr[e]));
+                        for (int e = 0; e < RK / 4; ++e) {
+                            if (4 * e < r) {
+                                const float4 v = *reinterpret_cast<const float4 *>(src + xch_off(row, e, r));
+                                Lr[4 * e] = pr ? __fadd_rn(Lr[4 * e], v.x) : v.x;
+                                Lr[4 * e + 1] = pr ? __fadd_rn(Lr[4 * e + 1], v.y) : v.y;
+                                Lr[4 * e + 2] = pr ? __fadd_rn(Lr[4 * e + 2], v.z) : v.z;
+                                Lr[4 * e + 3] = pr ? __fadd_rn(Lr[4 * e + 3], v.w) : v.w;
+                            }
+                        }
+                    }
+                    // tell every peer we have consumed its partial (the values are in registers)
+                    tc::named_bar(1, 128);
+                    if (ew == 0 && lane < C && lane != (int)crank) tc::mbar_arrive_remote(tc::map_cluster(pdone, lane));
                 }
-            }
-            const float sl = __fdiv_rn(amax, 127.0f);
-            const float rsl = amax > 0.f ? __fdiv_rn(127.0f, amax) : 0.f;
-            constexpr float MAGIC_L = 12582912.0f + 128.0f;
-            uint32_t lw[RK / 4];  // int8 codes, four per word
-            uint32_t lb[RK / 2];  // the same codes as bf16 pairs (exact integers)
+                // ---- per-token low-rank codes: Lq = nearest(L * sV * 127 / max|L * sV|), one fma
+                float amax = 0.f;
 #pragma unroll
-            for (int e = 0; e < RK / 4; ++e) lw[e] = 0;
-#pragma unroll
-            for (int e = 0; e < RK; e += 2) {
-                float f0 = 0.f, f1 = 0.f;
-                if (e < r) {
-                    const float t0 = __fmaf_rn(Lr[e], rsl, MAGIC_L);
-                    const float t1 = __fmaf_rn(Lr[e + 1], rsl, MAGIC_L);
-                    const uint32_t u0 = __float_as_uint(t0) & 0xffu, u1 = __float_as_uint(t1) & 0xffu;  // q + 128
-                    lw[e >> 2] |= ((u0 ^ 0x80u) << ((e & 3) * 8)) | ((u1 ^ 0x80u) << (((e + 1) & 3) * 8));
-                    f0 = __fsub_rn(t0, MAGIC_L);
-                    f1 = __fsub_rn(t1, MAGIC_L);
+                for (int e = 0; e < RK; ++e) {
+                    if (e < r) {
+                        Lr[e] = __fmul_rn(Lr[e], __ldg(p.basis_scale + (int64_t)b * r + e));
+                        amax = fmaxf(amax, fabsf(Lr[e]));
+                    }
                 }
-                lb[e >> 1] = pack_bf16x2(f0, f1);
-            }
-            if (h == 0) {
+                const float sl = __fdiv_rn(amax, 127.0f);
+                const float rsl = amax > 0.f ? __fdiv_rn(127.0f, amax) : 0.f;
+                constexpr float MAGIC_L = 12582912.0f + 128.0f;
+                uint32_t lw[RK / 4];  // int8 codes, four per word
+                uint32_t lb[RK / 2];  // the same codes as bf16 pairs (exact integers)
+#pragma unroll
+                for (int e = 0; e < RK / 4; ++e) lw[e] = 0;
+#pragma unroll
+                for (int e = 0; e < RK; e += 2) {
+                    float f0 = 0.f, f1 = 0.f;
+                    if (e < r) {
+                        const float t0 = __fmaf_rn(Lr[e], rsl, MAGIC_L);
+                        const float t1 = __fmaf_rn(Lr[e + 1], rsl, MAGIC_L);
+                        const uint32_t u0 = __float_as_uint(t0) & 0xffu, u1 = __float_as_uint(t1) & 0xffu;  // q + 128
+                        lw[e >> 2] |= ((u0 ^ 0x80u) << ((e & 3) * 8)) | ((u1 ^ 0x80u) << (((e + 1) & 3) * 8));
+                        f0 = __fsub_rn(t0, MAGIC_L);
+                        f1 = __fsub_rn(t1, MAGIC_L);
+                    }
+                    lb[e >> 1] = pack_bf16x2(f0, f1);
+                }
 #pragma unroll
                 for (int c16 = 0; c16 < LB / 16; ++c16)
                     *reinterpret_cast<uint4 *>(lqt + swz<LB>(row, c16)) =
@@ -497,15 +511,17 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK, EW>::THREADS, 1)
                         if (4 * e < r) dst[e] = lw[e];
                     p.lrs[trow] = sl;
                 }
-            }
-            tc::fence_proxy_async();
-            __syncwarp();
-            if (lane == 0) tc::mbar_arrive(lqready);
-
-            // ---- outlier table of slice b (indices ascending); the first barrier
-            // keeps the old table until every epilogue warp has left the previous slice
+                slr[(nb & 1) * ROWS + row] = sl;
+                tc::fence_proxy_async();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(lqready);
+            } while (0);
+            // ---- the row's low-rank scale for every warp; outlier table of slice b
+            // (indices ascending), rebuilt when the slice changes
+            tc::named_bar(2, ETH);
+            if (!ok) break;
+            const float sl = slr[(nb & 1) * ROWS + row];
             if (p.k && b != cur_slice) {
-                tc::named_bar(2, ETH);
                 for (int gi = etid; gi < ngs_mine; gi += ETH) {
                     const int64_t lo = c_lo + 64 * (int64_t)gi;
                     uint64_t m = 0;
@@ -529,71 +545,56 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK, EW>::THREADS, 1)
                 if (!(ok = tc::mbar_wait(&fullB[s], (j / NB) & 1, abort))) break;
                 if (!(ok = tc::mbar_wait(&tfull[tb2], (j / NT) & 1, abort))) break;
                 tc::tc_fence_after();
-                const int64_t c0 = c_lo + (int64_t)ck * CH + h * 64;  // first channel of my columns
+                const int64_t c0 = c_lo + (int64_t)ck * CH + 32 * h;  // my first channel
                 const uint8_t *xt = ringB + s * L::SLOT_B;
-                float2 w[NC / 2];
+                const uint8_t *box = xt + (h >> 1) * ROWS * 128;    // my X columns: box h / 2, chunks 4 (h & 1) ..
+                float2 w[16];
                 {
-                    // with 64 columns both TMEM reads go out before the first wait
-                    constexpr int IN = NP <= 2 ? NP : 1;
-                    uint32_t I[IN][32];
-                    const uint32_t tbase = tm_p + tb2 * CH + ((uint32_t)(q * 32) << 16) + h * 64;
-                    if constexpr (NP <= 2) {
+                    uint32_t I[32];
+                    tc::tmem_ld32(tm_p + tb2 * CH + ((uint32_t)(q * 32) << 16) + 32 * h, I);
+                    uint4 xv4[4];
 #pragma unroll
-                        for (int jj = 0; jj < NP; ++jj) tc::tmem_ld32(tbase + 32 * jj, I[jj]);
-                        tc::tmem_ld_wait();
-                    }
+                    for (int c16 = 0; c16 < 4; ++c16)
+                        xv4[c16] = *reinterpret_cast<const uint4 *>(box + swz<128>(row, (h & 1) * 4 + c16));
+                    tc::tmem_ld_wait();
 #pragma unroll
-                    for (int jj = 0; jj < NP; ++jj) {
-                        uint32_t (&Ij)[32] = I[NP <= 2 ? jj : 0];
-                        if constexpr (NP > 2) {
-                            tc::tmem_ld32(tbase + 32 * jj, Ij);
-                            tc::tmem_ld_wait();
-                        }
-                        const uint8_t *box = xt + (h + (jj >> 1)) * ROWS * 128;
+                    for (int c16 = 0; c16 < 4; ++c16) {
+                        const uint32_t wd[4] = {xv4[c16].x, xv4[c16].y, xv4[c16].z, xv4[c16].w};
 #pragma unroll
-                        for (int c16 = 0; c16 < 4; ++c16) {
-                            const uint4 v = *reinterpret_cast<const uint4 *>(box + swz<128>(row, (jj & 1) * 4 + c16));
-                            const uint32_t wd[4] = {v.x, v.y, v.z, v.w};
-#pragma unroll
-                            for (int e = 0; e < 4; ++e) {
-                                const float2 xv = make_float2(__uint_as_float(wd[e] << 16),
-                                                              __uint_as_float(wd[e] & 0xffff0000u));
-                                const float2 iv = make_float2(__uint_as_float(Ij[8 * c16 + 2 * e]),
-                                                              __uint_as_float(Ij[8 * c16 + 2 * e + 1]));
-                                w[16 * jj + 4 * c16 + e] = fma2(iv, nsl2, xv);  // x - I * sL, one rounding
-                            }
+                        for (int e = 0; e < 4; ++e) {
+                            const float2 xv = make_float2(__uint_as_float(wd[e] << 16),
+                                                          __uint_as_float(wd[e] & 0xffff0000u));
+                            const float2 iv = make_float2(__uint_as_float(I[8 * c16 + 2 * e]),
+                                                          __uint_as_float(I[8 * c16 + 2 * e + 1]));
+                            w[4 * c16 + e] = fma2(iv, nsl2, xv);  // x - I * sL, one rounding
                         }
                     }
                 }
                 tc::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(&tempty[tb2]);
-                // outlier channels of my columns: verbatim copy, residual zeroed.
-                // Mask and slot base come from the slice's table (warp-uniform).
+                // outlier channels of my 32 (warp-uniform mask): verbatim copy, residual zeroed
                 if (p.k) {
+                    const int gi = (int)((c0 - c_lo) >> 6);
+                    const uint64_t om64 = omask[gi];
+                    const uint32_t om = (uint32_t)(om64 >> (32 * (h & 1)));
+                    if (om) {
+                        const int below = obelow[gi] + ((h & 1) ? __popc((uint32_t)om64) : 0);
 #pragma unroll
-                    for (int g = 0; g < NC / 64; ++g) {
-                        const int gi = (int)((c0 - c_lo) >> 6) + g;
-                        const uint64_t om = omask[gi];
-                        if (om) {
-                            const int below = obelow[gi];
-                            const uint8_t *box = xt + (h + g) * ROWS * 128;
+                        for (int c8 = 0; c8 < 4; ++c8) {
+                            const uint32_t m8 = (om >> (8 * c8)) & 0xffu;
+                            if (!m8) continue;
 #pragma unroll
-                            for (int c8 = 0; c8 < 8; ++c8) {
-                                const uint32_t m8 = (uint32_t)(om >> (8 * c8)) & 0xffu;
-                                if (!m8) continue;
-#pragma unroll
-                                for (int e8 = 0; e8 < 8; ++e8) {
-                                    if ((m8 >> e8) & 1u) {
-                                        const int e = 8 * c8 + e8;
-                                        const int slot = below + __popcll(om & ((1ull << e) - 1ull));
-                                        const uint16_t bits =
-                                            *reinterpret_cast<const uint16_t *>(box + swz<128>(row, c8) + 2 * e8);
-                                        if (p.ostage) ost[row * p.k + slot] = bits;
-                                        else if (rv) p.outl[trow * p.k + slot] = bits;
-                                        if (e & 1) w[g * 32 + e / 2].y = 0.f;
-                                        else w[g * 32 + e / 2].x = 0.f;
-                                    }
+                            for (int e8 = 0; e8 < 8; ++e8) {
+                                if ((m8 >> e8) & 1u) {
+                                    const int e = 8 * c8 + e8;
+                                    const int slot = below + __popc(om & ((1u << e) - 1u));
+                                    const uint16_t bits = *reinterpret_cast<const uint16_t *>(
+                                        box + swz<128>(row, (h & 1) * 4 + c8) + 2 * e8);
+                                    if (p.ostage) ost[row * p.k + slot] = bits;
+                                    else if (rv) p.outl[trow * p.k + slot] = bits;
+                                    if (e & 1) w[e >> 1].y = 0.f;
+                                    else w[e >> 1].x = 0.f;
                                 }
                             }
                         }
@@ -601,100 +602,125 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK, EW>::THREADS, 1)
                 }
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(&emptyB[s]);  // X and basis tile no longer needed
-                if constexpr (WHT) wht128_pairs(*reinterpret_cast<float2(*)[64]>(&w[0]));
-                // absmax of each 32-column piece, combined over the pieces of a group
-                float am[NP];
+                if constexpr (WHT) {
+                    // 128-point rotation over the q-group: stages m = 1..16 inside my 32
+                    // channels, m = 32 and 64 across the 4 quarters through shared memory
+                    float (&v)[32] = *reinterpret_cast<float(*)[32]>(&w[0]);
 #pragma unroll
-                for (int pc = 0; pc < NP; ++pc) {
-                    float a[16];  // balanced tree: four levels instead of a 32-long chain
+                    for (int m = 1; m < 32; m <<= 1) {
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) a[e] = fmaxf(fabsf(w[16 * pc + e].x), fabsf(w[16 * pc + e].y));
+                        for (int e = 0; e < 32; ++e) {
+                            if (!(e & m)) {
+                                const float a = v[e], c = v[e + m];
+                                v[e] = __fadd_rn(a, c);
+                                v[e + m] = __fsub_rn(a, c);
+                            }
+                        }
+                    }
+                    tc::named_bar(qid, 128);  // the previous chunk's exchange has been read
+                    float *mine = wx + (h * ROWS + row) * 32;
+#pragma unroll
+                    for (int c4 = 0; c4 < 8; ++c4)
+                        *reinterpret_cast<float4 *>(mine + ((c4 ^ (row & 7)) << 2)) =
+                            make_float4(v[4 * c4], v[4 * c4 + 1], v[4 * c4 + 2], v[4 * c4 + 3]);
+                    tc::named_bar(qid, 128);
+#pragma unroll
+                    for (int c4 = 0; c4 < 8; ++c4) {
+                        float4 x4[4];
+#pragma unroll
+                        for (int hh = 0; hh < 4; ++hh)
+                            x4[hh] = *reinterpret_cast<const float4 *>(wx + (hh * ROWS + row) * 32 + ((c4 ^ (row & 7)) << 2));
+                        const float *a0 = &x4[0].x, *a1 = &x4[1].x, *a2 = &x4[2].x, *a3 = &x4[3].x;
+#pragma unroll
+                        for (int jj = 0; jj < 4; ++jj) {
+                            const float s01 = __fadd_rn(a0[jj], a1[jj]), d01 = __fsub_rn(a0[jj], a1[jj]);
+                            const float s23 = __fadd_rn(a2[jj], a3[jj]), d23 = __fsub_rn(a2[jj], a3[jj]);
+                            float o;
+                            if (h == 0) o = __fadd_rn(s01, s23);
+                            else if (h == 1) o = __fadd_rn(d01, d23);
+                            else if (h == 2) o = __fsub_rn(s01, s23);
+                            else o = __fsub_rn(d01, d23);
+                            v[4 * c4 + jj] = o;
+                        }
+                    }
+                }
+                // absmax of my 32 (balanced tree), then over the group's threads
+                float am;
+                {
+                    float a[16];
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) a[e] = fmaxf(fabsf(w[e].x), fabsf(w[e].y));
 #pragma unroll
                     for (int st = 8; st > 0; st >>= 1)
 #pragma unroll
                         for (int e = 0; e < st; ++e) a[e] = fmaxf(a[e], a[e + st]);
-                    am[pc] = a[0];
+                    am = a[0];
                 }
-                uint32_t packed[NC * BITS / 32];
-                float scv[NP];
+                float *ax = amx + (j & 1) * 4 * ROWS;
+                if (ppg > 1) ax[h * ROWS + row] = am;
+                // the q-group's staging buffer (j & 1) is free once its store of chunk j - 2 has read it
+                if (qleader) tc::bulk_wait_read<1>();
+                tc::named_bar(qid, 128);
+                float gam = am;
+                if (ppg == 2) gam = fmaxf(am, ax[(h ^ 1) * ROWS + row]);
+                else if (ppg == 4)
+                    gam = fmaxf(fmaxf(ax[row], ax[ROWS + row]), fmaxf(ax[2 * ROWS + row], ax[3 * ROWS + row]));
+                const float sc = __fdiv_rn(gam, (float)qmax);
+                const float rs = gam > 0.f ? __fdiv_rn((float)qmax, gam) : 0.f;
+                const float2 rs2 = make_float2(rs, rs);
                 constexpr float MAGIC = 12582912.0f + (float)off;
                 const float2 magic2 = make_float2(MAGIC, MAGIC);
-                float rs = 0.f;
+                uint8_t *cb = cst + (q * 2 + (j & 1)) * L::QST;
+                if constexpr (BITS == 4) {
+                    uint32_t pk[4];
 #pragma unroll
-                for (int pc = 0; pc < NP; ++pc) {
-                    if (pc % ppg == 0) {  // first piece of a group: its scale and reciprocal
-                        float gam = am[pc];
-                        if (G >= 64) gam = fmaxf(gam, am[pc ^ 1]);
-                        if constexpr (NC == 128) {
-                            if (G >= 128) gam = fmaxf(gam, fmaxf(am[pc ^ 2], am[pc ^ 3]));
-                        }
-                        scv[pc] = __fdiv_rn(gam, (float)qmax);
-                        rs = gam > 0.f ? __fdiv_rn((float)qmax, gam) : 0.f;
-                    }
-                    const float2 rs2 = make_float2(rs, rs);
+                    for (int wd = 0; wd < 4; ++wd)
+                        pk[wd] = pack_codes<4>(fma2(w[4 * wd], rs2, magic2), fma2(w[4 * wd + 1], rs2, magic2),
+                                               fma2(w[4 * wd + 2], rs2, magic2), fma2(w[4 * wd + 3], rs2, magic2));
+                    *reinterpret_cast<uint4 *>(cb + swz<CROW>(lane, h)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                } else {
+                    uint32_t pk[8];
+                    const float2 z = make_float2(0.f, 0.f);
 #pragma unroll
-                    for (int wd = 0; wd < BITS; ++wd) {  // BITS words of codes per 32-column piece
-                        if constexpr (BITS == 4) {
-                            const int pp = 16 * pc + 4 * wd;  // 8 columns = 4 pairs per word
-                            packed[pc * 4 + wd] = pack_codes<4>(
-                                fma2(w[pp], rs2, magic2), fma2(w[pp + 1], rs2, magic2), fma2(w[pp + 2], rs2, magic2),
-                                fma2(w[pp + 3], rs2, magic2));
-                        } else {
-                            const int pp = 16 * pc + 2 * wd;  // 4 columns = 2 pairs per word
-                            const float2 z = make_float2(0.f, 0.f);
-                            packed[pc * 8 + wd] =
-                                pack_codes<8>(fma2(w[pp], rs2, magic2), fma2(w[pp + 1], rs2, magic2), z, z);
-                        }
-                    }
+                    for (int wd = 0; wd < 8; ++wd)
+                        pk[wd] = pack_codes<8>(fma2(w[2 * wd], rs2, magic2), fma2(w[2 * wd + 1], rs2, magic2), z, z);
+                    *reinterpret_cast<uint4 *>(cb + swz<CROW>(lane, 2 * h)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                    *reinterpret_cast<uint4 *>(cb + swz<CROW>(lane, 2 * h + 1)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
                 }
-                // ---- staging: codes (TMA-stored per chunk) and scales (flushed every FL chunks).
-                // Staging buffer j & 1 was last read by the store of chunk j - 2.
-                if (issuer) tc::bulk_wait_read<1>();
-                tc::named_bar(3, ETH);
-                {
-                    uint8_t *cb = cst + (j & 1) * L::CST;
-#pragma unroll
-                    for (int e = 0; e < NC * BITS / 128; ++e) {
-                        const int c16 = h * (NC * BITS / 128) + e;  // 16-byte chunk of the row
-                        *reinterpret_cast<uint4 *>(cb + swz<CROW>(row, c16)) =
-                            make_uint4(packed[4 * e], packed[4 * e + 1], packed[4 * e + 2], packed[4 * e + 3]);
-                    }
-                    float *srow = sst + row * spp + (ck % FL) * gpc;
-#pragma unroll
-                    for (int pc = 0; pc < NP; ++pc)
-                        if (pc % ppg == 0) srow[(h * 64 + 32 * pc) / G] = scv[pc];
-                }
+                if ((h % ppg) == 0) sst[row * spp + (ck % FL) * gpc + (32 * h) / G] = sc;
                 tc::fence_proxy_async();
-                tc::named_bar(3, ETH);
-                if (issuer) {
-                    tc::tma_store_3d(&tm_c, cst + (j & 1) * L::CST, (int)((c_lo + (int64_t)ck * CH) * BITS / 8),
-                                     tb * ROWS, b);
+                tc::named_bar(qid, 128);
+                if (qleader) {
+                    tc::tma_store_3d(&tm_c, cb, (int)((c_lo + (int64_t)ck * CH) * BITS / 8), tb * ROWS + 32 * q, b);
                     tc::bulk_commit();
                 }
                 if ((ck % FL) == FL - 1 || ck == nk2 - 1) {
-                    // the staged scales of chunks ck - ck % FL .. ck: consecutive threads
-                    // take consecutive scales of a token row
+                    // the q-group's staged scales of chunks ck - ck % FL .. ck: consecutive
+                    // threads take consecutive scales of a token row
                     const int n = (ck % FL + 1) * gpc;
                     const int64_t g0 = (c_lo + (int64_t)(ck - ck % FL) * CH) / G;
-                    for (int i = etid; i < nrows * n; i += ETH) {
+                    const int qrows = nrows - 32 * q < 32 ? (nrows - 32 * q > 0 ? nrows - 32 * q : 0) : 32;
+                    for (int i = h * 32 + lane; i < qrows * n; i += 128) {
                         const int rr = i / n, e = i - rr * n;
-                        p.scales[((int64_t)b * p.T + (int64_t)tb * ROWS + rr) * ngr + g0 + e] = sst[rr * spp + e];
+                        p.scales[((int64_t)b * p.T + (int64_t)tb * ROWS + 32 * q + rr) * ngr + g0 + e] =
+                            sst[(32 * q + rr) * spp + e];
                     }
                 }
             }
             if (ok && p.k && p.ostage) {
                 // the block's outliers of this slice: slots [s_lo, s_lo + s_n) of each row
+                tc::named_bar(3, ETH);
                 const int s_lo = obelow[0];
                 const int s_n = obelow[ngs_mine - 1] + __popcll(omask[ngs_mine - 1]) - s_lo;
                 if (s_n > 0)
                     for (int i = etid; i < nrows * s_n; i += ETH) {
-                        const int rr = i / s_n, sl = s_lo + (i - rr * s_n);
-                        p.outl[((int64_t)b * p.T + (int64_t)tb * ROWS + rr) * p.k + sl] = ost[rr * p.k + sl];
+                        const int rr = i / s_n, sl2 = s_lo + (i - rr * s_n);
+                        p.outl[((int64_t)b * p.T + (int64_t)tb * ROWS + rr) * p.k + sl2] = ost[rr * p.k + sl2];
                     }
                 tc::named_bar(3, ETH);  // read out before the next block stages its outliers
             }
         }
-        if (issuer) tc::bulk_wait<0>();  // code stores complete before the CTA exits
+        if (qleader) tc::bulk_wait<0>();  // code stores complete before the CTA exits
         // do not exit while a peer may still read our partial buffer
         if (C > 1 && ok && nb > 0) {
             if (lane == 0) tc::mbar_wait_cluster(pdone, (nb - 1) & 1, abort);
@@ -711,9 +737,9 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK, EW>::THREADS, 1)
     if (C > 1) tc::cluster_sync();
 }
 
-template <int BITS, bool WHT, int RK, int EW>
+template <int BITS, bool WHT, int RK>
 int launch_encode(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cudaStream_t stream) {
-    using L = EncLayout<BITS, WHT, RK, EW>;
+    using L = EncLayout<BITS, WHT, RK>;
     const int64_t T = d->tokens, H = d->channels, B = d->batch;
     const int r = d->rank;
     const int64_t rowb = H * BITS / 8;
@@ -725,7 +751,8 @@ int launch_encode(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cuda
     if ((st = make_map_3d(&m_vt, d->basis_t, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, H, r, B, H, (int64_t)r * H, 64, r,
                           CU_TENSOR_MAP_SWIZZLE_128B)))
         return st;
-    if ((st = make_map_3d(&m_c, d->codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rowb, T, B, rowb, T * rowb, L::CROW, ROWS,
+    // codes leave per row quarter: boxes of 32 token rows x one chunk's code bytes
+    if ((st = make_map_3d(&m_c, d->codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rowb, T, B, rowb, T * rowb, L::CROW, 32,
                           tma_swz<L::CROW>())))
         return st;
     EncParams p{};
@@ -753,13 +780,20 @@ int launch_encode(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cuda
         EncParams t = p;
         return L::plan(t, 2, c, r, ngs_of(c), d->group, k, 0) <= SMEM_MAX;
     };
-    // smallest cluster whose per-CTA slice keeps the second sweep's L2 window
-    // small, within 64 KB of exchange buffers (C * 128 * r * 4 bytes)
+    // Cluster size: splitting a block's channels over C CTAs shortens each
+    // CTA's sweep but costs a projection exchange per block (measured on B200
+    // at 16384 x 4096: C = 1 115 us, 2 121 us, 4 190 us), so stay at one CTA
+    // per block up to 8192 channels (2 MB per 128-token block) and split wider
+    // activations in slices of at most 4096 channels, within 64 KB of exchange
+    // buffers (C * 128 * r * 4 bytes) and the shared memory.
     int C = 1;
-    while (C < 8 && (H / C > 1536) && p.nunits / (C * 2) >= 1 && (2 * C) * ROWS * r * 4 <= 64 * 1024 && fits(2 * C))
+    while (C < 8 && H / C > 8192 / (C > 1 ? 2 : 1) && p.nunits / (C * 2) >= 1 && (2 * C) * ROWS * r * 4 <= 64 * 1024 &&
+           fits(2 * C))
         C *= 2;
     if (C > p.nunits) C = p.nunits;
-    int na = 4, ostage = k > 0;
+    // the deepest projection ring that fits (phase 1 streams X from HBM: the
+    // more 16 KB steps in flight, the closer to the copy bandwidth)
+    int na = MAXNA, ostage = k > 0;
     while (L::plan(p, na, C, r, ngs_of(C), d->group, k, ostage) > SMEM_MAX) {
         if (na > 3) --na;
         else if (ostage) ostage = 0;
@@ -771,7 +805,7 @@ int launch_encode(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cuda
     p.nblocks = (int64_t)p.ntb * B;
     int maxc = num_sms() / C;
     p.nclusters = (int)(p.nblocks < maxc ? p.nblocks : maxc);
-    auto kern = cg_encode_tc_kernel<BITS, WHT, RK, EW>;
+    auto kern = cg_encode_tc_kernel<BITS, WHT, RK>;
     ACT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     cudaLaunchConfig_t cfg{};
     cfg.gridDim = dim3((unsigned)(p.nclusters * C), 1, 1);
@@ -804,21 +838,18 @@ bool act_cg_encode_tc_supported(const actcomp_cg_desc *d) {
 int act_cg_encode_tc(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cudaStream_t s) {
     using namespace act::cgenc;
     if (d->tokens == 0) return ACT_OK;
-    const bool wide = d->wht || d->group == 128;  // a group or rotation block spans 128 channels
-    const int rk = d->rank <= 16 ? 16 : (d->rank <= 32 ? 32 : 64);
-#define ACT_ENC_RK(B, W, E)                                            \
-    do {                                                               \
-        if (rk == 16) return launch_encode<B, W, 16, E>(d, x, ldx, s); \
-        if (rk == 32) return launch_encode<B, W, 32, E>(d, x, ldx, s); \
-        return launch_encode<B, W, 64, E>(d, x, ldx, s);               \
+#define ACT_ENC_RK(B, W)                                            \
+    do {                                                            \
+        if (rk == 16) return launch_encode<B, W, 16>(d, x, ldx, s); \
+        if (rk == 32) return launch_encode<B, W, 32>(d, x, ldx, s); \
+        return launch_encode<B, W, 64>(d, x, ldx, s);               \
     } while (0)
+    const int rk = d->rank <= 16 ? 16 : (d->rank <= 32 ? 32 : 64);
     if (d->bits == 4) {
-        if (d->wht) ACT_ENC_RK(4, true, 4);
-        if (wide) ACT_ENC_RK(4, false, 4);
-        ACT_ENC_RK(4, false, 8);
+        if (d->wht) ACT_ENC_RK(4, true);
+        ACT_ENC_RK(4, false);
     }
-    if (d->wht) ACT_ENC_RK(8, true, 4);
-    if (wide) ACT_ENC_RK(8, false, 4);
-    ACT_ENC_RK(8, false, 8);
+    if (d->wht) ACT_ENC_RK(8, true);
+    ACT_ENC_RK(8, false);
 #undef ACT_ENC_RK
 }
