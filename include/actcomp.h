@@ -137,9 +137,13 @@ int actcomp_cg_consume(const actcomp_cg_desc *d, int32_t op, const uint16_t *y, 
 /* Softmax backward with the saved probabilities read from compressed form:
  * dS = (dP - rowsum(dP * P^)) * P^ per row (softmax_backward.py:6,45).  Each
  * slice is one (batch, head) S x S probability matrix (T == H == S); causal != 0
- * forces P^[i][j] = 0 for j > i.  dp / ds: batch x S x S bf16, row stride ld. */
+ * forces P^[i][j] = 0 for j > i.  dp / ds: batch x S x S bf16, row stride ld.
+ * With a workspace of actcomp_cg_softmax_workspace() bytes (per-row partial
+ * dot products and row sums) P^ is formed by the tensor-core decode in two
+ * passes; with workspace == NULL a CUDA-core kernel reconstructs P^ itself. */
+size_t actcomp_cg_softmax_workspace(const actcomp_cg_desc *d);
 int actcomp_cg_softmax_bwd(const actcomp_cg_desc *d, const uint16_t *dp, uint16_t *ds, int64_t ld, int32_t causal,
-                           void *stream);
+                           void *workspace, size_t workspace_bytes, void *stream);
 
 /* Weight gradient dW = xhat^T * dy with xhat reconstructed inside the GEMM
  * (extraction_fuse_matmul.py:224 triton_matmul_decompress, consumer math of

@@ -127,12 +127,23 @@ def test_softmax_backward_on_compressed_probabilities(O, causal):
     basis = actcomp.Basis.from_vectors(torch.from_numpy(np.stack(Vs)).cuda())
     c = actcomp.encode(p3.cuda(), basis, None, bits=4, group=64)
     dp = (torch.randn(p3.shape, generator=torch.Generator().manual_seed(6)) * 0.02).to(torch.bfloat16)
-    ds = bits(actcomp.softmax_backward(c, dp.cuda(), causal=causal))
+    ds = bits(actcomp.softmax_backward(c, dp.cuda(), causal=causal))  # tensor-core passes
     ph = bits(actcomp.decode(c)).reshape(-1, S, S)
     if causal:
         ph = np.where(np.tril(np.ones((S, S), bool)), ph, np.uint16(0))
     ref = O.softmax_bwd(ph, bits(dp))
     assert O.rel_fro(ds, ref) < 1e-3
+    # the CUDA-core kernel (no workspace) computes the same
+    import ctypes
+
+    from actcomp import _lib
+
+    dpg = dp.cuda().contiguous()
+    out = torch.empty_like(dpg)
+    d = c.desc()
+    assert _lib.load().actcomp_cg_softmax_bwd(ctypes.byref(d), dpg.data_ptr(), out.data_ptr(), S, int(causal), None,
+                                                0, torch.cuda.current_stream().cuda_stream) == 0
+    assert O.rel_fro(bits(out), ref) < 1e-3
 
 
 @pytest.mark.parametrize("T,H,N", [(256, 256, 384), (512, 384, 200)])

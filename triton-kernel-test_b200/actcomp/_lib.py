@@ -88,7 +88,9 @@ SIGNATURES = {
     "actcomp_cg_encode": (ctypes.c_int, [ctypes.POINTER(CgDesc), c_vp, c_i64, c_vp]),
     "actcomp_cg_decode": (ctypes.c_int, [ctypes.POINTER(CgDesc), c_vp, c_i64, c_vp]),
     "actcomp_cg_consume": (ctypes.c_int, [ctypes.POINTER(CgDesc), c_i32, c_vp, c_i64, c_vp, c_i64, c_vp]),
-    "actcomp_cg_softmax_bwd": (ctypes.c_int, [ctypes.POINTER(CgDesc), c_vp, c_vp, c_i64, c_i32, c_vp]),
+    "actcomp_cg_softmax_workspace": (ctypes.c_size_t, [ctypes.POINTER(CgDesc)]),
+    "actcomp_cg_softmax_bwd": (ctypes.c_int, [ctypes.POINTER(CgDesc), c_vp, c_vp, c_i64, c_i32, c_vp,
+                                              ctypes.c_size_t, c_vp]),
     "actcomp_cg_dw_workspace": (ctypes.c_size_t, [ctypes.POINTER(CgDesc), c_i64]),
     "actcomp_cg_dw": (ctypes.c_int, [ctypes.POINTER(CgDesc), c_vp, c_i64, c_i64, c_vp, c_i32, c_i64, c_vp,
                                      ctypes.c_size_t, c_vp]),

@@ -249,7 +249,8 @@ def gelu_backward(c: Compressed, dy: torch.Tensor) -> torch.Tensor:
     return _consume(c, _lib.ACT_OP_GELU_BWD, dy)
 
 
-def softmax_backward(c: Compressed, dp: torch.Tensor, causal: bool = False) -> torch.Tensor:
+def softmax_backward(c: Compressed, dp: torch.Tensor, causal: bool = False,
+                     workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
     """(dP - rowsum(dP * P)) * P with P read from compressed form
     (softmax_backward.py:6).  c holds one S x S slice per (batch, head);
     dp is (..., S, S) with the same number of slices."""
@@ -260,7 +261,11 @@ def softmax_backward(c: Compressed, dp: torch.Tensor, causal: bool = False) -> t
         raise ValueError("dP does not match the compressed probabilities")
     ds = torch.empty_like(dp3)
     d = c.desc()
-    call("actcomp_cg_softmax_bwd", ctypes.byref(d), dp3.data_ptr(), ds.data_ptr(), S, int(causal), _stream(dp3))
+    if workspace is None:  # partial dot products and row sums of the two tensor-core passes
+        workspace = torch.empty((_lib.load().actcomp_cg_softmax_workspace(ctypes.byref(d)),), dtype=torch.uint8,
+                                device=dp3.device)
+    call("actcomp_cg_softmax_bwd", ctypes.byref(d), dp3.data_ptr(), ds.data_ptr(), S, int(causal),
+         workspace.data_ptr(), workspace.numel(), _stream(dp3))
     return ds.reshape(dp.shape)
 
 

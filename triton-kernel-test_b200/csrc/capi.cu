@@ -32,6 +32,9 @@ bool act_cg_encode_tc_supported(const actcomp_cg_desc *d);
 int act_cg_encode_tc(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cudaStream_t s);
 int act_cg_softmax_simt(const actcomp_cg_desc *d, const uint16_t *dp, uint16_t *ds, int64_t ld, int causal,
                         cudaStream_t s);
+size_t act_cg_softmax_tc_workspace(const actcomp_cg_desc *d);
+int act_cg_softmax_tc(const actcomp_cg_desc *d, const uint16_t *dp, uint16_t *ds, int64_t ld, int causal,
+                      void *workspace, cudaStream_t s);
 
 using namespace act;
 
@@ -105,13 +108,21 @@ extern "C" int actcomp_cg_consume(const actcomp_cg_desc *d, int32_t op, const ui
     return act_cg_consume_tc(d, op, y, ldy, out, ldo, as_stream(stream));
 }
 
+extern "C" size_t actcomp_cg_softmax_workspace(const actcomp_cg_desc *d) {
+    if (!d || d->tokens <= 0 || d->channels <= 0 || d->batch <= 0) return 0;
+    return act_cg_softmax_tc_workspace(d);
+}
+
 extern "C" int actcomp_cg_softmax_bwd(const actcomp_cg_desc *d, const uint16_t *dp, uint16_t *ds, int64_t ld,
-                                      int32_t causal, void *stream) {
+                                      int32_t causal, void *workspace, size_t workspace_bytes, void *stream) {
     int st = validate_desc(d);
     if (st) return st;
     ACT_CHECK(d->tokens == d->channels, ACT_E_INVALID);
     if ((st = check_rows(dp, ld, d->channels)) || (st = check_rows(ds, ld, d->channels))) return st;
-    return act_cg_softmax_simt(d, dp, ds, ld, causal != 0, as_stream(stream));
+    if (!workspace) return act_cg_softmax_simt(d, dp, ds, ld, causal != 0, as_stream(stream));
+    ACT_CHECK(workspace_bytes >= act_cg_softmax_tc_workspace(d), ACT_E_WORKSPACE);
+    ACT_CHECK(aligned(workspace, 16), ACT_E_ALIGN);
+    return act_cg_softmax_tc(d, dp, ds, ld, causal != 0, workspace, as_stream(stream));
 }
 
 extern "C" size_t actcomp_cg_dw_workspace(const actcomp_cg_desc *d, int64_t N) {

@@ -27,6 +27,11 @@ constexpr int CH = 128;    // channels per tile (MMA N)
 constexpr int ROWS = 128;  // tokens per tile (MMA M)
 constexpr int NT = 4;      // TMEM accumulators (4 x 128 columns): the MMA runs up to NT tiles ahead
 constexpr int WST = 32 * 64;  // one warp's output staging buffer: 32 rows x 32 bf16
+// internal consumer ops of the softmax backward (outside the public op enum)
+constexpr int OP_SMAX_DOT = 16;  // partial[row][tile][quarter] = sum over my 32 columns of P^ * dP
+constexpr int OP_SMAX_BWD = 17;  // dS = (dP - rowsum) * P^
+template <int OP>
+constexpr bool is_smax() { return OP == OP_SMAX_DOT || OP == OP_SMAX_BWD; }
 
 struct DecParams {
     int64_t T, H;
@@ -41,6 +46,11 @@ struct DecParams {
     int off_ot;   // shared-memory offset of the outlier table
     int tq, trem;              // tiles per CTA: tq, and one more for the first trem CTAs
     int off_ost, ostb;         // outlier staging: 2 slots of ostb bytes (128 rows x k bf16) at off_ost
+    // softmax backward passes: per (row, tile, column quarter) partial dot
+    // products of dP and P^, their per-row sums, causal mask of P^
+    float *partials;
+    const float *rowsum;
+    int causal;
     const int8_t *vqs;         // basis_qs tile operand (layout in include/actcomp.h), or null
 };
 
@@ -269,12 +279,13 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
         // ahead into a register queue so the global-load latency (~1-2 us under
         // load) hides behind PD tiles of work
         constexpr int PD = 4;
-        float qsc[PD], qsl[PD];
+        float qsc[PD], qsl[PD], qrs[PD];
         TileWalk tw(t_lo, p.ncc, p.ntb), nw = tw;  // this tile, the one PD ahead
         const int gshift = 31 - __clz(p.group);
-        auto load_scalars = [&](int64_t tile, const TileWalk &at, float &vsc, float &vsl) {
+        auto load_scalars = [&](int64_t tile, const TileWalk &at, float &vsc, float &vsl, float &vrs) {
             vsc = 0.f;
             vsl = 0.f;
+            vrs = 0.f;
             if (tile >= t_hi) return;
             const int64_t t = (int64_t)at.tb * ROWS + r;
             if (t >= p.T) return;
@@ -282,10 +293,11 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
             const int64_t c = (int64_t)at.cc * CH + 32 * h;
             if (c < p.H) vsc = __ldg(p.scales + trow * ngr + (c >> gshift));
             if (RB) vsl = __ldg(p.lr_scale + trow);
+            if constexpr (OP == OP_SMAX_BWD) vrs = __ldg(p.rowsum + trow);
         };
 #pragma unroll
         for (int d = 0; d < PD; ++d) {
-            load_scalars(t_lo + d, nw, qsc[d], qsl[d]);
+            load_scalars(t_lo + d, nw, qsc[d], qsl[d], qrs[d]);
             nw.next();
         }
 
@@ -295,13 +307,14 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
             const int s = i % L::S, b = i % NT, ob = i & 1;
             const uint32_t ph = (i / L::S) & 1, bph = (i / NT) & 1;
             const int cc = tw.cc, tb = tw.tb, sl_b = tw.b;
-            const float sc = qsc[0], sl = qsl[0];
+            const float sc = qsc[0], sl = qsl[0], rsum = qrs[0];
 #pragma unroll
             for (int d = 0; d + 1 < PD; ++d) {
                 qsc[d] = qsc[d + 1];
                 qsl[d] = qsl[d + 1];
+                qrs[d] = qrs[d + 1];
             }
-            load_scalars(tile + PD, nw, qsc[PD - 1], qsl[PD - 1]);
+            load_scalars(tile + PD, nw, qsc[PD - 1], qsl[PD - 1], qrs[PD - 1]);
             nw.next();
 
             // outlier table of the slice: per 32-channel group a mask and the
@@ -472,7 +485,19 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
                     }
                 }
             }
+            if constexpr (is_smax<OP>()) {
+                // causal probabilities: P^[t][c] = 0 above the diagonal (c > t)
+                if (p.causal) {
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) {
+                        const int64_t col = c_first + 2 * e;
+                        if (col > t) w[e].x = 0.f;
+                        if (col + 1 > t) w[e].y = 0.f;
+                    }
+                }
+            }
             // second operand and consumer op
+            float dot = 0.f;  // OP_SMAX_DOT: P^ . dP over my 32 columns, in column order
             if constexpr (OP != ACT_OP_DECODE) {
                 const uint8_t *box = smem + s * L::STAGE + L::VQ + L::CODES + (h >> 1) * ROWS * 128;
 #pragma unroll
@@ -482,7 +507,15 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
 #pragma unroll
                     for (int e = 0; e < 4; ++e) {
                         float2 &x2 = w[4 * c16 + e];
-                        x2 = make_float2(apply_op<OP>(x2.x, lo_bf(wd[e])), apply_op<OP>(x2.y, hi_bf(wd[e])));
+                        if constexpr (OP == OP_SMAX_DOT) {
+                            dot = __fmaf_rn(x2.x, lo_bf(wd[e]), dot);
+                            dot = __fmaf_rn(x2.y, hi_bf(wd[e]), dot);
+                        } else if constexpr (OP == OP_SMAX_BWD) {
+                            x2 = make_float2(__fmul_rn(__fsub_rn(lo_bf(wd[e]), rsum), x2.x),
+                                             __fmul_rn(__fsub_rn(hi_bf(wd[e]), rsum), x2.y));
+                        } else {
+                            x2 = make_float2(apply_op<OP>(x2.x, lo_bf(wd[e])), apply_op<OP>(x2.y, hi_bf(wd[e])));
+                        }
                     }
                 }
             }
@@ -492,6 +525,10 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
                 tc::mbar_arrive(&empty[s]);
                 // last tile of this token block in my range: its outlier slot is free
                 if (p.k && (tw.cc == p.ncc - 1 || tile == t_hi - 1)) tc::mbar_arrive(&lqempty[(elq - 1) & 1]);
+            }
+            if constexpr (OP == OP_SMAX_DOT) {  // the partial goes out, no tile
+                if (rv) p.partials[trow * (4 * p.ncc) + 4 * cc + h] = dot;
+                continue;
             }
 
             // each warp stores its own 32 x 32 sub-tile: staging buffer ob of the
@@ -526,9 +563,16 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
     }
 }
 
+// softmax passes: where the partial dot products go / the row sums come from
+struct SmaxArgs {
+    float *partials = nullptr;
+    const float *rowsum = nullptr;
+    int causal = 0;
+};
+
 template <int BITS, int OP, bool WHT, int RB>
 int launch_decode(const actcomp_cg_desc *d, const uint16_t *y, int64_t ldy, uint16_t *out, int64_t ldo,
-                  cudaStream_t stream) {
+                  cudaStream_t stream, const SmaxArgs &sx = SmaxArgs()) {
     using L = DecLayout<BITS, OP, WHT, RB>;
     const int64_t T = d->tokens, H = d->channels, B = d->batch;
     const int r = d->rank;
@@ -567,6 +611,9 @@ int launch_decode(const actcomp_cg_desc *d, const uint16_t *y, int64_t ldy, uint
     p.n32 = (int)((H + 31) / 32);
     p.off_ot = L::OT_OFF;
     p.vqs = d->basis_qs;
+    p.partials = sx.partials;
+    p.rowsum = sx.rowsum;
+    p.causal = sx.causal;
     p.off_ost = L::ost_off(p.n32);
     p.ostb = (ROWS * p.k * 2 + 15) & ~15;
     const int smem = L::total(p.n32, p.k);
@@ -582,16 +629,26 @@ int launch_decode(const actcomp_cg_desc *d, const uint16_t *y, int64_t ldy, uint
 
 template <int BITS, int OP>
 int dispatch_rb(const actcomp_cg_desc *d, const uint16_t *y, int64_t ldy, uint16_t *out, int64_t ldo,
-                cudaStream_t s) {
+                cudaStream_t s, const SmaxArgs &sx = SmaxArgs()) {
     const int rb = d->rank == 0 ? 0 : (d->rank <= 32 ? 32 : 64);
     if (d->wht) {
-        if (rb == 0) return launch_decode<BITS, OP, true, 0>(d, y, ldy, out, ldo, s);
-        if (rb == 32) return launch_decode<BITS, OP, true, 32>(d, y, ldy, out, ldo, s);
-        return launch_decode<BITS, OP, true, 64>(d, y, ldy, out, ldo, s);
+        if (rb == 0) return launch_decode<BITS, OP, true, 0>(d, y, ldy, out, ldo, s, sx);
+        if (rb == 32) return launch_decode<BITS, OP, true, 32>(d, y, ldy, out, ldo, s, sx);
+        return launch_decode<BITS, OP, true, 64>(d, y, ldy, out, ldo, s, sx);
     }
-    if (rb == 0) return launch_decode<BITS, OP, false, 0>(d, y, ldy, out, ldo, s);
-    if (rb == 32) return launch_decode<BITS, OP, false, 32>(d, y, ldy, out, ldo, s);
-    return launch_decode<BITS, OP, false, 64>(d, y, ldy, out, ldo, s);
+    if (rb == 0) return launch_decode<BITS, OP, false, 0>(d, y, ldy, out, ldo, s, sx);
+    if (rb == 32) return launch_decode<BITS, OP, false, 32>(d, y, ldy, out, ldo, s, sx);
+    return launch_decode<BITS, OP, false, 64>(d, y, ldy, out, ldo, s, sx);
+}
+
+// row sums of the softmax partials, in a fixed order (deterministic)
+__global__ void smax_rowsum_kernel(const float *partials, int64_t rows, int per_row, float *rowsum) {
+    const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
+    if (i >= rows) return;
+    const float *pp = partials + i * per_row;
+    float acc = 0.f;
+    for (int j = 0; j < per_row; ++j) acc = __fadd_rn(acc, pp[j]);
+    rowsum[i] = acc;
 }
 
 }  // namespace cgtc
@@ -617,4 +674,32 @@ int act_cg_consume_tc(const actcomp_cg_desc *d, int op, const uint16_t *y, int64
         case ACT_OP_SILU_BWD: return dispatch_rb<8, ACT_OP_SILU_BWD>(d, y, ldy, out, ldo, s);
         default: return dispatch_rb<8, ACT_OP_GELU_BWD>(d, y, ldy, out, ldo, s);
     }
+}
+
+// Softmax backward over compressed probabilities on the tensor-core decode:
+// pass 1 forms P^ tile by tile and writes the partial dot products of each
+// 32-column quarter with dP, a small kernel sums them per row in a fixed
+// order, pass 2 forms P^ again and writes dS = (dP - rowsum) * P^.
+size_t act_cg_softmax_tc_workspace(const actcomp_cg_desc *d) {
+    const int64_t rows = d->batch * d->tokens, ncc = (d->channels + 127) / 128;
+    return (size_t)(rows * (4 * ncc + 1) * 4);
+}
+
+int act_cg_softmax_tc(const actcomp_cg_desc *d, const uint16_t *dp, uint16_t *ds, int64_t ld, int causal,
+                      void *workspace, cudaStream_t s) {
+    using namespace act::cgtc;
+    if (d->tokens == 0) return ACT_OK;
+    const int64_t rows = d->batch * d->tokens, ncc = (d->channels + 127) / 128;
+    SmaxArgs sx;
+    sx.partials = static_cast<float *>(workspace);
+    float *rowsum = sx.partials + rows * 4 * ncc;
+    sx.rowsum = rowsum;
+    sx.causal = causal;
+    int st = d->bits == 4 ? dispatch_rb<4, OP_SMAX_DOT>(d, dp, ld, ds, ld, s, sx)
+                          : dispatch_rb<8, OP_SMAX_DOT>(d, dp, ld, ds, ld, s, sx);
+    if (st) return st;
+    smax_rowsum_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, s>>>(sx.partials, rows, (int)(4 * ncc), rowsum);
+    if ((st = act::launch_status())) return st;
+    return d->bits == 4 ? dispatch_rb<4, OP_SMAX_BWD>(d, dp, ld, ds, ld, s, sx)
+                        : dispatch_rb<8, OP_SMAX_BWD>(d, dp, ld, ds, ld, s, sx);
 }
