@@ -213,6 +213,8 @@ def cpu_baseline(T_sample, H, bits, group, rank, k, reps_seconds=10.0, max_reps=
     encode + decode of a T_sample-token slice of the config-2 activation."""
     import numpy as np
 
+    # all host cores (torchrun sets OMP_NUM_THREADS=1; the oracle's OpenMP reads it when it loads)
+    os.environ["OMP_NUM_THREADS"] = str(os.cpu_count())
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import oracle as O
     import torch
@@ -249,6 +251,8 @@ def run_reference(args):
         return
     T_sample = 4096  # a quarter of the config-2 activation per step keeps K + W steps within a few minutes
     H, bits, group, r, k = 4096, 4, 64, 32, 16
+    # all host cores (torchrun sets OMP_NUM_THREADS=1; the oracle's OpenMP reads it when it loads)
+    os.environ["OMP_NUM_THREADS"] = str(os.cpu_count())
     sys.path.insert(0, os.path.join(ROOT, "oracle"))
     import numpy as np
     import oracle as O
@@ -473,7 +477,7 @@ def run_gpu(args):
             "error": {"rel_fro": (st[0] / st[1]) ** 0.5 if st[1] else None, "max_abs": st[2],
                       "changed_values": st[3]},
         }
-        if not args.no_cpu_baseline:
+        if not args.no_cpu_baseline and world == 1:  # the CPU baseline is an N=1 figure
             line["cpu_baseline"] = cpu_baseline(T, H, bits, group, r, k)
         print(json.dumps(line), flush=True)
     if world > 1:
