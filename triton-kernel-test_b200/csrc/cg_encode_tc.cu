@@ -318,7 +318,9 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK>::THREADS, 1)
                     if (!(ok = tc::mbar_wait(&emptyB[s], ((i / NB) & 1) ^ 1, abort))) break;
                     uint8_t *st = ringB + s * L::SLOT_B;
                     tc::mbar_arrive_expect_tx(&fullB[s], 2 * ROWS * 128 + CH * LB);
-                    const int x = (int)(c_lo + ck * CH);
+                    // the residual sweep runs backwards over the slice: it starts on the
+                    // X columns the projection sweep streamed last, still in L2
+                    const int x = (int)(c_lo + (nk2 - 1 - ck) * CH);
                     tc::tma_load_3d(st, &tm_x, &fullB[s], x, tb * ROWS, b);
                     tc::tma_load_3d(st + ROWS * 128, &tm_x, &fullB[s], x + 64, tb * ROWS, b);
                     // the chunk's basis rows: one contiguous tile of the prepared operand
@@ -545,7 +547,8 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK>::THREADS, 1)
                 if (!(ok = tc::mbar_wait(&fullB[s], (j / NB) & 1, abort))) break;
                 if (!(ok = tc::mbar_wait(&tfull[tb2], (j / NT) & 1, abort))) break;
                 tc::tc_fence_after();
-                const int64_t c0 = c_lo + (int64_t)ck * CH + 32 * h;  // my first channel
+                const int cx = nk2 - 1 - ck;                          // chunk (backward sweep)
+                const int64_t c0 = c_lo + (int64_t)cx * CH + 32 * h;  // my first channel
                 const uint8_t *xt = ringB + s * L::SLOT_B;
                 const uint8_t *box = xt + (h >> 1) * ROWS * 128;    // my X columns: box h / 2, chunks 4 (h & 1) ..
                 float2 w[16];
@@ -691,19 +694,20 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK>::THREADS, 1)
                 tc::fence_proxy_async();
                 tc::named_bar(qid, 128);
                 if (qleader) {
-                    tc::tma_store_3d(&tm_c, cb, (int)((c_lo + (int64_t)ck * CH) * BITS / 8), tb * ROWS + 32 * q, b);
+                    tc::tma_store_3d(&tm_c, cb, (int)((c_lo + (int64_t)cx * CH) * BITS / 8), tb * ROWS + 32 * q, b);
                     tc::bulk_commit();
                 }
                 if ((ck % FL) == FL - 1 || ck == nk2 - 1) {
-                    // the q-group's staged scales of chunks ck - ck % FL .. ck: consecutive
-                    // threads take consecutive scales of a token row
-                    const int n = (ck % FL + 1) * gpc;
-                    const int64_t g0 = (c_lo + (int64_t)(ck - ck % FL) * CH) / G;
+                    // the q-group's staged scales of the last nch chunks: staging slot p
+                    // holds chunk cx + (nch - 1 - p), so chunks cx .. cx + nch - 1 form one
+                    // contiguous run per row; consecutive threads take consecutive scales
+                    const int nch = ck % FL + 1, n = nch * gpc;
+                    const int64_t g0 = (c_lo + (int64_t)cx * CH) / G;
                     const int qrows = nrows - 32 * q < 32 ? (nrows - 32 * q > 0 ? nrows - 32 * q : 0) : 32;
                     for (int i = h * 32 + lane; i < qrows * n; i += 128) {
                         const int rr = i / n, e = i - rr * n;
                         p.scales[((int64_t)b * p.T + (int64_t)tb * ROWS + 32 * q + rr) * ngr + g0 + e] =
-                            sst[(32 * q + rr) * spp + e];
+                            sst[(32 * q + rr) * spp + (nch - 1 - e / gpc) * gpc + e % gpc];
                     }
                 }
             }
