@@ -53,6 +53,13 @@ CASES = [
     (96, 5120, 16, 0, 4, 128, True),    # config-3 width
     (64, 11008, 32, 16, 4, 64, False),  # config-2 SiLU-input width: 86 chunks split unevenly over 4 CTAs
     (72, 4096, 64, 7, 8, 32, False),
+    # the row decode (H a multiple of 512, no rotation): rank 0 with outliers,
+    # rank 16 without, rank 48 with an odd outlier count (unaligned outlier rows
+    # in the partial last token block), several token blocks per CTA range
+    (300, 1024, 0, 5, 4, 64, False),
+    (129, 1536, 16, 0, 8, 128, False),
+    (260, 2560, 48, 33, 4, 32, False),
+    (1100, 512, 32, 16, 4, 64, False),
 ]
 
 
@@ -168,13 +175,14 @@ def test_channel_topk_matches_oracle(O):
         assert list(idx) == list(O.topk_channels(O.channel_absmax(xb), k))
 
 
-def test_batched_slices_are_independent(O):
+@pytest.mark.parametrize("H", [256, 512])
+def test_batched_slices_are_independent(O, H):
     """batch > 1 with a different basis per slice equals per-slice encodes."""
     import actcomp
 
     xs, Vs = [], []
     for s in range(3):
-        xb, V, _ = make_case(O, 64, 256, 16, 0, seed=20 + s)
+        xb, V, _ = make_case(O, 64, H, 16, 0, seed=20 + s)
         xs.append(xb)
         Vs.append(V)
     basis = actcomp.Basis.from_vectors(torch.from_numpy(np.stack(Vs)).cuda())

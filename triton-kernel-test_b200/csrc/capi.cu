@@ -33,6 +33,7 @@ int act_cg_encode_tc(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, c
 int act_cg_softmax_simt(const actcomp_cg_desc *d, const uint16_t *dp, uint16_t *ds, int64_t ld, int causal,
                         cudaStream_t s);
 size_t act_cg_softmax_tc_workspace(const actcomp_cg_desc *d);
+int act_cg_decode_rows(const actcomp_cg_desc *d, uint16_t *out, int64_t ldo, cudaStream_t s);
 int act_cg_softmax_tc(const actcomp_cg_desc *d, const uint16_t *dp, uint16_t *ds, int64_t ld, int causal,
                       void *workspace, cudaStream_t s);
 
@@ -68,6 +69,14 @@ extern "C" int actcomp_clear_device_error(void *stream) {
     return ACT_OK;
 }
 
+// Decode: the row kernel where it covers the format, else the piece kernel
+// (rotation, narrow H); both give the same bits.
+static int decode_tc(const actcomp_cg_desc *d, uint16_t *xhat, int64_t ldo, cudaStream_t s) {
+    const int st = act_cg_decode_rows(d, xhat, ldo, s);
+    if (st != ACT_E_UNSUPPORTED) return st;
+    return act_cg_consume_tc(d, ACT_OP_DECODE, nullptr, 0, xhat, ldo, s);
+}
+
 // Vector access requirements shared by the encode/decode kernels.
 static int check_rows(const void *p, int64_t ld, int64_t H) {
     ACT_CHECK(p, ACT_E_INVALID);
@@ -95,7 +104,7 @@ extern "C" int actcomp_cg_decode(const actcomp_cg_desc *d, uint16_t *xhat, int64
     int st = validate_desc(d);
     if (st) return st;
     if ((st = check_rows(xhat, ldo, d->channels))) return st;
-    return act_cg_consume_tc(d, ACT_OP_DECODE, nullptr, 0, xhat, ldo, as_stream(stream));
+    return decode_tc(d, xhat, ldo, as_stream(stream));
 }
 
 extern "C" int actcomp_cg_consume(const actcomp_cg_desc *d, int32_t op, const uint16_t *y, int64_t ldy,
@@ -105,6 +114,7 @@ extern "C" int actcomp_cg_consume(const actcomp_cg_desc *d, int32_t op, const ui
     ACT_CHECK(op >= ACT_OP_DECODE && op <= ACT_OP_GELU_BWD, ACT_E_INVALID);
     if ((st = check_rows(out, ldo, d->channels))) return st;
     if (op != ACT_OP_DECODE && (st = check_rows(y, ldy, d->channels))) return st;
+    if (op == ACT_OP_DECODE) return decode_tc(d, out, ldo, as_stream(stream));
     return act_cg_consume_tc(d, op, y, ldy, out, ldo, as_stream(stream));
 }
 
@@ -145,7 +155,7 @@ extern "C" int actcomp_cg_dw(const actcomp_cg_desc *d, const uint16_t *dy, int64
     ACT_CHECK(aligned(workspace, 256), ACT_E_ALIGN);
     cudaStream_t s = as_stream(stream);
     uint16_t *xhat = static_cast<uint16_t *>(workspace);
-    if ((st = act_cg_consume_tc(d, ACT_OP_DECODE, nullptr, 0, xhat, d->channels, s))) return st;
+    if ((st = decode_tc(d, xhat, d->channels, s))) return st;
     actcomp_gemm_args g{};
     g.M = d->channels;
     g.N = N;

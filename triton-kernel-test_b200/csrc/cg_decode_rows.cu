@@ -1,0 +1,581 @@
+// cg_decode_rows.cu -- tensor-core decode of the channel-group format with
+// whole tile rows per thread (the decode for unrotated formats).
+//
+// One tile = 128 tokens x 128 channels; each CTA walks one contiguous range
+// of tiles (persistent, one CTA per SM).  Roles:
+//   warp 0      producer: per tile one bulk copy of the prepared bf16 basis
+//               tile (128 channels x r) and one TMA load of the residual codes
+//               into an S-stage ring; per token block one bulk copy of its
+//               low-rank codes (128 x r int8) and of its outlier values;
+//   warp 1      MMA: per token block converts the low-rank codes to bf16 (exact
+//               integers) in a swizzled operand tile; per tile one
+//               tcgen05.mma kind::f16 (M=128, N=128, K=16 steps) gives
+//               I = Lq . Vq^T as exact fp32 integers in TMEM (every product and
+//               partial sum is an integer below 2^24), one accumulator per
+//               epilogue group;
+//   warps 2-17  epilogue: four groups of four warps, group g takes the tiles
+//               g, g+4, g+8, ... of the range; a thread owns one token row of
+//               the tile and all 128 channels, processed as four 32-channel
+//               pieces: xhat = bf16(fma(I, sL, (u - 2^(b-1)) * s)), outlier
+//               channels verbatim; each warp stores its 32 x 32 piece by TMA.
+// Per-tile costs (waits, scalars, arrivals) are paid once per 128 channels of
+// a row instead of once per 32, and the low-rank term needs no int32 -> float
+// conversion.  Arithmetic is that of oracle/actcomp_oracle.c (cg_decode).
+#include <cudaTypedefs.h>
+
+#include "tc_ptx.cuh"
+
+namespace act {
+namespace cgrow {
+
+constexpr int ROWS = 128, CH = 128;
+constexpr int NG = 4;          // epilogue groups = TMEM accumulators (4 x 128 columns)
+constexpr int EW = 4 * NG;     // epilogue warps
+constexpr int THREADS = 64 + 32 * EW;
+constexpr int WST = 32 * 64;   // one output staging buffer: 32 rows x 32 bf16 (64-byte rows)
+constexpr int PD = 2;          // per-row scalars prefetched PD group tiles ahead
+
+struct RowParams {
+    int64_t T, H;
+    int rank, k, group, batch;
+    int ntb, ncc;
+    int64_t ntiles;
+    int tq, trem;          // tiles per CTA: tq, one more for the first trem CTAs
+    int S;                 // ring stages
+    int n32;               // 32-channel groups of H
+    int ostage;            // outlier values staged in shared memory per token block
+    int ostb;              // bytes of one outlier slot
+    const float *scales;
+    const float *lr_scale;
+    const int8_t *lrq;
+    const uint16_t *outliers;
+    const int32_t *idx;
+    const uint16_t *vqb;   // basis_qb tile operand
+    int off_stg, off_lqb, off_lqi, off_ost, off_bar, off_ot;
+};
+
+template <int BITS, int RK>
+struct RowLayout {
+    static constexpr int LB = 2 * RK;                  // bytes of one bf16 operand row
+    static constexpr int VQ = RK ? CH * LB : 0;         // basis tile
+    static constexpr int CODE_ROW = CH * BITS / 8;      // code bytes of one token row of a tile
+    static constexpr int CODES = ROWS * CODE_ROW;
+    static constexpr int STAGE = VQ + CODES;
+    static constexpr int LQB = RK ? ROWS * LB : 0;      // bf16 low-rank operand of a token block
+    // returns the shared-memory bytes, or 0 if S < 3 stages would fit
+    static int plan(RowParams &p, int nsl) {
+        const int lqi = p.rank ? ROWS * p.rank : 0;
+        const int fixed_no_ost = EW * 2 * WST + 2 * LQB + 2 * ((lqi + 1023) & ~1023) + 1024 /*bars*/ +
+                                 ((nsl * p.n32 * 8 + 15) & ~15) + 1024 /*align*/;
+        const int ostb = (ROWS * p.k * 2 + 15) & ~15;
+        for (int ost = p.k ? 1 : 0; ost >= 0; --ost) {
+            const int fixed = fixed_no_ost + (ost ? 2 * ostb : 0);
+            for (int S = 6; S >= 3; --S) {
+                if (S * STAGE + fixed <= 227 * 1024) {
+                    p.S = S;
+                    p.ostage = ost;
+                    p.ostb = ostb;
+                    p.off_stg = S * STAGE;
+                    p.off_lqb = p.off_stg + EW * 2 * WST;
+                    p.off_lqi = p.off_lqb + 2 * LQB;
+                    p.off_ost = p.off_lqi + 2 * ((lqi + 1023) & ~1023);
+                    p.off_bar = p.off_ost + (ost ? 2 * ostb : 0);
+                    p.off_ot = p.off_bar + 1024;
+                    return p.off_ot + ((nsl * p.n32 * 8 + 15) & ~15) + 1024;
+                }
+            }
+        }
+        return 0;
+    }
+};
+
+template <int PITCH>
+__device__ __forceinline__ int swz(int r, int c) {
+    if constexpr (PITCH == 128) return r * 128 + ((c ^ (r & 7)) << 4);
+    else if constexpr (PITCH == 64) return r * 64 + ((c ^ ((r >> 1) & 3)) << 4);
+    else return r * 32 + ((c ^ ((r >> 2) & 1)) << 4);
+}
+template <int PITCH>
+__host__ __device__ constexpr tc::Swizzle swz_mode() {
+    return PITCH == 128 ? tc::SW_128B : (PITCH == 64 ? tc::SW_64B : tc::SW_32B);
+}
+
+// Coordinates of consecutive tiles (channel chunk fastest), no divisions per step.
+struct Walk {
+    int cc, tb, b, ncc, ntb;
+    __device__ Walk(int64_t first, int ncc_, int ntb_) : ncc(ncc_), ntb(ntb_) {
+        cc = (int)(first % ncc);
+        const int64_t bt = first / ncc;
+        tb = (int)(bt % ntb);
+        b = (int)(bt / ntb);
+    }
+    __device__ __forceinline__ void next() {
+        if (++cc == ncc) {
+            cc = 0;
+            if (++tb == ntb) {
+                tb = 0;
+                ++b;
+            }
+        }
+    }
+    __device__ __forceinline__ int64_t block() const { return (int64_t)b * ntb + tb; }
+};
+
+// Outlier values of token block (tb, b): rows tb*128.. of the T x k matrix,
+// one contiguous run; staged when its size and start are 16-byte multiples.
+__device__ __forceinline__ uint32_t ost_bytes(const RowParams &p, int tb, int b, const uint16_t *&src) {
+    const int64_t rows = (p.T - (int64_t)tb * ROWS) < ROWS ? (p.T - (int64_t)tb * ROWS) : ROWS;
+    src = p.outliers + ((int64_t)b * p.T + (int64_t)tb * ROWS) * p.k;
+    if (!p.ostage) return 0;
+    const int64_t bytes = rows * p.k * 2;
+    if ((bytes & 15) || (reinterpret_cast<uintptr_t>(src) & 15)) return 0;
+    return (uint32_t)bytes;
+}
+
+template <int BITS, int RK>
+__global__ void __launch_bounds__(THREADS, 1)
+    cg_decode_rows_kernel(const __grid_constant__ CUtensorMap tm_codes, const __grid_constant__ CUtensorMap tm_out,
+                          RowParams p) {
+    using L = RowLayout<BITS, RK>;
+    constexpr int LB = L::LB;
+    constexpr int off = 1 << (BITS - 1);
+    extern __shared__ uint8_t smem_raw[];
+    uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+    const int S = p.S;
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + p.off_bar);
+    uint64_t *empty = full + 6;
+    uint64_t *tfull = empty + 6;
+    uint64_t *tempty = tfull + NG;
+    uint64_t *lqfull = tempty + NG;  // [2] token-block slots loaded
+    uint64_t *lqempty = lqfull + 2;  // [2] ... and no longer read
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(lqempty + 2);
+    volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
+    uint8_t *lqb = smem + p.off_lqb;
+    uint8_t *lqi = smem + p.off_lqi;
+    uint8_t *ostbuf = smem + p.off_ost;
+    const int lqi_slot = ((p.rank * ROWS) + 1023) & ~1023;
+    const bool use_ost = p.k > 0 && p.ostage;
+    const bool blockbuf = RK > 0 || use_ost;
+    const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+    const int i_blk = blockIdx.x;
+    const int64_t t_lo = (int64_t)i_blk * p.tq + (i_blk < p.trem ? i_blk : p.trem);
+    const int64_t t_hi = t_lo + p.tq + (i_blk < p.trem ? 1 : 0);
+    const int64_t tps = (int64_t)p.ntb * p.ncc;  // tiles per slice
+    const int b_lo = (int)(t_lo / tps);
+
+    if (threadIdx.x == 0) {
+        for (int s = 0; s < S; ++s) {
+            tc::mbar_init(&full[s], 1);
+            tc::mbar_init(&empty[s], 4 + (RK ? 1 : 0));
+        }
+        for (int g = 0; g < NG; ++g) {
+            tc::mbar_init(&tfull[g], 1);
+            tc::mbar_init(&tempty[g], 4);
+        }
+        for (int b = 0; b < 2; ++b) {
+            tc::mbar_init(&lqfull[b], 1);
+            // the MMA warp's commit, plus 4 arrivals per tile of the block (the
+            // warps of the group that decodes it) when outliers are staged
+            tc::mbar_init(&lqempty[b], (RK ? 1 : 0) + (use_ost ? 4 * p.ncc : 0));
+        }
+        *abort = 0;
+        tc::fence_mbar_init();
+    }
+    if (RK && warp == 1) {
+        tc::tmem_alloc(tmem_slot, NG * CH);
+        tc::tmem_relinquish();
+    }
+    // outlier table of every slice this range touches: per 32-channel group a
+    // mask of its outlier channels and the number of outliers below it
+    if (warp >= 2 && p.k) {
+        uint32_t *omask = reinterpret_cast<uint32_t *>(smem + p.off_ot);
+        const int b_hi = (int)((t_hi - 1) / tps);
+        const int n = (b_hi - b_lo + 1) * p.n32;
+        for (int e = threadIdx.x - 64; e < n; e += 32 * EW) {
+            const int bs = b_lo + e / p.n32;
+            const int64_t lo = 32 * (int64_t)(e % p.n32);
+            uint32_t m = 0;
+            int below = 0;
+            for (int j = 0; j < p.k; ++j) {
+                const int64_t c = __ldg(p.idx + (int64_t)bs * p.k + j);
+                below += c < lo;
+                if (c >= lo && c < lo + 32) m |= 1u << (c - lo);
+            }
+            omask[2 * e] = m;
+            omask[2 * e + 1] = (uint32_t)below;
+        }
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    tc::tc_fence_after();
+    const uint32_t tmem = RK ? *tmem_slot : 0;
+
+    if (warp == 0) {
+        // ------------------------------------------------------------ producer
+        if (lane == 0) {
+            tc::prefetch_tmap(&tm_codes);
+            int i = 0, nlq = 0;
+            Walk tw(t_lo, p.ncc, p.ntb);
+            for (int64_t tile = t_lo; tile < t_hi; ++tile, ++i, tw.next()) {
+                const int s = i % S;
+                const uint32_t ph = (i / S) & 1;
+                if (blockbuf && (tile == t_lo || tw.cc == 0)) {
+                    const int ls = nlq & 1;
+                    if (!tc::mbar_wait(&lqempty[ls], ((nlq >> 1) & 1) ^ 1, abort)) break;
+                    const uint16_t *osrc = nullptr;
+                    const uint32_t obytes = p.k ? ost_bytes(p, tw.tb, tw.b, osrc) : 0;
+                    const int64_t rows =
+                        (p.T - (int64_t)tw.tb * ROWS) < ROWS ? (p.T - (int64_t)tw.tb * ROWS) : ROWS;
+                    const uint32_t lbytes = RK ? (uint32_t)(rows * p.rank) : 0;
+                    tc::mbar_arrive_expect_tx(&lqfull[ls], lbytes + obytes);
+                    if (RK)
+                        tc::bulk_load(lqi + ls * lqi_slot, p.lrq + ((int64_t)tw.b * p.T + (int64_t)tw.tb * ROWS) * p.rank,
+                                      lbytes, &lqfull[ls]);
+                    if (obytes) tc::bulk_load(ostbuf + ls * p.ostb, osrc, obytes, &lqfull[ls]);
+                    ++nlq;
+                }
+                if (!tc::mbar_wait(&empty[s], ph ^ 1, abort)) break;
+                uint8_t *st = smem + s * L::STAGE;
+                tc::mbar_arrive_expect_tx(&full[s], L::STAGE);
+                if constexpr (RK > 0)
+                    tc::bulk_load(st, p.vqb + ((int64_t)tw.b * p.ncc + tw.cc) * (CH * LB / 2), L::VQ, &full[s]);
+                tc::tma_load_3d(st + L::VQ, &tm_codes, &full[s], tw.cc * L::CODE_ROW, tw.tb * ROWS, tw.b);
+            }
+        }
+    } else if (warp == 1) {
+        // ------------------------------------------------------------ MMA
+        if constexpr (RK > 0) {
+            constexpr uint32_t idesc = tc::idesc_f16(ROWS, CH, true, false, false);
+            constexpr tc::Swizzle SW = swz_mode<LB>();
+            const int nkq = (p.rank + 15) / 16;
+            int i = 0, mlq = 0;
+            bool ok = true;
+            Walk tw(t_lo, p.ncc, p.ntb);
+            for (int64_t tile = t_lo; tile < t_hi && ok; ++tile, ++i, tw.next()) {
+                const int s = i % S, acc = i & (NG - 1);
+                const uint32_t ph = (i / S) & 1, aph = (i / NG) & 1;
+                if (tile == t_lo || tw.cc == 0) {
+                    // a new token block: its low-rank codes as a bf16 operand tile
+                    const int ls = mlq & 1;
+                    int okw = 1;
+                    if (lane == 0) okw = tc::mbar_wait(&lqfull[ls], (mlq >> 1) & 1, abort);
+                    if (!(ok = __shfl_sync(0xffffffffu, okw, 0) != 0)) break;
+                    const int8_t *src = reinterpret_cast<const int8_t *>(lqi + ls * lqi_slot);
+                    uint8_t *dst = lqb + ls * L::LQB;
+                    for (int e = lane; e < ROWS * (LB / 16); e += 32) {
+                        const int row = e / (LB / 16), c16 = e % (LB / 16);  // 8 values per 16-byte chunk
+                        uint32_t w[4];
+#pragma unroll
+                        for (int h = 0; h < 4; ++h) {
+                            const int j = c16 * 8 + 2 * h;
+                            const float f0 = j < p.rank ? (float)src[row * p.rank + j] : 0.f;
+                            const float f1 = j + 1 < p.rank ? (float)src[row * p.rank + j + 1] : 0.f;
+                            w[h] = pack_bf16x2(f0, f1);
+                        }
+                        *reinterpret_cast<uint4 *>(dst + swz<LB>(row, c16)) = make_uint4(w[0], w[1], w[2], w[3]);
+                    }
+                    tc::fence_proxy_async();
+                    __syncwarp();
+                    ++mlq;
+                }
+                const int ls = (mlq - 1) & 1;
+                int okw = 1;
+                if (lane == 0) {
+                    okw = tc::mbar_wait(&full[s], ph, abort) && tc::mbar_wait(&tempty[acc], aph ^ 1, abort);
+                    if (okw) {
+                        tc::tc_fence_after();
+                        const uint8_t *st = smem + s * L::STAGE;
+                        const uint8_t *a = lqb + ls * L::LQB;
+                        for (int kk = 0; kk < nkq; ++kk) {
+                            const uint64_t ad = tc::smem_desc(a + kk * 32, 16, 8 * LB, SW);
+                            const uint64_t bd = tc::smem_desc(st + kk * 32, 16, 8 * LB, SW);
+                            tc::mma_f16(tmem + acc * CH, ad, bd, idesc, kk > 0);
+                        }
+                        tc::mma_commit(&tfull[acc]);
+                        tc::mma_commit(&empty[s]);
+                        // last tile of this token block in the range: the slot frees when these MMAs complete
+                        if (tw.cc == p.ncc - 1 || tile == t_hi - 1) tc::mma_commit(&lqempty[ls]);
+                    }
+                }
+                ok = __shfl_sync(0xffffffffu, okw, 0) != 0;
+            }
+        }
+    } else {
+        // ------------------------------------------------------------ epilogue
+        const int ew = warp - 2;
+        const int g = ew >> 2;   // group: tiles g, g + 4, ...
+        const int q = warp & 3;  // TMEM lane quadrant = row quarter
+        const int r = q * 32 + lane;
+        const int ngr = (int)(p.H / p.group);
+        const int gshift = 31 - __clz(p.group);
+        const uint32_t *otab = reinterpret_cast<const uint32_t *>(smem + p.off_ot);
+        uint8_t *stg = smem + p.off_stg + ew * (2 * WST);
+
+        // per-row scalars of a tile: the group scales of its 128 channels and
+        // the low-rank scale, loaded PD group tiles ahead
+        float4 qsc[PD];
+        float qsl[PD];
+        auto load_scalars = [&](int64_t tile, const Walk &at, float4 &vsc, float &vsl) {
+            vsc = make_float4(0.f, 0.f, 0.f, 0.f);
+            vsl = 0.f;
+            if (tile >= t_hi) return;
+            const int64_t t = (int64_t)at.tb * ROWS + r;
+            if (t >= p.T) return;
+            const int64_t trow = (int64_t)at.b * p.T + t;
+            const float *sp = p.scales + trow * ngr + (((int64_t)at.cc * CH) >> gshift);
+            if (p.group == 32) {
+                vsc = __ldg(reinterpret_cast<const float4 *>(sp));
+            } else if (p.group == 64) {
+                const float2 v = __ldg(reinterpret_cast<const float2 *>(sp));
+                vsc = make_float4(v.x, v.x, v.y, v.y);
+            } else {
+                const float v = __ldg(sp);
+                vsc = make_float4(v, v, v, v);
+            }
+            if (RK) vsl = __ldg(p.lr_scale + trow);
+        };
+        auto step4 = [](Walk &w) {
+#pragma unroll
+            for (int e = 0; e < NG; ++e) w.next();
+        };
+        Walk tw(t_lo + g < t_hi ? t_lo + g : t_lo, p.ncc, p.ntb), nw = tw;
+#pragma unroll
+        for (int d = 0; d < PD; ++d) {
+            load_scalars(t_lo + g + NG * d, nw, qsc[d], qsl[d]);
+            step4(nw);
+        }
+        const int64_t blk_lo = t_lo / p.ncc;
+        int64_t cur_blk = -1;
+        const uint16_t *ovals = nullptr;
+        int j = 0;
+        for (int64_t tile = t_lo + g; tile < t_hi; tile += NG, ++j, step4(tw)) {
+            const int i = (int)(tile - t_lo);
+            const int s = i % S;
+            const uint32_t ph = (i / S) & 1, aph = j & 1;
+            const int cc = tw.cc, tb = tw.tb, b = tw.b;
+            const float4 sc4 = qsc[0];
+            const float sl = qsl[0];
+#pragma unroll
+            for (int d = 0; d + 1 < PD; ++d) {
+                qsc[d] = qsc[d + 1];
+                qsl[d] = qsl[d + 1];
+            }
+            load_scalars(tile + NG * PD, nw, qsc[PD - 1], qsl[PD - 1]);
+            step4(nw);
+
+            const int64_t blk = tw.block();
+            if (p.k && blk != cur_blk) {  // a new token block for this warp: where its outlier values are
+                const uint16_t *osrc = nullptr;
+                const uint32_t ob = ost_bytes(p, tb, b, osrc);
+                ovals = osrc;
+                if (use_ost) {
+                    const int seq = (int)(blk - blk_lo);
+                    if (!tc::mbar_wait(&lqfull[seq & 1], (seq >> 1) & 1, abort)) break;
+                    if (ob) ovals = reinterpret_cast<const uint16_t *>(ostbuf + (seq & 1) * p.ostb);
+                }
+                cur_blk = blk;
+            }
+            bool ok = tc::mbar_wait(&full[s], ph, abort);
+            if (RK) ok = ok && tc::mbar_wait(&tfull[g], aph, abort);
+            if (!ok) break;
+            tc::tc_fence_after();
+            const int64_t t = (int64_t)tb * ROWS + r;
+            const bool rv = t < p.T;
+            const uint8_t *ct = smem + s * L::STAGE + L::VQ;
+            const uint32_t *ot = otab + 2 * ((int64_t)(b - b_lo) * p.n32 + (((int64_t)cc * CH) >> 5));
+
+#pragma unroll 1
+            for (int k = 0; k < 4; ++k) {
+                uint32_t I[32];
+                if constexpr (RK > 0) tc::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + g * CH + 32 * k, I);
+                uint32_t wd[BITS];
+                if constexpr (BITS == 4) {
+                    const uint4 v = *reinterpret_cast<const uint4 *>(ct + swz<64>(r, k));
+                    wd[0] = v.x; wd[1] = v.y; wd[2] = v.z; wd[3] = v.w;
+                } else {
+                    const uint4 v0 = *reinterpret_cast<const uint4 *>(ct + swz<128>(r, 2 * k));
+                    const uint4 v1 = *reinterpret_cast<const uint4 *>(ct + swz<128>(r, 2 * k + 1));
+                    wd[0] = v0.x; wd[1] = v0.y; wd[2] = v0.z; wd[3] = v0.w;
+                    wd[4] = v1.x; wd[5] = v1.y; wd[6] = v1.z; wd[7] = v1.w;
+                }
+                if (k == 3) {  // the codes of this stage have been read
+                    __syncwarp();
+                    if (lane == 0) tc::mbar_arrive(&empty[s]);
+                }
+                const float sc = k == 0 ? sc4.x : (k == 1 ? sc4.y : (k == 2 ? sc4.z : sc4.w));
+                float2 w[16];
+                {
+                    const float2 sc2 = make_float2(sc, sc);
+                    constexpr float UOFF = 8388608.0f + (float)off;
+                    const float2 uoff2 = make_float2(UOFF, UOFF);
+                    // code u -> float 2^23 + u by one byte permute against 0x4B000000
+                    constexpr uint32_t K4B = 0x4B000000u;
+#pragma unroll
+                    for (int wi = 0; wi < BITS; ++wi) {
+                        if constexpr (BITS == 4) {
+                            const uint32_t ev = wd[wi] & 0x0F0F0F0Fu, od = (wd[wi] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+                            for (int m = 0; m < 4; ++m) {
+                                const float2 f = make_float2(__uint_as_float(__byte_perm(ev, K4B, 0x7540u | m)),
+                                                             __uint_as_float(__byte_perm(od, K4B, 0x7540u | m)));
+                                w[4 * wi + m] = mul2(sub2(f, uoff2), sc2);
+                            }
+                        } else {
+#pragma unroll
+                            for (int m = 0; m < 2; ++m) {
+                                const float2 f =
+                                    make_float2(__uint_as_float(__byte_perm(wd[wi], K4B, 0x7540u | (2 * m))),
+                                                __uint_as_float(__byte_perm(wd[wi], K4B, 0x7541u + 2 * m)));
+                                w[2 * wi + m] = mul2(sub2(f, uoff2), sc2);
+                            }
+                        }
+                    }
+                }
+                if constexpr (RK > 0) {
+                    tc::tmem_ld_wait();
+                    const float2 sl2 = make_float2(sl, sl);
+#pragma unroll
+                    for (int e = 0; e < 16; ++e)
+                        w[e] = fma2(make_float2(__uint_as_float(I[2 * e]), __uint_as_float(I[2 * e + 1])), sl2, w[e]);
+                    if (k == 3) {  // the accumulator has been read
+                        tc::tc_fence_before();
+                        __syncwarp();
+                        if (lane == 0) tc::mbar_arrive(&tempty[g]);
+                    }
+                }
+                // outlier channels of this piece (warp-uniform mask): verbatim values
+                if (p.k) {
+                    const uint32_t om = ot[2 * k];
+                    if (om && (int64_t)cc * CH + 32 * k < p.H) {
+                        const int below = (int)ot[2 * k + 1];
+#pragma unroll
+                        for (int c8 = 0; c8 < 4; ++c8) {
+                            const uint32_t m8 = (om >> (8 * c8)) & 0xffu;
+                            if (!m8) continue;
+#pragma unroll
+                            for (int e8 = 0; e8 < 8; ++e8) {
+                                if ((m8 >> e8) & 1u) {
+                                    const int e = 8 * c8 + e8;
+                                    const int slot = below + __popc(om & ((1u << e) - 1u));
+                                    const float v = rv ? bf2f(ovals[r * p.k + slot]) : 0.f;
+                                    if (e & 1) w[e >> 1].y = v;
+                                    else w[e >> 1].x = v;
+                                }
+                            }
+                        }
+                    }
+                }
+                // store the 32 x 32 piece: buffer k & 1 is free once the store
+                // issued two pieces ago has read it
+                uint8_t *buf = stg + (k & 1) * WST;
+                if (lane == 0) tc::bulk_wait_read<1>();
+                __syncwarp();
+#pragma unroll
+                for (int c16 = 0; c16 < 4; ++c16) {
+                    const int e = 4 * c16;
+                    uint4 v;
+                    v.x = pack_bf16x2(w[e].x, w[e].y);
+                    v.y = pack_bf16x2(w[e + 1].x, w[e + 1].y);
+                    v.z = pack_bf16x2(w[e + 2].x, w[e + 2].y);
+                    v.w = pack_bf16x2(w[e + 3].x, w[e + 3].y);
+                    *reinterpret_cast<uint4 *>(buf + swz<64>(lane, c16)) = v;
+                }
+                tc::fence_proxy_async();
+                __syncwarp();
+                if (lane == 0) {
+                    tc::tma_store_3d(&tm_out, buf, cc * CH + 32 * k, tb * ROWS + 32 * q, b);
+                    tc::bulk_commit();
+                }
+            }
+            // the outlier slot of this block: 4 arrivals per tile, plus those of
+            // the block's tiles outside the range (first and last tile of the range)
+            if (use_ost && lane == 0) {
+                uint32_t n = 1;
+                if (tile == t_lo) n += (uint32_t)cc;
+                if (tile == t_hi - 1) n += (uint32_t)(p.ncc - 1 - cc);
+                tc::mbar_arrive_cnt(&lqempty[(int)(blk - blk_lo) & 1], n);
+            }
+        }
+        if (lane == 0) tc::bulk_wait<0>();
+    }
+    tc::tc_fence_before();
+    __syncthreads();
+    if (RK && warp == 1) {
+        tc::tc_fence_after();
+        tc::tmem_dealloc(tmem, NG * CH);
+    }
+}
+
+template <int BITS, int RK>
+int launch(const actcomp_cg_desc *d, uint16_t *out, int64_t ldo, cudaStream_t stream) {
+    using L = RowLayout<BITS, RK>;
+    const int64_t T = d->tokens, H = d->channels, B = d->batch;
+    CUtensorMap m_codes{}, m_out{};
+    int st;
+    const int64_t rowb = H * BITS / 8;
+    if ((st = make_map_3d(&m_codes, d->codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rowb, T, B, rowb, T * rowb,
+                          L::CODE_ROW, ROWS, BITS == 4 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B)))
+        return st;
+    if ((st = make_map_3d(&m_out, out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, H, T, B, ldo, T * ldo, 32, 32,
+                          CU_TENSOR_MAP_SWIZZLE_64B)))
+        return st;
+    RowParams p{};
+    p.T = T;
+    p.H = H;
+    p.rank = d->rank;
+    p.k = d->n_outlier;
+    p.group = d->group;
+    p.batch = d->batch;
+    p.ntb = (int)((T + ROWS - 1) / ROWS);
+    p.ncc = (int)(H / CH);
+    p.ntiles = (int64_t)p.ntb * p.ncc * B;
+    p.n32 = (int)(H / 32);
+    p.scales = d->scales;
+    p.lr_scale = d->lr_scale;
+    p.lrq = d->lr_codes;
+    p.outliers = d->outliers;
+    p.idx = d->outlier_idx;
+    p.vqb = d->basis_qb;
+    const int grid = (int)(p.ntiles < num_sms() ? p.ntiles : num_sms());
+    p.tq = (int)(p.ntiles / grid);
+    p.trem = (int)(p.ntiles % grid);
+    const int64_t tps = (int64_t)p.ntb * p.ncc;
+    const int64_t span = p.tq + (p.trem ? 1 : 0);
+    const int nsl = (int)((span - 1) / tps + 2 < B ? (span - 1) / tps + 2 : B);
+    const int smem = L::plan(p, nsl);
+    if (!smem) return ACT_E_UNSUPPORTED;
+    auto kern = cg_decode_rows_kernel<BITS, RK>;
+    ACT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+    kern<<<grid, THREADS, smem, stream>>>(m_codes, m_out, p);
+    return launch_status();
+}
+
+}  // namespace cgrow
+}  // namespace act
+
+// Decode through the row kernel, or ACT_E_UNSUPPORTED (before launching) for
+// formats it does not cover: rotation, H not a multiple of 512 (a group of
+// warps must never skip a token block), a rank without the bf16 basis
+// operand, or unaligned low-rank codes.
+int act_cg_decode_rows(const actcomp_cg_desc *d, uint16_t *out, int64_t ldo, cudaStream_t s) {
+    using namespace act::cgrow;
+    if (d->tokens == 0) return ACT_OK;
+    if (d->wht || d->channels % 512 != 0 || !act::aligned(d->scales, 16)) return ACT_E_UNSUPPORTED;
+    if (d->rank && (!d->basis_qb || !act::aligned(d->basis_qb, 16) || !act::aligned(d->lr_codes, 16)))
+        return ACT_E_UNSUPPORTED;
+    const int rk = d->rank == 0 ? 0 : (d->rank <= 16 ? 16 : (d->rank <= 32 ? 32 : 64));
+    if (d->bits == 4) {
+        switch (rk) {
+            case 0: return launch<4, 0>(d, out, ldo, s);
+            case 16: return launch<4, 16>(d, out, ldo, s);
+            case 32: return launch<4, 32>(d, out, ldo, s);
+            default: return launch<4, 64>(d, out, ldo, s);
+        }
+    }
+    switch (rk) {
+        case 0: return launch<8, 0>(d, out, ldo, s);
+        case 16: return launch<8, 16>(d, out, ldo, s);
+        case 32: return launch<8, 32>(d, out, ldo, s);
+        default: return launch<8, 64>(d, out, ldo, s);
+    }
+}

@@ -30,6 +30,10 @@ __device__ __forceinline__ void fence_mbar_init() {
 __device__ __forceinline__ void mbar_arrive(uint64_t *bar) {
     asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
 }
+// `count` arrivals at once
+__device__ __forceinline__ void mbar_arrive_cnt(uint64_t *bar, uint32_t count) {
+    asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
+}
 __device__ __forceinline__ void mbar_arrive_expect_tx(uint64_t *bar, uint32_t bytes) {
     asm volatile("mbarrier.arrive.expect_tx.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(bytes)
                  : "memory");
@@ -48,9 +52,11 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
 // Once *abort is set every later wait returns false at once, so a kernel that
 // lost a producer drains and exits instead of hanging.
 __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort) {
+    // the abort word is read every 64th poll: a waiting warp issues little
+    // more than the try_wait itself, leaving issue slots to working warps
     for (uint32_t i = 0; i < (1u << 24); ++i) {
         if (mbar_try_wait(bar, parity)) return true;
-        if (*abort) return false;
+        if ((i & 63u) == 63u && *abort) return false;
     }
     *abort = 1;
     atomicOr(&g_device_error, DEV_ERR_MBAR_TIMEOUT);
