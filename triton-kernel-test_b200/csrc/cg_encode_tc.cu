@@ -183,7 +183,8 @@ __device__ __forceinline__ uint32_t pack_codes(float2 t0, float2 t1, float2 t2, 
 template <int BITS, bool WHT, int RK>
 __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK>::THREADS, 1)
     cg_encode_tc_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_vt,
-                        const __grid_constant__ CUtensorMap tm_c, EncParams p) {
+                        const __grid_constant__ CUtensorMap tm_c, const __grid_constant__ CUtensorMap tm_cw,
+                        EncParams p) {
     using L = EncLayout<BITS, WHT, RK>;
     constexpr int LB = L::LB;
     constexpr int qmax = (1 << (BITS - 1)) - 1, off = 1 << (BITS - 1);
@@ -391,6 +392,10 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK>::THREADS, 1)
         const int spp = FL * gpc + 4;  // staged scales per token row (padded)
         const int ngr = (int)(p.H / G);
         const bool qleader = (h == 0 && lane == 0);  // issues the q-group's code stores
+        // groups of 32 or 64 channels without rotation: every warp stores its own
+        // codes and scales, and only the two warps of a 64-channel group meet
+        const bool solo = !WHT && ppg <= 2;
+        const int gshift = 31 - __clz(G);
         int j = 0, nb = 0;
         bool ok = true;
         for (int64_t blk = cluster; blk < p.nblocks && ok; blk += p.nclusters, ++nb) {
@@ -660,33 +665,65 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK>::THREADS, 1)
                     am = a[0];
                 }
                 float *ax = amx + (j & 1) * 4 * ROWS;
-                if (ppg > 1) ax[h * ROWS + row] = am;
-                // the q-group's staging buffer (j & 1) is free once its store of chunk j - 2 has read it
-                if (qleader) tc::bulk_wait_read<1>();
-                tc::named_bar(qid, 128);
                 float gam = am;
-                if (ppg == 2) gam = fmaxf(am, ax[(h ^ 1) * ROWS + row]);
-                else if (ppg == 4)
-                    gam = fmaxf(fmaxf(ax[row], ax[ROWS + row]), fmaxf(ax[2 * ROWS + row], ax[3 * ROWS + row]));
+                if (solo) {
+                    // groups of 64: the pair of warps (h, h ^ 1) shares its absmax; the
+                    // slot (j & 1) is rewritten two chunks later, after the pair's next barrier
+                    if (ppg == 2) {
+                        ax[h * ROWS + row] = am;
+                        tc::named_bar(4 + 2 * q + (h >> 1), 64);
+                        gam = fmaxf(am, ax[(h ^ 1) * ROWS + row]);
+                    }
+                } else {
+                    if (ppg > 1) ax[h * ROWS + row] = am;
+                    // the q-group's staging buffer (j & 1) is free once its store of chunk j - 2 has read it
+                    if (qleader) tc::bulk_wait_read<1>();
+                    tc::named_bar(qid, 128);
+                    if (ppg == 2) gam = fmaxf(am, ax[(h ^ 1) * ROWS + row]);
+                    else if (ppg == 4)
+                        gam = fmaxf(fmaxf(ax[row], ax[ROWS + row]), fmaxf(ax[2 * ROWS + row], ax[3 * ROWS + row]));
+                }
                 const float sc = __fdiv_rn(gam, (float)qmax);
                 const float rs = gam > 0.f ? __fdiv_rn((float)qmax, gam) : 0.f;
                 const float2 rs2 = make_float2(rs, rs);
                 constexpr float MAGIC = 12582912.0f + (float)off;
                 const float2 magic2 = make_float2(MAGIC, MAGIC);
-                uint8_t *cb = cst + (q * 2 + (j & 1)) * L::QST;
+                uint32_t pk[BITS];
                 if constexpr (BITS == 4) {
-                    uint32_t pk[4];
 #pragma unroll
                     for (int wd = 0; wd < 4; ++wd)
                         pk[wd] = pack_codes<4>(fma2(w[4 * wd], rs2, magic2), fma2(w[4 * wd + 1], rs2, magic2),
                                                fma2(w[4 * wd + 2], rs2, magic2), fma2(w[4 * wd + 3], rs2, magic2));
-                    *reinterpret_cast<uint4 *>(cb + swz<CROW>(lane, h)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
                 } else {
-                    uint32_t pk[8];
                     const float2 z = make_float2(0.f, 0.f);
 #pragma unroll
                     for (int wd = 0; wd < 8; ++wd)
                         pk[wd] = pack_codes<8>(fma2(w[2 * wd], rs2, magic2), fma2(w[2 * wd + 1], rs2, magic2), z, z);
+                }
+                if (solo) {
+                    // this warp's 32 rows x 32 channels of codes leave by their own TMA
+                    // store; buffer (j & 1) is free once the store of chunk j - 2 has read it
+                    uint8_t *cb = cst + (ew * 2 + (j & 1)) * (L::QST / 4);
+                    if (lane == 0) tc::bulk_wait_read<1>();
+                    __syncwarp();
+#pragma unroll
+                    for (int c16 = 0; c16 < BITS / 4; ++c16)
+                        *reinterpret_cast<uint4 *>(cb + lane * (CROW / 4) + 16 * c16) =
+                            make_uint4(pk[4 * c16], pk[4 * c16 + 1], pk[4 * c16 + 2], pk[4 * c16 + 3]);
+                    if ((h % ppg) == 0 && rv) p.scales[trow * ngr + (c0 >> gshift)] = sc;
+                    tc::fence_proxy_async();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tc::tma_store_3d(&tm_cw, cb, (int)((c_lo + (int64_t)cx * CH) * BITS / 8) + h * (CROW / 4),
+                                         tb * ROWS + 32 * q, b);
+                        tc::bulk_commit();
+                    }
+                    continue;
+                }
+                uint8_t *cb = cst + (q * 2 + (j & 1)) * L::QST;
+                if constexpr (BITS == 4) {
+                    *reinterpret_cast<uint4 *>(cb + swz<CROW>(lane, h)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                } else {
                     *reinterpret_cast<uint4 *>(cb + swz<CROW>(lane, 2 * h)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
                     *reinterpret_cast<uint4 *>(cb + swz<CROW>(lane, 2 * h + 1)) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
                 }
@@ -724,7 +761,7 @@ __global__ void __launch_bounds__(EncLayout<BITS, WHT, RK>::THREADS, 1)
                 tc::named_bar(3, ETH);  // read out before the next block stages its outliers
             }
         }
-        if (qleader) tc::bulk_wait<0>();  // code stores complete before the CTA exits
+        if (lane == 0) tc::bulk_wait<0>();  // code stores complete before the CTA exits
         // do not exit while a peer may still read our partial buffer
         if (C > 1 && ok && nb > 0) {
             if (lane == 0) tc::mbar_wait_cluster(pdone, (nb - 1) & 1, abort);
@@ -747,7 +784,7 @@ int launch_encode(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cuda
     const int64_t T = d->tokens, H = d->channels, B = d->batch;
     const int r = d->rank;
     const int64_t rowb = H * BITS / 8;
-    CUtensorMap m_x{}, m_vt{}, m_c{};
+    CUtensorMap m_x{}, m_vt{}, m_c{}, m_cw{};
     int st;
     if ((st = make_map_3d(&m_x, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, H, T, B, ldx, T * ldx, 64, ROWS,
                           CU_TENSOR_MAP_SWIZZLE_128B)))
@@ -758,6 +795,10 @@ int launch_encode(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cuda
     // codes leave per row quarter: boxes of 32 token rows x one chunk's code bytes
     if ((st = make_map_3d(&m_c, d->codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rowb, T, B, rowb, T * rowb, L::CROW, 32,
                           tma_swz<L::CROW>())))
+        return st;
+    // ... or per warp: 32 token rows x 32 channels' code bytes
+    if ((st = make_map_3d(&m_cw, d->codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rowb, T, B, rowb, T * rowb, L::CROW / 4, 32,
+                          CU_TENSOR_MAP_SWIZZLE_NONE)))
         return st;
     EncParams p{};
     p.T = T;
@@ -823,7 +864,7 @@ int launch_encode(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cuda
     attr[0].val.clusterDim.z = 1;
     cfg.attrs = attr;
     cfg.numAttrs = 1;
-    ACT_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, m_x, m_vt, m_c, p));
+    ACT_CUDA_TRY(cudaLaunchKernelEx(&cfg, kern, m_x, m_vt, m_c, m_cw, p));
     return ACT_OK;
 }
 
