@@ -185,26 +185,6 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc::tmem_alloc(tmem_slot, NG * CH);
         tc::tmem_relinquish();
     }
-    // outlier table of every slice this range touches: per 32-channel group a
-    // mask of its outlier channels and the number of outliers below it
-    if (warp >= 2 && p.k) {
-        uint32_t *omask = reinterpret_cast<uint32_t *>(smem + p.off_ot);
-        const int b_hi = (int)((t_hi - 1) / tps);
-        const int n = (b_hi - b_lo + 1) * p.n32;
-        for (int e = threadIdx.x - 64; e < n; e += 32 * EW) {
-            const int bs = b_lo + e / p.n32;
-            const int64_t lo = 32 * (int64_t)(e % p.n32);
-            uint32_t m = 0;
-            int below = 0;
-            for (int j = 0; j < p.k; ++j) {
-                const int64_t c = __ldg(p.idx + (int64_t)bs * p.k + j);
-                below += c < lo;
-                if (c >= lo && c < lo + 32) m |= 1u << (c - lo);
-            }
-            omask[2 * e] = m;
-            omask[2 * e + 1] = (uint32_t)below;
-        }
-    }
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
@@ -262,17 +242,27 @@ __global__ void __launch_bounds__(THREADS, 1)
                     if (!(ok = __shfl_sync(0xffffffffu, okw, 0) != 0)) break;
                     const int8_t *src = reinterpret_cast<const int8_t *>(lqi + ls * lqi_slot);
                     uint8_t *dst = lqb + ls * L::LQB;
-                    for (int e = lane; e < ROWS * (LB / 16); e += 32) {
-                        const int row = e / (LB / 16), c16 = e % (LB / 16);  // 8 values per 16-byte chunk
-                        uint32_t w[4];
+                    // 8 codes (one 8-byte load) per 16-byte chunk of the bf16 tile;
+                    // chunks past the rank are zero
+                    const int cpr = LB / 16;  // chunks per row
+                    for (int e = lane; e < ROWS * cpr; e += 32) {
+                        const int row = e / cpr, c16 = e - row * cpr;
+                        uint4 o = make_uint4(0u, 0u, 0u, 0u);
+                        if (8 * c16 < p.rank) {
+                            const uint2 v = *reinterpret_cast<const uint2 *>(src + row * p.rank + 8 * c16);
+                            const uint32_t in[2] = {v.x, v.y};
+                            uint32_t w[4];
 #pragma unroll
-                        for (int h = 0; h < 4; ++h) {
-                            const int j = c16 * 8 + 2 * h;
-                            const float f0 = j < p.rank ? (float)src[row * p.rank + j] : 0.f;
-                            const float f1 = j + 1 < p.rank ? (float)src[row * p.rank + j + 1] : 0.f;
-                            w[h] = pack_bf16x2(f0, f1);
+                            for (int h = 0; h < 4; ++h) {
+                                const uint32_t word = in[h >> 1];
+                                const int sh = (h & 1) * 16;
+                                const float f0 = (float)(int)(int8_t)(word >> sh);
+                                const float f1 = (float)(int)(int8_t)(word >> (sh + 8));
+                                w[h] = pack_bf16x2(f0, f1);
+                            }
+                            o = make_uint4(w[0], w[1], w[2], w[3]);
                         }
-                        *reinterpret_cast<uint4 *>(dst + swz<LB>(row, c16)) = make_uint4(w[0], w[1], w[2], w[3]);
+                        *reinterpret_cast<uint4 *>(dst + swz<LB>(row, c16)) = o;
                     }
                     tc::fence_proxy_async();
                     __syncwarp();
@@ -310,6 +300,28 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int gshift = 31 - __clz(p.group);
         const uint32_t *otab = reinterpret_cast<const uint32_t *>(smem + p.off_ot);
         uint8_t *stg = smem + p.off_stg + ew * (2 * WST);
+        // outlier table of every slice this range touches: per 32-channel group a
+        // mask of its outlier channels and the number of outliers below it (built
+        // here, after the producer has started its loads)
+        if (p.k) {
+            uint32_t *omask = reinterpret_cast<uint32_t *>(smem + p.off_ot);
+            const int b_hi = (int)((t_hi - 1) / tps);
+            const int n = (b_hi - b_lo + 1) * p.n32;
+            for (int e = threadIdx.x - 64; e < n; e += 32 * EW) {
+                const int bs = b_lo + e / p.n32;
+                const int64_t lo = 32 * (int64_t)(e % p.n32);
+                uint32_t m = 0;
+                int below = 0;
+                for (int j = 0; j < p.k; ++j) {
+                    const int64_t c = __ldg(p.idx + (int64_t)bs * p.k + j);
+                    below += c < lo;
+                    if (c >= lo && c < lo + 32) m |= 1u << (c - lo);
+                }
+                omask[2 * e] = m;
+                omask[2 * e + 1] = (uint32_t)below;
+            }
+            tc::named_bar(1, 32 * EW);  // complete before any epilogue warp reads it
+        }
 
         // per-row scalars of a tile: the group scales of its 128 channels and
         // the low-rank scale, loaded PD group tiles ahead
