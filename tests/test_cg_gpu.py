@@ -60,6 +60,9 @@ CASES = [
     (129, 1536, 16, 0, 8, 128, False),
     (260, 2560, 48, 33, 4, 32, False),
     (1100, 512, 32, 16, 4, 64, False),
+    # more token blocks than SMs: some CTAs of the row encode take two blocks
+    # (separate projection / residual rings, double-buffered low-rank tiles)
+    (19277, 1024, 32, 8, 4, 64, False),
 ]
 
 
@@ -175,7 +178,7 @@ def test_channel_topk_matches_oracle(O):
         assert list(idx) == list(O.topk_channels(O.channel_absmax(xb), k))
 
 
-@pytest.mark.parametrize("H", [256, 512])
+@pytest.mark.parametrize("H", [256, 512, 1024])
 def test_batched_slices_are_independent(O, H):
     """batch > 1 with a different basis per slice equals per-slice encodes."""
     import actcomp
@@ -191,3 +194,34 @@ def test_batched_slices_are_independent(O, H):
     for s in range(3):
         cs = gpu_encode(xs[s], Vs[s], np.zeros(0, np.int32), 4, 64, False)
         assert np.array_equal(xh[s], bits(actcomp.decode(cs)))
+
+
+def test_batched_encode_with_outliers_crossing_slices(O):
+    """Two slices of 9700 tokens (152 token blocks: some CTAs encode a block of
+    each slice, so the per-slice outlier tables change inside a CTA) with a
+    different basis and outlier set per slice: every slice bit-exact against
+    the oracle given the kernel's low-rank codes."""
+    import actcomp
+
+    T, H, r, k = 9700, 1024, 16, 4
+    xs, Vs, idxs = [], [], []
+    for s_ in range(2):
+        xb, V, idx = make_case(O, T, H, r, k, seed=40 + s_)
+        xs.append(xb)
+        Vs.append(V)
+        idxs.append(idx)
+    basis = actcomp.Basis.from_vectors(torch.from_numpy(np.stack(Vs)).cuda())
+    oi = torch.from_numpy(np.stack(idxs)).cuda()
+    c = actcomp.encode(to_bf16(np.stack(xs)), basis, oi, bits=4, group=64)
+    torch.cuda.synchronize()
+    codes = c.codes.cpu().numpy().reshape(2, T, -1)
+    scales = c.scales.cpu().numpy().reshape(2, T, -1)
+    Lq = c.lr_codes.cpu().numpy().reshape(2, T, r)
+    sL = c.lr_scale.cpu().numpy().reshape(2, T)
+    outl = bits(c.outliers).reshape(2, T, k)
+    for s_ in range(2):
+        _, Vq, _ = O.basis_prepare(Vs[s_])
+        co, so, oo = O.encode_given_lr(xs[s_], Lq[s_], sL[s_], Vq, idxs[s_], 4, 64, False)
+        assert np.array_equal(codes[s_], co), f"slice {s_}: codes differ"
+        assert np.array_equal(scales[s_], so), f"slice {s_}: scales differ"
+        assert np.array_equal(outl[s_], oo), f"slice {s_}: outliers differ"

@@ -30,6 +30,7 @@ int act_cg_consume_tc(const actcomp_cg_desc *d, int op, const uint16_t *y, int64
                       cudaStream_t s);
 bool act_cg_encode_tc_supported(const actcomp_cg_desc *d);
 int act_cg_encode_tc(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cudaStream_t s);
+int act_cg_encode_rows(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cudaStream_t s);
 int act_cg_softmax_simt(const actcomp_cg_desc *d, const uint16_t *dp, uint16_t *ds, int64_t ld, int causal,
                         cudaStream_t s);
 size_t act_cg_softmax_tc_workspace(const actcomp_cg_desc *d);
@@ -90,10 +91,12 @@ extern "C" int actcomp_cg_encode(const actcomp_cg_desc *d, const uint16_t *x, in
     if (st) return st;
     if ((st = check_rows(x, ldx, d->channels))) return st;
     if (d->rank) ACT_CHECK(d->basis_t && aligned(d->basis_t, 16), ACT_E_ALIGN);
+    // the row kernel, else the piece kernel (rotation, wide or narrow H), else
+    // the CUDA-core encode: each declines (ACT_E_UNSUPPORTED, before
+    // launching) what it does not cover, and all compute the same codes
+    st = act_cg_encode_rows(d, x, ldx, as_stream(stream));
+    if (st != ACT_E_UNSUPPORTED) return st;
     if (act_cg_encode_tc_supported(d)) {
-        // the tensor-core kernel declines (ACT_E_UNSUPPORTED, before launching)
-        // shapes whose buffers do not fit its shared memory; the CUDA-core
-        // encode computes the same codes
         st = act_cg_encode_tc(d, x, ldx, as_stream(stream));
         if (st != ACT_E_UNSUPPORTED) return st;
     }
