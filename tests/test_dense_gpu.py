@@ -63,7 +63,10 @@ def _ref(a, b):
     return a.float() @ b.float()
 
 
-@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 192), (200, 136, 72), (64, 48, 8), (1024, 1000, 520)])
+# (4000, 4864, 136): enough 256 x 256 tiles for the two-accumulator kernel,
+# with a partial last M tile and a partial last K step
+@pytest.mark.parametrize("M,N,K", [(128, 256, 64), (256, 512, 192), (200, 136, 72), (64, 48, 8), (1024, 1000, 520),
+                                   (4000, 4864, 136)])
 @pytest.mark.parametrize("layout", ["nn", "tn", "nt", "tt"])
 def test_gemm_layouts(M, N, K, layout):
     import actcomp

@@ -1,12 +1,14 @@
 // tc_gemm.cu -- dense GEMM on the 5th-generation tensor cores (tcgen05).
 //
 // C[b] = A[b] * B[b] with bf16/fp16 operands and fp32 accumulation in TMEM.
-// One CTA computes one 128 x BN output tile:
-//   warp 0      TMA producer: 128x64 A and BNx64 B tiles (128-byte swizzle)
-//               into a 4-stage shared-memory ring, mbarrier complete_tx;
+// One CTA computes one 128 x BN output tile, or (large problems) one 256 x 256
+// tile as two M = 128 accumulators sharing each B tile:
+//   warp 0      TMA producer: 128x64 A (one or two) and BNx64 B tiles
+//               (128-byte swizzle) into a 4- or 3-stage shared-memory ring,
+//               mbarrier complete_tx;
 //   warp 1      TMEM allocator and MMA issuer (one elected thread issues
-//               tcgen05.mma M=128 N=BN K=16, commits each stage back to the
-//               producer and the finished accumulator to the epilogue);
+//               tcgen05.mma M=128 N=BN K=16 per accumulator, commits each stage
+//               back to the producer and the finished tile to the epilogue);
 //   warps 2..5  epilogue: tcgen05.ld 32x32b (one accumulator row per
 //               thread), optional leaky_relu, convert, store.
 // Both operands may be K-major or MN-major in global memory; the tile layout
@@ -50,13 +52,18 @@ int make_map_3d(CUtensorMap *map, const void *base, CUtensorMapDataType dt, int 
 
 namespace gemm {
 
-constexpr int BM = 128, BK = 64, STAGES = 4, THREADS = 192;
+constexpr int BM = 128, BK = 64, THREADS = 192;
 
-template <int BN>
+// MA = 1: one 128 x BN tile per CTA, 4 stages.  MA = 2: a 256 x BN tile as two
+// M = 128 accumulators (2 x BN TMEM columns) that share every B tile, so each
+// 64-deep K step moves 2 x 16 KB of A and one B tile for twice the MMAs
+// (a third less operand traffic per FLOP from L2), 3 stages.
+template <int BN, int MA>
 struct Smem {
-    static constexpr int A_BYTES = BM * BK * 2;  // 16 KB
+    static constexpr int A_BYTES = BM * BK * 2;  // 16 KB per accumulator
     static constexpr int B_BYTES = BN * BK * 2;
-    static constexpr int STAGE = A_BYTES + B_BYTES;
+    static constexpr int STAGE = MA * A_BYTES + B_BYTES;
+    static constexpr int STAGES = MA == 1 ? 4 : 3;
     static constexpr int TILES = STAGE * STAGES;
     static constexpr int TOTAL = TILES + 1024 /*align slack*/ + 256 /*barriers*/;
 };
@@ -104,13 +111,14 @@ __device__ __forceinline__ void store_row32(T *dst, const float (&v)[32], int va
     }
 }
 
-template <int BN, typename TOut>
+template <int BN, int MA, typename TOut>
 __global__ void __launch_bounds__(THREADS, 1)
     gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p,
                 int bf16) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    using S = Smem<BN>;
+    using S = Smem<BN, MA>;
+    constexpr int STAGES = S::STAGES;
     uint64_t *full = reinterpret_cast<uint64_t *>(smem + S::TILES);
     uint64_t *empty = full + STAGES;
     uint64_t *acc_full = empty + STAGES;
@@ -118,7 +126,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * BM, bz = blockIdx.z;
+    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * (BM * MA), bz = blockIdx.z;
     const int kblocks = (int)((p.K + BK - 1) / BK);
 
     if (threadIdx.x == 0) {
@@ -131,7 +139,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         tc::fence_mbar_init();
     }
     if (warp == 1) {
-        tc::tmem_alloc(tmem_slot, BN);
+        tc::tmem_alloc(tmem_slot, BN * MA);
         tc::tmem_relinquish();
     }
     tc::tc_fence_before();
@@ -147,14 +155,19 @@ __global__ void __launch_bounds__(THREADS, 1)
             const uint32_t ph = (kb / STAGES) & 1;
             if (!tc::mbar_wait(&empty[s], ph ^ 1, abort)) break;
             uint8_t *a = smem + s * S::STAGE;
-            uint8_t *b = a + S::A_BYTES;
+            uint8_t *b = a + MA * S::A_BYTES;
             tc::mbar_arrive_expect_tx(&full[s], S::STAGE);
             const int k0 = kb * BK;
-            if (!p.a_mn) {
-                tc::tma_load_3d(a, &tmA, &full[s], k0, m0, bz);
-            } else {
-                tc::tma_load_3d(a, &tmA, &full[s], m0, k0, bz);
-                tc::tma_load_3d(a + 8192, &tmA, &full[s], m0 + 64, k0, bz);
+#pragma unroll
+            for (int h = 0; h < MA; ++h) {
+                uint8_t *ah = a + h * S::A_BYTES;
+                const int mh = m0 + BM * h;
+                if (!p.a_mn) {
+                    tc::tma_load_3d(ah, &tmA, &full[s], k0, mh, bz);
+                } else {
+                    tc::tma_load_3d(ah, &tmA, &full[s], mh, k0, bz);
+                    tc::tma_load_3d(ah + 8192, &tmA, &full[s], mh + 64, k0, bz);
+                }
             }
             if (!p.b_mn) {
                 tc::tma_load_3d(b, &tmB, &full[s], k0, n0, bz);
@@ -171,21 +184,24 @@ __global__ void __launch_bounds__(THREADS, 1)
             if (!tc::mbar_wait(&full[s], ph, abort)) break;
             tc::tc_fence_after();
             uint8_t *a = smem + s * S::STAGE;
-            uint8_t *b = a + S::A_BYTES;
+            uint8_t *b = a + MA * S::A_BYTES;
 #pragma unroll
             for (int kk = 0; kk < BK / 16; ++kk) {
-                const uint64_t ad = p.a_mn ? tc::smem_desc(a + kk * 2048, 8192, 1024, tc::SW_128B)
-                                           : tc::smem_desc(a + kk * 32, 16, 1024, tc::SW_128B);
                 const uint64_t bd = p.b_mn ? tc::smem_desc(b + kk * 2048, 8192, 1024, tc::SW_128B)
                                            : tc::smem_desc(b + kk * 32, 16, 1024, tc::SW_128B);
-                tc::mma_f16(tmem, ad, bd, idesc, (kb | kk) != 0);
+#pragma unroll
+                for (int h = 0; h < MA; ++h) {
+                    uint8_t *ah = a + h * S::A_BYTES;
+                    const uint64_t ad = p.a_mn ? tc::smem_desc(ah + kk * 2048, 8192, 1024, tc::SW_128B)
+                                               : tc::smem_desc(ah + kk * 32, 16, 1024, tc::SW_128B);
+                    tc::mma_f16(tmem + h * BN, ad, bd, idesc, (kb | kk) != 0);
+                }
             }
             tc::mma_commit(&empty[s]);
         }
         tc::mma_commit(acc_full);
     } else if (warp >= 2) {
         const int q = warp & 3;  // TMEM lane quadrant this warp may access
-        const int row = m0 + q * 32 + lane;
         const bool ok = tc::mbar_wait(acc_full, 0, abort);
         tc::tc_fence_after();
         if (ok) {
@@ -194,9 +210,11 @@ __global__ void __launch_bounds__(THREADS, 1)
                                 (reinterpret_cast<uintptr_t>(p.C) % 16 == 0) &&
                                 ((p.sc_batch * (int64_t)sizeof(TOut)) % 16 == 0);
 #pragma unroll 1
-            for (int c = 0; c < BN / 32; ++c) {
+            for (int hc = 0; hc < MA * (BN / 32); ++hc) {
+                const int h = hc / (BN / 32), c = hc % (BN / 32);
+                const int row = m0 + BM * h + q * 32 + lane;
                 uint32_t r[32];
-                tc::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + c * 32, r);
+                tc::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + h * BN + c * 32, r);
                 tc::tmem_ld_wait();
                 const int col = n0 + c * 32;
                 if (row >= p.M || col >= p.N) continue;
@@ -216,7 +234,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     __syncthreads();
     if (warp == 1) {
         tc::tc_fence_after();
-        tc::tmem_dealloc(tmem, BN);
+        tc::tmem_dealloc(tmem, BN * MA);
     }
 }
 
@@ -228,6 +246,10 @@ int gemm_launch(const actcomp_gemm_args *g, cudaStream_t stream) {
     const CUtensorMapDataType dt = bf16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
     const int a_mn = g->a_kmajor ? 0 : 1, b_mn = g->b_kmajor ? 0 : 1;
     const int BN = g->N <= 128 ? 128 : 256;
+    // two accumulators per CTA where M fills them and there are enough tiles
+    // to keep every SM busy
+    const bool two = BN == 256 && g->M > 128 &&
+                     ((g->N + 255) / 256) * ((g->M + 255) / 256) * g->batch >= 2 * num_sms();
     CUtensorMap tmA, tmB;
     int st;
     const uint64_t batch = (uint64_t)g->batch;
@@ -247,22 +269,29 @@ int gemm_launch(const actcomp_gemm_args *g, cudaStream_t stream) {
                          CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
     Params p{g->M, g->N, g->K, a_mn, b_mn, g->C, g->ldc, g->sc_batch, g->c_dtype, g->activation};
-    dim3 grid((unsigned)((g->N + BN - 1) / BN), (unsigned)((g->M + BM - 1) / BM), (unsigned)g->batch);
+    dim3 grid((unsigned)((g->N + BN - 1) / BN), (unsigned)((g->M + BM * (two ? 2 : 1) - 1) / (BM * (two ? 2 : 1))),
+              (unsigned)g->batch);
     auto launch = [&](auto kern, int smem) -> int {
         ACT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
         kern<<<grid, THREADS, smem, stream>>>(tmA, tmB, p, bf16 ? 1 : 0);
         return launch_status();
     };
     if (BN == 128) {
-        const int smem = Smem<128>::TOTAL;
-        if (g->c_dtype == 0) return launch(gemm_kernel<128, float>, smem);
-        if (g->c_dtype == 1) return launch(gemm_kernel<128, __nv_bfloat16>, smem);
-        return launch(gemm_kernel<128, __half>, smem);
+        const int smem = Smem<128, 1>::TOTAL;
+        if (g->c_dtype == 0) return launch(gemm_kernel<128, 1, float>, smem);
+        if (g->c_dtype == 1) return launch(gemm_kernel<128, 1, __nv_bfloat16>, smem);
+        return launch(gemm_kernel<128, 1, __half>, smem);
     }
-    const int smem = Smem<256>::TOTAL;
-    if (g->c_dtype == 0) return launch(gemm_kernel<256, float>, smem);
-    if (g->c_dtype == 1) return launch(gemm_kernel<256, __nv_bfloat16>, smem);
-    return launch(gemm_kernel<256, __half>, smem);
+    if (two) {
+        const int smem = Smem<256, 2>::TOTAL;
+        if (g->c_dtype == 0) return launch(gemm_kernel<256, 2, float>, smem);
+        if (g->c_dtype == 1) return launch(gemm_kernel<256, 2, __nv_bfloat16>, smem);
+        return launch(gemm_kernel<256, 2, __half>, smem);
+    }
+    const int smem = Smem<256, 1>::TOTAL;
+    if (g->c_dtype == 0) return launch(gemm_kernel<256, 1, float>, smem);
+    if (g->c_dtype == 1) return launch(gemm_kernel<256, 1, __nv_bfloat16>, smem);
+    return launch(gemm_kernel<256, 1, __half>, smem);
 }
 
 }  // namespace act
