@@ -514,7 +514,7 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
                             x2 = make_float2(__fmul_rn(__fsub_rn(lo_bf(wd[e]), rsum), x2.x),
                                              __fmul_rn(__fsub_rn(hi_bf(wd[e]), rsum), x2.y));
                         } else {
-                            x2 = make_float2(apply_op<OP>(x2.x, lo_bf(wd[e])), apply_op<OP>(x2.y, hi_bf(wd[e])));
+                            x2 = apply_op2<OP>(x2, make_float2(lo_bf(wd[e]), hi_bf(wd[e])));
                         }
                     }
                 }

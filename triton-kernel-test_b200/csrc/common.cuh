@@ -149,11 +149,41 @@ __device__ __forceinline__ float2 sub2(float2 a, float2 b) {
     return d;
 }
 
+// The same formulas on pairs of elements: every add / multiply is a packed
+// f32x2 instruction (each half rounded exactly as the scalar one), exp and the
+// reciprocal stay per element.
+__device__ __forceinline__ float2 silu_bwd_f2(float2 x, float2 g) {
+    const float2 one = make_float2(1.0f, 1.0f);
+    const float2 s = make_float2(hw_rcp(__fadd_rn(1.0f, hw_exp(-x.x))), hw_rcp(__fadd_rn(1.0f, hw_exp(-x.y))));
+    return mul2(g, mul2(s, add2(one, mul2(x, sub2(one, s)))));
+}
+__device__ __forceinline__ float2 gelu_bwd_f2(float2 x, float2 g) {
+    const float gamma = 0.7978845608028654f, kappa = 0.044715f;
+    const float2 one = make_float2(1.0f, 1.0f), two = make_float2(2.0f, 2.0f), half = make_float2(0.5f, 0.5f);
+    const float2 gm = make_float2(gamma, gamma), kp = make_float2(kappa, kappa);
+    const float tk = __fmul_rn(3.0f, kappa);
+    const float2 tk2 = make_float2(tk, tk);
+    const float2 x2 = mul2(x, x);
+    const float2 y = mul2(gm, add2(x, mul2(kp, mul2(x2, x))));
+    const float2 e = add2(make_float2(hw_exp(__fmul_rn(2.0f, y.x)), hw_exp(__fmul_rn(2.0f, y.y))), one);
+    const float2 th = sub2(one, mul2(two, make_float2(hw_rcp(e.x), hw_rcp(e.y))));
+    const float2 inner = mul2(mul2(sub2(one, mul2(th, th)), gm), add2(one, mul2(tk2, x2)));
+    const float2 d = mul2(half, add2(add2(one, th), mul2(x, inner)));
+    return mul2(d, g);
+}
+
 template <int OP>
 __device__ __forceinline__ float apply_op(float xhat, float y) {
     if constexpr (OP == ACT_OP_MUL) return __fmul_rn(xhat, y);
     else if constexpr (OP == ACT_OP_SILU_BWD) return silu_bwd_f(xhat, y);
     else if constexpr (OP == ACT_OP_GELU_BWD) return gelu_bwd_f(xhat, y);
+    else return xhat;
+}
+template <int OP>
+__device__ __forceinline__ float2 apply_op2(float2 xhat, float2 y) {
+    if constexpr (OP == ACT_OP_MUL) return mul2(xhat, y);
+    else if constexpr (OP == ACT_OP_SILU_BWD) return silu_bwd_f2(xhat, y);
+    else if constexpr (OP == ACT_OP_GELU_BWD) return gelu_bwd_f2(xhat, y);
     else return xhat;
 }
 
