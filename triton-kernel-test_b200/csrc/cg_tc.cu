@@ -497,7 +497,9 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
                 }
             }
             // second operand and consumer op
-            float dot = 0.f;  // OP_SMAX_DOT: P^ . dP over my 32 columns, in column order
+            // OP_SMAX_DOT: P^ . dP over my 32 columns, even and odd columns in two
+            // running sums (packed), added at the end
+            float2 dot2 = make_float2(0.f, 0.f);
             if constexpr (OP != ACT_OP_DECODE) {
                 const uint8_t *box = smem + s * L::STAGE + L::VQ + L::CODES + (h >> 1) * ROWS * 128;
 #pragma unroll
@@ -508,11 +510,9 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
                     for (int e = 0; e < 4; ++e) {
                         float2 &x2 = w[4 * c16 + e];
                         if constexpr (OP == OP_SMAX_DOT) {
-                            dot = __fmaf_rn(x2.x, lo_bf(wd[e]), dot);
-                            dot = __fmaf_rn(x2.y, hi_bf(wd[e]), dot);
+                            dot2 = fma2(x2, make_float2(lo_bf(wd[e]), hi_bf(wd[e])), dot2);
                         } else if constexpr (OP == OP_SMAX_BWD) {
-                            x2 = make_float2(__fmul_rn(__fsub_rn(lo_bf(wd[e]), rsum), x2.x),
-                                             __fmul_rn(__fsub_rn(hi_bf(wd[e]), rsum), x2.y));
+                            x2 = mul2(sub2(make_float2(lo_bf(wd[e]), hi_bf(wd[e])), make_float2(rsum, rsum)), x2);
                         } else {
                             x2 = apply_op2<OP>(x2, make_float2(lo_bf(wd[e]), hi_bf(wd[e])));
                         }
@@ -527,7 +527,7 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
                 if (p.k && (tw.cc == p.ncc - 1 || tile == t_hi - 1)) tc::mbar_arrive(&lqempty[(elq - 1) & 1]);
             }
             if constexpr (OP == OP_SMAX_DOT) {  // the partial goes out, no tile
-                if (rv) p.partials[trow * (4 * p.ncc) + 4 * cc + h] = dot;
+                if (rv) p.partials[trow * (4 * p.ncc) + 4 * cc + h] = __fadd_rn(dot2.x, dot2.y);
                 continue;
             }
 
