@@ -566,13 +566,15 @@ int launch(const actcomp_cg_desc *d, uint16_t *out, int64_t ldo, cudaStream_t st
 }  // namespace act
 
 // Decode through the row kernel, or ACT_E_UNSUPPORTED (before launching) for
-// formats it does not cover: rotation, H not a multiple of 512 (a group of
-// warps must never skip a token block), a rank without the bf16 basis
-// operand, or unaligned low-rank codes.
+// formats it does not cover: rotation, H not a multiple of 128 or below 512
+// (with at least 4 tiles per token block no group of warps skips a block in
+// the middle of its range, which the per-block barrier phases rely on), a
+// rank without the bf16 basis operand, or unaligned low-rank codes.
 int act_cg_decode_rows(const actcomp_cg_desc *d, uint16_t *out, int64_t ldo, cudaStream_t s) {
     using namespace act::cgrow;
     if (d->tokens == 0) return ACT_OK;
-    if (d->wht || d->channels % 512 != 0 || !act::aligned(d->scales, 16)) return ACT_E_UNSUPPORTED;
+    if (d->wht || d->channels % CH != 0 || d->channels < 4 * CH || !act::aligned(d->scales, 16))
+        return ACT_E_UNSUPPORTED;
     if (d->rank && (!d->basis_qb || !act::aligned(d->basis_qb, 16) || !act::aligned(d->lr_codes, 16)))
         return ACT_E_UNSUPPORTED;
     const int rk = d->rank == 0 ? 0 : (d->rank <= 16 ? 16 : (d->rank <= 32 ? 32 : 64));

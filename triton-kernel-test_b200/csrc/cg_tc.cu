@@ -51,6 +51,7 @@ struct DecParams {
     float *partials;
     const float *rowsum;
     int causal;
+    int tri;                   // walk only the tiles on or below the diagonal (causal softmax passes)
     const int8_t *vqs;         // basis_qs tile operand (layout in include/actcomp.h), or null
 };
 
@@ -90,18 +91,33 @@ __device__ __forceinline__ int swz(int r, int c) {
 // Coordinates (channel chunk cc, token block tb, slice b) of consecutive
 // tiles in cc-fastest order, advanced without divisions.  Each CTA walks one
 // contiguous range of tiles, so consecutive tiles share their token block (and
-// its low-rank codes) and read neighbouring code columns.
+// its low-rank codes) and read neighbouring code columns.  tri: only the tiles
+// on or below the diagonal (cc <= tb) of square slices -- causal probabilities
+// are zero above it, so the softmax passes never visit those tiles.
 struct TileWalk {
     int cc, tb, b;
     int ncc, ntb;
-    __device__ TileWalk(int64_t first, int ncc_, int ntb_) : ncc(ncc_), ntb(ntb_) {
-        cc = (int)(first % ncc);
-        const int64_t bt = first / ncc;
-        tb = (int)(bt % ntb);
-        b = (int)(bt / ntb);
+    bool tri;
+    __device__ TileWalk(int64_t first, int ncc_, int ntb_, bool tri_) : ncc(ncc_), ntb(ntb_), tri(tri_) {
+        if (!tri) {
+            cc = (int)(first % ncc);
+            const int64_t bt = first / ncc;
+            tb = (int)(bt % ntb);
+            b = (int)(bt / ntb);
+        } else {  // tile u of a slice: tb = the largest t with t (t + 1) / 2 <= u
+            const int64_t per = (int64_t)ntb * (ntb + 1) / 2;
+            b = (int)(first / per);
+            const int64_t u = first % per;
+            int t = (int)((sqrtf(8.0f * (float)u + 1.0f) - 1.0f) * 0.5f);
+            while ((int64_t)(t + 1) * (t + 2) / 2 <= u) ++t;
+            while (t > 0 && (int64_t)t * (t + 1) / 2 > u) --t;
+            tb = t;
+            cc = (int)(u - (int64_t)t * (t + 1) / 2);
+        }
     }
+    __device__ __forceinline__ int last_cc() const { return tri ? tb : ncc - 1; }
     __device__ __forceinline__ void next() {
-        if (++cc == ncc) {
+        if (++cc > last_cc()) {
             cc = 0;
             if (++tb == ntb) {
                 tb = 0;
@@ -194,7 +210,7 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
             }
             tc::prefetch_tmap(&tm_codes);
             int i = 0, nlq = 0;
-            TileWalk tw(t_lo, p.ncc, p.ntb);
+            TileWalk tw(t_lo, p.ncc, p.ntb, p.tri != 0);
             for (int64_t tile = t_lo; tile < t_hi; ++tile, ++i, tw.next()) {
                 const int s = i % L::S;
                 const uint32_t ph = (i / L::S) & 1;
@@ -234,7 +250,7 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
                 constexpr uint32_t idesc = tc::idesc_i8(ROWS, CH);
                 constexpr tc::Swizzle SW = RB == 32 ? tc::SW_32B : tc::SW_64B;
                 int i = 0, mlq = 0;
-                TileWalk tw(t_lo, p.ncc, p.ntb);
+                TileWalk tw(t_lo, p.ncc, p.ntb, p.tri != 0);
                 for (int64_t tile = t_lo; tile < t_hi; ++tile, ++i, tw.next()) {
                     const int s = i % L::S, b = i % NT;
                     const uint32_t ph = (i / L::S) & 1, bph = (i / NT) & 1;
@@ -257,7 +273,7 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
                     tc::mma_commit(&tfull[b]);
                     tc::mma_commit(&empty[s]);
                     // last tile of this token block in my range: the slot frees once these MMAs complete
-                    if (tw.cc == p.ncc - 1 || tile == t_hi - 1) tc::mma_commit(&lqempty[lslot]);
+                    if (tw.cc == tw.last_cc() || tile == t_hi - 1) tc::mma_commit(&lqempty[lslot]);
                 }
             }
         }
@@ -280,7 +296,7 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
         // load) hides behind PD tiles of work
         constexpr int PD = 4;
         float qsc[PD], qsl[PD], qrs[PD];
-        TileWalk tw(t_lo, p.ncc, p.ntb), nw = tw;  // this tile, the one PD ahead
+        TileWalk tw(t_lo, p.ncc, p.ntb, p.tri != 0), nw = tw;  // this tile, the one PD ahead
         const int gshift = 31 - __clz(p.group);
         auto load_scalars = [&](int64_t tile, const TileWalk &at, float &vsc, float &vsl, float &vrs) {
             vsc = 0.f;
@@ -524,7 +540,7 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
             if (lane == 0) {
                 tc::mbar_arrive(&empty[s]);
                 // last tile of this token block in my range: its outlier slot is free
-                if (p.k && (tw.cc == p.ncc - 1 || tile == t_hi - 1)) tc::mbar_arrive(&lqempty[(elq - 1) & 1]);
+                if (p.k && (tw.cc == tw.last_cc() || tile == t_hi - 1)) tc::mbar_arrive(&lqempty[(elq - 1) & 1]);
             }
             if constexpr (OP == OP_SMAX_DOT) {  // the partial goes out, no tile
                 if (rv) p.partials[trow * (4 * p.ncc) + 4 * cc + h] = __fadd_rn(dot2.x, dot2.y);
@@ -607,7 +623,8 @@ int launch_decode(const actcomp_cg_desc *d, const uint16_t *y, int64_t ldy, uint
     p.idx = d->outlier_idx;
     p.ntb = (int)((T + ROWS - 1) / ROWS);
     p.ncc = (int)((H + CH - 1) / CH);
-    p.ntiles = (int64_t)p.ntb * p.ncc * B;
+    p.tri = is_smax<OP>() && sx.causal && T == H;
+    p.ntiles = p.tri ? (int64_t)p.ntb * (p.ntb + 1) / 2 * B : (int64_t)p.ntb * p.ncc * B;
     p.n32 = (int)((H + 31) / 32);
     p.off_ot = L::OT_OFF;
     p.vqs = d->basis_qs;
@@ -642,13 +659,32 @@ int dispatch_rb(const actcomp_cg_desc *d, const uint16_t *y, int64_t ldy, uint16
 }
 
 // row sums of the softmax partials, in a fixed order (deterministic)
-__global__ void smax_rowsum_kernel(const float *partials, int64_t rows, int per_row, float *rowsum) {
+// (causal: the partials of the tiles on or below the diagonal, the only ones written)
+__global__ void smax_rowsum_kernel(const float *partials, int64_t rows, int per_row, int64_t T, int causal,
+                                   float *rowsum) {
     const int64_t i = (int64_t)blockIdx.x * blockDim.x + threadIdx.x;
     if (i >= rows) return;
     const float *pp = partials + i * per_row;
+    const int n = causal ? 4 * (int)((i % T) / ROWS + 1) : per_row;
     float acc = 0.f;
-    for (int j = 0; j < per_row; ++j) acc = __fadd_rn(acc, pp[j]);
+    for (int j = 0; j < n; ++j) acc = __fadd_rn(acc, pp[j]);
     rowsum[i] = acc;
+}
+
+// dS = 0 above the diagonal blocks of causal probabilities (the tiles the
+// second pass does not visit): columns [128 (t / 128 + 1), T) of every row,
+// eight bf16 per 16-byte store where aligned
+__global__ void smax_zero_upper_kernel(uint16_t *ds, int64_t ld, int64_t T, int64_t rows) {
+    const int64_t stride = (int64_t)gridDim.x * blockDim.x;
+    for (int64_t i = blockIdx.y; i < rows; i += gridDim.y) {
+        const int64_t c0 = ((i % T) / ROWS + 1) * ROWS;
+        if (c0 >= T) continue;
+        uint16_t *row = ds + i * ld;
+        const int64_t n8 = (T - c0) / 8;
+        for (int64_t j = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; j < n8; j += stride)
+            reinterpret_cast<uint4 *>(row + c0)[j] = make_uint4(0u, 0u, 0u, 0u);
+        for (int64_t c = c0 + 8 * n8 + blockIdx.x * blockDim.x + threadIdx.x; c < T; c += stride) row[c] = 0;
+    }
 }
 
 }  // namespace cgtc
@@ -698,8 +734,14 @@ int act_cg_softmax_tc(const actcomp_cg_desc *d, const uint16_t *dp, uint16_t *ds
     int st = d->bits == 4 ? dispatch_rb<4, OP_SMAX_DOT>(d, dp, ld, ds, ld, s, sx)
                           : dispatch_rb<8, OP_SMAX_DOT>(d, dp, ld, ds, ld, s, sx);
     if (st) return st;
-    smax_rowsum_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, s>>>(sx.partials, rows, (int)(4 * ncc), rowsum);
+    const int tri = causal && d->tokens == d->channels;
+    smax_rowsum_kernel<<<(unsigned)((rows + 255) / 256), 256, 0, s>>>(sx.partials, rows, (int)(4 * ncc), d->tokens,
+                                                                      tri, rowsum);
     if ((st = act::launch_status())) return st;
+    if (tri) {
+        smax_zero_upper_kernel<<<dim3(2, (unsigned)(rows < 65535 ? rows : 65535)), 256, 0, s>>>(ds, ld, d->tokens, rows);
+        if ((st = act::launch_status())) return st;
+    }
     return d->bits == 4 ? dispatch_rb<4, OP_SMAX_BWD>(d, dp, ld, ds, ld, s, sx)
                         : dispatch_rb<8, OP_SMAX_BWD>(d, dp, ld, ds, ld, s, sx);
 }
