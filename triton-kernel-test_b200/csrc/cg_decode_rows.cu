@@ -17,7 +17,8 @@
 //               g, g+4, g+8, ... of the range; a thread owns one token row of
 //               the tile and all 128 channels, processed as four 32-channel
 //               pieces: xhat = bf16(fma(I, sL, (u - 2^(b-1)) * s)), outlier
-//               channels verbatim; each warp stores its 32 x 32 piece by TMA.
+//               channels verbatim; each warp stores its 32 rows x 64 channels
+//               (two pieces) with one TMA store.
 // Per-tile costs (waits, scalars, arrivals) are paid once per 128 channels of
 // a row instead of once per 32, and the low-rank term needs no int32 -> float
 // conversion.  Arithmetic is that of oracle/actcomp_oracle.c (cg_decode).
@@ -32,7 +33,7 @@ constexpr int ROWS = 128, CH = 128;
 constexpr int NG = 4;          // epilogue groups = TMEM accumulators (4 x 128 columns)
 constexpr int EW = 4 * NG;     // epilogue warps
 constexpr int THREADS = 64 + 32 * EW;
-constexpr int WST = 32 * 64;   // one output staging buffer: 32 rows x 32 bf16 (64-byte rows)
+constexpr int WSTG = 32 * 128; // one warp's output staging: 32 rows x 64 bf16 (128-byte rows)
 constexpr int PD = 2;          // per-row scalars prefetched PD group tiles ahead
 
 struct RowParams {
@@ -65,7 +66,7 @@ struct RowLayout {
     // returns the shared-memory bytes, or 0 if S < 3 stages would fit
     static int plan(RowParams &p, int nsl) {
         const int lqi = p.rank ? ROWS * p.rank : 0;
-        const int fixed_no_ost = EW * 2 * WST + 2 * LQB + 2 * ((lqi + 1023) & ~1023) + 1024 /*bars*/ +
+        const int fixed_no_ost = EW * WSTG + 2 * LQB + 2 * ((lqi + 1023) & ~1023) + 1024 /*bars*/ +
                                  ((nsl * p.n32 * 8 + 15) & ~15) + 1024 /*align*/;
         const int ostb = (ROWS * p.k * 2 + 15) & ~15;
         for (int ost = p.k ? 1 : 0; ost >= 0; --ost) {
@@ -76,7 +77,7 @@ struct RowLayout {
                     p.ostage = ost;
                     p.ostb = ostb;
                     p.off_stg = S * STAGE;
-                    p.off_lqb = p.off_stg + EW * 2 * WST;
+                    p.off_lqb = p.off_stg + EW * WSTG;
                     p.off_lqi = p.off_lqb + 2 * LQB;
                     p.off_ost = p.off_lqi + 2 * ((lqi + 1023) & ~1023);
                     p.off_bar = p.off_ost + (ost ? 2 * ostb : 0);
@@ -299,7 +300,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         const int ngr = (int)(p.H / p.group);
         const int gshift = 31 - __clz(p.group);
         const uint32_t *otab = reinterpret_cast<const uint32_t *>(smem + p.off_ot);
-        uint8_t *stg = smem + p.off_stg + ew * (2 * WST);
+        uint8_t *stg = smem + p.off_stg + ew * WSTG;
         // outlier table of every slice this range touches: per 32-channel group a
         // mask of its outlier channels and the number of outliers below it (built
         // here, after the producer has started its loads)
@@ -477,11 +478,14 @@ __global__ void __launch_bounds__(THREADS, 1)
                         }
                     }
                 }
-                // store the 32 x 32 piece: buffer k & 1 is free once the store
-                // issued two pieces ago has read it
-                uint8_t *buf = stg + (k & 1) * WST;
-                if (lane == 0) tc::bulk_wait_read<1>();
-                __syncwarp();
+                // pieces 2h and 2h + 1 fill the warp's 32 rows x 64 channels
+                // (128-byte swizzled rows) and leave by one TMA store; the buffer
+                // is free once the previous half's store has read it
+                uint8_t *buf = stg;
+                if ((k & 1) == 0) {
+                    if (lane == 0) tc::bulk_wait_read<0>();
+                    __syncwarp();
+                }
 #pragma unroll
                 for (int c16 = 0; c16 < 4; ++c16) {
                     const int e = 4 * c16;
@@ -490,13 +494,15 @@ __global__ void __launch_bounds__(THREADS, 1)
                     v.y = pack_bf16x2(w[e + 1].x, w[e + 1].y);
                     v.z = pack_bf16x2(w[e + 2].x, w[e + 2].y);
                     v.w = pack_bf16x2(w[e + 3].x, w[e + 3].y);
-                    *reinterpret_cast<uint4 *>(buf + swz<64>(lane, c16)) = v;
+                    *reinterpret_cast<uint4 *>(buf + swz<128>(lane, 4 * (k & 1) + c16)) = v;
                 }
-                tc::fence_proxy_async();
-                __syncwarp();
-                if (lane == 0) {
-                    tc::tma_store_3d(&tm_out, buf, cc * CH + 32 * k, tb * ROWS + 32 * q, b);
-                    tc::bulk_commit();
+                if (k & 1) {
+                    tc::fence_proxy_async();
+                    __syncwarp();
+                    if (lane == 0) {
+                        tc::tma_store_3d(&tm_out, buf, cc * CH + 64 * (k >> 1), tb * ROWS + 32 * q, b);
+                        tc::bulk_commit();
+                    }
                 }
             }
             // the outlier slot of this block: 4 arrivals per tile, plus those of
@@ -528,8 +534,8 @@ int launch(const actcomp_cg_desc *d, uint16_t *out, int64_t ldo, cudaStream_t st
     if ((st = make_map_3d(&m_codes, d->codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rowb, T, B, rowb, T * rowb,
                           L::CODE_ROW, ROWS, BITS == 4 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B)))
         return st;
-    if ((st = make_map_3d(&m_out, out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, H, T, B, ldo, T * ldo, 32, 32,
-                          CU_TENSOR_MAP_SWIZZLE_64B)))
+    if ((st = make_map_3d(&m_out, out, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, H, T, B, ldo, T * ldo, 64, 32,
+                          CU_TENSOR_MAP_SWIZZLE_128B)))
         return st;
     RowParams p{};
     p.T = T;
