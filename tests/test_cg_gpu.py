@@ -51,7 +51,9 @@ CASES = [
     (200, 2048, 32, 16, 4, 64, False),
     (130, 4096, 32, 16, 4, 64, False),
     (96, 5120, 16, 0, 4, 128, True),    # config-3 width
-    (64, 11008, 32, 16, 4, 64, False),  # config-2 SiLU-input width: 86 chunks split unevenly over 4 CTAs
+    (64, 11008, 32, 16, 4, 64, False),  # config-2 SiLU-input width (row encode, 86 chunks per block)
+    (40, 16384, 32, 8, 4, 64, False),   # widest row encode
+    (48, 9216, 16, 0, 4, 128, True),    # rotation above 8192 channels: the cluster encode (72 chunks over 4 CTAs)
     (72, 4096, 64, 7, 8, 32, False),
     # the row decode (H a multiple of 512, no rotation): rank 0 with outliers,
     # rank 16 without, rank 48 with an odd outlier count (unaligned outlier rows

@@ -1,5 +1,5 @@
 // cg_encode_rows.cu -- channel-group encode with whole chunk rows per thread
-// (the encode for unrotated formats with 1024..8192 channels).
+// (the encode for unrotated formats with 1024..16384 channels).
 //
 // One CTA per block of 128 tokens at a time (grid-stride over blocks).  Roles:
 //   warp 0      phase-1 producer: TMA streams X[128 x 64] and V^T[r x 64]
@@ -651,13 +651,13 @@ int launch(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cudaStream_
 
 // Row encode, or ACT_E_UNSUPPORTED (before launching) for formats it does not
 // cover: rotation, a rank outside 16..64, no bf16 basis operand, H outside
-// 1024..8192 or not a multiple of 128 (an epilogue group must have a chunk in
+// 1024..16384 or not a multiple of 128 (an epilogue group must have a chunk in
 // every block, and one CTA covers a block's channels), unaligned scales.
 int act_cg_encode_rows(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cudaStream_t s) {
     using namespace act::cgencr;
     if (d->tokens == 0) return ACT_OK;
     if (d->wht || d->rank < 16 || d->rank > 64 || d->rank % 16 || !d->basis_qb) return ACT_E_UNSUPPORTED;
-    if (d->channels % CH || d->channels < 1024 || d->channels > 8192) return ACT_E_UNSUPPORTED;
+    if (d->channels % CH || d->channels < 1024 || d->channels > 16384) return ACT_E_UNSUPPORTED;
     if (!act::aligned(d->scales, 16) || !act::aligned(d->basis_qb, 16)) return ACT_E_UNSUPPORTED;
     const int rk = d->rank <= 16 ? 16 : (d->rank <= 32 ? 32 : 64);
     if (d->bits == 4) {
