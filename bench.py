@@ -384,6 +384,21 @@ def run_gpu(args):
         components[f"gelu_bwd_fused_{T5}x{H5}"] = {"ms": ms_gelu, "GB/s": gb / (ms_gelu * 1e-3) / 1e9,
                                                   "frac_of_hbm": gb / (ms_gelu * 1e-3) / 1e9 / hbm, "bytes": gb}
         del c5, dy5
+        # config 3: the rotated format -- 128-point Walsh-Hadamard before int4
+        # group-128 quantisation, r = 16, no outlier channels -- on a 32768 x 5120
+        # heavy-tailed activation: encode and decode (the inverse rotation fused)
+        T3, H3, r3 = 2 * T, 5120, 16
+        x3 = synthetic.heavy_tailed_activation(T3, H3, seed=400 + rank, device=dev)
+        b3 = actcomp.Basis.fit(x3[:4096], r3)
+        c3 = actcomp.encode(x3, b3, None, bits=4, group=128, wht=True)
+        ms_e3 = time_steps(lambda: actcomp.encode(x3, b3, None, bits=4, group=128, wht=True), max(3, args.steps // 2),
+                           1, flush, world, clk)
+        ms_d3 = time_steps(lambda: actcomp.decode(c3), max(3, args.steps // 2), 1, flush, world, clk)
+        wb = encode_bytes(T3, H3, 4, 128, r3, 0)
+        for name, ms3 in ((f"encode_wht_{T3}x{H3}", ms_e3), (f"decode_wht_{T3}x{H3}", ms_d3)):
+            components[name] = {"ms": ms3, "GB/s": wb / (ms3 * 1e-3) / 1e9,
+                                "frac_of_hbm": wb / (ms3 * 1e-3) / 1e9 / hbm, "bytes": wb}
+        del x3, b3, c3
         # config 5: softmax backward on compressed causal probabilities P (8, 32, 2048, 2048), one basis for all heads
         Bh, NH, S = 8, 32, 2048
         P = torch.empty((Bh * NH, S, S), dtype=torch.bfloat16, device=dev)
