@@ -53,7 +53,10 @@ CASES = [
     (96, 5120, 16, 0, 4, 128, True),    # config-3 width
     (64, 11008, 32, 16, 4, 64, False),  # config-2 SiLU-input width (row encode, 86 chunks per block)
     (40, 16384, 32, 8, 4, 64, False),   # widest row encode
-    (48, 9216, 16, 0, 4, 128, True),    # rotation above 8192 channels: the cluster encode (72 chunks over 4 CTAs)
+    (32, 20480, 16, 0, 4, 128, True),   # above 16384 channels: the cluster encode (160 chunks over 8 CTAs)
+    # the row encode with the rotation: int8 groups of 64 with outliers, int4 groups of 32
+    (100, 2048, 32, 5, 8, 64, True),
+    (64, 3072, 16, 9, 4, 32, True),
     (72, 4096, 64, 7, 8, 32, False),
     # the row decode (H a multiple of 512, no rotation): rank 0 with outliers,
     # rank 16 without, rank 48 with an odd outlier count (unaligned outlier rows

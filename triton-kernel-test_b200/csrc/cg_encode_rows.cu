@@ -1,5 +1,5 @@
 // cg_encode_rows.cu -- channel-group encode with whole chunk rows per thread
-// (the encode for unrotated formats with 1024..16384 channels).
+// (the encode for 1024..16384 channels, with or without the rotation).
 //
 // One CTA per block of 128 tokens at a time (grid-stride over blocks).  Roles:
 //   warp 0      phase-1 producer: TMA streams X[128 x 64] and V^T[r x 64]
@@ -17,7 +17,10 @@
 //               owns one token row of a chunk and all its 128 channels.  Pass 1,
 //               per 32-channel piece: residual fma(-I, sL, x), outlier channels
 //               copied out and zeroed, piece absmax, residual written back over
-//               I in TMEM.  Pass 2: group scales (one correctly rounded division
+//               I in TMEM.  With the rotation, pass 1 also applies the butterfly
+//               stages 1..16 inside each piece, and stages 32 and 64 then combine
+//               the four pieces eight TMEM columns at a time (oracle stage order).
+//               Pass 2: group scales (one correctly rounded division
 //               each, as the oracle), residual read back, codes packed and staged;
 //               each warp stores its 32 rows of codes with one TMA store and
 //               writes its rows' scales directly.
@@ -119,7 +122,7 @@ __device__ __forceinline__ uint32_t pack_codes(float2 t0, float2 t1, float2 t2, 
     }
 }
 
-template <int BITS, int RK>
+template <int BITS, int RK, bool WHT>
 __global__ void __launch_bounds__(THREADS, 1)
     cg_encode_rows_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_vt,
                           const __grid_constant__ CUtensorMap tm_c, Params p) {
@@ -466,7 +469,23 @@ __global__ void __launch_bounds__(THREADS, 1)
                             }
                         }
                     }
-                    {
+                    if constexpr (WHT) {
+                        // rotation stages m = 1..16 inside the piece, (a, b) -> (a + b, a - b)
+                        // in the oracle's stage order; stages 32 and 64 combine the pieces
+                        // after pass 1, through TMEM
+                        float(&v)[32] = *reinterpret_cast<float(*)[32]>(&w[0]);
+#pragma unroll
+                        for (int m = 1; m < 32; m <<= 1) {
+#pragma unroll
+                            for (int e = 0; e < 32; ++e) {
+                                if (!(e & m)) {
+                                    const float a = v[e], c = v[e + m];
+                                    v[e] = __fadd_rn(a, c);
+                                    v[e + m] = __fsub_rn(a, c);
+                                }
+                            }
+                        }
+                    } else {
                         float a[16];
 #pragma unroll
                         for (int e = 0; e < 16; ++e) a[e] = fmaxf(fabsf(w[e].x), fabsf(w[e].y));
@@ -491,6 +510,41 @@ __global__ void __launch_bounds__(THREADS, 1)
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(&emptyB[s]);
                 tc::tmem_st_wait();
+                if constexpr (WHT) {
+                    // rotation stages 32 (pieces 0-1, 2-3) and 64 (0-2, 1-3), eight
+                    // columns of every piece at a time; piece absmax of the result
+#pragma unroll 1
+                    for (int jj = 0; jj < 4; ++jj) {
+                        uint32_t u0[8], u1[8], u2[8], u3[8];
+                        tc::tmem_ld8(acc + 8 * jj, u0);
+                        tc::tmem_ld8(acc + 32 + 8 * jj, u1);
+                        tc::tmem_ld8(acc + 64 + 8 * jj, u2);
+                        tc::tmem_ld8(acc + 96 + 8 * jj, u3);
+                        tc::tmem_ld_wait();
+#pragma unroll
+                        for (int i = 0; i < 8; ++i) {
+                            const float a0 = __uint_as_float(u0[i]), a1 = __uint_as_float(u1[i]);
+                            const float a2 = __uint_as_float(u2[i]), a3 = __uint_as_float(u3[i]);
+                            const float s01 = __fadd_rn(a0, a1), d01 = __fsub_rn(a0, a1);
+                            const float s23 = __fadd_rn(a2, a3), d23 = __fsub_rn(a2, a3);
+                            const float o0 = __fadd_rn(s01, s23), o1 = __fadd_rn(d01, d23);
+                            const float o2 = __fsub_rn(s01, s23), o3 = __fsub_rn(d01, d23);
+                            am0 = fmaxf(am0, fabsf(o0));
+                            am1 = fmaxf(am1, fabsf(o1));
+                            am2 = fmaxf(am2, fabsf(o2));
+                            am3 = fmaxf(am3, fabsf(o3));
+                            u0[i] = __float_as_uint(o0);
+                            u1[i] = __float_as_uint(o1);
+                            u2[i] = __float_as_uint(o2);
+                            u3[i] = __float_as_uint(o3);
+                        }
+                        tc::tmem_st8(acc + 8 * jj, u0);
+                        tc::tmem_st8(acc + 32 + 8 * jj, u1);
+                        tc::tmem_st8(acc + 64 + 8 * jj, u2);
+                        tc::tmem_st8(acc + 96 + 8 * jj, u3);
+                    }
+                    tc::tmem_st_wait();
+                }
                 // ---- pass 2: group scales (one correctly rounded division each), codes
                 float scv[4], rsv[4];
                 {
@@ -587,7 +641,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
-template <int BITS, int RK>
+template <int BITS, int RK, bool WHT>
 int launch(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cudaStream_t stream) {
     using L = Layout<BITS, RK>;
     const int64_t T = d->tokens, H = d->channels, B = d->batch;
@@ -640,7 +694,7 @@ int launch(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cudaStream_
         else return ACT_E_UNSUPPORTED;
     }
     const int smem = L::plan(p, na, nb, alias, k, ostage);
-    auto kern = cg_encode_rows_kernel<BITS, RK>;
+    auto kern = cg_encode_rows_kernel<BITS, RK, WHT>;
     ACT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     kern<<<p.ngrid, THREADS, smem, stream>>>(m_x, m_vt, m_c, p);
     return launch_status();
@@ -650,22 +704,27 @@ int launch(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cudaStream_
 }  // namespace act
 
 // Row encode, or ACT_E_UNSUPPORTED (before launching) for formats it does not
-// cover: rotation, a rank outside 16..64, no bf16 basis operand, H outside
+// cover: a rank outside 16..64, no bf16 basis operand, H outside
 // 1024..16384 or not a multiple of 128 (an epilogue group must have a chunk in
 // every block, and one CTA covers a block's channels), unaligned scales.
 int act_cg_encode_rows(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cudaStream_t s) {
     using namespace act::cgencr;
     if (d->tokens == 0) return ACT_OK;
-    if (d->wht || d->rank < 16 || d->rank > 64 || d->rank % 16 || !d->basis_qb) return ACT_E_UNSUPPORTED;
+    if (d->rank < 16 || d->rank > 64 || d->rank % 16 || !d->basis_qb) return ACT_E_UNSUPPORTED;
     if (d->channels % CH || d->channels < 1024 || d->channels > 16384) return ACT_E_UNSUPPORTED;
     if (!act::aligned(d->scales, 16) || !act::aligned(d->basis_qb, 16)) return ACT_E_UNSUPPORTED;
     const int rk = d->rank <= 16 ? 16 : (d->rank <= 32 ? 32 : 64);
+#define ACT_ENCR_RK(B, W)                                     \
+    do {                                                      \
+        if (rk == 16) return launch<B, 16, W>(d, x, ldx, s);  \
+        if (rk == 32) return launch<B, 32, W>(d, x, ldx, s);  \
+        return launch<B, 64, W>(d, x, ldx, s);                \
+    } while (0)
     if (d->bits == 4) {
-        if (rk == 16) return launch<4, 16>(d, x, ldx, s);
-        if (rk == 32) return launch<4, 32>(d, x, ldx, s);
-        return launch<4, 64>(d, x, ldx, s);
+        if (d->wht) ACT_ENCR_RK(4, true);
+        ACT_ENCR_RK(4, false);
     }
-    if (rk == 16) return launch<8, 16>(d, x, ldx, s);
-    if (rk == 32) return launch<8, 32>(d, x, ldx, s);
-    return launch<8, 64>(d, x, ldx, s);
+    if (d->wht) ACT_ENCR_RK(8, true);
+    ACT_ENCR_RK(8, false);
+#undef ACT_ENCR_RK
 }
