@@ -71,7 +71,7 @@ extern "C" int actcomp_clear_device_error(void *stream) {
 }
 
 // Decode: the row kernel where it covers the format, else the piece kernel
-// (rotation, narrow H); both give the same bits.
+// (narrow H); both give the same bits.
 static int decode_tc(const actcomp_cg_desc *d, uint16_t *xhat, int64_t ldo, cudaStream_t s) {
     const int st = act_cg_decode_rows(d, xhat, ldo, s);
     if (st != ACT_E_UNSUPPORTED) return st;

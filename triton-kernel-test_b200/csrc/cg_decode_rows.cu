@@ -1,5 +1,5 @@
 // cg_decode_rows.cu -- tensor-core decode of the channel-group format with
-// whole tile rows per thread (the decode for unrotated formats).
+// whole tile rows per thread.
 //
 // One tile = 128 tokens x 128 channels; each CTA walks one contiguous range
 // of tiles (persistent, one CTA per SM).  Roles:
@@ -19,6 +19,10 @@
 //               pieces: xhat = bf16(fma(I, sL, (u - 2^(b-1)) * s)), outlier
 //               channels verbatim; each warp stores its 32 rows x 64 channels
 //               (two pieces) with one TMA store.
+// Rotated formats run two epilogue groups (8 warps, up to 204 registers per
+// thread): a thread dequantises its whole 128-channel row, applies the seven
+// butterfly stages in registers and scales by 1/128, then adds the low-rank
+// term piece by piece.
 // Per-tile costs (waits, scalars, arrivals) are paid once per 128 channels of
 // a row instead of once per 32, and the low-rank term needs no int32 -> float
 // conversion.  Arithmetic is that of oracle/actcomp_oracle.c (cg_decode).
@@ -30,9 +34,17 @@ namespace act {
 namespace cgrow {
 
 constexpr int ROWS = 128, CH = 128;
-constexpr int NG = 4;          // epilogue groups = TMEM accumulators (4 x 128 columns)
-constexpr int EW = 4 * NG;     // epilogue warps
-constexpr int THREADS = 64 + 32 * EW;
+// Epilogue geometry: NG groups of four warps = NG TMEM accumulators of 128
+// columns.  Unrotated: 4 groups, a thread works on 32 channels at a time.
+// Rotated: 2 groups, so that a thread (up to 204 registers at 320 threads)
+// holds its whole 128-channel row for the seven butterfly stages.
+template <bool WHT>
+struct Geo {
+    static constexpr int NG = WHT ? 2 : 4;
+    static constexpr int EW = 4 * NG;
+    static constexpr int THREADS = 64 + 32 * EW;
+};
+
 constexpr int WSTG = 32 * 128; // one warp's output staging: 32 rows x 64 bf16 (128-byte rows)
 constexpr int PD = 2;          // per-row scalars prefetched PD group tiles ahead
 
@@ -64,7 +76,7 @@ struct RowLayout {
     static constexpr int STAGE = VQ + CODES;
     static constexpr int LQB = RK ? ROWS * LB : 0;      // bf16 low-rank operand of a token block
     // returns the shared-memory bytes, or 0 if S < 3 stages would fit
-    static int plan(RowParams &p, int nsl) {
+    static int plan(RowParams &p, int nsl, int EW) {
         const int lqi = p.rank ? ROWS * p.rank : 0;
         const int fixed_no_ost = EW * WSTG + 2 * LQB + 2 * ((lqi + 1023) & ~1023) + 1024 /*bars*/ +
                                  ((nsl * p.n32 * 8 + 15) & ~15) + 1024 /*align*/;
@@ -133,11 +145,52 @@ __device__ __forceinline__ uint32_t ost_bytes(const RowParams &p, int tb, int b,
     return (uint32_t)bytes;
 }
 
-template <int BITS, int RK>
-__global__ void __launch_bounds__(THREADS, 1)
+// Residual of piece k (32 channels) of row r of a tile's codes:
+// w = (u - 2^(b-1)) * s, the code u converted exactly to 2^23 + u by one byte
+// permute against 0x4B000000 (int4 codes split into even and odd channels first).
+template <int BITS, int OFF>
+__device__ __forceinline__ void dequant_piece(const uint8_t *ct, int r, int k, float sc, float2 (&w)[16]) {
+    uint32_t wd[BITS];
+    if constexpr (BITS == 4) {
+        const uint4 v = *reinterpret_cast<const uint4 *>(ct + swz<64>(r, k));
+        wd[0] = v.x; wd[1] = v.y; wd[2] = v.z; wd[3] = v.w;
+    } else {
+        const uint4 v0 = *reinterpret_cast<const uint4 *>(ct + swz<128>(r, 2 * k));
+        const uint4 v1 = *reinterpret_cast<const uint4 *>(ct + swz<128>(r, 2 * k + 1));
+        wd[0] = v0.x; wd[1] = v0.y; wd[2] = v0.z; wd[3] = v0.w;
+        wd[4] = v1.x; wd[5] = v1.y; wd[6] = v1.z; wd[7] = v1.w;
+    }
+    const float2 sc2 = make_float2(sc, sc);
+    constexpr float UOFF = 8388608.0f + (float)OFF;
+    const float2 uoff2 = make_float2(UOFF, UOFF);
+    constexpr uint32_t K4B = 0x4B000000u;
+#pragma unroll
+    for (int wi = 0; wi < BITS; ++wi) {
+        if constexpr (BITS == 4) {
+            const uint32_t ev = wd[wi] & 0x0F0F0F0Fu, od = (wd[wi] >> 4) & 0x0F0F0F0Fu;
+#pragma unroll
+            for (int m = 0; m < 4; ++m) {
+                const float2 f = make_float2(__uint_as_float(__byte_perm(ev, K4B, 0x7540u | m)),
+                                             __uint_as_float(__byte_perm(od, K4B, 0x7540u | m)));
+                w[4 * wi + m] = mul2(sub2(f, uoff2), sc2);
+            }
+        } else {
+#pragma unroll
+            for (int m = 0; m < 2; ++m) {
+                const float2 f = make_float2(__uint_as_float(__byte_perm(wd[wi], K4B, 0x7540u | (2 * m))),
+                                             __uint_as_float(__byte_perm(wd[wi], K4B, 0x7541u + 2 * m)));
+                w[2 * wi + m] = mul2(sub2(f, uoff2), sc2);
+            }
+        }
+    }
+}
+
+template <int BITS, int RK, bool WHT>
+__global__ void __launch_bounds__(Geo<WHT>::THREADS, 1)
     cg_decode_rows_kernel(const __grid_constant__ CUtensorMap tm_codes, const __grid_constant__ CUtensorMap tm_out,
                           RowParams p) {
     using L = RowLayout<BITS, RK>;
+    constexpr int NG = Geo<WHT>::NG, EW = Geo<WHT>::EW;
     constexpr int LB = L::LB;
     constexpr int off = 1 << (BITS - 1);
     extern __shared__ uint8_t smem_raw[];
@@ -397,10 +450,47 @@ __global__ void __launch_bounds__(THREADS, 1)
             const uint8_t *ct = smem + s * L::STAGE + L::VQ;
             const uint32_t *ot = otab + 2 * ((int64_t)(b - b_lo) * p.n32 + (((int64_t)cc * CH) >> 5));
 
-#pragma unroll 1
+            // rotated formats: the whole row's residual, dequantised and rotated
+            // back (stages 1..64 in the oracle's order, then * 1/128) before the
+            // low-rank term is added piece by piece
+            float2 wr[WHT ? 64 : 1];
+            if constexpr (WHT) {
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                    const float sc = k == 0 ? sc4.x : (k == 1 ? sc4.y : (k == 2 ? sc4.z : sc4.w));
+                    dequant_piece<BITS, off>(ct, r, k, sc, *reinterpret_cast<float2(*)[16]>(&wr[16 * k]));
+                }
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&empty[s]);  // the codes of this stage have been read
+#pragma unroll
+                for (int i = 0; i < 64; ++i) {
+                    const float a = wr[i].x, c = wr[i].y;
+                    wr[i] = make_float2(__fadd_rn(a, c), __fsub_rn(a, c));
+                }
+#pragma unroll
+                for (int m2 = 1; m2 < 64; m2 <<= 1) {  // stage m = 2 * m2 on element pairs
+#pragma unroll
+                    for (int i = 0; i < 64; ++i) {
+                        if (!(i & m2)) {
+                            const float2 a = wr[i], c = wr[i + m2];
+                            wr[i] = add2(a, c);
+                            wr[i + m2] = sub2(a, c);
+                        }
+                    }
+                }
+                const float2 inv = make_float2(0.0078125f, 0.0078125f);
+#pragma unroll
+                for (int i = 0; i < 64; ++i) wr[i] = mul2(wr[i], inv);
+            }
+#pragma unroll(WHT ? 4 : 1)
             for (int k = 0; k < 4; ++k) {
                 uint32_t I[32];
                 if constexpr (RK > 0) tc::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + g * CH + 32 * k, I);
+                float2 w[16];
+                if constexpr (WHT) {
+#pragma unroll
+                    for (int e = 0; e < 16; ++e) w[e] = wr[16 * k + e];
+                } else {
                 uint32_t wd[BITS];
                 if constexpr (BITS == 4) {
                     const uint4 v = *reinterpret_cast<const uint4 *>(ct + swz<64>(r, k));
@@ -416,7 +506,6 @@ __global__ void __launch_bounds__(THREADS, 1)
                     if (lane == 0) tc::mbar_arrive(&empty[s]);
                 }
                 const float sc = k == 0 ? sc4.x : (k == 1 ? sc4.y : (k == 2 ? sc4.z : sc4.w));
-                float2 w[16];
                 {
                     const float2 sc2 = make_float2(sc, sc);
                     constexpr float UOFF = 8388608.0f + (float)off;
@@ -444,6 +533,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                         }
                     }
                 }
+                }  // unrotated
                 if constexpr (RK > 0) {
                     tc::tmem_ld_wait();
                     const float2 sl2 = make_float2(sl, sl);
@@ -524,7 +614,7 @@ __global__ void __launch_bounds__(THREADS, 1)
     }
 }
 
-template <int BITS, int RK>
+template <int BITS, int RK, bool WHT>
 int launch(const actcomp_cg_desc *d, uint16_t *out, int64_t ldo, cudaStream_t stream) {
     using L = RowLayout<BITS, RK>;
     const int64_t T = d->tokens, H = d->channels, B = d->batch;
@@ -560,11 +650,11 @@ int launch(const actcomp_cg_desc *d, uint16_t *out, int64_t ldo, cudaStream_t st
     const int64_t tps = (int64_t)p.ntb * p.ncc;
     const int64_t span = p.tq + (p.trem ? 1 : 0);
     const int nsl = (int)((span - 1) / tps + 2 < B ? (span - 1) / tps + 2 : B);
-    const int smem = L::plan(p, nsl);
+    const int smem = L::plan(p, nsl, Geo<WHT>::EW);
     if (!smem) return ACT_E_UNSUPPORTED;
-    auto kern = cg_decode_rows_kernel<BITS, RK>;
+    auto kern = cg_decode_rows_kernel<BITS, RK, WHT>;
     ACT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-    kern<<<grid, THREADS, smem, stream>>>(m_codes, m_out, p);
+    kern<<<grid, Geo<WHT>::THREADS, smem, stream>>>(m_codes, m_out, p);
     return launch_status();
 }
 
@@ -572,30 +662,32 @@ int launch(const actcomp_cg_desc *d, uint16_t *out, int64_t ldo, cudaStream_t st
 }  // namespace act
 
 // Decode through the row kernel, or ACT_E_UNSUPPORTED (before launching) for
-// formats it does not cover: rotation, H not a multiple of 128 or below 512
+// formats it does not cover: H not a multiple of 128 or below 512
 // (with at least 4 tiles per token block no group of warps skips a block in
 // the middle of its range, which the per-block barrier phases rely on), a
 // rank without the bf16 basis operand, or unaligned low-rank codes.
 int act_cg_decode_rows(const actcomp_cg_desc *d, uint16_t *out, int64_t ldo, cudaStream_t s) {
     using namespace act::cgrow;
     if (d->tokens == 0) return ACT_OK;
-    if (d->wht || d->channels % CH != 0 || d->channels < 4 * CH || !act::aligned(d->scales, 16))
+    if (d->channels % CH != 0 || d->channels < 4 * CH || !act::aligned(d->scales, 16))
         return ACT_E_UNSUPPORTED;
     if (d->rank && (!d->basis_qb || !act::aligned(d->basis_qb, 16) || !act::aligned(d->lr_codes, 16)))
         return ACT_E_UNSUPPORTED;
     const int rk = d->rank == 0 ? 0 : (d->rank <= 16 ? 16 : (d->rank <= 32 ? 32 : 64));
+#define ACT_DECR(B, W)                                       \
+    do {                                                     \
+        switch (rk) {                                        \
+            case 0: return launch<B, 0, W>(d, out, ldo, s);   \
+            case 16: return launch<B, 16, W>(d, out, ldo, s); \
+            case 32: return launch<B, 32, W>(d, out, ldo, s); \
+            default: return launch<B, 64, W>(d, out, ldo, s); \
+        }                                                    \
+    } while (0)
     if (d->bits == 4) {
-        switch (rk) {
-            case 0: return launch<4, 0>(d, out, ldo, s);
-            case 16: return launch<4, 16>(d, out, ldo, s);
-            case 32: return launch<4, 32>(d, out, ldo, s);
-            default: return launch<4, 64>(d, out, ldo, s);
-        }
+        if (d->wht) ACT_DECR(4, true);
+        ACT_DECR(4, false);
     }
-    switch (rk) {
-        case 0: return launch<8, 0>(d, out, ldo, s);
-        case 16: return launch<8, 16>(d, out, ldo, s);
-        case 32: return launch<8, 32>(d, out, ldo, s);
-        default: return launch<8, 64>(d, out, ldo, s);
-    }
+    if (d->wht) ACT_DECR(8, true);
+    ACT_DECR(8, false);
+#undef ACT_DECR
 }
