@@ -91,7 +91,7 @@ extern "C" int actcomp_cg_encode(const actcomp_cg_desc *d, const uint16_t *x, in
     if (st) return st;
     if ((st = check_rows(x, ldx, d->channels))) return st;
     if (d->rank) ACT_CHECK(d->basis_t && aligned(d->basis_t, 16), ACT_E_ALIGN);
-    // the row kernel, else the piece kernel (rotation, wide or narrow H), else
+    // the row kernel, else the piece kernel (above 16384 or below 1024 channels), else
     // the CUDA-core encode: each declines (ACT_E_UNSUPPORTED, before
     // launching) what it does not cover, and all compute the same codes
     st = act_cg_encode_rows(d, x, ldx, as_stream(stream));
