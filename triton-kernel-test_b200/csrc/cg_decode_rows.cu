@@ -19,7 +19,7 @@
 //               pieces: xhat = bf16(fma(I, sL, (u - 2^(b-1)) * s)), outlier
 //               channels verbatim; each warp stores its 32 rows x 64 channels
 //               (two pieces) with one TMA store.
-// Rotated formats run two epilogue groups (8 warps, up to 204 registers per
+// Rotated formats run two epilogue groups (8 warps, up to 168 registers per
 // thread): a thread dequantises its whole 128-channel row, applies the seven
 // butterfly stages in registers and scales by 1/128, then adds the low-rank
 // term piece by piece.
@@ -36,8 +36,9 @@ namespace cgrow {
 constexpr int ROWS = 128, CH = 128;
 // Epilogue geometry: NG groups of four warps = NG TMEM accumulators of 128
 // columns.  Unrotated: 4 groups, a thread works on 32 channels at a time.
-// Rotated: 2 groups, so that a thread (up to 204 registers at 320 threads)
-// holds its whole 128-channel row for the seven butterfly stages.
+// Rotated: 2 groups, so that a thread (up to 168 registers: 10 warps put three
+// on some SM sub-partitions) holds its whole 128-channel row for the seven
+// butterfly stages; the row still spills a few dozen registers.
 template <bool WHT>
 struct Geo {
     static constexpr int NG = WHT ? 2 : 4;
