@@ -59,7 +59,7 @@ struct Params {
     int na, nb;       // ring stages
     int ngs;          // 64-channel groups of H (outlier table entries)
     int ostage;       // outlier values staged per block (else written directly)
-    int off_ringB, off_lqt, off_bar, off_stg, off_ot, off_ost;
+    int off_ringB, off_lqt, off_bar, off_stg, off_ot, off_ost, off_sv;
 };
 
 template <int BITS, int RK>
@@ -84,7 +84,10 @@ struct Layout {
         p.off_stg = p.off_bar + 1024;
         p.off_ot = p.off_stg + EW * WSTG;
         p.off_ost = p.off_ot + ((p.ngs * 12 + 15) & ~15);
-        return p.off_ost + (ostage ? ((ROWS * k * 2 + 15) & ~15) : 0) + 1024;
+        // group 0's per-warp copies of the slice's basis scales (4 x 64 floats),
+        // then the low-rank scales of the last two blocks (2 x 128 floats)
+        p.off_sv = p.off_ost + (ostage ? ((ROWS * k * 2 + 15) & ~15) : 0);
+        return p.off_sv + 4 * 64 * 4 + 2 * ROWS * 4 + 1024;
     }
 };
 
@@ -316,8 +319,13 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int nrows = (int)((p.T - (int64_t)tb * ROWS) < ROWS ? (p.T - (int64_t)tb * ROWS) : ROWS);
             const int ls = nb & 1;
             float sl = 0.f;
+            float *svw = reinterpret_cast<float *>(smem + p.off_sv) + 64 * (warp & 3);  // group 0 only
+            float *slr = reinterpret_cast<float *>(smem + p.off_sv) + 4 * 64;       // [2][128]
             if (g == 0 && ok) do {
                 // ---- projection -> per-token low-rank codes (group 0: one token row per thread)
+                // the slice's basis scales into this warp's copy while the projection streams
+                for (int e = lane; e < r; e += 32) svw[e] = __ldg(p.basis_scale + (int64_t)b * r + e);
+                __syncwarp();
                 if (!(ok = tc::mbar_wait(lfull, nb & 1, abort))) break;
                 tc::tc_fence_after();
                 float Lr[RK];
@@ -340,7 +348,7 @@ __global__ void __launch_bounds__(THREADS, 1)
 #pragma unroll
                 for (int e = 0; e < RK; ++e) {
                     if (e < r) {
-                        Lr[e] = __fmul_rn(Lr[e], __ldg(p.basis_scale + (int64_t)b * r + e));
+                        Lr[e] = __fmul_rn(Lr[e], svw[e]);
                         amax = fmaxf(amax, fabsf(Lr[e]));
                     }
                 }
@@ -378,6 +386,9 @@ __global__ void __launch_bounds__(THREADS, 1)
                         if (4 * e < r) dst[e] = lw[e];
                     p.lrs[trow] = sl;
                 }
+                // for groups 1 and 2 (slot nb & 1 is rewritten for block nb + 2, after
+                // every group has passed its first chunk of block nb)
+                slr[ls * ROWS + row] = sl;
                 tc::fence_proxy_async();
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(&lqready[ls]);
@@ -406,7 +417,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                 if (j % NGR != g || !ok) continue;
                 if (!have_sl) {  // the block's low-rank scales are written (group 0)
                     if (!(ok = tc::mbar_wait(&lqready[ls], (nb >> 1) & 1, abort))) continue;
-                    sl = rv ? __ldcg(p.lrs + trow) : 0.f;
+                    sl = slr[ls * ROWS + row];
                     have_sl = true;
                 }
                 const int s = j % NB;
