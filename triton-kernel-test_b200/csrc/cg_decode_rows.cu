@@ -36,15 +36,23 @@ namespace cgrow {
 constexpr int ROWS = 128, CH = 128;
 // Epilogue geometry: NG groups of four warps = NG TMEM accumulators of 128
 // columns.  Unrotated: 4 groups, a thread works on 32 channels at a time.
-// Rotated: 2 groups, so that a thread (up to 168 registers: 10 warps put three
-// on some SM sub-partitions) holds its whole 128-channel row for the seven
-// butterfly stages; the row still spills a few dozen registers.
+// Rotated: 2 groups (up to 168 registers a thread: 10 warps put three on some
+// SM sub-partitions).  Stages 1..32 of the 128-point transform stay inside each
+// 64-channel half of a row, so a thread rotates one half at a time in registers
+// and parks it in its warp's 128 TMEM scratch columns (after the accumulators),
+// where stage 64 runs 8 columns at a time: 64 values live instead of the row.
 template <bool WHT>
 struct Geo {
     static constexpr int NG = WHT ? 2 : 4;
     static constexpr int EW = 4 * NG;
     static constexpr int THREADS = 64 + 32 * EW;
 };
+// TMEM columns a block allocates: the accumulators, plus 128 scratch columns per
+// group for the rotated formats
+template <int RK, bool WHT>
+constexpr uint32_t tmem_cols() {
+    return WHT ? (RK ? 512u : 256u) : (RK ? 4u * 128u : 0u);
+}
 
 constexpr int WSTG = 32 * 128; // one warp's output staging: 32 rows x 64 bf16 (128-byte rows)
 constexpr int PD = 2;          // per-row scalars prefetched PD group tiles ahead
@@ -186,6 +194,28 @@ __device__ __forceinline__ void dequant_piece(const uint8_t *ct, int r, int k, f
     }
 }
 
+// Stages 1..32 of the oracle's butterfly order on one 64-channel half held as
+// 32 channel pairs: stage 1 inside each pair, stage 2 * m2 between pairs i and
+// i + m2.
+__device__ __forceinline__ void wht_half(float2 (&w)[32]) {
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+        const float a = w[i].x, c = w[i].y;
+        w[i] = make_float2(__fadd_rn(a, c), __fsub_rn(a, c));
+    }
+#pragma unroll
+    for (int m2 = 1; m2 < 32; m2 <<= 1) {
+#pragma unroll
+        for (int i = 0; i < 32; ++i) {
+            if (!(i & m2)) {
+                const float2 a = w[i], c = w[i + m2];
+                w[i] = add2(a, c);
+                w[i + m2] = sub2(a, c);
+            }
+        }
+    }
+}
+
 template <int BITS, int RK, bool WHT>
 __global__ void __launch_bounds__(Geo<WHT>::THREADS, 1)
     cg_decode_rows_kernel(const __grid_constant__ CUtensorMap tm_codes, const __grid_constant__ CUtensorMap tm_out,
@@ -236,14 +266,15 @@ __global__ void __launch_bounds__(Geo<WHT>::THREADS, 1)
         *abort = 0;
         tc::fence_mbar_init();
     }
-    if (RK && warp == 1) {
-        tc::tmem_alloc(tmem_slot, NG * CH);
+    constexpr uint32_t TCOLS = tmem_cols<RK, WHT>();
+    if (TCOLS && warp == 1) {
+        tc::tmem_alloc(tmem_slot, TCOLS);
         tc::tmem_relinquish();
     }
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
-    const uint32_t tmem = RK ? *tmem_slot : 0;
+    const uint32_t tmem = TCOLS ? *tmem_slot : 0;
 
     if (warp == 0) {
         // ------------------------------------------------------------ producer
@@ -451,46 +482,62 @@ __global__ void __launch_bounds__(Geo<WHT>::THREADS, 1)
             const uint8_t *ct = smem + s * L::STAGE + L::VQ;
             const uint32_t *ot = otab + 2 * ((int64_t)(b - b_lo) * p.n32 + (((int64_t)cc * CH) >> 5));
 
-            // rotated formats: the whole row's residual, dequantised and rotated
-            // back (stages 1..64 in the oracle's order, then * 1/128) before the
-            // low-rank term is added piece by piece
-            float2 wr[WHT ? 64 : 1];
+            // rotated formats: the row's residual dequantised and rotated back in
+            // the oracle's order (stages 1, 2, ..., 64, then * 1/128).  Each
+            // 64-channel half takes stages 1..32 in registers and is parked in
+            // this warp's 128 TMEM scratch columns; stage 64 and the scaling run
+            // there 8 columns at a time, and the pieces come back like I.
+            const uint32_t scr = tmem + ((uint32_t)(q * 32) << 16) + (RK ? NG * CH : 0) + CH * g;
             if constexpr (WHT) {
 #pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                    const float sc = k == 0 ? sc4.x : (k == 1 ? sc4.y : (k == 2 ? sc4.z : sc4.w));
-                    dequant_piece<BITS, off>(ct, r, k, sc, *reinterpret_cast<float2(*)[16]>(&wr[16 * k]));
-                }
-                __syncwarp();
-                if (lane == 0) tc::mbar_arrive(&empty[s]);  // the codes of this stage have been read
-#pragma unroll
-                for (int i = 0; i < 64; ++i) {
-                    const float a = wr[i].x, c = wr[i].y;
-                    wr[i] = make_float2(__fadd_rn(a, c), __fsub_rn(a, c));
-                }
-#pragma unroll
-                for (int m2 = 1; m2 < 64; m2 <<= 1) {  // stage m = 2 * m2 on element pairs
-#pragma unroll
-                    for (int i = 0; i < 64; ++i) {
-                        if (!(i & m2)) {
-                            const float2 a = wr[i], c = wr[i + m2];
-                            wr[i] = add2(a, c);
-                            wr[i + m2] = sub2(a, c);
-                        }
+                for (int h = 0; h < 2; ++h) {
+                    float2 wh[32];
+                    dequant_piece<BITS, off>(ct, r, 2 * h, h ? sc4.z : sc4.x,
+                                             *reinterpret_cast<float2(*)[16]>(&wh[0]));
+                    dequant_piece<BITS, off>(ct, r, 2 * h + 1, h ? sc4.w : sc4.y,
+                                             *reinterpret_cast<float2(*)[16]>(&wh[16]));
+                    if (h) {
+                        __syncwarp();
+                        if (lane == 0) tc::mbar_arrive(&empty[s]);  // the codes of this stage have been read
                     }
+                    wht_half(wh);
+                    tc::tmem_st32(scr + 64 * h, *reinterpret_cast<const uint32_t(*)[32]>(&wh[0]));
+                    tc::tmem_st32(scr + 64 * h + 32, *reinterpret_cast<const uint32_t(*)[32]>(&wh[16]));
                 }
+                tc::tmem_st_wait();
                 const float2 inv = make_float2(0.0078125f, 0.0078125f);
 #pragma unroll
-                for (int i = 0; i < 64; ++i) wr[i] = mul2(wr[i], inv);
+                for (int c8 = 0; c8 < 8; ++c8) {  // stage 64: channel c of the first half with c + 64
+                    uint32_t A[8], C[8];
+                    tc::tmem_ld8(scr + 8 * c8, A);
+                    tc::tmem_ld8(scr + 64 + 8 * c8, C);
+                    tc::tmem_ld_wait();
+#pragma unroll
+                    for (int e = 0; e < 4; ++e) {
+                        const float2 a = make_float2(__uint_as_float(A[2 * e]), __uint_as_float(A[2 * e + 1]));
+                        const float2 c = make_float2(__uint_as_float(C[2 * e]), __uint_as_float(C[2 * e + 1]));
+                        const float2 lo = mul2(add2(a, c), inv), hi = mul2(sub2(a, c), inv);
+                        A[2 * e] = __float_as_uint(lo.x);
+                        A[2 * e + 1] = __float_as_uint(lo.y);
+                        C[2 * e] = __float_as_uint(hi.x);
+                        C[2 * e + 1] = __float_as_uint(hi.y);
+                    }
+                    tc::tmem_st8(scr + 8 * c8, A);
+                    tc::tmem_st8(scr + 64 + 8 * c8, C);
+                }
+                tc::tmem_st_wait();
             }
 #pragma unroll(WHT ? 4 : 1)
             for (int k = 0; k < 4; ++k) {
                 uint32_t I[32];
                 if constexpr (RK > 0) tc::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + g * CH + 32 * k, I);
                 float2 w[16];
-                if constexpr (WHT) {
+                if constexpr (WHT) {  // the piece, back from the scratch columns
+                    uint32_t F[32];
+                    tc::tmem_ld32(scr + 32 * k, F);
+                    tc::tmem_ld_wait();
 #pragma unroll
-                    for (int e = 0; e < 16; ++e) w[e] = wr[16 * k + e];
+                    for (int e = 0; e < 16; ++e) w[e] = make_float2(__uint_as_float(F[2 * e]), __uint_as_float(F[2 * e + 1]));
                 } else {
                 uint32_t wd[BITS];
                 if constexpr (BITS == 4) {
@@ -609,9 +656,9 @@ __global__ void __launch_bounds__(Geo<WHT>::THREADS, 1)
     }
     tc::tc_fence_before();
     __syncthreads();
-    if (RK && warp == 1) {
+    if (TCOLS && warp == 1) {
         tc::tc_fence_after();
-        tc::tmem_dealloc(tmem, NG * CH);
+        tc::tmem_dealloc(tmem, TCOLS);
     }
 }
 
