@@ -58,6 +58,10 @@ CASES = [
     (100, 2048, 32, 5, 8, 64, True),
     (64, 3072, 16, 9, 4, 32, True),
     (72, 4096, 64, 7, 8, 32, False),
+    # the rotated row decode: no low rank (its TMEM scratch columns start at 0)
+    # with int8 codes and outliers; several token blocks per CTA range
+    (150, 1024, 0, 4, 8, 64, True),
+    (3000, 1024, 16, 3, 4, 128, True),
     # the row decode (H a multiple of 512, no rotation): rank 0 with outliers,
     # rank 16 without, rank 48 with an odd outlier count (unaligned outlier rows
     # in the partial last token block), several token blocks per CTA range
