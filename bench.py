@@ -457,13 +457,14 @@ def run_gpu(args):
     # streamed in token chunks (every token row is encoded on its own, so chunking changes no bit):
     # chunk i's H2D, chunk i-1's encode + decode and chunk i-2's D2H run on three streams, so that
     # the two PCIe directions overlap
-    E2E_CHUNKS = 8
+    E2E_CHUNKS = 9
     xh_host = torch.empty((T, H), dtype=torch.bfloat16, pin_memory=True)
     x_host = x.cpu().pin_memory()
     x_dev = torch.empty_like(x)
     xd_dev = torch.empty_like(x)
     s_in, s_cmp, s_out = torch.cuda.Stream(), torch.cuda.Stream(), torch.cuda.Stream()
-    cut = [T * i // E2E_CHUNKS // 128 * 128 for i in range(E2E_CHUNKS)] + [T]
+    # half-size first and last chunks: the pipeline fills and drains on one H2D / D2H of T/16 tokens
+    cut = [0] + [(T // 16 + T * i // 8) // 128 * 128 for i in range(E2E_CHUNKS - 1)] + [T]
 
     def e2e_step():
         cur = torch.cuda.current_stream()
