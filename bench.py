@@ -242,14 +242,26 @@ def cpu_baseline(T_sample, H, bits, group, rank, k, reps_seconds=10.0, max_reps=
                       f"median of {len(times)} runs ({sum(times):.1f} s of CPU work), {t:.3f} s each"}
 
 
+def _synthetic_module():
+    """actcomp/synthetic.py loaded by file path: the reference arm must not
+    import the actcomp package (importing it maps libactcomp.so)."""
+    import importlib.util
+
+    spec = importlib.util.spec_from_file_location(
+        "_bench_synthetic", os.path.join(ROOT, "triton-kernel-test_b200", "actcomp", "synthetic.py"))
+    mod = importlib.util.module_from_spec(spec)
+    spec.loader.exec_module(mod)
+    return mod
+
+
 def run_reference(args):
     rank = int(os.environ.get("RANK", "0"))
     cfg = {"workload": "config-2 encode+decode, 16384 x 4096 bf16 per rank, r=32 k=16 int4 g64",
-           "tokens_per_rank": 16384, "channels": 4096, "rank": 32, "n_outlier": 16, "bits": 4, "group": 64,
-           "global_batch": 16384 * args.gpus, "parallelism": f"token-shard x{args.gpus}"}
+           "tokens_per_rank": args.tokens, "channels": 4096, "rank": 32, "n_outlier": 16, "bits": 4, "group": 64,
+           "global_batch": args.tokens * args.gpus, "parallelism": f"token-shard x{args.gpus}"}
     if rank != 0:
         return
-    T_sample = 4096  # a quarter of the config-2 activation per step keeps K + W steps within a few minutes
+    T_sample = args.tokens  # the whole config-2 activation per step (about 0.3 s on 16 cores)
     H, bits, group, r, k = 4096, 4, 64, 32, 16
     # all host cores (torchrun sets OMP_NUM_THREADS=1; the oracle's OpenMP reads it when it loads)
     os.environ["OMP_NUM_THREADS"] = str(os.cpu_count())
@@ -258,8 +270,7 @@ def run_reference(args):
     import oracle as O
     import torch
 
-    from actcomp import synthetic
-
+    synthetic = _synthetic_module()
     x, ch = synthetic.lowrank_activation(T_sample, H, n_outlier=k, seed=0)
     xb = x.view(torch.int16).numpy().view(np.uint16)
     V = np.linalg.qr(np.random.default_rng(0).standard_normal((H, r)))[0].astype(np.float32)

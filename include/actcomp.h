@@ -172,7 +172,10 @@ int actcomp_cg_dw(const actcomp_cg_desc *d, const uint16_t *dy, int64_t N, int64
  *   (on other streams or host threads) race on it -- serialise them.
  *   The first call on each device, with that device current, looks up the
  *   scratch's address (cudaGetSymbolAddress); make that first call before any
- *   stream capture. */
+ *   stream capture.  The address is cached per device together with the id of
+ *   the context it belongs to: after cudaDeviceReset the next call sees a new
+ *   context and looks the address up again (so that call, too, should come
+ *   before any capture). */
 #define ACTCOMP_DW_STATIC_SCRATCH_BYTES ((size_t)32 << 20)
 int actcomp_cg_dw_static(const actcomp_cg_desc *d, const uint16_t *dy, int64_t N, int64_t lddy, void *dw,
                          int32_t dw_dtype, int64_t lddw, void *stream);

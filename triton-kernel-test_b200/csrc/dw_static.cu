@@ -2,6 +2,8 @@
 // workspace: the decoded activation goes to a file-scope device array owned by
 // the library (ACTCOMP_DW_STATIC_SCRATCH_BYTES per device).  No device memory
 // is allocated on the call path.
+#include <cuda.h>
+
 #include <mutex>
 
 #include "common.cuh"
@@ -14,7 +16,37 @@ static __device__ __align__(256) unsigned char g_dw_scratch[ACTCOMP_DW_STATIC_SC
 namespace {
 constexpr int kMaxDevices = 64;
 std::mutex g_scratch_mu;
-void *g_scratch_addr[kMaxDevices];  // device address of g_dw_scratch, looked up on the first call per device
+void *g_scratch_addr[kMaxDevices];            // device address of g_dw_scratch in the context below
+unsigned long long g_scratch_ctx[kMaxDevices];  // unique id of the context the address belongs to
+
+// Unique id of the calling thread's current CUDA context (driver API through
+// the runtime's entry-point query, so the library needs no libcuda at link
+// time), or 0 when the driver cannot tell.  A context destroyed and created
+// again (cudaDeviceReset, then any runtime call) gets a new id, and with it
+// the module's device arrays move, so the cached address is looked up again.
+unsigned long long current_context_id() {
+    using GetCurrent = CUresult (*)(CUcontext *);
+    using GetId = CUresult (*)(CUcontext, unsigned long long *);
+    static GetCurrent get_current = nullptr;
+    static GetId get_id = nullptr;
+    static bool tried = false;
+    if (!tried) {  // called under g_scratch_mu
+        tried = true;
+        void *p = nullptr;
+        cudaDriverEntryPointQueryResult q;
+        if (cudaGetDriverEntryPoint("cuCtxGetCurrent", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_current = reinterpret_cast<GetCurrent>(p);
+        if (cudaGetDriverEntryPoint("cuCtxGetId", &p, cudaEnableDefault, &q) == cudaSuccess &&
+            q == cudaDriverEntryPointSuccess)
+            get_id = reinterpret_cast<GetId>(p);
+    }
+    CUcontext ctx = nullptr;
+    unsigned long long id = 0;
+    if (!get_current || !get_id || get_current(&ctx) != CUDA_SUCCESS || !ctx || get_id(ctx, &id) != CUDA_SUCCESS)
+        return 0;
+    return id;
+}
 }  // namespace
 
 extern "C" int actcomp_cg_dw_static(const actcomp_cg_desc *d, const uint16_t *dy, int64_t N, int64_t lddy, void *dw,
@@ -29,10 +61,14 @@ extern "C" int actcomp_cg_dw_static(const actcomp_cg_desc *d, const uint16_t *dy
     void *scratch = nullptr;
     {
         std::lock_guard<std::mutex> lock(g_scratch_mu);
-        if (!g_scratch_addr[dev]) {
+        const unsigned long long ctx = current_context_id();
+        // first call on this device, its context was re-created since the lookup, or the
+        // driver cannot identify the context (then the cheap host-side lookup runs every call)
+        if (!g_scratch_addr[dev] || ctx != g_scratch_ctx[dev] || ctx == 0) {
             void *p = nullptr;
             ACT_CUDA_TRY(cudaGetSymbolAddress(&p, g_dw_scratch));  // this device is current
             g_scratch_addr[dev] = p;
+            g_scratch_ctx[dev] = ctx;
         }
         scratch = g_scratch_addr[dev];
     }
