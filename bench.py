@@ -34,11 +34,13 @@ FALLBACK_PEAKS = {"hbm_gbs": 6650.0, "bf16_tflops": 1590.0, "bf16_tflops_sustain
 
 # ---------------------------------------------------------------- algorithmic work
 def packed_bytes_per_row(H, bits, group, rank, k):
-    return H * bits // 8 + (H // group) * 4 + rank + (4 if rank else 0) + 2 * k
+    """codes + float32 group scales + float32 projection L + bf16 outlier values."""
+    return H * bits // 8 + (H // group) * 4 + 4 * rank + 2 * k
 
 
 def basis_bytes(H, rank):
-    return rank * H * 2 + H * rank + rank * 4
+    """The bf16 basis, read once."""
+    return rank * H * 2
 
 
 def encode_bytes(T, H, bits, group, rank, k):
@@ -232,8 +234,8 @@ def cpu_baseline(T_sample, H, bits, group, rank, k, reps_seconds=10.0, max_reps=
     while len(times) < max_reps and (len(times) < 2 or time.perf_counter() < t_end):
         t0 = time.perf_counter()
         enc = O.encode(xb, prep, idx, bits, group, False)
-        O.decode(enc["codes"], enc["scales"], enc["lr_codes"], enc["lr_scale"], prep[1], enc["outliers"], idx, H,
-                 bits, group, False)
+        O.decode(enc["codes"], enc["scales"], enc["lowrank"], prep[1], enc["outliers"], idx, H, bits, group,
+                 False)
         times.append(time.perf_counter() - t0)
     t = statistics.median(times)
     work = encode_bytes(T_sample, H, bits, group, rank, k) + decode_bytes(T_sample, H, bits, group, rank, k)
@@ -279,8 +281,8 @@ def run_reference(args):
 
     def step():
         enc = O.encode(xb, prep, idx, bits, group, False)
-        O.decode(enc["codes"], enc["scales"], enc["lr_codes"], enc["lr_scale"], prep[1], enc["outliers"], idx, H,
-                 bits, group, False)
+        O.decode(enc["codes"], enc["scales"], enc["lowrank"], prep[1], enc["outliers"], idx, H, bits, group,
+                 False)
 
     for _ in range(args.warmup):
         step()

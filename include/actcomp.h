@@ -30,7 +30,7 @@
 extern "C" {
 #endif
 
-#define ACTCOMP_ABI_VERSION 1
+#define ACTCOMP_ABI_VERSION 2
 
 enum actcomp_status {
     ACT_OK = 0,
@@ -55,31 +55,34 @@ int actcomp_clear_device_error(void *stream);
 
 /* ========================================================= channel-group format
  * One compressed activation: `batch` independent slices, each a T x H bf16
- * matrix (T tokens / rows, H channels / columns).  All buffers hold the slices
- * back to back, slice i at offset i * (per-slice size):
+ * matrix X (T tokens / rows, H channels / columns), stored as
+ *   X = L . V^T + R,   L = X . V  (the projection onto a rank-r basis V),
+ * with R the residual, its outlier channels kept verbatim and the rest
+ * (optionally rotated by a 128-point Walsh-Hadamard transform per 128-channel
+ * block) quantised to int4/int8 codes with per-token group-absmax scales.
+ * All buffers hold the slices back to back, slice i at offset i * (per-slice size):
  *   codes       uint8   T x (H*bits/8)   int4: channel 2j in the low nibble
  *   scales      float   T x (H/group)    per-token group absmax / qmax
- *   lr_codes    int8    T x rank         low-rank coefficients (may be NULL if rank == 0)
- *   lr_scale    float   T                per-token coefficient scale
+ *   lowrank     float   T x rank         L = X . V, float32 (may be NULL if rank == 0)
  *   outliers    bf16    T x n_outlier    verbatim values of the outlier channels
  *   outlier_idx int32   n_outlier        ascending channel indices
- *   basis_t     bf16    rank x H         V^T for the projection
- *   basis_q     int8    H x rank         quantised basis for the reconstruction
- *   basis_scale float   rank             per basis vector scale of basis_q
- *   basis_qb    bf16    tile operand     basis_q as (exact) bf16 integers in the
- *                                        tensor-core encode's shared-memory layout
- *                                        (may be NULL: the encode then runs on CUDA cores)
- *   basis_qs    int8    tile operand     basis_q in the tensor-core decode's
- *                                        shared-memory layout (may be NULL: the decode
- *                                        then gathers basis_q tiles itself)
- * Tile operands: per slice ceil(H/128) tiles of 128 channels; tile t row `row`
- * (channel 128 t + row) holds the row's rank values in W bytes -- basis_qb:
- * W = 2 * RK, RK = rank rounded up to 16, 32 or 64, value j at byte 2 j;
- * basis_qs: W = 32 (rank <= 32) or 64, value j at byte j -- with the 16-byte
- * chunk c of the row stored at chunk c ^ s(row), s = (row >> 2) & 1 for W = 32,
+ *   basis_t     bf16    rank x H         V^T (the projection reads it)
+ *   basis       bf16    H x rank         V (the CUDA-core reconstruction reads it)
+ *   basis_tile  bf16    tile operand     V in the tensor-core kernels' shared-memory
+ *                                        layout (may be NULL: the CUDA-core kernels run)
+ * The basis is bf16: V is rounded to bf16 once, by actcomp_cg_basis_prepare,
+ * and every kernel (and any checker) uses those values.  The low-rank term
+ * L . V^T enters the arithmetic in float32; the tensor cores form it from L
+ * split exactly into three bf16 pieces, L = hi + mid + lo (hi = bf16(L),
+ * mid = bf16(L - hi), lo = L - hi - mid), each multiplied by the bf16 basis
+ * with float32 accumulation.
+ * Tile operand: per slice ceil(H/128) tiles of 128 channels; tile t row `row`
+ * (channel 128 t + row) holds the row's rank values in W = 2 * RK bytes, RK =
+ * rank rounded up to 16, 32 or 64, value j at byte 2 j, with the 16-byte chunk
+ * c of the row stored at chunk c ^ s(row), s = (row >> 2) & 1 for W = 32,
  * (row >> 1) & 3 for W = 64, row & 7 for W = 128 (the swizzled K-major layout
- * tcgen05.mma reads), zero beyond the rank and beyond H.  Sizes: batch *
- * ceil(H/128) * 128 * W bytes.  actcomp_cg_basis_prepare writes both.
+ * tcgen05.mma reads), zero beyond the rank and beyond H.  Size: batch *
+ * ceil(H/128) * 128 * W bytes.
  * bits in {4, 8}; group in {32, 64, 128} dividing H; rank in {0, 16, 32, 48, 64};
  * 0 <= n_outlier <= 64; wht requires H % 128 == 0 and group <= 128.          */
 typedef struct actcomp_cg_desc {
@@ -93,25 +96,21 @@ typedef struct actcomp_cg_desc {
     int32_t batch;
     uint8_t *codes;
     float *scales;
-    int8_t *lr_codes;
-    float *lr_scale;
+    float *lowrank;
     uint16_t *outliers;
     const int32_t *outlier_idx;
     const uint16_t *basis_t;
-    const int8_t *basis_q;
-    const float *basis_scale;
-    const uint16_t *basis_qb;
-    const int8_t *basis_qs;
+    const uint16_t *basis;
+    const uint16_t *basis_tile;
 } actcomp_cg_desc;
 
-/* Quantise a basis V (batch x H x rank, float32 row-major) into basis_t,
- * basis_q, basis_scale and (if non-NULL) the tile operands basis_qb and
- * basis_qs (layouts above; both are fully written, padding included).  No
- * reference counterpart (the reference takes l, r as given,
+/* Round a basis V (batch x H x rank, float32 row-major) to bf16 and write it as
+ * basis_t (batch x rank x H), basis (batch x H x rank) and, if non-NULL, the
+ * tile operand basis_tile (layout above, padding included).  No reference
+ * counterpart (the reference takes its factors l, r as given,
  * low_rank_extraction_fuse_compression_quantization.py:118). */
 int actcomp_cg_basis_prepare(const float *V, int64_t H, int32_t rank, int32_t batch, uint16_t *basis_t,
-                             int8_t *basis_q, float *basis_scale, uint16_t *basis_qb, int8_t *basis_qs,
-                             void *stream);
+                             uint16_t *basis, uint16_t *basis_tile, void *stream);
 
 /* Encode x (batch x T x H bf16, row stride ldx elements, slice stride T*ldx)
  * into the buffers of d.  Replaces low_rank_addition_fuse_compression_quantization

@@ -19,19 +19,30 @@
  *      fixtures in tests/golden (made by tests/golden/make_golden.py).
  *
  *  (2) Channel-group format ("cg_*"): the encode the north star describes --
- *      rank-r projection onto a basis V, top-k outlier channels kept verbatim,
- *      optional 128-wide Walsh-Hadamard rotation, int4/int8 codes with
- *      per-token group-absmax scales.  The reference has no code for this
- *      variant (its closest relatives are extraction_outlier_channel.py:11-14
- *      for the channel gather and the encode math of K2), so this part of the
- *      oracle is "parity unpinned" by the reference; it is pinned by its own
- *      algebraic properties (tests/test_oracle.py).
+ *      L = X . V (projection onto a rank-r basis V), residual R = X - L . V^T,
+ *      top-k outlier channels kept verbatim, optional 128-wide Walsh-Hadamard
+ *      rotation, int4/int8 codes with per-token group-absmax scales.  The
+ *      reference has no code for this variant (its closest relatives are
+ *      extraction_outlier_channel.py:11-14 for the channel gather and the
+ *      encode math of K2, low_rank_extraction_fuse_compression_quantization.py
+ *      :66-100), so this part is "parity unpinned" by the reference; it is
+ *      checked against an independent PyTorch statement of the north-star math
+ *      (oracle/northstar.py) and by its own algebraic tests.
  *
- * Every floating-point step below is a single IEEE-754 binary32 operation with
- * round-to-nearest-even, in the order written, so the CUDA kernels can match
- * it bit for bit.  The only exception is cg_project (a K=H reduction whose
- * order the tensor cores choose); it is computed in binary64 and the tests
- * compare the GPU's low-rank codes to it within one code step.
+ * Rounding points (the CUDA kernels follow them):
+ *   - the basis V is rounded to bf16 once; every product below uses those values;
+ *   - L[t,j] = the float32 rounding of the exact sum over c of X[t,c] * V[c,j];
+ *   - the low-rank term P[t,c] = the float32 rounding of the exact sum over j of
+ *     L[t,j] * V[c,j];
+ *   - the residual is the float32 difference X - P; the reconstruction is the
+ *     float32 sum P + dequantised residual, rounded once to the output type.
+ * The exact sums are taken in binary64 (the products are exact there and the
+ * sums are exact to far below a float32 ulp).  The tensor cores form the same
+ * sums in float32 with their own internal order, so GPU and oracle agree to a
+ * few float32 ulps of each sum; a code can differ only where the quantiser's
+ * input sits that close to a rounding boundary (the tests count and attribute
+ * every such case).  Everything else is one IEEE-754 binary32 operation with
+ * round-to-nearest-even, in the order written.
  *
  * Build: oracle/Makefile -> oracle/_build/libactcomp_oracle.so
  */
@@ -68,11 +79,8 @@ static inline float rne_bf(float f) { return bf2f(f2bf(f)); }
  * reciprocal instead of dividing, and the single fused rounding is what a GPU
  * computes with one fma whatever the compiler contracts.
  *
- * Basis preparation.  V is H x r (column j = basis vector j).
- *   sV[j]    = max_c |V[c,j]| / 127
- *   Vq[c,j]  = clamp(nearest(V[c,j] * (127 / max_c |V[c,j]|)), -127, 127)
- *   Vt[j,c]  = bf16_rne(V[c,j])                          (projection basis)
- */
+ * Basis preparation.  V is H x r (column j = basis vector j), rounded to bf16:
+ *   Vb[c,j] = bf16_rne(V[c,j]),  Vt[j,c] = Vb[c,j].                           */
 static inline float rscale_of(float amax, float qmax) { return amax > 0.f ? qmax / amax : 0.f; }
 static inline int code_of(float v, float rs, int qmax) {
     float t = fmaf(v, rs, 12582912.0f) - 12582912.0f;
@@ -80,21 +88,13 @@ static inline int code_of(float v, float rs, int qmax) {
     if (t < -(float)qmax) t = -(float)qmax;
     return (int)t;
 }
-void cg_basis_prepare(const float *V, int64_t H, int r, uint16_t *Vt, int8_t *Vq, float *sV) {
-    for (int j = 0; j < r; ++j) {
-        float amax = 0.f;
-        for (int64_t c = 0; c < H; ++c) {
-            float a = fabsf(V[c * r + j]);
-            if (a > amax) amax = a;
+void cg_basis_prepare(const float *V, int64_t H, int r, uint16_t *Vt, uint16_t *Vb) {
+    for (int64_t c = 0; c < H; ++c)
+        for (int j = 0; j < r; ++j) {
+            const uint16_t h = f2bf(V[c * r + j]);
+            Vb[c * r + j] = h;
+            Vt[(int64_t)j * H + c] = h;
         }
-        sV[j] = amax / 127.0f;
-        const float rs = rscale_of(amax, 127.0f);
-        for (int64_t c = 0; c < H; ++c) {
-            float v = V[c * r + j];
-            Vq[c * r + j] = (int8_t)code_of(v, rs, 127);
-            Vt[(int64_t)j * H + c] = f2bf(v);
-        }
-    }
 }
 
 /* L[t,j] = sum_c X[t,c] * Vt[j,c], accumulated in binary64, rounded once. */
@@ -114,33 +114,18 @@ void cg_project(const void *X, int x_f32, int64_t T, int64_t H, int64_t ldx, con
     }
 }
 
-/* Per-token quantisation of the low-rank coefficients.
- *   Lt[j]  = L[t,j] * sV[j]
- *   sL[t]  = max_j |Lt[j]| / 127
- *   Lq[t,j]= clamp(nearest(Lt[j] * (127 / max_j |Lt[j]|)), -127, 127)          */
-void cg_lr_quantize(const float *L, int64_t T, int r, const float *sV, int8_t *Lq, float *sL) {
-#pragma omp parallel for schedule(static)
-    for (int64_t t = 0; t < T; ++t) {
-        float lt[256];
-        float amax = 0.f;
-        for (int j = 0; j < r; ++j) {
-            lt[j] = L[t * r + j] * sV[j];
-            float a = fabsf(lt[j]);
-            if (a > amax) amax = a;
-        }
-        sL[t] = amax / 127.0f;
-        const float rs = rscale_of(amax, 127.0f);
-        for (int j = 0; j < r; ++j) Lq[t * r + j] = (int8_t)code_of(lt[j], rs, 127);
-    }
-}
-
-/* I[t,c] = sum_j Lq[t,j]*Vq[c,j], an exact integer (|I| < 2^21 for r <= 64);
- * the low-rank term enters the arithmetic only as fma(+-I, sL[t], .), one
- * rounding. */
-static inline float lowrank_int(const int8_t *lq, const int8_t *vq, int r) {
-    int32_t acc = 0;
-    for (int j = 0; j < r; ++j) acc += (int32_t)lq[j] * (int32_t)vq[j];
+/* P[t,c] = sum_j L[t,j] * Vb[c,j]: every product is exact in binary64
+ * (24 x 8 significant bits), the sum of at most 64 of them is rounded once to
+ * binary32. */
+static inline float lowrank_term(const float *l, const uint16_t *vb, int r) {
+    double acc = 0.0;
+    for (int j = 0; j < r; ++j) acc += (double)l[j] * (double)bf2f(vb[j]);
     return (float)acc;
+}
+void cg_lowrank(const float *L, const uint16_t *Vb, int64_t T, int64_t H, int r, float *P) {
+#pragma omp parallel for schedule(static)
+    for (int64_t t = 0; t < T; ++t)
+        for (int64_t c = 0; c < H; ++c) P[t * H + c] = lowrank_term(L + t * r, Vb + c * r, r);
 }
 
 /* Unnormalised 128-point Walsh-Hadamard butterflies, stage m = 1,2,...,64:
@@ -155,17 +140,17 @@ static void wht128(float *x) {
             }
 }
 
-/* Encode one token row given its low-rank codes (see file header, part 2).
+/* Encode given the projection L (see file header, part 2).
  * X row -> codes (H*bits/8 bytes), scales (H/group), outliers (k values).
- *   R[c]   = fma(-I[t,c], sL[t], X[c])         (binary32, one rounding)
+ *   R[c]   = X[c] - P[t,c]                     (binary32, P = lowrank_term)
  *   O[j]   = X[idx[j]] (verbatim);  R[idx[j]] = 0
  *   W      = wht ? WHT128(R) per 128-block : R
  *   s      = max_{c in group} |W[c]| / qmax,  qmax = 2^(bits-1) - 1
  *   q      = clamp(nearest(W[c] * (qmax / max_{c in group} |W[c]|)), -qmax, qmax)
  *   u      = q + 2^(bits-1); int4 packs channel 2i in the low nibble.      */
-void cg_encode_given_lr(const void *X, int x_f32, int64_t T, int64_t H, int64_t ldx, const int8_t *Lq,
-                        const float *sL, const int8_t *Vq, int r, const int32_t *idx, int k, int bits,
-                        int group, int wht, uint8_t *codes, float *scales, void *outl) {
+void cg_encode_given_lr(const void *X, int x_f32, int64_t T, int64_t H, int64_t ldx, const float *L,
+                        const uint16_t *Vb, int r, const int32_t *idx, int k, int bits, int group, int wht,
+                        uint8_t *codes, float *scales, void *outl) {
     const int qmax = (1 << (bits - 1)) - 1;
     const int off = 1 << (bits - 1);
     const int64_t row_bytes = H * bits / 8;
@@ -177,7 +162,7 @@ void cg_encode_given_lr(const void *X, int x_f32, int64_t T, int64_t H, int64_t 
         for (int64_t t = 0; t < T; ++t) {
             for (int64_t c = 0; c < H; ++c) {
                 float xv = x_f32 ? ((const float *)X)[t * ldx + c] : bf2f(((const uint16_t *)X)[t * ldx + c]);
-                w[c] = r ? fmaf(-lowrank_int(Lq + t * r, Vq + c * r, r), sL[t], xv) : xv;
+                w[c] = r ? xv - lowrank_term(L + t * r, Vb + c * r, r) : xv;
             }
             for (int j = 0; j < k; ++j) {
                 int64_t c = idx[j];
@@ -216,10 +201,11 @@ void cg_encode_given_lr(const void *X, int x_f32, int64_t T, int64_t H, int64_t 
 /* Decode (see file header, part 2):
  *   w  = (float)(u - 2^(bits-1)) * s
  *   r^ = wht ? WHT128(w) * (1/128) : w
- *   x^ = out_dtype(fma(I[t,c], sL[t], r^));  x^[idx[j]] = O[j] verbatim.     */
-void cg_decode(const uint8_t *codes, const float *scales, const int8_t *Lq, const float *sL, const int8_t *Vq,
-               int r, const void *outl, const int32_t *idx, int k, int64_t T, int64_t H, int bits, int group,
-               int wht, int x_f32, void *Xhat) {
+ *   x^ = out_dtype(P[t,c] + r^)  (binary32 sum, one rounding to the output type);
+ *   x^[idx[j]] = O[j] verbatim.                                              */
+void cg_decode(const uint8_t *codes, const float *scales, const float *L, const uint16_t *Vb, int r,
+               const void *outl, const int32_t *idx, int k, int64_t T, int64_t H, int bits, int group, int wht,
+               int x_f32, void *Xhat) {
     const int off = 1 << (bits - 1);
     const int64_t row_bytes = H * bits / 8;
     const int64_t ngroups = H / group;
@@ -239,7 +225,7 @@ void cg_decode(const uint8_t *codes, const float *scales, const int8_t *Lq, cons
                     for (int i = 0; i < 128; ++i) w[b + i] = w[b + i] * 0.0078125f;
                 }
             for (int64_t c = 0; c < H; ++c) {
-                float v = r ? fmaf(lowrank_int(Lq + t * r, Vq + c * r, r), sL[t], w[c]) : w[c];
+                float v = r ? lowrank_term(L + t * r, Vb + c * r, r) + w[c] : w[c];
                 if (x_f32)
                     ((float *)Xhat)[t * H + c] = v;
                 else

@@ -79,18 +79,17 @@ def bf16_to_f32(h: np.ndarray) -> np.ndarray:
 
 # ------------------------------------------------------------------ channel-group format
 def basis_prepare(V: np.ndarray):
-    """V (H x r) float32 -> (Vt bf16 bits r x H, Vq int8 H x r, sV float32 r)."""
+    """V (H x r) float32 -> (Vt bf16 bits r x H, Vb bf16 bits H x r): the basis rounded to bf16."""
     V = _c(V, np.float32)
     H, r = V.shape
     Vt = np.empty((r, H), np.uint16)
-    Vq = np.empty((H, r), np.int8)
-    sV = np.empty((r,), np.float32)
-    lib().cg_basis_prepare(_p(V), I64(H), I32(r), _p(Vt), _p(Vq), _p(sV))
-    return Vt, Vq, sV
+    Vb = np.empty((H, r), np.uint16)
+    lib().cg_basis_prepare(_p(V), I64(H), I32(r), _p(Vt), _p(Vb))
+    return Vt, Vb
 
 
 def project(X: np.ndarray, Vt: np.ndarray) -> np.ndarray:
-    """L = X @ Vt^T accumulated in binary64 (X bf16 bits or float32)."""
+    """L = X @ Vt^T, exact sum rounded once to float32 (X bf16 bits or float32)."""
     x_f32 = X.dtype == np.float32
     X = _c(X, np.float32 if x_f32 else np.uint16)
     T, H = X.shape
@@ -100,60 +99,81 @@ def project(X: np.ndarray, Vt: np.ndarray) -> np.ndarray:
     return L
 
 
-def lr_quantize(L: np.ndarray, sV: np.ndarray):
+def lowrank(L: np.ndarray, Vb: np.ndarray) -> np.ndarray:
+    """P = L @ Vb^T, exact sum rounded once to float32 (the low-rank term)."""
     L = _c(L, np.float32)
     T, r = L.shape
-    Lq = np.empty((T, r), np.int8)
-    sL = np.empty((T,), np.float32)
-    lib().cg_lr_quantize(_p(L), I64(T), I32(r), _p(_c(sV, np.float32)), _p(Lq), _p(sL))
-    return Lq, sL
+    H = Vb.shape[0]
+    P = np.empty((T, H), np.float32)
+    lib().cg_lowrank(_p(L), _p(_c(Vb, np.uint16)), I64(T), I64(H), I32(r), _p(P))
+    return P
 
 
-def encode_given_lr(X, Lq, sL, Vq, idx, bits, group, wht):
-    """Channel-group encode of X given its low-rank codes -> (codes, scales, outliers)."""
+def encode_given_lr(X, L, Vb, idx, bits, group, wht):
+    """Channel-group encode of X given its projection L -> (codes, scales, outliers)."""
     x_f32 = X.dtype == np.float32
     X = _c(X, np.float32 if x_f32 else np.uint16)
     T, H = X.shape
-    r = 0 if Lq is None else Lq.shape[1]
+    r = 0 if L is None else L.shape[1]
     idx = _c(idx if idx is not None else np.zeros(0), np.int32)
     k = idx.shape[0]
     codes = np.empty((T, H * bits // 8), np.uint8)
     scales = np.empty((T, H // group), np.float32)
     outl = np.empty((T, k), np.float32 if x_f32 else np.uint16)
-    Lq_ = _c(Lq, np.int8) if r else np.zeros((T, 1), np.int8)
-    sL_ = _c(sL, np.float32) if r else np.zeros((T,), np.float32)
-    Vq_ = _c(Vq, np.int8) if r else np.zeros((H, 1), np.int8)
-    lib().cg_encode_given_lr(_p(X), I32(int(x_f32)), I64(T), I64(H), I64(H), _p(Lq_), _p(sL_), _p(Vq_), I32(r),
-                             _p(idx), I32(k), I32(bits), I32(group), I32(int(wht)), _p(codes), _p(scales), _p(outl))
+    L_ = _c(L, np.float32) if r else np.zeros((T, 1), np.float32)
+    Vb_ = _c(Vb, np.uint16) if r else np.zeros((H, 1), np.uint16)
+    lib().cg_encode_given_lr(_p(X), I32(int(x_f32)), I64(T), I64(H), I64(H), _p(L_), _p(Vb_), I32(r), _p(idx),
+                             I32(k), I32(bits), I32(group), I32(int(wht)), _p(codes), _p(scales), _p(outl))
     return codes, scales, outl
 
 
 def encode(X, V_prepared, idx, bits, group, wht):
-    """Full channel-group encode: projection (binary64), low-rank codes, residual codes."""
-    Vt, Vq, sV = V_prepared
-    if Vt.shape[0]:
-        L = project(X, Vt)
-        Lq, sL = lr_quantize(L, sV)
-    else:
-        Lq = sL = None
-    codes, scales, outl = encode_given_lr(X, Lq, sL, Vq, idx, bits, group, wht)
-    return dict(codes=codes, scales=scales, outliers=outl, lr_codes=Lq, lr_scale=sL)
+    """Full channel-group encode: projection (exact sums), residual codes."""
+    Vt, Vb = V_prepared
+    L = project(X, Vt) if Vt.shape[0] else None
+    codes, scales, outl = encode_given_lr(X, L, Vb, idx, bits, group, wht)
+    return dict(codes=codes, scales=scales, outliers=outl, lowrank=L)
 
 
-def decode(codes, scales, Lq, sL, Vq, outl, idx, H, bits, group, wht, x_f32=False):
+def decode(codes, scales, L, Vb, outl, idx, H, bits, group, wht, x_f32=False):
     T = codes.shape[0]
-    r = 0 if Lq is None else Lq.shape[1]
+    r = 0 if L is None else L.shape[1]
     idx = _c(idx if idx is not None else np.zeros(0), np.int32)
     k = idx.shape[0]
     out = np.empty((T, H), np.float32 if x_f32 else np.uint16)
-    Lq_ = _c(Lq, np.int8) if r else np.zeros((T, 1), np.int8)
-    sL_ = _c(sL, np.float32) if r else np.zeros((T,), np.float32)
-    Vq_ = _c(Vq, np.int8) if r else np.zeros((H, 1), np.int8)
+    L_ = _c(L, np.float32) if r else np.zeros((T, 1), np.float32)
+    Vb_ = _c(Vb, np.uint16) if r else np.zeros((H, 1), np.uint16)
     outl_ = _c(outl, np.float32 if x_f32 else np.uint16) if k else np.zeros((T, 1), np.uint16)
-    lib().cg_decode(_p(_c(codes, np.uint8)), _p(_c(scales, np.float32)), _p(Lq_), _p(sL_), _p(Vq_), I32(r),
-                    _p(outl_), _p(idx), I32(k), I64(T), I64(H), I32(bits), I32(group), I32(int(wht)),
-                    I32(int(x_f32)), _p(out))
+    lib().cg_decode(_p(_c(codes, np.uint8)), _p(_c(scales, np.float32)), _p(L_), _p(Vb_), I32(r), _p(outl_),
+                    _p(idx), I32(k), I64(T), I64(H), I32(bits), I32(group), I32(int(wht)), I32(int(x_f32)),
+                    _p(out))
     return out
+
+
+def quantizer_inputs(X, L, Vb, idx, bits, group, wht):
+    """The value each code rounds, w * (qmax / absmax), in binary64 from the
+    oracle's own residual (T x H), for attributing code differences to
+    rounding ties."""
+    x_f32 = X.dtype == np.float32
+    x = (X if x_f32 else bf16_to_f32(X)).astype(np.float32)
+    T, H = x.shape
+    w = x - lowrank(L, Vb) if L is not None and L.shape[1] else x.copy()
+    if idx is not None and len(idx):
+        w[:, np.asarray(idx)] = 0.0
+    if wht:
+        w = w.reshape(T, H // 128, 128)
+        m = 1
+        while m < 128:  # the oracle's butterfly order, binary32
+            w = w.reshape(T, H // 128, 128 // (2 * m), 2, m)
+            a, b = w[:, :, :, 0, :].copy(), w[:, :, :, 1, :].copy()
+            w[:, :, :, 0, :] = a + b
+            w[:, :, :, 1, :] = a - b
+            m *= 2
+        w = w.reshape(T, H)
+    qmax = (1 << (bits - 1)) - 1
+    g = np.abs(w).reshape(T, H // group, group).max(-1)
+    rs = np.where(g > 0, np.float32(qmax) / np.where(g > 0, g, 1).astype(np.float32), 0).astype(np.float32)
+    return w.astype(np.float64) * np.repeat(rs, group, axis=1).astype(np.float64)
 
 
 def channel_absmax(X):
@@ -266,3 +286,121 @@ def unpack_codes(codes: np.ndarray, bits: int) -> np.ndarray:
     lo = codes & 0xF
     hi = codes >> 4
     return np.stack([lo, hi], axis=-1).reshape(codes.shape[0], -1)
+
+
+# ------------------------------------------------------------------ parity with tie attribution
+def compare_encode(codes, scales, X, L, Vb, idx, bits, group, wht, tie_eps=2e-3, max_frac=1e-4, scale_rtol=1e-4):
+    """Compare kernel codes/scales with the oracle's, given the same projection L.
+
+    The kernels sum the low-rank term on the tensor cores in float32 (a few
+    ulps from the oracle's exact sum), so a code may differ where the value it
+    rounds sits within that distance of a rounding tie.  Returns a dict of
+    counts; ``ok`` holds when every differing code is off by one, its oracle
+    input lies within ``tie_eps`` of a tie, differing codes are at most
+    ``max_frac`` of all codes, and every scale agrees to ``scale_rtol``
+    relative (a group's absmax element moves by the same few ulps; with the
+    rotation the residual is a sum of 128 such values)."""
+    ref_codes, ref_scales, ref_outl = encode_given_lr(X, L, Vb, idx, bits, group, wht)
+    off = 1 << (bits - 1)
+    a = unpack_codes(np.asarray(codes), bits).astype(np.int32) - off
+    b = unpack_codes(ref_codes, bits).astype(np.int32) - off
+    diff = a != b
+    n_diff = int(diff.sum())
+    out = {"codes": int(a.size), "codes_differing": n_diff, "max_code_step": int(np.abs(a - b).max(initial=0)),
+           "max_tie_distance": 0.0}
+    if n_diff:
+        pre = quantizer_inputs(X, L, Vb, idx, bits, group, wht)
+        tie = np.abs(pre - np.floor(pre) - 0.5)
+        out["max_tie_distance"] = float(tie[diff].max())
+    s_a = np.asarray(scales, np.float64)
+    s_b = ref_scales.astype(np.float64)
+    rel = np.abs(s_a - s_b) / np.maximum(np.abs(s_b), 1e-30)
+    out["scales_differing"] = int((s_a != s_b).sum())
+    out["max_scale_rel"] = float(rel.max(initial=0.0))
+    out["ok"] = (out["max_code_step"] <= 1 and out["max_tie_distance"] < tie_eps and n_diff <= max_frac * a.size
+                 and out["max_scale_rel"] < scale_rtol)
+    out["ref"] = (ref_codes, ref_scales, ref_outl)
+    return out
+
+
+def _wht_f32(w):
+    """The oracle's unnormalised butterflies (stages 1, 2, ..., 64) per 128-channel block, binary32."""
+    T, H = w.shape
+    w = w.reshape(T, H // 128, 128).copy()
+    m = 1
+    while m < 128:
+        v = w.reshape(T, H // 128, 128 // (2 * m), 2, m)
+        a_, b_ = v[:, :, :, 0, :].copy(), v[:, :, :, 1, :].copy()
+        v[:, :, :, 0, :] = a_ + b_
+        v[:, :, :, 1, :] = a_ - b_
+        m *= 2
+    return w.reshape(T, H)
+
+
+def decode_prerounding(codes, scales, L, Vb, H, bits, group, wht):
+    """The oracle decode's binary32 value before its bf16 rounding, and the
+    magnitude that bounds a float32 evaluation's error: sum_j |L_j V_j| + |w|
+    (the low-rank sum often cancels, so its rounding error scales with its
+    terms, not with its result)."""
+    off = 1 << (bits - 1)
+    u = unpack_codes(np.asarray(codes), bits).astype(np.float32) - np.float32(off)
+    w = (u * np.repeat(np.asarray(scales, np.float32), group, axis=1)).astype(np.float32)
+    if wht:
+        w = (_wht_f32(w) * np.float32(0.0078125)).astype(np.float32)
+    if L is not None and L.shape[1]:
+        P = lowrank(L, Vb)
+        terms = np.abs(L.astype(np.float64)) @ np.abs(bf16_to_f32(Vb).astype(np.float64)).T
+    else:
+        P = np.zeros_like(w)
+        terms = 0.0
+    return (P + w).astype(np.float32), terms + np.abs(w)
+
+
+def _bf16_step(f):
+    """Spacing of bf16 values at |f| (0 at zero)."""
+    m, e = np.frexp(np.abs(f).astype(np.float64))
+    return np.where(f == 0, 0.0, np.ldexp(1.0, e - 8))
+
+
+def compare_decode(xh, ref, codes, scales, L, Vb, idx, H, bits, group, wht, ulps=64, max_frac=1e-3):
+    """A kernel decode (bf16 bits) against the oracle's decode of the same
+    buffers.  The kernels sum the low-rank term on the tensor cores (a few
+    float32 ulps of its terms from the oracle's exact sum), so a kernel value
+    may differ from the oracle's where it is the bf16 rounding of some value
+    within ``ulps`` ulps of sum_j |L_j V_j| + |w| of the oracle's binary32
+    value v (a rounding tie of v).  ``ok`` when every difference is such a case and they are at most
+    ``max_frac`` of all values; ``worst`` describes the furthest one."""
+    xh = np.asarray(xh, np.uint16)
+    ref = np.asarray(ref, np.uint16)
+    d = xh != ref
+    n = int(d.sum())
+    out = {"values": int(xh.size), "differing": n, "max_tie_ulps": 0.0, "ok": True}
+    if n:
+        v, mag = decode_prerounding(codes, scales, L, Vb, H, bits, group, wht)
+        fa = bf16_to_f32(xh[d]).astype(np.float64)
+        vd = v[d].astype(np.float64)
+        # how far v must move (in ulps of the summands) for fa to be its bf16 rounding
+        excess = np.maximum(np.abs(fa - vd) - 0.5 * _bf16_step(fa), 0.0)
+        dist = excess / (np.maximum(mag[d].astype(np.float64), 1e-30) * 2.0 ** -24)
+        out["max_tie_ulps"] = float(dist.max())
+        w = int(np.argmax(dist))
+        rows, cols = np.nonzero(d)
+        out["worst"] = {"row": int(rows[w]), "col": int(cols[w]), "kernel": float(fa[w]),
+                        "oracle": float(bf16_to_f32(ref[d])[w]), "v": float(vd[w]), "mag": float(mag[d][w])}
+        out["ok"] = out["max_tie_ulps"] <= ulps and n <= max_frac * xh.size
+    return out
+
+
+def compare_bf16(a, b, max_frac=1e-4):
+    """Two bf16 tensors (bit arrays) that should agree except where a float32
+    sum of a few ulps' difference crossed a bf16 rounding boundary: differing
+    values must be one bf16 step apart and at most ``max_frac`` of all."""
+    a = np.asarray(a, np.uint16)
+    b = np.asarray(b, np.uint16)
+    d = a != b
+    n = int(d.sum())
+    fa = bf16_to_f32(a[d]).astype(np.float64)
+    fb = bf16_to_f32(b[d]).astype(np.float64)
+    ulp = np.abs(fb) * 2.0 ** -7  # one bf16 step (7 explicit mantissa bits), upper bound
+    step_ok = bool(np.all(np.abs(fa - fb) <= ulp + 1e-38))
+    return {"values": int(a.size), "differing": n, "ok": step_ok and n <= max_frac * a.size}

@@ -34,7 +34,7 @@ def test_abi_version_and_strerror():
     from actcomp import _lib
 
     lib = _lib.load()
-    assert lib.actcomp_abi_version() == 1
+    assert lib.actcomp_abi_version() == _lib.ABI_VERSION == 2
     assert lib.actcomp_strerror(0) == b"ok"
     assert lib.actcomp_strerror(-6) == b"workspace missing or too small"
 

@@ -1,10 +1,16 @@
 """GPU parity of the channel-group format against the CPU oracle.
 
-Protocol: the basis quantisation, the residual codes, scales and outliers
-given the kernel's low-rank codes, and every reconstruction are bit-exact.
-The low-rank codes themselves come from a length-H tensor-core reduction
-whose order is the hardware's; they must agree with the oracle's binary64
-projection to within one code step (and almost all exactly)."""
+Protocol:
+* the bf16 basis and the outlier values are bit-exact;
+* the projection L (a length-H float32 sum on the tensor cores) is within
+  1e-5 of the sum of absolute products of the oracle's exact sum;
+* given the kernel's L, codes and scales equal the oracle's except where the
+  quantiser's input sits within 2e-3 of a rounding tie (the tensor cores sum
+  the low-rank term L . V^T in their own float32 order, a few ulps from the
+  oracle's exact sum); at most 1e-4 of the codes may differ, each by one step;
+* the decode of the kernel's buffers equals the oracle's decode of the same
+  buffers except for values one bf16 step apart at rounding ties (at most
+  1e-4 of them)."""
 import numpy as np
 import pytest
 import torch
@@ -75,40 +81,64 @@ CASES = [
 ]
 
 
+def check_projection(O, xb, L, Vt):
+    """L from the kernel against the oracle's exact sums: a float32
+    accumulation over H/16 tensor-core steps is within (H/16) * 2^-22 *
+    sum |x v| of the exact sum (one ulp of loss per step, truncation included)."""
+    L_o = O.project(xb, Vt)
+    H = xb.shape[1]
+    xf = np.abs(O.bf16_to_f32(xb).astype(np.float64))
+    bound = (H / 16) * 2.0 ** -22 * (xf @ np.abs(O.bf16_to_f32(Vt).astype(np.float64)).T) + 1e-30
+    err = np.abs(L.astype(np.float64) - L_o)
+    assert np.all(err <= bound), f"projection differs from the oracle: max err/bound {float((err / bound).max()):.3f}"
+    return L_o
+
+
 @pytest.mark.parametrize("T,H,r,k,b,g,wht", CASES)
 def test_encode_decode_parity(O, T, H, r, k, b, g, wht):
     xb, V, idx = make_case(O, T, H, r, k)
     c = gpu_encode(xb, V, idx, b, g, wht)
+    L = Vb = None
     if r:
-        Vt, Vq, sV = O.basis_prepare(V)
+        Vt, Vb = O.basis_prepare(V)
         assert np.array_equal(bits(c.basis.basis_t[0]), Vt)
-        assert np.array_equal(c.basis.basis_q[0].cpu().numpy(), Vq)
-        assert np.array_equal(c.basis.basis_scale[0].cpu().numpy(), sV)
-        Lq_o, sL_o = O.lr_quantize(O.project(xb, Vt), sV)
-        Lq = c.lr_codes.cpu().numpy()
-        sL = c.lr_scale.cpu().numpy()
-        assert np.abs(Lq.astype(int) - Lq_o.astype(int)).max() <= 1
-        assert (Lq == Lq_o).mean() > 0.98
-        # sL = max|L * sV| / 127 with L an fp32 tensor-core sum of H products in
-        # the hardware's order: relative error vs binary64 well under H * 2^-24
-        np.testing.assert_allclose(sL, sL_o, rtol=1e-4)
-    else:
-        Vq = np.zeros((H, 0), np.int8)
-        Lq = sL = None
-    codes, scales, outl = O.encode_given_lr(xb, Lq, sL, Vq, idx, b, g, wht)
-    assert np.array_equal(c.codes.cpu().numpy(), codes), "codes differ"
-    assert np.array_equal(c.scales.cpu().numpy(), scales), "scales differ"
+        assert np.array_equal(bits(c.basis.basis[0]), Vb)
+        L = c.lowrank.cpu().numpy()
+        check_projection(O, xb, L, Vt)
+    codes, scales = c.codes.cpu().numpy(), c.scales.cpu().numpy()
+    cmp = O.compare_encode(codes, scales, xb, L, Vb, idx, b, g, wht)
+    assert cmp["ok"], {k_: v for k_, v in cmp.items() if k_ != "ref"}
+    outl = cmp["ref"][2]
     if k:
         assert np.array_equal(bits(c.outliers), outl)
-    # decode of the GPU buffers, bit for bit
+    # decode of the GPU buffers
     import actcomp
 
     xh = bits(actcomp.decode(c))
-    ref = O.decode(codes, scales, Lq, sL, Vq, outl if k else None, idx, H, b, g, wht)
-    assert np.array_equal(xh, ref)
+    ref = O.decode(codes, scales, L, Vb, outl if k else None, idx, H, b, g, wht)
+    dcmp = O.compare_decode(xh, ref, codes, scales, L, Vb, idx, H, b, g, wht)
+    assert dcmp["ok"], str(dcmp)
     # and the reconstruction is close to the input (without outlier channels an
     # int4 group that holds a x30 channel is coarse, hence the looser bound)
     assert O.rel_fro(xh, xb) < ((0.06 if k else 0.2) if b == 4 else 0.01)
+
+
+@pytest.mark.parametrize("T,H,r,k,b,g,wht", [CASES[0], CASES[8], CASES[9], CASES[10]])
+def test_codes_against_the_oracle_projection(O, T, H, r, k, b, g, wht):
+    """End to end: the kernel's codes against the oracle's codes computed from
+    the oracle's own projection.  The two projections differ by float32
+    summation order only, so the codes may differ only at rounding ties."""
+    xb, V, idx = make_case(O, T, H, r, k, seed=11)
+    c = gpu_encode(xb, V, idx, b, g, wht)
+    Vt, Vb = O.basis_prepare(V)
+    L_o = O.project(xb, Vt)
+    # the two projections differ by up to ~1e-5 of the terms: the residual (and
+    # a group's absmax) moves by that much relative to the low-rank term
+    cmp = O.compare_encode(c.codes.cpu().numpy(), c.scales.cpu().numpy(), xb, L_o, Vb, idx, b, g, wht, max_frac=1e-3,
+                           scale_rtol=1e-2)
+    print(f"T={T} H={H}: codes differing from the oracle's own projection {cmp['codes_differing']} of "
+          f"{cmp['codes']}, max tie distance {cmp['max_tie_distance']:.2e}")
+    assert cmp["ok"], {k_: v for k_, v in cmp.items() if k_ != "ref"}
 
 
 @pytest.mark.parametrize("op", ["silu", "gelu", "mul"])
@@ -208,8 +238,8 @@ def test_batched_slices_are_independent(O, H):
 def test_batched_encode_with_outliers_crossing_slices(O):
     """Two slices of 9700 tokens (152 token blocks: some CTAs encode a block of
     each slice, so the per-slice outlier tables change inside a CTA) with a
-    different basis and outlier set per slice: every slice bit-exact against
-    the oracle given the kernel's low-rank codes."""
+    different basis and outlier set per slice: every slice matches the oracle
+    given the kernel's projection."""
     import actcomp
 
     T, H, r, k = 9700, 1024, 16, 4
@@ -225,12 +255,10 @@ def test_batched_encode_with_outliers_crossing_slices(O):
     torch.cuda.synchronize()
     codes = c.codes.cpu().numpy().reshape(2, T, -1)
     scales = c.scales.cpu().numpy().reshape(2, T, -1)
-    Lq = c.lr_codes.cpu().numpy().reshape(2, T, r)
-    sL = c.lr_scale.cpu().numpy().reshape(2, T)
+    L = c.lowrank.cpu().numpy().reshape(2, T, r)
     outl = bits(c.outliers).reshape(2, T, k)
     for s_ in range(2):
-        _, Vq, _ = O.basis_prepare(Vs[s_])
-        co, so, oo = O.encode_given_lr(xs[s_], Lq[s_], sL[s_], Vq, idxs[s_], 4, 64, False)
-        assert np.array_equal(codes[s_], co), f"slice {s_}: codes differ"
-        assert np.array_equal(scales[s_], so), f"slice {s_}: scales differ"
-        assert np.array_equal(outl[s_], oo), f"slice {s_}: outliers differ"
+        _, Vb = O.basis_prepare(Vs[s_])
+        cmp = O.compare_encode(codes[s_], scales[s_], xs[s_], L[s_], Vb, idxs[s_], 4, 64, False)
+        assert cmp["ok"], f"slice {s_}: {dict((k_, v) for k_, v in cmp.items() if k_ != 'ref')}"
+        assert np.array_equal(outl[s_], cmp["ref"][2]), f"slice {s_}: outliers differ"

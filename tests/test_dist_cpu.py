@@ -37,7 +37,7 @@ def _case(T=96, H=256, r=16, k=4, seed=3):
 
 def _stats(O, xb, prep, idx, bits=4, group=64):
     e = O.encode(xb, prep, idx, bits, group, False)
-    xh = O.decode(e["codes"], e["scales"], e["lr_codes"], e["lr_scale"], prep[1], e["outliers"], idx, xb.shape[1],
+    xh = O.decode(e["codes"], e["scales"], e["lowrank"], prep[1], e["outliers"], idx, xb.shape[1],
                   bits, group, False)
     a = O.bf16_to_f32(xh).astype(np.float64)
     b = O.bf16_to_f32(xb).astype(np.float64)

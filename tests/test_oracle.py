@@ -96,7 +96,7 @@ def test_cg_roundtrip_error_is_quantisation_error(O, bits, group, wht):
     xb = O.f32_to_bf16(x)
     prep = O.basis_prepare(_basis(O.bf16_to_f32(xb), 16))
     enc = O.encode(xb, prep, ch, bits, group, wht)
-    xh = O.decode(enc["codes"], enc["scales"], enc["lr_codes"], enc["lr_scale"], prep[1], enc["outliers"], ch, 256,
+    xh = O.decode(enc["codes"], enc["scales"], enc["lowrank"], prep[1], enc["outliers"], ch, 256,
                   bits, group, wht)
     err = O.rel_fro(xh, xb)
     assert err < (0.05 if bits == 4 else 0.01)
@@ -112,25 +112,27 @@ def test_cg_wht_inverse_is_identity(O):
     the inverse rotation, so the error is the 8-bit quantisation error only."""
     rng = np.random.default_rng(1)
     xb = O.f32_to_bf16(rng.standard_normal((8, 256)).astype(np.float32))
-    enc = O.encode(xb, (np.zeros((0, 256), np.uint16), np.zeros((256, 0), np.int8), np.zeros(0, np.float32)), None,
-                   8, 128, True)
-    xh = O.decode(enc["codes"], enc["scales"], None, None, None, None, None, 256, 8, 128, True)
+    enc = O.encode(xb, (np.zeros((0, 256), np.uint16), np.zeros((256, 0), np.uint16)), None, 8, 128, True)
+    xh = O.decode(enc["codes"], enc["scales"], None, None, None, None, 256, 8, 128, True)
     assert O.rel_fro(xh, xb) < 8e-3
 
 
-def test_cg_lowrank_term_is_exact_integer(O):
-    """The reconstruction term depends only on (Lq, sL, Vq): two encodes of
-    inputs that differ only in the residual share it exactly."""
+def test_cg_lowrank_term_is_the_rounded_exact_sum(O):
+    """The low-rank term is L . V^T summed exactly and rounded once: decoding an
+    all-zero residual gives bf16(float32(exact L . V^T)), and the residual of
+    the encode is x - that term."""
     x, ch = _lowrank_x(16, 128, seed=3)
     xb = O.f32_to_bf16(x)
-    prep = O.basis_prepare(_basis(O.bf16_to_f32(xb), 16))
-    L = O.project(xb, prep[0])
-    Lq, sL = O.lr_quantize(L, prep[2])
+    Vt, Vb = O.basis_prepare(_basis(O.bf16_to_f32(xb), 16))
+    L = O.project(xb, Vt)
+    exact = (L.astype(np.float64) @ O.bf16_to_f32(Vb).astype(np.float64).T).astype(np.float32)
+    assert np.array_equal(O.lowrank(L, Vb), exact)
     zero_codes = np.full((16, 64), 0x88, np.uint8)
-    xh = O.decode(zero_codes, np.zeros((16, 2), np.float32), Lq, sL, prep[1], None, None, 128, 4, 64, False)
-    # decode of an all-zero residual is bf16(fma(I, sL, 0)) = bf16(I * sL), I exact
-    ref = (Lq.astype(np.int64) @ prep[1].astype(np.int64).T).astype(np.float32) * sL[:, None]
-    assert np.array_equal(xh, O.f32_to_bf16(ref))
+    xh = O.decode(zero_codes, np.zeros((16, 2), np.float32), L, Vb, None, None, 128, 4, 64, False)
+    assert np.array_equal(xh, O.f32_to_bf16(exact))
+    # the projection is the exact product sum rounded once
+    Lx = (O.bf16_to_f32(xb).astype(np.float64) @ O.bf16_to_f32(Vt).astype(np.float64).T).astype(np.float32)
+    assert np.array_equal(L, Lx)
 
 
 def test_topk_channel_selection(O):
@@ -145,7 +147,7 @@ def test_fp32_activation_config1_shape(O):
     prep = O.basis_prepare(_basis(x, 16))
     enc = O.encode(x, prep, ch, 8, 128, False)
     assert enc["outliers"].dtype == np.float32
-    xh = O.decode(enc["codes"], enc["scales"], enc["lr_codes"], enc["lr_scale"], prep[1], enc["outliers"], ch, 512,
+    xh = O.decode(enc["codes"], enc["scales"], enc["lowrank"], prep[1], enc["outliers"], ch, 512,
                   8, 128, False, x_f32=True)
     assert np.array_equal(xh[:, ch], x[:, ch])
     assert O.rel_fro(xh, x) < 5e-3

@@ -17,6 +17,8 @@ c_i64 = ctypes.c_int64
 c_i32 = ctypes.c_int32
 c_vp = ctypes.c_void_p
 
+ABI_VERSION = 2  # ACTCOMP_ABI_VERSION in include/actcomp.h
+
 ACT_OK = 0
 ACT_E_INVALID = -1
 ACT_E_UNSUPPORTED = -2
@@ -42,9 +44,8 @@ class CgDesc(ctypes.Structure):
     _fields_ = [
         ("tokens", c_i64), ("channels", c_i64),
         ("bits", c_i32), ("group", c_i32), ("rank", c_i32), ("n_outlier", c_i32), ("wht", c_i32), ("batch", c_i32),
-        ("codes", c_vp), ("scales", c_vp), ("lr_codes", c_vp), ("lr_scale", c_vp), ("outliers", c_vp),
-        ("outlier_idx", c_vp), ("basis_t", c_vp), ("basis_q", c_vp), ("basis_scale", c_vp), ("basis_qb", c_vp),
-        ("basis_qs", c_vp),
+        ("codes", c_vp), ("scales", c_vp), ("lowrank", c_vp), ("outliers", c_vp), ("outlier_idx", c_vp),
+        ("basis_t", c_vp), ("basis", c_vp), ("basis_tile", c_vp),
     ]
 
 
@@ -84,7 +85,7 @@ SIGNATURES = {
     "actcomp_abi_version": (ctypes.c_int, []),
     "actcomp_last_device_error": (ctypes.c_int, [c_vp, ctypes.POINTER(ctypes.c_uint32)]),
     "actcomp_clear_device_error": (ctypes.c_int, [c_vp]),
-    "actcomp_cg_basis_prepare": (ctypes.c_int, [c_vp, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp, c_vp, c_vp]),
+    "actcomp_cg_basis_prepare": (ctypes.c_int, [c_vp, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp]),
     "actcomp_cg_encode": (ctypes.c_int, [ctypes.POINTER(CgDesc), c_vp, c_i64, c_vp]),
     "actcomp_cg_decode": (ctypes.c_int, [ctypes.POINTER(CgDesc), c_vp, c_i64, c_vp]),
     "actcomp_cg_consume": (ctypes.c_int, [ctypes.POINTER(CgDesc), c_i32, c_vp, c_i64, c_vp, c_i64, c_vp]),
@@ -131,8 +132,8 @@ def load() -> ctypes.CDLL:
             fn = getattr(lib, name)
             fn.restype = res
             fn.argtypes = args
-        if lib.actcomp_abi_version() != 1:
-            raise ImportError(f"{LIB_PATH}: ABI version {lib.actcomp_abi_version()} != 1")
+        if lib.actcomp_abi_version() != ABI_VERSION:
+            raise ImportError(f"{LIB_PATH}: ABI version {lib.actcomp_abi_version()} != {ABI_VERSION}")
         _lib = lib
         return lib
 

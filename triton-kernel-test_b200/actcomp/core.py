@@ -36,32 +36,38 @@ def _need_cuda(*ts: Optional[torch.Tensor]) -> None:
 # ====================================================================== basis
 @dataclass
 class Basis:
-    """A rank-r basis V (H x r per slice) prepared for the kernels.
+    """A rank-r basis V (H x r per slice), rounded to bf16 and laid out for the kernels.
 
-    ``basis_t`` (batch, r, H) bf16 is V^T for the projection; ``basis_q``
-    (batch, H, r) int8 with ``basis_scale`` (batch, r) is the quantised basis of
-    the reconstruction, whose integer products the kernels sum exactly;
-    ``basis_qb`` (bf16) and ``basis_qs`` (int8) hold the same integers in the
-    tensor-core encode's and decode's shared-memory tile layouts (see
-    include/actcomp.h); without them those kernels fall back to slower paths."""
+    ``basis_t`` (batch, r, H) is V^T for the projection, ``basis`` (batch, H, r)
+    is V for the CUDA-core reconstruction, ``basis_tile`` holds V in the
+    tensor-core kernels' shared-memory tile layout (include/actcomp.h); without
+    it those kernels decline and the CUDA-core kernels run.  All three hold the
+    same bf16 values: the format's basis is V rounded to bf16 once."""
 
     basis_t: torch.Tensor
-    basis_q: torch.Tensor
-    basis_scale: torch.Tensor
-    basis_qb: Optional[torch.Tensor] = None
-    basis_qs: Optional[torch.Tensor] = None
+    basis: torch.Tensor
+    basis_tile: Optional[torch.Tensor] = None
 
     @property
     def rank(self) -> int:
-        return self.basis_q.shape[-1]
+        return self.basis.shape[-1]
 
     @property
     def channels(self) -> int:
-        return self.basis_q.shape[-2]
+        return self.basis.shape[-2]
 
     @property
     def batch(self) -> int:
-        return self.basis_q.shape[0]
+        return self.basis.shape[0]
+
+    def vectors(self) -> torch.Tensor:
+        """The basis as float32 (batch, H, r): the exact values every kernel uses."""
+        return self.basis.to(torch.float32)
+
+    @staticmethod
+    def tile_numel(H: int, r: int, batch: int = 1) -> int:
+        rk = 16 if r <= 16 else (32 if r <= 32 else 64)
+        return batch * ((H + 127) // 128) * 128 * rk
 
     @staticmethod
     def from_vectors(V: torch.Tensor) -> "Basis":
@@ -72,15 +78,11 @@ class Basis:
         V = V.to(torch.float32).contiguous()
         b, H, r = V.shape
         bt = torch.empty((b, r, H), dtype=BF16, device=V.device)
-        bq = torch.empty((b, H, r), dtype=torch.int8, device=V.device)
-        bs = torch.empty((b, r), dtype=torch.float32, device=V.device)
-        rows = b * ((H + 127) // 128) * 128
-        rk = 16 if r <= 16 else (32 if r <= 32 else 64)
-        bqb = torch.empty((rows * rk,), dtype=BF16, device=V.device)  # tile operands (layout in actcomp.h)
-        bqs = torch.empty((rows * (32 if r <= 32 else 64),), dtype=torch.int8, device=V.device)
-        call("actcomp_cg_basis_prepare", V.data_ptr(), H, r, b, bt.data_ptr(), bq.data_ptr(), bs.data_ptr(),
-             bqb.data_ptr(), bqs.data_ptr(), _stream(V))
-        return Basis(bt, bq, bs, bqb, bqs)
+        bv = torch.empty((b, H, r), dtype=BF16, device=V.device)
+        tile = torch.empty((Basis.tile_numel(H, r, b),), dtype=BF16, device=V.device)  # layout in actcomp.h
+        call("actcomp_cg_basis_prepare", V.data_ptr(), H, r, b, bt.data_ptr(), bv.data_ptr(), tile.data_ptr(),
+             _stream(V))
+        return Basis(bt, bv, tile)
 
     @staticmethod
     def fit(x: torch.Tensor, rank: int) -> "Basis":
@@ -103,7 +105,7 @@ class Compressed:
     """One activation (batch x T x H bf16) in the channel-group format.
 
     Buffers (per slice, back to back): codes (T, H*bits/8) uint8, scales
-    (T, H/group) float32, lr_codes (T, r) int8, lr_scale (T,) float32,
+    (T, H/group) float32, lowrank (T, r) float32 = the projection X . V,
     outliers (T, k) bf16; outlier_idx (batch, k) int32 and the basis are
     shared inputs."""
 
@@ -115,8 +117,7 @@ class Compressed:
     batch: int
     codes: torch.Tensor
     scales: torch.Tensor
-    lr_codes: Optional[torch.Tensor]
-    lr_scale: Optional[torch.Tensor]
+    lowrank: Optional[torch.Tensor]
     outliers: Optional[torch.Tensor]
     outlier_idx: Optional[torch.Tensor]
     basis: Optional[Basis]
@@ -137,7 +138,7 @@ class Compressed:
     def buffers(self) -> dict:
         out = {"codes": self.codes, "scales": self.scales}
         if self.rank:
-            out.update(lr_codes=self.lr_codes, lr_scale=self.lr_scale)
+            out["lowrank"] = self.lowrank
         if self.n_outlier:
             out["outliers"] = self.outliers
         return out
@@ -151,13 +152,11 @@ class Compressed:
         d.tokens, d.channels, d.bits, d.group = self.tokens, self.channels, self.bits, self.group
         d.rank, d.n_outlier, d.wht, d.batch = self.rank, self.n_outlier, int(self.wht), self.batch
         d.codes, d.scales = _ptr(self.codes), _ptr(self.scales)
-        d.lr_codes, d.lr_scale = _ptr(self.lr_codes), _ptr(self.lr_scale)
+        d.lowrank = _ptr(self.lowrank)
         d.outliers, d.outlier_idx = _ptr(self.outliers), _ptr(self.outlier_idx)
         if self.basis is not None:
-            d.basis_t, d.basis_q, d.basis_scale = (self.basis.basis_t.data_ptr(), self.basis.basis_q.data_ptr(),
-                                                    self.basis.basis_scale.data_ptr())
-            d.basis_qb = _ptr(self.basis.basis_qb)
-            d.basis_qs = _ptr(self.basis.basis_qs)
+            d.basis_t, d.basis = self.basis.basis_t.data_ptr(), self.basis.basis.data_ptr()
+            d.basis_tile = _ptr(self.basis.basis_tile)
         return d
 
     def with_buffers(self, **bufs) -> "Compressed":
@@ -172,8 +171,7 @@ def empty_like_layout(tokens: int, channels: int, *, bits: int, group: int, rank
     bufs = {
         "codes": torch.empty((T, channels * bits // 8), dtype=torch.uint8, **kw),
         "scales": torch.empty((T, channels // group), dtype=torch.float32, **kw),
-        "lr_codes": torch.empty((T, rank), dtype=torch.int8, **kw) if rank else None,
-        "lr_scale": torch.empty((T,), dtype=torch.float32, **kw) if rank else None,
+        "lowrank": torch.empty((T, rank), dtype=torch.float32, **kw) if rank else None,
         "outliers": torch.empty((T, n_outlier), dtype=BF16, **kw) if n_outlier else None,
     }
     return bufs
@@ -189,9 +187,10 @@ def _rows(x: torch.Tensor) -> tuple[torch.Tensor, int, int, int]:
 
 def encode(x: torch.Tensor, basis: Optional[Basis] = None, outlier_idx: Optional[torch.Tensor] = None, *,
            bits: int = 4, group: int = 64, wht: bool = False) -> Compressed:
-    """Compress x ((T, H) or (batch, T, H) bf16) in one pass: projection onto
-    the basis, verbatim outlier channels, optional 128-wide Walsh-Hadamard
-    rotation of the residual, int4/int8 codes with per-token group scales."""
+    """Compress x ((T, H) or (batch, T, H) bf16): projection L = x . V onto the
+    basis, residual x - L . V^T with its outlier channels kept verbatim,
+    optional 128-wide Walsh-Hadamard rotation of the residual, int4/int8 codes
+    with per-token group-absmax scales."""
     _need_cuda(x)
     if x.dtype != BF16:
         raise TypeError("encode expects a bfloat16 activation")
@@ -207,8 +206,8 @@ def encode(x: torch.Tensor, basis: Optional[Basis] = None, outlier_idx: Optional
         if k == 0:
             outlier_idx = None
     bufs = empty_like_layout(T, H, bits=bits, group=group, rank=rank, n_outlier=k, batch=batch, device=x.device)
-    c = Compressed(T, H, bits, group, bool(wht), batch, bufs["codes"], bufs["scales"], bufs["lr_codes"],
-                   bufs["lr_scale"], bufs["outliers"], outlier_idx, basis)
+    c = Compressed(T, H, bits, group, bool(wht), batch, bufs["codes"], bufs["scales"], bufs["lowrank"],
+                   bufs["outliers"], outlier_idx, basis)
     d = c.desc()
     call("actcomp_cg_encode", ctypes.byref(d), x3.data_ptr(), ldx, _stream(x))
     return c

@@ -78,7 +78,7 @@ class Offloader:
         if self._pool is None:
             return
         h.done.synchronize()
-        bufs = {k: getattr(h.host, k) for k in ("codes", "scales", "lr_codes", "lr_scale", "outliers")}
+        bufs = {k: getattr(h.host, k) for k in ("codes", "scales", "lowrank", "outliers")}
         self._pool.setdefault(_layout_key(h.host), []).append(bufs)
 
     # ------------------------------------------------------------------ device -> host
@@ -97,8 +97,8 @@ class Offloader:
             t.record_stream(self.stream)
         # the layout without the device buffers (so they can be freed)
         empty = lambda t: None if t is None else torch.empty(0, dtype=t.dtype)
-        meta = c.with_buffers(codes=empty(c.codes), scales=empty(c.scales), lr_codes=empty(c.lr_codes),
-                              lr_scale=empty(c.lr_scale), outliers=empty(c.outliers))
+        meta = c.with_buffers(codes=empty(c.codes), scales=empty(c.scales), lowrank=empty(c.lowrank),
+                              outliers=empty(c.outliers))
         return HostActivation(meta=meta, host=host, done=done)
 
     # ------------------------------------------------------------------ host -> device

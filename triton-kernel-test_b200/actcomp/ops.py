@@ -12,7 +12,7 @@ import torch
 
 from . import core, refcompat
 
-_U8, _I8, _F32, _BF = torch.uint8, torch.int8, torch.float32, torch.bfloat16
+_U8, _F32, _BF = torch.uint8, torch.float32, torch.bfloat16
 
 
 def _empty(shape, dtype, like):
@@ -55,60 +55,54 @@ def _(l, r, x):
 
 
 # ---------------------------------------------------------------- channel-group format
-def _basis(basis_t, basis_q, basis_scale, basis_qb=None, basis_qs=None):
-    if basis_q is None or basis_q.numel() == 0:
+def _basis(basis_t, basis, basis_tile=None):
+    if basis is None or basis.numel() == 0:
         return None
-    return core.Basis(basis_t, basis_q, basis_scale, basis_qb, basis_qs)
+    return core.Basis(basis_t, basis, basis_tile)
 
 
 @torch.library.custom_op("actcomp::cg_encode", mutates_args=())
-def cg_encode(x: torch.Tensor, basis_t: Optional[torch.Tensor], basis_q: Optional[torch.Tensor],
-              basis_scale: Optional[torch.Tensor], basis_qb: Optional[torch.Tensor],
-              outlier_idx: Optional[torch.Tensor], bits: int, group: int,
-              wht: bool) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
-    c = core.encode(x, _basis(basis_t, basis_q, basis_scale, basis_qb), outlier_idx, bits=bits, group=group, wht=wht)
+def cg_encode(x: torch.Tensor, basis_t: Optional[torch.Tensor], basis: Optional[torch.Tensor],
+              basis_tile: Optional[torch.Tensor], outlier_idx: Optional[torch.Tensor], bits: int, group: int,
+              wht: bool) -> tuple[torch.Tensor, torch.Tensor, torch.Tensor, torch.Tensor]:
+    c = core.encode(x, _basis(basis_t, basis, basis_tile), outlier_idx, bits=bits, group=group, wht=wht)
     e = x.new_empty((0,))
-    return (c.codes, c.scales, c.lr_codes if c.rank else e.to(_I8), c.lr_scale if c.rank else e.to(_F32),
-            c.outliers if c.n_outlier else e)
+    return (c.codes, c.scales, c.lowrank if c.rank else e.to(_F32), c.outliers if c.n_outlier else e)
 
 
 @cg_encode.register_fake
-def _(x, basis_t, basis_q, basis_scale, basis_qb, outlier_idx, bits, group, wht):
+def _(x, basis_t, basis, basis_tile, outlier_idx, bits, group, wht):
     T = x.numel() // x.shape[-1]
     H = x.shape[-1]
-    r = 0 if basis_q is None else basis_q.shape[-1]
+    r = 0 if basis is None else basis.shape[-1]
     k = 0 if outlier_idx is None else outlier_idx.shape[-1]
-    return (_empty((T, H * bits // 8), _U8, x), _empty((T, H // group), _F32, x), _empty((T, r), _I8, x),
-            _empty((T if r else 0,), _F32, x), _empty((T, k) if k else (0,), _BF, x))
+    return (_empty((T, H * bits // 8), _U8, x), _empty((T, H // group), _F32, x),
+            _empty((T, r) if r else (0,), _F32, x), _empty((T, k) if k else (0,), _BF, x))
 
 
-def _compressed(shape, codes, scales, lr_codes, lr_scale, outliers, outlier_idx, basis_t, basis_q, basis_scale,
-                basis_qs, bits, group, wht):
+def _compressed(shape, codes, scales, lowrank, outliers, outlier_idx, basis_t, basis, basis_tile, bits, group, wht):
     batch = shape[0] if len(shape) == 3 else 1
     T, H = shape[-2], shape[-1]
-    basis = _basis(basis_t, basis_q, basis_scale, None, basis_qs)
+    b = _basis(basis_t, basis, basis_tile)
     k = 0 if outlier_idx is None else outlier_idx.shape[-1]
-    return core.Compressed(T, H, bits, group, wht, batch, codes, scales, lr_codes if basis else None,
-                           lr_scale if basis else None, outliers if k else None,
-                           outlier_idx.reshape(batch, -1) if k else None, basis)
+    return core.Compressed(T, H, bits, group, wht, batch, codes, scales, lowrank if b else None,
+                           outliers if k else None, outlier_idx.reshape(batch, -1) if k else None, b)
 
 
 @torch.library.custom_op("actcomp::cg_consume", mutates_args=())
-def cg_consume(shape: list[int], codes: torch.Tensor, scales: torch.Tensor, lr_codes: torch.Tensor,
-               lr_scale: torch.Tensor, outliers: torch.Tensor, outlier_idx: Optional[torch.Tensor],
-               basis_t: Optional[torch.Tensor], basis_q: Optional[torch.Tensor], basis_scale: Optional[torch.Tensor],
-               basis_qs: Optional[torch.Tensor], bits: int, group: int, wht: bool, op: int,
-               y: Optional[torch.Tensor]) -> torch.Tensor:
-    c = _compressed(shape, codes, scales, lr_codes, lr_scale, outliers, outlier_idx, basis_t, basis_q, basis_scale,
-                    basis_qs, bits, group, wht)
+def cg_consume(shape: list[int], codes: torch.Tensor, scales: torch.Tensor, lowrank: torch.Tensor,
+               outliers: torch.Tensor, outlier_idx: Optional[torch.Tensor], basis_t: Optional[torch.Tensor],
+               basis: Optional[torch.Tensor], basis_tile: Optional[torch.Tensor], bits: int, group: int, wht: bool,
+               op: int, y: Optional[torch.Tensor]) -> torch.Tensor:
+    c = _compressed(shape, codes, scales, lowrank, outliers, outlier_idx, basis_t, basis, basis_tile, bits, group,
+                    wht)
     if op == 0:
         return core.decode(c).reshape(shape)
     return core._consume(c, op, y.reshape(shape)).reshape(shape)
 
 
 @cg_consume.register_fake
-def _(shape, codes, scales, lr_codes, lr_scale, outliers, outlier_idx, basis_t, basis_q, basis_scale, basis_qs, bits,
-      group, wht, op, y):
+def _(shape, codes, scales, lowrank, outliers, outlier_idx, basis_t, basis, basis_tile, bits, group, wht, op, y):
     return _empty(tuple(shape), _BF, codes)
 
 

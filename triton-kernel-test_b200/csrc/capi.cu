@@ -28,8 +28,6 @@ int act_cg_consume_simt(const actcomp_cg_desc *d, int op, const uint16_t *y, int
                         int64_t ldo, cudaStream_t s);
 int act_cg_consume_tc(const actcomp_cg_desc *d, int op, const uint16_t *y, int64_t ldy, uint16_t *out, int64_t ldo,
                       cudaStream_t s);
-bool act_cg_encode_tc_supported(const actcomp_cg_desc *d);
-int act_cg_encode_tc(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cudaStream_t s);
 int act_cg_encode_rows(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cudaStream_t s);
 int act_cg_softmax_simt(const actcomp_cg_desc *d, const uint16_t *dp, uint16_t *ds, int64_t ld, int causal,
                         cudaStream_t s);
@@ -71,11 +69,14 @@ extern "C" int actcomp_clear_device_error(void *stream) {
 }
 
 // Decode: the row kernel where it covers the format, else the piece kernel
-// (narrow H); both give the same bits.
+// (narrow H), else the CUDA-core kernel.  Each declines (ACT_E_UNSUPPORTED,
+// before launching anything) what it does not cover.
 static int decode_tc(const actcomp_cg_desc *d, uint16_t *xhat, int64_t ldo, cudaStream_t s) {
-    const int st = act_cg_decode_rows(d, xhat, ldo, s);
+    int st = act_cg_decode_rows(d, xhat, ldo, s);
     if (st != ACT_E_UNSUPPORTED) return st;
-    return act_cg_consume_tc(d, ACT_OP_DECODE, nullptr, 0, xhat, ldo, s);
+    st = act_cg_consume_tc(d, ACT_OP_DECODE, nullptr, 0, xhat, ldo, s);
+    if (st != ACT_E_UNSUPPORTED) return st;
+    return act_cg_consume_simt(d, ACT_OP_DECODE, nullptr, 0, xhat, ldo, s);
 }
 
 // Vector access requirements shared by the encode/decode kernels.
@@ -91,15 +92,11 @@ extern "C" int actcomp_cg_encode(const actcomp_cg_desc *d, const uint16_t *x, in
     if (st) return st;
     if ((st = check_rows(x, ldx, d->channels))) return st;
     if (d->rank) ACT_CHECK(d->basis_t && aligned(d->basis_t, 16), ACT_E_ALIGN);
-    // the row kernel, else the piece kernel (above 16384 or below 1024 channels), else
-    // the CUDA-core encode: each declines (ACT_E_UNSUPPORTED, before
-    // launching) what it does not cover, and all compute the same codes
+    // the tensor-core row encode, else (rank 0, H outside 1024..16384 or not a
+    // multiple of 128, no basis tile) the CUDA-core encode; the row encode
+    // declines (ACT_E_UNSUPPORTED, before launching) what it does not cover
     st = act_cg_encode_rows(d, x, ldx, as_stream(stream));
     if (st != ACT_E_UNSUPPORTED) return st;
-    if (act_cg_encode_tc_supported(d)) {
-        st = act_cg_encode_tc(d, x, ldx, as_stream(stream));
-        if (st != ACT_E_UNSUPPORTED) return st;
-    }
     return act_cg_encode_simt(d, x, ldx, as_stream(stream));
 }
 
@@ -118,7 +115,9 @@ extern "C" int actcomp_cg_consume(const actcomp_cg_desc *d, int32_t op, const ui
     if ((st = check_rows(out, ldo, d->channels))) return st;
     if (op != ACT_OP_DECODE && (st = check_rows(y, ldy, d->channels))) return st;
     if (op == ACT_OP_DECODE) return decode_tc(d, out, ldo, as_stream(stream));
-    return act_cg_consume_tc(d, op, y, ldy, out, ldo, as_stream(stream));
+    st = act_cg_consume_tc(d, op, y, ldy, out, ldo, as_stream(stream));
+    if (st != ACT_E_UNSUPPORTED) return st;
+    return act_cg_consume_simt(d, op, y, ldy, out, ldo, as_stream(stream));
 }
 
 extern "C" size_t actcomp_cg_softmax_workspace(const actcomp_cg_desc *d) {
@@ -135,7 +134,9 @@ extern "C" int actcomp_cg_softmax_bwd(const actcomp_cg_desc *d, const uint16_t *
     if (!workspace) return act_cg_softmax_simt(d, dp, ds, ld, causal != 0, as_stream(stream));
     ACT_CHECK(workspace_bytes >= act_cg_softmax_tc_workspace(d), ACT_E_WORKSPACE);
     ACT_CHECK(aligned(workspace, 16), ACT_E_ALIGN);
-    return act_cg_softmax_tc(d, dp, ds, ld, causal != 0, workspace, as_stream(stream));
+    st = act_cg_softmax_tc(d, dp, ds, ld, causal != 0, workspace, as_stream(stream));
+    if (st != ACT_E_UNSUPPORTED) return st;
+    return act_cg_softmax_simt(d, dp, ds, ld, causal != 0, as_stream(stream));
 }
 
 extern "C" size_t actcomp_cg_dw_workspace(const actcomp_cg_desc *d, int64_t N) {
@@ -195,10 +196,7 @@ extern "C" int actcomp_cg_copy(const actcomp_cg_desc *dst, const actcomp_cg_desc
     int st;
     if ((st = cp(dst->codes, src->codes, T * H * src->bits / 8))) return st;
     if ((st = cp(dst->scales, src->scales, T * (H / src->group) * 4))) return st;
-    if (src->rank) {
-        if ((st = cp(dst->lr_codes, src->lr_codes, T * src->rank))) return st;
-        if ((st = cp(dst->lr_scale, src->lr_scale, T * 4))) return st;
-    }
+    if (src->rank && (st = cp(dst->lowrank, src->lowrank, T * src->rank * 4))) return st;
     if (src->n_outlier && (st = cp(dst->outliers, src->outliers, T * src->n_outlier * 2))) return st;
     return ACT_OK;
 }

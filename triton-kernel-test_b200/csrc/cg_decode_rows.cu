@@ -6,17 +6,15 @@
 //   warp 0      producer: per tile one bulk copy of the prepared bf16 basis
 //               tile (128 channels x r) and one TMA load of the residual codes
 //               into an S-stage ring; per token block one bulk copy of its
-//               low-rank codes (128 x r int8) and of its outlier values;
-//   warp 1      MMA: per token block converts the low-rank codes to bf16 (exact
-//               integers) in a swizzled operand tile; per tile one
-//               tcgen05.mma kind::f16 (M=128, N=128, K=16 steps) gives
-//               I = Lq . Vq^T as exact fp32 integers in TMEM (every product and
-//               partial sum is an integer below 2^24), one accumulator per
-//               epilogue group;
+//               projection L (128 x r float32) and of its outlier values;
+//   warp 1      MMA: per token block splits L into its three exact bf16 pieces
+//               (three swizzled operand tiles); per tile tcgen05.mma kind::f16
+//               (M=128, N=128, K=16 steps, three pieces) gives the low-rank term
+//               P = L . V^T in float32 in TMEM, one accumulator per epilogue group;
 //   warps 2-17  epilogue: four groups of four warps, group g takes the tiles
 //               g, g+4, g+8, ... of the range; a thread owns one token row of
 //               the tile and all 128 channels, processed as four 32-channel
-//               pieces: xhat = bf16(fma(I, sL, (u - 2^(b-1)) * s)), outlier
+//               pieces: xhat = bf16(P + (u - 2^(b-1)) * s), outlier
 //               channels verbatim; each warp stores its 32 rows x 64 channels
 //               (two pieces) with one TMA store.
 // Rotated formats run two epilogue groups (8 warps, up to 168 registers per
@@ -24,8 +22,9 @@
 // butterfly stages in registers and scales by 1/128, then adds the low-rank
 // term piece by piece.
 // Per-tile costs (waits, scalars, arrivals) are paid once per 128 channels of
-// a row instead of once per 32, and the low-rank term needs no int32 -> float
-// conversion.  Arithmetic is that of oracle/actcomp_oracle.c (cg_decode).
+// a row instead of once per 32.  Arithmetic is that of oracle/actcomp_oracle.c
+// (cg_decode), except that the tensor cores sum the low-rank term in their own
+// order (a few float32 ulps).
 #include <cudaTypedefs.h>
 
 #include "tc_ptx.cuh"
@@ -68,11 +67,10 @@ struct RowParams {
     int ostage;            // outlier values staged in shared memory per token block
     int ostb;              // bytes of one outlier slot
     const float *scales;
-    const float *lr_scale;
-    const int8_t *lrq;
+    const float *lr;       // projection L, T x rank float32 per slice
     const uint16_t *outliers;
     const int32_t *idx;
-    const uint16_t *vqb;   // basis_qb tile operand
+    const uint16_t *vtile; // basis tile operand
     int off_stg, off_lqb, off_lqi, off_ost, off_bar, off_ot;
 };
 
@@ -83,10 +81,10 @@ struct RowLayout {
     static constexpr int CODE_ROW = CH * BITS / 8;      // code bytes of one token row of a tile
     static constexpr int CODES = ROWS * CODE_ROW;
     static constexpr int STAGE = VQ + CODES;
-    static constexpr int LQB = RK ? ROWS * LB : 0;      // bf16 low-rank operand of a token block
+    static constexpr int LQB = RK ? 3 * ROWS * LB : 0;  // the three bf16 pieces of a token block's L
     // returns the shared-memory bytes, or 0 if S < 3 stages would fit
     static int plan(RowParams &p, int nsl, int EW) {
-        const int lqi = p.rank ? ROWS * p.rank : 0;
+        const int lqi = p.rank ? ROWS * p.rank * 4 : 0;  // float32 L of a token block
         const int fixed_no_ost = EW * WSTG + 2 * LQB + 2 * ((lqi + 1023) & ~1023) + 1024 /*bars*/ +
                                  ((nsl * p.n32 * 8 + 15) & ~15) + 1024 /*align*/;
         const int ostb = (ROWS * p.k * 2 + 15) & ~15;
@@ -238,7 +236,7 @@ __global__ void __launch_bounds__(Geo<WHT>::THREADS, 1)
     uint8_t *lqb = smem + p.off_lqb;
     uint8_t *lqi = smem + p.off_lqi;
     uint8_t *ostbuf = smem + p.off_ost;
-    const int lqi_slot = ((p.rank * ROWS) + 1023) & ~1023;
+    const int lqi_slot = ((p.rank * ROWS * 4) + 1023) & ~1023;
     const bool use_ost = p.k > 0 && p.ostage;
     const bool blockbuf = RK > 0 || use_ost;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -292,10 +290,10 @@ __global__ void __launch_bounds__(Geo<WHT>::THREADS, 1)
                     const uint32_t obytes = p.k ? ost_bytes(p, tw.tb, tw.b, osrc) : 0;
                     const int64_t rows =
                         (p.T - (int64_t)tw.tb * ROWS) < ROWS ? (p.T - (int64_t)tw.tb * ROWS) : ROWS;
-                    const uint32_t lbytes = RK ? (uint32_t)(rows * p.rank) : 0;
+                    const uint32_t lbytes = RK ? (uint32_t)(rows * p.rank * 4) : 0;
                     tc::mbar_arrive_expect_tx(&lqfull[ls], lbytes + obytes);
                     if (RK)
-                        tc::bulk_load(lqi + ls * lqi_slot, p.lrq + ((int64_t)tw.b * p.T + (int64_t)tw.tb * ROWS) * p.rank,
+                        tc::bulk_load(lqi + ls * lqi_slot, p.lr + ((int64_t)tw.b * p.T + (int64_t)tw.tb * ROWS) * p.rank,
                                       lbytes, &lqfull[ls]);
                     if (obytes) tc::bulk_load(ostbuf + ls * p.ostb, osrc, obytes, &lqfull[ls]);
                     ++nlq;
@@ -304,7 +302,7 @@ __global__ void __launch_bounds__(Geo<WHT>::THREADS, 1)
                 uint8_t *st = smem + s * L::STAGE;
                 tc::mbar_arrive_expect_tx(&full[s], L::STAGE);
                 if constexpr (RK > 0)
-                    tc::bulk_load(st, p.vqb + ((int64_t)tw.b * p.ncc + tw.cc) * (CH * LB / 2), L::VQ, &full[s]);
+                    tc::bulk_load(st, p.vtile + ((int64_t)tw.b * p.ncc + tw.cc) * (CH * LB / 2), L::VQ, &full[s]);
                 tc::tma_load_3d(st + L::VQ, &tm_codes, &full[s], tw.cc * L::CODE_ROW, tw.tb * ROWS, tw.b);
             }
         }
@@ -321,34 +319,38 @@ __global__ void __launch_bounds__(Geo<WHT>::THREADS, 1)
                 const int s = i % S, acc = i & (NG - 1);
                 const uint32_t ph = (i / S) & 1, aph = (i / NG) & 1;
                 if (tile == t_lo || tw.cc == 0) {
-                    // a new token block: its low-rank codes as a bf16 operand tile
+                    // a new token block: its projection as three bf16 operand tiles
                     const int ls = mlq & 1;
                     int okw = 1;
                     if (lane == 0) okw = tc::mbar_wait(&lqfull[ls], (mlq >> 1) & 1, abort);
                     if (!(ok = __shfl_sync(0xffffffffu, okw, 0) != 0)) break;
-                    const int8_t *src = reinterpret_cast<const int8_t *>(lqi + ls * lqi_slot);
+                    const float *src = reinterpret_cast<const float *>(lqi + ls * lqi_slot);
                     uint8_t *dst = lqb + ls * L::LQB;
-                    // 8 codes (one 8-byte load) per 16-byte chunk of the bf16 tile;
-                    // chunks past the rank are zero
+                    // 8 coefficients (two 16-byte loads) per 16-byte chunk of each
+                    // piece tile; chunks past the rank and rows past T are zero
                     const int cpr = LB / 16;  // chunks per row
+                    const int64_t rows_here = p.T - (int64_t)tw.tb * ROWS;
                     for (int e = lane; e < ROWS * cpr; e += 32) {
                         const int row = e / cpr, c16 = e - row * cpr;
-                        uint4 o = make_uint4(0u, 0u, 0u, 0u);
-                        if (8 * c16 < p.rank) {
-                            const uint2 v = *reinterpret_cast<const uint2 *>(src + row * p.rank + 8 * c16);
-                            const uint32_t in[2] = {v.x, v.y};
-                            uint32_t w[4];
+                        uint32_t ph[4] = {0u, 0u, 0u, 0u}, pm[4] = {0u, 0u, 0u, 0u}, pl[4] = {0u, 0u, 0u, 0u};
+                        if (8 * c16 < p.rank && row < rows_here) {
+                            const float4 v0 = *reinterpret_cast<const float4 *>(src + row * p.rank + 8 * c16);
+                            const float4 v1 = *reinterpret_cast<const float4 *>(src + row * p.rank + 8 * c16 + 4);
+                            const float in[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
 #pragma unroll
                             for (int h = 0; h < 4; ++h) {
-                                const uint32_t word = in[h >> 1];
-                                const int sh = (h & 1) * 16;
-                                const float f0 = (float)(int)(int8_t)(word >> sh);
-                                const float f1 = (float)(int)(int8_t)(word >> (sh + 8));
-                                w[h] = pack_bf16x2(f0, f1);
+                                float h0, m0, l0, h1, m1, l1;
+                                split3_bf16(in[2 * h], h0, m0, l0);
+                                split3_bf16(in[2 * h + 1], h1, m1, l1);
+                                ph[h] = pack_bf16x2(h0, h1);
+                                pm[h] = pack_bf16x2(m0, m1);
+                                pl[h] = pack_bf16x2(l0, l1);
                             }
-                            o = make_uint4(w[0], w[1], w[2], w[3]);
                         }
-                        *reinterpret_cast<uint4 *>(dst + swz<LB>(row, c16)) = o;
+                        const int o = swz<LB>(row, c16);
+                        *reinterpret_cast<uint4 *>(dst + o) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
+                        *reinterpret_cast<uint4 *>(dst + ROWS * LB + o) = make_uint4(pm[0], pm[1], pm[2], pm[3]);
+                        *reinterpret_cast<uint4 *>(dst + 2 * ROWS * LB + o) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
                     }
                     tc::fence_proxy_async();
                     __syncwarp();
@@ -362,11 +364,13 @@ __global__ void __launch_bounds__(Geo<WHT>::THREADS, 1)
                         tc::tc_fence_after();
                         const uint8_t *st = smem + s * L::STAGE;
                         const uint8_t *a = lqb + ls * L::LQB;
-                        for (int kk = 0; kk < nkq; ++kk) {
-                            const uint64_t ad = tc::smem_desc(a + kk * 32, 16, 8 * LB, SW);
-                            const uint64_t bd = tc::smem_desc(st + kk * 32, 16, 8 * LB, SW);
-                            tc::mma_f16(tmem + acc * CH, ad, bd, idesc, kk > 0);
-                        }
+                        // P = hi . V^T + mid . V^T + lo . V^T
+                        for (int pc = 0; pc < 3; ++pc)
+                            for (int kk = 0; kk < nkq; ++kk) {
+                                const uint64_t ad = tc::smem_desc(a + pc * ROWS * LB + kk * 32, 16, 8 * LB, SW);
+                                const uint64_t bd = tc::smem_desc(st + kk * 32, 16, 8 * LB, SW);
+                                tc::mma_f16(tmem + acc * CH, ad, bd, idesc, (pc | kk) > 0);
+                            }
                         tc::mma_commit(&tfull[acc]);
                         tc::mma_commit(&empty[s]);
                         // last tile of this token block in the range: the slot frees when these MMAs complete
@@ -409,13 +413,11 @@ __global__ void __launch_bounds__(Geo<WHT>::THREADS, 1)
             tc::named_bar(1, 32 * EW);  // complete before any epilogue warp reads it
         }
 
-        // per-row scalars of a tile: the group scales of its 128 channels and
-        // the low-rank scale, loaded PD group tiles ahead
+        // per-row scalars of a tile: the group scales of its 128 channels,
+        // loaded PD group tiles ahead
         float4 qsc[PD];
-        float qsl[PD];
-        auto load_scalars = [&](int64_t tile, const Walk &at, float4 &vsc, float &vsl) {
+        auto load_scalars = [&](int64_t tile, const Walk &at, float4 &vsc) {
             vsc = make_float4(0.f, 0.f, 0.f, 0.f);
-            vsl = 0.f;
             if (tile >= t_hi) return;
             const int64_t t = (int64_t)at.tb * ROWS + r;
             if (t >= p.T) return;
@@ -430,7 +432,6 @@ __global__ void __launch_bounds__(Geo<WHT>::THREADS, 1)
                 const float v = __ldg(sp);
                 vsc = make_float4(v, v, v, v);
             }
-            if (RK) vsl = __ldg(p.lr_scale + trow);
         };
         auto step4 = [](Walk &w) {
 #pragma unroll
@@ -439,7 +440,7 @@ __global__ void __launch_bounds__(Geo<WHT>::THREADS, 1)
         Walk tw(t_lo + g < t_hi ? t_lo + g : t_lo, p.ncc, p.ntb), nw = tw;
 #pragma unroll
         for (int d = 0; d < PD; ++d) {
-            load_scalars(t_lo + g + NG * d, nw, qsc[d], qsl[d]);
+            load_scalars(t_lo + g + NG * d, nw, qsc[d]);
             step4(nw);
         }
         const int64_t blk_lo = t_lo / p.ncc;
@@ -452,13 +453,9 @@ __global__ void __launch_bounds__(Geo<WHT>::THREADS, 1)
             const uint32_t ph = (i / S) & 1, aph = j & 1;
             const int cc = tw.cc, tb = tw.tb, b = tw.b;
             const float4 sc4 = qsc[0];
-            const float sl = qsl[0];
 #pragma unroll
-            for (int d = 0; d + 1 < PD; ++d) {
-                qsc[d] = qsc[d + 1];
-                qsl[d] = qsl[d + 1];
-            }
-            load_scalars(tile + NG * PD, nw, qsc[PD - 1], qsl[PD - 1]);
+            for (int d = 0; d + 1 < PD; ++d) qsc[d] = qsc[d + 1];
+            load_scalars(tile + NG * PD, nw, qsc[PD - 1]);
             step4(nw);
 
             const int64_t blk = tw.block();
@@ -584,10 +581,9 @@ __global__ void __launch_bounds__(Geo<WHT>::THREADS, 1)
                 }  // unrotated
                 if constexpr (RK > 0) {
                     tc::tmem_ld_wait();
-                    const float2 sl2 = make_float2(sl, sl);
 #pragma unroll
                     for (int e = 0; e < 16; ++e)
-                        w[e] = fma2(make_float2(__uint_as_float(I[2 * e]), __uint_as_float(I[2 * e + 1])), sl2, w[e]);
+                        w[e] = add2(make_float2(__uint_as_float(I[2 * e]), __uint_as_float(I[2 * e + 1])), w[e]);
                     if (k == 3) {  // the accumulator has been read
                         tc::tc_fence_before();
                         __syncwarp();
@@ -687,11 +683,10 @@ int launch(const actcomp_cg_desc *d, uint16_t *out, int64_t ldo, cudaStream_t st
     p.ntiles = (int64_t)p.ntb * p.ncc * B;
     p.n32 = (int)(H / 32);
     p.scales = d->scales;
-    p.lr_scale = d->lr_scale;
-    p.lrq = d->lr_codes;
+    p.lr = d->lowrank;
     p.outliers = d->outliers;
     p.idx = d->outlier_idx;
-    p.vqb = d->basis_qb;
+    p.vtile = d->basis_tile;
     const int grid = (int)(p.ntiles < num_sms() ? p.ntiles : num_sms());
     p.tq = (int)(p.ntiles / grid);
     p.trem = (int)(p.ntiles % grid);
@@ -713,13 +708,13 @@ int launch(const actcomp_cg_desc *d, uint16_t *out, int64_t ldo, cudaStream_t st
 // formats it does not cover: H not a multiple of 128 or below 512
 // (with at least 4 tiles per token block no group of warps skips a block in
 // the middle of its range, which the per-block barrier phases rely on), a
-// rank without the bf16 basis operand, or unaligned low-rank codes.
+// rank without the basis tile operand, or an unaligned projection.
 int act_cg_decode_rows(const actcomp_cg_desc *d, uint16_t *out, int64_t ldo, cudaStream_t s) {
     using namespace act::cgrow;
     if (d->tokens == 0) return ACT_OK;
     if (d->channels % CH != 0 || d->channels < 4 * CH || !act::aligned(d->scales, 16))
         return ACT_E_UNSUPPORTED;
-    if (d->rank && (!d->basis_qb || !act::aligned(d->basis_qb, 16) || !act::aligned(d->lr_codes, 16)))
+    if (d->rank && (!d->basis_tile || !act::aligned(d->basis_tile, 16) || !act::aligned(d->lowrank, 16)))
         return ACT_E_UNSUPPORTED;
     const int rk = d->rank == 0 ? 0 : (d->rank <= 16 ? 16 : (d->rank <= 32 ? 32 : 64));
 #define ACT_DECR(B, W)                                       \

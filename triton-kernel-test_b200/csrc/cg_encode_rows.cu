@@ -10,25 +10,27 @@
 //               channels, so that it starts on the columns the projection left
 //               in L2) TMA re-reads X[128 x 128] and bulk-copies the chunk's
 //               prepared bf16 basis tile;
-//   warp 3      residual MMA: I = Lq . Vq^T (kind::f16 on exact bf16 integers,
-//               fp32 accumulator exact) into one of three TMEM accumulators;
+//   warp 3      low-rank MMA: P = L . V^T (kind::f16, L as its three exact bf16
+//               pieces against the bf16 basis, fp32 accumulation) into one of
+//               three TMEM accumulators;
 //   warps 4-15  epilogue: three groups of four warps; group g takes chunks
 //               g, g+3, g+6, ... (counted over all blocks of the CTA); a thread
 //               owns one token row of a chunk and all its 128 channels.  Pass 1,
-//               per 32-channel piece: residual fma(-I, sL, x), outlier channels
+//               per 32-channel piece: residual x - P, outlier channels
 //               copied out and zeroed, piece absmax, residual written back over
-//               I in TMEM.  With the rotation, pass 1 also applies the butterfly
+//               P in TMEM.  With the rotation, pass 1 also applies the butterfly
 //               stages 1..16 inside each piece, and stages 32 and 64 then combine
 //               the four pieces eight TMEM columns at a time (oracle stage order).
 //               Pass 2: group scales (one correctly rounded division
 //               each, as the oracle), residual read back, codes packed and staged;
 //               each warp stores its 32 rows of codes with one TMA store and
 //               writes its rows' scales directly.
-//   Group 0 also turns the projection into the per-token low-rank codes Lq
-//   (bf16 operand tile, double-buffered) and their scale sL.
+//   Group 0 also stores the projection L (float32) and writes its three bf16
+//   pieces as the low-rank MMA's operand tiles (double-buffered).
 // No two epilogue warps exchange data inside a chunk: no named barriers on the
-// chunk path.  Arithmetic matches oracle/actcomp_oracle.c (cg_encode_given_lr)
-// bit for bit given the projection.
+// chunk path.  Arithmetic is that of oracle/actcomp_oracle.c
+// (cg_encode_given_lr) given the projection, except that the tensor cores sum
+// the low-rank term in their own order (a few float32 ulps).
 #include <cudaTypedefs.h>
 
 #include "tc_ptx.cuh"
@@ -45,13 +47,11 @@ constexpr int MAXNA = 6, MAXNB = 4;
 struct Params {
     int64_t T, H;
     int rank, k, group, batch;
-    const float *basis_scale;
     float *scales;
-    int8_t *lrq;
-    float *lrs;
+    float *lr;
     uint16_t *outl;
     const int32_t *idx;
-    const uint16_t *vqb;
+    const uint16_t *vtile;
     int nk2;          // 128-channel chunks per block
     int ntb;          // token blocks per slice
     int64_t nblocks;
@@ -67,7 +67,7 @@ struct Layout {
     static constexpr int LB = 2 * RK;
     static constexpr int SLOT_A = 16 * 1024 + RK * 128;
     static constexpr int SLOT_B = 32 * 1024 + CH * LB;
-    static constexpr int LQT = ROWS * LB;
+    static constexpr int LQT = 3 * ROWS * LB;  // the three bf16 pieces of L, one tile each
     static constexpr int CROW = CH * BITS / 8;  // code bytes of one token row of a chunk
     static constexpr int WSTG = 32 * CROW;      // one warp's code staging (32 rows)
     // alias: every CTA encodes one block, so the residual ring may reuse the
@@ -84,10 +84,8 @@ struct Layout {
         p.off_stg = p.off_bar + 1024;
         p.off_ot = p.off_stg + EW * WSTG;
         p.off_ost = p.off_ot + ((p.ngs * 12 + 15) & ~15);
-        // group 0's per-warp copies of the slice's basis scales (4 x 64 floats),
-        // then the low-rank scales of the last two blocks (2 x 128 floats)
         p.off_sv = p.off_ost + (ostage ? ((ROWS * k * 2 + 15) & ~15) : 0);
-        return p.off_sv + 4 * 64 * 4 + 2 * ROWS * 4 + 1024;
+        return p.off_sv + 1024;
     }
 };
 
@@ -137,15 +135,15 @@ __global__ void __launch_bounds__(THREADS, 1)
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     const int NA = p.na, NB = p.nb;
     uint8_t *ringA = smem, *ringB = smem + p.off_ringB;
-    uint8_t *lqt = smem + p.off_lqt;  // [2] bf16 low-rank code tiles
+    uint8_t *lqt = smem + p.off_lqt;  // [2] x 3 bf16 piece tiles of L
     uint64_t *fullA = reinterpret_cast<uint64_t *>(smem + p.off_bar);
     uint64_t *emptyA = fullA + MAXNA;
     uint64_t *fullB = emptyA + MAXNA;
     uint64_t *emptyB = fullB + MAXNB;
     uint64_t *tfull = emptyB + MAXNB;  // [NGR]
     uint64_t *tempty = tfull + NGR;    // [NGR]
-    uint64_t *lqready = tempty + NGR;  // [2] low-rank codes of a block written (by group 0)
-    uint64_t *lqfree = lqready + 2;    // [2] the residual MMAs of a block have read its code tile
+    uint64_t *lqready = tempty + NGR;  // [2] the piece tiles of a block written (by group 0)
+    uint64_t *lqfree = lqready + 2;    // [2] the low-rank MMAs of a block have read its piece tiles
     uint64_t *lfull = lqfree + 2;      // projection accumulator complete
     uint64_t *lempty = lfull + 1;      // ... and read
     uint64_t *lseen = lempty + 1;      // the phase-2 producer has observed lfull of the block
@@ -254,13 +252,13 @@ __global__ void __launch_bounds__(THREADS, 1)
                     const int x = (nk2 - 1 - ck) * CH;  // backward sweep
                     tc::tma_load_3d(st, &tm_x, &fullB[s], x, tb * ROWS, b);
                     tc::tma_load_3d(st + ROWS * 128, &tm_x, &fullB[s], x + 64, tb * ROWS, b);
-                    tc::bulk_load(st + 32 * 1024, p.vqb + ((int64_t)b * nk2 + x / CH) * (CH * LB / 2), CH * LB,
+                    tc::bulk_load(st + 32 * 1024, p.vtile + ((int64_t)b * nk2 + x / CH) * (CH * LB / 2), CH * LB,
                                   &fullB[s]);
                 }
             }
         }
     } else if (warp == 3) {
-        // ------------------------------------------------------------ residual MMA
+        // ------------------------------------------------------------ low-rank MMA
         if (lane == 0) {
             constexpr uint32_t id_q = tc::idesc_f16(ROWS, CH, true, false, false);
             constexpr tc::Swizzle SWQ = swz_mode<LB>();
@@ -278,11 +276,13 @@ __global__ void __launch_bounds__(THREADS, 1)
                     if (!(ok = tc::mbar_wait(&tempty[acc], ((i / NGR) & 1) ^ 1, abort))) break;
                     tc::tc_fence_after();
                     uint8_t *st = ringB + s * L::SLOT_B;
-                    for (int kk = 0; kk < nkq; ++kk) {
-                        const uint64_t ad = tc::smem_desc(a + kk * 32, 16, 8 * LB, SWQ);
-                        const uint64_t bd = tc::smem_desc(st + 32 * 1024 + kk * 32, 16, 8 * LB, SWQ);
-                        tc::mma_f16(tm_p + acc * CH, ad, bd, id_q, kk > 0);
-                    }
+                    // P = hi . V^T + mid . V^T + lo . V^T
+                    for (int pc = 0; pc < 3; ++pc)
+                        for (int kk = 0; kk < nkq; ++kk) {
+                            const uint64_t ad = tc::smem_desc(a + pc * ROWS * LB + kk * 32, 16, 8 * LB, SWQ);
+                            const uint64_t bd = tc::smem_desc(st + 32 * 1024 + kk * 32, 16, 8 * LB, SWQ);
+                            tc::mma_f16(tm_p + acc * CH, ad, bd, id_q, (pc | kk) > 0);
+                        }
                     tc::mma_commit(&tfull[acc]);
                     tc::mma_commit(&emptyB[s]);
                 }
@@ -318,77 +318,52 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int64_t trow = (int64_t)b * p.T + t;
             const int nrows = (int)((p.T - (int64_t)tb * ROWS) < ROWS ? (p.T - (int64_t)tb * ROWS) : ROWS);
             const int ls = nb & 1;
-            float sl = 0.f;
-            float *svw = reinterpret_cast<float *>(smem + p.off_sv) + 64 * (warp & 3);  // group 0 only
-            float *slr = reinterpret_cast<float *>(smem + p.off_sv) + 4 * 64;       // [2][128]
             if (g == 0 && ok) do {
-                // ---- projection -> per-token low-rank codes (group 0: one token row per thread)
-                // the slice's basis scales into this warp's copy while the projection streams
-                for (int e = lane; e < r; e += 32) svw[e] = __ldg(p.basis_scale + (int64_t)b * r + e);
-                __syncwarp();
+                // ---- projection -> L (float32, stored) and its three bf16 pieces
+                // (group 0: one token row per thread)
                 if (!(ok = tc::mbar_wait(lfull, nb & 1, abort))) break;
+                // the piece tiles' slot is free once the low-rank MMAs of block nb - 2 completed
+                if (nb >= 2 && !(ok = tc::mbar_wait(&lqfree[ls], ((nb >> 1) & 1) ^ 1, abort))) break;
                 tc::tc_fence_after();
-                float Lr[RK];
-                {
+                uint8_t *lq = lqt + ls * L::LQT;
+                // 32 coefficients at a time: L to global memory, pieces to the tiles
+#pragma unroll
+                for (int jj = 0; jj < (RK + 31) / 32; ++jj) {
+                    constexpr int NC = RK < 32 ? RK : 32;
                     uint32_t v[32];
+                    tc::tmem_ld32(tm_l + ((uint32_t)(q * 32) << 16) + 32 * jj, v);
+                    tc::tmem_ld_wait();
+                    float Lr[NC];
 #pragma unroll
-                    for (int jj = 0; jj < (RK + 31) / 32; ++jj) {
-                        tc::tmem_ld32(tm_l + ((uint32_t)(q * 32) << 16) + 32 * jj, v);
-                        tc::tmem_ld_wait();
+                    for (int e = 0; e < NC; ++e) Lr[e] = 32 * jj + e < r ? __uint_as_float(v[e]) : 0.f;
+                    if (rv) {
+                        float4 *dst = reinterpret_cast<float4 *>(p.lr + trow * r + 32 * jj);
 #pragma unroll
-                        for (int e = 0; e < 32; ++e)
-                            if (32 * jj + e < RK) Lr[32 * jj + e] = __uint_as_float(v[e]);
+                        for (int e = 0; e < NC / 4; ++e)
+                            if (32 * jj + 4 * e < r)
+                                dst[e] = make_float4(Lr[4 * e], Lr[4 * e + 1], Lr[4 * e + 2], Lr[4 * e + 3]);
+                    }
+#pragma unroll
+                    for (int c8 = 0; c8 < NC / 8; ++c8) {  // 8 coefficients = one 16-byte chunk per piece
+                        uint32_t ph[4], pm[4], pl[4];
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            float h0, m0, l0, h1, m1, l1;
+                            split3_bf16(Lr[8 * c8 + 2 * e], h0, m0, l0);
+                            split3_bf16(Lr[8 * c8 + 2 * e + 1], h1, m1, l1);
+                            ph[e] = pack_bf16x2(h0, h1);
+                            pm[e] = pack_bf16x2(m0, m1);
+                            pl[e] = pack_bf16x2(l0, l1);
+                        }
+                        const int o = swz<LB>(row, 4 * jj + c8);
+                        *reinterpret_cast<uint4 *>(lq + o) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
+                        *reinterpret_cast<uint4 *>(lq + ROWS * LB + o) = make_uint4(pm[0], pm[1], pm[2], pm[3]);
+                        *reinterpret_cast<uint4 *>(lq + 2 * ROWS * LB + o) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
                     }
                 }
                 tc::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(lempty);
-                // Lq = nearest(L * sV * 127 / max|L * sV|), one fma
-                float amax = 0.f;
-#pragma unroll
-                for (int e = 0; e < RK; ++e) {
-                    if (e < r) {
-                        Lr[e] = __fmul_rn(Lr[e], svw[e]);
-                        amax = fmaxf(amax, fabsf(Lr[e]));
-                    }
-                }
-                sl = __fdiv_rn(amax, 127.0f);
-                const float rsl = amax > 0.f ? __fdiv_rn(127.0f, amax) : 0.f;
-                constexpr float MAGIC_L = 12582912.0f + 128.0f;
-                uint32_t lw[RK / 4];
-                uint32_t lb[RK / 2];
-#pragma unroll
-                for (int e = 0; e < RK / 4; ++e) lw[e] = 0;
-#pragma unroll
-                for (int e = 0; e < RK; e += 2) {
-                    float f0 = 0.f, f1 = 0.f;
-                    if (e < r) {
-                        const float t0 = __fmaf_rn(Lr[e], rsl, MAGIC_L);
-                        const float t1 = __fmaf_rn(Lr[e + 1], rsl, MAGIC_L);
-                        const uint32_t u0 = __float_as_uint(t0) & 0xffu, u1 = __float_as_uint(t1) & 0xffu;  // q + 128
-                        lw[e >> 2] |= ((u0 ^ 0x80u) << ((e & 3) * 8)) | ((u1 ^ 0x80u) << (((e + 1) & 3) * 8));
-                        f0 = __fsub_rn(t0, MAGIC_L);
-                        f1 = __fsub_rn(t1, MAGIC_L);
-                    }
-                    lb[e >> 1] = pack_bf16x2(f0, f1);
-                }
-                // the code tile slot is free once the residual MMAs of block nb - 2 completed
-                if (nb >= 2 && !(ok = tc::mbar_wait(&lqfree[ls], ((nb >> 1) & 1) ^ 1, abort))) break;
-                uint8_t *lq = lqt + ls * L::LQT;
-#pragma unroll
-                for (int c16 = 0; c16 < LB / 16; ++c16)
-                    *reinterpret_cast<uint4 *>(lq + swz<LB>(row, c16)) =
-                        make_uint4(lb[4 * c16], lb[4 * c16 + 1], lb[4 * c16 + 2], lb[4 * c16 + 3]);
-                if (rv) {
-                    uint32_t *dst = reinterpret_cast<uint32_t *>(p.lrq + trow * r);
-#pragma unroll
-                    for (int e = 0; e < RK / 4; ++e)
-                        if (4 * e < r) dst[e] = lw[e];
-                    p.lrs[trow] = sl;
-                }
-                // for groups 1 and 2 (slot nb & 1 is rewritten for block nb + 2, after
-                // every group has passed its first chunk of block nb)
-                slr[ls * ROWS + row] = sl;
                 tc::fence_proxy_async();
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(&lqready[ls]);
@@ -412,14 +387,8 @@ __global__ void __launch_bounds__(THREADS, 1)
                 cur_slice = b;
             }
             // ---- residual codes: this group's chunks of the block
-            bool have_sl = g == 0;
             for (int ck = 0; ck < nk2; ++ck, ++j) {
                 if (j % NGR != g || !ok) continue;
-                if (!have_sl) {  // the block's low-rank scales are written (group 0)
-                    if (!(ok = tc::mbar_wait(&lqready[ls], (nb >> 1) & 1, abort))) continue;
-                    sl = slr[ls * ROWS + row];
-                    have_sl = true;
-                }
                 const int s = j % NB;
                 const uint32_t acc = tm_p + (uint32_t)(g * CH) + ((uint32_t)(q * 32) << 16);
                 if (!(ok = tc::mbar_wait(&fullB[s], (j / NB) & 1, abort))) continue;
@@ -428,7 +397,6 @@ __global__ void __launch_bounds__(THREADS, 1)
                 const int cx = nk2 - 1 - ck;  // chunk index (backward sweep)
                 const int64_t c0 = (int64_t)cx * CH;
                 const uint8_t *xt = ringB + s * L::SLOT_B;
-                const float2 nsl2 = make_float2(-sl, -sl);
                 float am0 = 0.f, am1 = 0.f, am2 = 0.f, am3 = 0.f;
                 // ---- pass 1: residual, outliers, piece absmax; residual back into TMEM
 #pragma unroll 1
@@ -450,7 +418,7 @@ __global__ void __launch_bounds__(THREADS, 1)
                             const float2 xv = make_float2(__uint_as_float(wd[e] << 16), __uint_as_float(wd[e] & 0xffff0000u));
                             const float2 iv = make_float2(__uint_as_float(I[8 * c16 + 2 * e]),
                                                           __uint_as_float(I[8 * c16 + 2 * e + 1]));
-                            w[4 * c16 + e] = fma2(iv, nsl2, xv);  // x - I * sL, one rounding
+                            w[4 * c16 + e] = sub2(xv, iv);  // x - P, one rounding
                         }
                     }
                     // outlier channels of this piece (warp-uniform mask): verbatim copy, residual zeroed
@@ -677,13 +645,11 @@ int launch(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cudaStream_
     p.k = d->n_outlier;
     p.group = d->group;
     p.batch = d->batch;
-    p.basis_scale = d->basis_scale;
     p.scales = d->scales;
-    p.lrq = d->lr_codes;
-    p.lrs = d->lr_scale;
+    p.lr = d->lowrank;
     p.outl = d->outliers;
     p.idx = d->outlier_idx;
-    p.vqb = d->basis_qb;
+    p.vtile = d->basis_tile;
     p.nk2 = (int)(H / CH);
     p.ngs = (int)(H / 64);
     p.ntb = (int)((T + ROWS - 1) / ROWS);
@@ -715,15 +681,15 @@ int launch(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cudaStream_
 }  // namespace act
 
 // Row encode, or ACT_E_UNSUPPORTED (before launching) for formats it does not
-// cover: a rank outside 16..64, no bf16 basis operand, H outside
+// cover: a rank outside 16..64, no basis tile operand, H outside
 // 1024..16384 or not a multiple of 128 (an epilogue group must have a chunk in
 // every block, and one CTA covers a block's channels), unaligned scales.
 int act_cg_encode_rows(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cudaStream_t s) {
     using namespace act::cgencr;
     if (d->tokens == 0) return ACT_OK;
-    if (d->rank < 16 || d->rank > 64 || d->rank % 16 || !d->basis_qb) return ACT_E_UNSUPPORTED;
+    if (d->rank < 16 || d->rank > 64 || d->rank % 16 || !d->basis_tile) return ACT_E_UNSUPPORTED;
     if (d->channels % CH || d->channels < 1024 || d->channels > 16384) return ACT_E_UNSUPPORTED;
-    if (!act::aligned(d->scales, 16) || !act::aligned(d->basis_qb, 16)) return ACT_E_UNSUPPORTED;
+    if (!act::aligned(d->scales, 16) || !act::aligned(d->basis_tile, 16)) return ACT_E_UNSUPPORTED;
     const int rk = d->rank <= 16 ? 16 : (d->rank <= 32 ? 32 : 64);
 #define ACT_ENCR_RK(B, W)                                     \
     do {                                                      \

@@ -8,9 +8,11 @@
 // butterfly stages, five shuffle stages).
 //
 // Arithmetic follows oracle/actcomp_oracle.c step for step (single binary32
-// operations, round-to-nearest-even, no contraction), so codes, scales and
-// reconstructions match it bit for bit; the low-rank term is an exact integer
-// dot product (dp4a) entering one fused multiply-add with the per-token scale.
+// operations, round-to-nearest-even, no contraction), and the two sums of the
+// format -- the projection L = X . V and the low-rank term L . V^T -- are
+// accumulated in binary64 (exact products, rounded once to binary32) like the
+// oracle's, so codes, scales and reconstructions match it bit for bit.  These
+// kernels serve the shapes the tensor-core kernels do not cover.
 #include "common.cuh"
 
 namespace act {
@@ -21,13 +23,11 @@ struct CgSlice {
     int bits, group, rank, k, wht;
     uint8_t *codes;
     float *scales;
-    int8_t *lrq;
-    float *lrs;
+    float *lr;
     uint16_t *outl;
     const int32_t *idx;
     const uint16_t *basis_t;
-    const int8_t *basis_q;
-    const float *basis_s;
+    const uint16_t *basis;
 };
 
 __device__ __forceinline__ CgSlice slice_of(const actcomp_cg_desc &d, int b) {
@@ -42,49 +42,48 @@ __device__ __forceinline__ CgSlice slice_of(const actcomp_cg_desc &d, int b) {
     const int64_t T = d.tokens, H = d.channels;
     s.codes = d.codes + (int64_t)b * T * (H * d.bits / 8);
     s.scales = d.scales + (int64_t)b * T * (H / d.group);
-    s.lrq = d.rank ? d.lr_codes + (int64_t)b * T * d.rank : nullptr;
-    s.lrs = d.rank ? d.lr_scale + (int64_t)b * T : nullptr;
+    s.lr = d.rank ? d.lowrank + (int64_t)b * T * d.rank : nullptr;
     s.outl = d.n_outlier ? d.outliers + (int64_t)b * T * d.n_outlier : nullptr;
     s.idx = d.n_outlier ? d.outlier_idx + (int64_t)b * d.n_outlier : nullptr;
     s.basis_t = d.rank ? d.basis_t + (int64_t)b * d.rank * H : nullptr;
-    s.basis_q = d.rank ? d.basis_q + (int64_t)b * H * d.rank : nullptr;
-    s.basis_s = d.rank ? d.basis_scale + (int64_t)b * d.rank : nullptr;
+    s.basis = d.rank ? d.basis + (int64_t)b * H * d.rank : nullptr;
     return s;
 }
 
-// exact low-rank integer term for channel c: sum_j lq[j] * Vq[c, j]
-__device__ __forceinline__ int32_t lr_dot(const uint32_t (&lw)[16], const int8_t *vq_row, int rank) {
-    int32_t acc = 0;
-    const uint4 *v = reinterpret_cast<const uint4 *>(vq_row);
+// low-rank term of channel c: sum_j L[j] * V[c, j], every product exact in
+// binary64, the sum rounded once to binary32 (oracle lowrank_term)
+__device__ __forceinline__ float lr_term(const float (&l)[64], const uint16_t *v_row, int rank) {
+    double acc = 0.0;
+    const uint4 *v = reinterpret_cast<const uint4 *>(v_row);
 #pragma unroll
-    for (int w4 = 0; w4 < 4; ++w4) {
-        if (w4 * 16 < rank) {
-            uint4 q = __ldg(v + w4);
-            acc = __dp4a((int)lw[w4 * 4 + 0], (int)q.x, acc);
-            acc = __dp4a((int)lw[w4 * 4 + 1], (int)q.y, acc);
-            acc = __dp4a((int)lw[w4 * 4 + 2], (int)q.z, acc);
-            acc = __dp4a((int)lw[w4 * 4 + 3], (int)q.w, acc);
+    for (int w8 = 0; w8 < 8; ++w8) {
+        if (w8 * 8 < rank) {
+            const uint4 q = __ldg(v + w8);
+            const uint32_t qw[4] = {q.x, q.y, q.z, q.w};
+#pragma unroll
+            for (int i = 0; i < 4; ++i) {
+                acc += (double)l[w8 * 8 + 2 * i] * (double)__uint_as_float(qw[i] << 16);
+                acc += (double)l[w8 * 8 + 2 * i + 1] * (double)__uint_as_float(qw[i] & 0xffff0000u);
+            }
         }
     }
-    return acc;
+    return (float)acc;
 }
 
-__device__ __forceinline__ void load_lr_row(const CgSlice &s, int64_t t, uint32_t (&lw)[16], float &sl) {
+__device__ __forceinline__ void load_lr_row(const CgSlice &s, int64_t t, float (&l)[64]) {
 #pragma unroll
-    for (int i = 0; i < 16; ++i) lw[i] = 0;
-    sl = 0.f;
+    for (int i = 0; i < 64; ++i) l[i] = 0.f;
     if (s.rank) {
-        const uint4 *p = reinterpret_cast<const uint4 *>(s.lrq + t * s.rank);
+        const float4 *p = reinterpret_cast<const float4 *>(s.lr + t * s.rank);
 #pragma unroll
-        for (int w4 = 0; w4 < 4; ++w4)
-            if (w4 * 16 < s.rank) {
-                uint4 q = __ldg(p + w4);
-                lw[w4 * 4 + 0] = q.x;
-                lw[w4 * 4 + 1] = q.y;
-                lw[w4 * 4 + 2] = q.z;
-                lw[w4 * 4 + 3] = q.w;
+        for (int w4 = 0; w4 < 16; ++w4)
+            if (w4 * 4 < s.rank) {
+                const float4 q = __ldg(p + w4);
+                l[4 * w4] = q.x;
+                l[4 * w4 + 1] = q.y;
+                l[4 * w4 + 2] = q.z;
+                l[4 * w4 + 3] = q.w;
             }
-        sl = __ldg(s.lrs + t);
     }
 }
 
@@ -143,36 +142,21 @@ __device__ __forceinline__ int64_t tile_operand_off(int64_t c, int j, int vbytes
     return (tile * 128 + row) * W + ((chunk ^ s) << 4) + (byte & 15);
 }
 
-__global__ void basis_prepare_kernel(const float *V, int64_t H, int rank, uint16_t *Vt, int8_t *Vq, float *sV,
-                                     uint16_t *Vqb, int8_t *Vqs) {
+// V rounded to bf16 and written in the three layouts of the format; one
+// thread per (channel, basis vector).
+__global__ void basis_prepare_kernel(const float *V, int64_t H, int rank, uint16_t *Vt, uint16_t *Vb,
+                                     uint16_t *tile) {
     const int b = blockIdx.y;
-    const int j = blockIdx.x;  // one block per basis vector
-    const float *v = V + (int64_t)b * H * rank;
-    __shared__ float red[32];
-    float amax = 0.f;
-    for (int64_t c = threadIdx.x; c < H; c += blockDim.x) amax = fmaxf(amax, fabsf(v[c * rank + j]));
-    amax = warp_max(amax);
-    if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = amax;
-    __syncthreads();
-    if (threadIdx.x < 32) {
-        float m = threadIdx.x < (blockDim.x >> 5) ? red[threadIdx.x] : 0.f;
-        m = warp_max(m);
-        if (threadIdx.x == 0) red[0] = m;
-    }
-    __syncthreads();
-    const float s = __fdiv_rn(red[0], 127.0f);
-    const float rs = red[0] > 0.f ? __fdiv_rn(127.0f, red[0]) : 0.f;
-    if (threadIdx.x == 0) sV[(int64_t)b * rank + j] = s;
-    const int rk = rank <= 16 ? 16 : (rank <= 32 ? 32 : 64);  // encode operand: 2 * rk bytes per row
-    const int rb = rank <= 32 ? 32 : 64;                       // decode operand: rb bytes per row
+    const int64_t n = H * rank;
+    const int rk = rank <= 16 ? 16 : (rank <= 32 ? 32 : 64);  // tile operand: 2 * rk bytes per row
     const int64_t ntile = (H + 127) / 128;
-    for (int64_t c = threadIdx.x; c < H; c += blockDim.x) {
-        float x = v[c * rank + j];
-        const int q = nearest_code(x, rs, 127);
-        Vq[(int64_t)b * H * rank + c * rank + j] = (int8_t)q;
-        if (Vqb) Vqb[((int64_t)b * ntile * 128 * 2 * rk + tile_operand_off(c, j, 2, 2 * rk)) / 2] = f2bf((float)q);
-        if (Vqs) Vqs[(int64_t)b * ntile * 128 * rb + tile_operand_off(c, j, 1, rb)] = (int8_t)q;
-        Vt[(int64_t)b * rank * H + (int64_t)j * H + c] = f2bf(x);
+    for (int64_t e = (int64_t)blockIdx.x * blockDim.x + threadIdx.x; e < n; e += (int64_t)gridDim.x * blockDim.x) {
+        const int64_t c = e / rank;
+        const int j = (int)(e - c * rank);
+        const uint16_t h = f2bf(V[(int64_t)b * n + e]);
+        Vb[(int64_t)b * n + e] = h;
+        Vt[(int64_t)b * n + (int64_t)j * H + c] = h;
+        if (tile) tile[((int64_t)b * ntile * 128 * 2 * rk + tile_operand_off(c, j, 2, 2 * rk)) / 2] = h;
     }
 }
 
@@ -231,9 +215,9 @@ __global__ void topk_kernel(float *score, int64_t H, int k, int32_t *idx) {
 }
 
 // ------------------------------------------------------------------ encode
-// Projection and low-rank codes: one warp per token.  L = x . V (binary32
-// accumulation in lane-strided order), then the per-token int8 quantisation
-// of L * sV exactly as cg_lr_quantize.
+// Projection: one warp per token.  L = x . V with the products exact in
+// binary64, lane-strided partial sums and a shuffle tree in binary64, rounded
+// once to binary32 (oracle cg_project).
 template <int RANK>
 __global__ void __launch_bounds__(256) cg_project_kernel(actcomp_cg_desc d, const uint16_t *x, int64_t ldx) {
     const int b = blockIdx.y;
@@ -242,47 +226,45 @@ __global__ void __launch_bounds__(256) cg_project_kernel(actcomp_cg_desc d, cons
     const int64_t warps = (int64_t)gridDim.x * (blockDim.x >> 5);
     const uint16_t *xs = x + (int64_t)b * s.T * ldx;
     for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < s.T; t += warps) {
-        float acc[RANK];
+        double acc[RANK];
 #pragma unroll
-        for (int j = 0; j < RANK; ++j) acc[j] = 0.f;
+        for (int j = 0; j < RANK; ++j) acc[j] = 0.0;
         const uint16_t *xr = xs + t * ldx;
         for (int64_t c = (int64_t)lane * 8; c < s.H; c += 256) {
-            uint4 xv = __ldg(reinterpret_cast<const uint4 *>(xr + c));
+            const bool full = c + 8 <= s.H;
             float xf[8];
-            const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
+            if (full) {
+                const uint4 xv = __ldg(reinterpret_cast<const uint4 *>(xr + c));
+                const uint32_t xw[4] = {xv.x, xv.y, xv.z, xv.w};
 #pragma unroll
-            for (int i = 0; i < 4; ++i) {
-                xf[2 * i] = __uint_as_float(xw[i] << 16);
-                xf[2 * i + 1] = __uint_as_float(xw[i] & 0xffff0000u);
+                for (int i = 0; i < 4; ++i) {
+                    xf[2 * i] = __uint_as_float(xw[i] << 16);
+                    xf[2 * i + 1] = __uint_as_float(xw[i] & 0xffff0000u);
+                }
+            } else {
+#pragma unroll
+                for (int i = 0; i < 8; ++i) xf[i] = c + i < s.H ? bf2f(xr[c + i]) : 0.f;
             }
 #pragma unroll
             for (int j = 0; j < RANK; ++j) {
-                uint4 vv = __ldg(reinterpret_cast<const uint4 *>(s.basis_t + (int64_t)j * s.H + c));
-                const uint32_t vw[4] = {vv.x, vv.y, vv.z, vv.w};
+                const uint16_t *vr = s.basis_t + (int64_t)j * s.H + c;
 #pragma unroll
-                for (int i = 0; i < 4; ++i) {
-                    acc[j] = __fmaf_rn(xf[2 * i], __uint_as_float(vw[i] << 16), acc[j]);
-                    acc[j] = __fmaf_rn(xf[2 * i + 1], __uint_as_float(vw[i] & 0xffff0000u), acc[j]);
-                }
+                for (int i = 0; i < 8; ++i)
+                    if (full || c + i < s.H) acc[j] += (double)xf[i] * (double)bf2f(vr[i]);
             }
         }
         // lane j ends up with coefficient j (and j + 32 when RANK == 64)
-        float mine0 = 0.f, mine1 = 0.f;
+        double mine0 = 0.0, mine1 = 0.0;
 #pragma unroll
         for (int j = 0; j < RANK; ++j) {
-            float v = warp_sum(acc[j]);
+            double v = acc[j];
+#pragma unroll
+            for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
             if (j == lane) mine0 = v;
             if (j == lane + 32) mine1 = v;
         }
-        const bool has0 = lane < RANK, has1 = lane + 32 < RANK;
-        float lt0 = has0 ? __fmul_rn(mine0, s.basis_s[lane]) : 0.f;
-        float lt1 = has1 ? __fmul_rn(mine1, s.basis_s[lane + 32]) : 0.f;
-        float amax = warp_max(fmaxf(fabsf(lt0), fabsf(lt1)));
-        float sl = __fdiv_rn(amax, 127.0f);
-        const float rs = amax > 0.f ? __fdiv_rn(127.0f, amax) : 0.f;
-        if (has0) s.lrq[t * RANK + lane] = (int8_t)nearest_code(lt0, rs, 127);
-        if (has1) s.lrq[t * RANK + lane + 32] = (int8_t)nearest_code(lt1, rs, 127);
-        if (lane == 0) s.lrs[t] = sl;
+        if (lane < RANK) s.lr[t * RANK + lane] = (float)mine0;
+        if (lane + 32 < RANK) s.lr[t * RANK + lane + 32] = (float)mine1;
     }
 }
 
@@ -303,9 +285,8 @@ __global__ void __launch_bounds__(256) cg_quant_kernel(actcomp_cg_desc d, const 
         const int64_t t = it / nchunk, ch = it % nchunk;
         const int64_t c0 = ch * 128 + lane * 4;
         const bool valid = c0 < s.H;
-        uint32_t lw[16];
-        float sl;
-        load_lr_row(s, t, lw, sl);
+        float l[64];
+        load_lr_row(s, t, l);
         float w[4] = {0.f, 0.f, 0.f, 0.f};
         uint2 xraw = make_uint2(0, 0);
         if (valid) {
@@ -314,8 +295,7 @@ __global__ void __launch_bounds__(256) cg_quant_kernel(actcomp_cg_desc d, const 
 #pragma unroll
             for (int i = 0; i < 4; ++i) {
                 float xv = __uint_as_float(i & 1 ? (xw[i >> 1] & 0xffff0000u) : (xw[i >> 1] << 16));
-                w[i] = s.rank ? __fmaf_rn(-__int2float_rn(lr_dot(lw, s.basis_q + (c0 + i) * s.rank, s.rank)), sl, xv)
-                              : xv;
+                w[i] = s.rank ? __fsub_rn(xv, lr_term(l, s.basis + (c0 + i) * s.rank, s.rank)) : xv;
             }
         }
         // outlier channels of this chunk: verbatim copy, residual zeroed
@@ -356,7 +336,7 @@ __global__ void __launch_bounds__(256) cg_quant_kernel(actcomp_cg_desc d, const 
 // Reconstruct four channels of one token (bit-exact with cg_decode) into bf16.
 template <int BITS>
 __device__ __forceinline__ void reconstruct4(const CgSlice &s, int64_t t, int64_t ch, int lane, bool valid,
-                                             const uint32_t (&lw)[16], float sl, uint16_t (&xh)[4]) {
+                                             const float (&l)[64], uint16_t (&xh)[4]) {
     const int off = 1 << (BITS - 1);
     const int64_t c0 = ch * 128 + lane * 4;
     float w[4] = {0.f, 0.f, 0.f, 0.f};
@@ -378,9 +358,7 @@ __device__ __forceinline__ void reconstruct4(const CgSlice &s, int64_t t, int64_
     }
 #pragma unroll
     for (int i = 0; i < 4; ++i) {
-        const float v = (s.rank && valid)
-                            ? __fmaf_rn(__int2float_rn(lr_dot(lw, s.basis_q + (c0 + i) * s.rank, s.rank)), sl, w[i])
-                            : w[i];
+        const float v = (s.rank && valid) ? __fadd_rn(lr_term(l, s.basis + (c0 + i) * s.rank, s.rank), w[i]) : w[i];
         xh[i] = f2bf(v);
     }
     if (s.k) {
@@ -408,11 +386,10 @@ __global__ void __launch_bounds__(256) cg_consume_kernel(actcomp_cg_desc d, cons
         const int64_t t = it / nchunk, ch = it % nchunk;
         const int64_t c0 = ch * 128 + lane * 4;
         const bool valid = c0 < s.H;
-        uint32_t lw[16];
-        float sl;
-        load_lr_row(s, t, lw, sl);
+        float l[64];
+        load_lr_row(s, t, l);
         uint16_t xh[4];
-        reconstruct4<BITS>(s, t, ch, lane, valid, lw, sl, xh);
+        reconstruct4<BITS>(s, t, ch, lane, valid, l, xh);
         if (!valid) continue;
         uint16_t o[4];
         if constexpr (OP == ACT_OP_DECODE) {
@@ -447,9 +424,8 @@ __global__ void __launch_bounds__(256) cg_softmax_bwd_kernel(actcomp_cg_desc d, 
     const uint16_t *dps = dp + (int64_t)b * s.T * ld;
     uint16_t *dss = ds + (int64_t)b * s.T * ld;
     for (int64_t t = (int64_t)blockIdx.x * (blockDim.x >> 5) + (threadIdx.x >> 5); t < s.T; t += warps) {
-        uint32_t lw[16];
-        float sl;
-        load_lr_row(s, t, lw, sl);
+        float l[64];
+        load_lr_row(s, t, l);
         const int64_t last = causal ? t : s.H - 1;  // last column with P != 0
         const int64_t nch = causal ? (last / 128 + 1) : nchunk;
         float acc = 0.f;
@@ -457,7 +433,7 @@ __global__ void __launch_bounds__(256) cg_softmax_bwd_kernel(actcomp_cg_desc d, 
             const int64_t c0 = ch * 128 + lane * 4;
             const bool valid = c0 < s.H;
             uint16_t xh[4];
-            reconstruct4<BITS>(s, t, ch, lane, valid, lw, sl, xh);
+            reconstruct4<BITS>(s, t, ch, lane, valid, l, xh);
             if (!valid) continue;
             uint2 g = __ldg(reinterpret_cast<const uint2 *>(dps + t * ld + c0));
             const uint32_t gw[2] = {g.x, g.y};
@@ -475,7 +451,7 @@ __global__ void __launch_bounds__(256) cg_softmax_bwd_kernel(actcomp_cg_desc d, 
             uint16_t o[4] = {0, 0, 0, 0};
             if (ch < nch) {
                 uint16_t xh[4];
-                reconstruct4<BITS>(s, t, ch, lane, valid, lw, sl, xh);
+                reconstruct4<BITS>(s, t, ch, lane, valid, l, xh);
                 if (!valid) continue;
                 uint2 g = __ldg(reinterpret_cast<const uint2 *>(dps + t * ld + c0));
                 const uint32_t gw[2] = {g.x, g.y};
@@ -510,8 +486,9 @@ int validate_desc(const actcomp_cg_desc *d) {
     ACT_CHECK(d->codes && d->scales, ACT_E_INVALID);
     ACT_CHECK(aligned(d->codes, 4) && aligned(d->scales, 4), ACT_E_ALIGN);
     if (d->rank) {
-        ACT_CHECK(d->lr_codes && d->lr_scale && d->basis_q && d->basis_scale, ACT_E_INVALID);
-        ACT_CHECK(aligned(d->lr_codes, 16) && aligned(d->basis_q, 16), ACT_E_ALIGN);
+        ACT_CHECK(d->lowrank && d->basis_t && d->basis, ACT_E_INVALID);
+        ACT_CHECK(aligned(d->lowrank, 16) && aligned(d->basis, 16) && aligned(d->basis_t, 16), ACT_E_ALIGN);
+        if (d->basis_tile) ACT_CHECK(aligned(d->basis_tile, 16), ACT_E_ALIGN);
     }
     if (d->n_outlier) ACT_CHECK(d->outliers && d->outlier_idx, ACT_E_INVALID);
     return ACT_OK;
@@ -529,18 +506,17 @@ static int grid_for(int64_t items_per_slice) {
 using namespace act;
 
 extern "C" int actcomp_cg_basis_prepare(const float *V, int64_t H, int32_t rank, int32_t batch, uint16_t *basis_t,
-                                        int8_t *basis_q, float *basis_scale, uint16_t *basis_qb, int8_t *basis_qs,
-                                        void *stream) {
-    ACT_CHECK(V && basis_t && basis_q && basis_scale, ACT_E_INVALID);
+                                        uint16_t *basis, uint16_t *basis_tile, void *stream) {
+    ACT_CHECK(V && basis_t && basis, ACT_E_INVALID);
     ACT_CHECK(H > 0 && rank > 0 && rank <= 64 && batch >= 1, ACT_E_INVALID);
     cudaStream_t s = as_stream(stream);
     const int64_t rows = batch * ((H + 127) / 128) * 128;
-    const int rk = rank <= 16 ? 16 : (rank <= 32 ? 32 : 64), rb = rank <= 32 ? 32 : 64;
+    const int rk = rank <= 16 ? 16 : (rank <= 32 ? 32 : 64);
     // padding (values past the rank, channels past H) reads as zero
-    if (basis_qb) ACT_CUDA_TRY(cudaMemsetAsync(basis_qb, 0, (size_t)(rows * 2 * rk), s));
-    if (basis_qs) ACT_CUDA_TRY(cudaMemsetAsync(basis_qs, 0, (size_t)(rows * rb), s));
-    dim3 grid((unsigned)rank, (unsigned)batch);
-    basis_prepare_kernel<<<grid, 256, 0, s>>>(V, H, rank, basis_t, basis_q, basis_scale, basis_qb, basis_qs);
+    if (basis_tile) ACT_CUDA_TRY(cudaMemsetAsync(basis_tile, 0, (size_t)(rows * 2 * rk), s));
+    const int64_t n = H * rank;
+    dim3 grid((unsigned)((n + 255) / 256 < 4096 ? (n + 255) / 256 : 4096), (unsigned)batch);
+    basis_prepare_kernel<<<grid, 256, 0, s>>>(V, H, rank, basis_t, basis, basis_tile);
     return launch_status();
 }
 
@@ -557,8 +533,8 @@ extern "C" int actcomp_cg_channel_topk(const uint16_t *x, int64_t T, int64_t H, 
     return launch_status();
 }
 
-// Encode entry point: SIMT path.  (The tensor-core encode in cg_tc.cu takes
-// over for the shapes it supports; see actcomp_cg_encode in capi.cu.)
+// Encode entry point: CUDA-core path.  (The tensor-core encode takes over for
+// the shapes it supports; see actcomp_cg_encode in capi.cu.)
 int act_cg_encode_simt(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cudaStream_t s) {
     if (d->tokens == 0) return ACT_OK;
     if (d->rank) {

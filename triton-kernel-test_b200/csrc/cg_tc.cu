@@ -2,19 +2,23 @@
 // decode and the fused consumers (elementwise product, SiLU and GELU backward).
 //
 // One tile = 128 tokens x 128 channels.  Per tile:
-//   TMA warp   loads the low-rank codes of the 128 tokens (128 x r int8), the
-//              quantised basis rows of the 128 channels (128 x r int8), the
+//   TMA warp   loads the prepared bf16 basis tile of the 128 channels, the
 //              residual codes (128 x 64 B for int4) and, for a consumer, the
-//              second operand (128 x 128 bf16) into a 2-4 stage ring;
-//   MMA warp   issues one tcgen05.mma kind::i8 (M=128, N=128, K=32) per 32
-//              basis vectors: I = Lq . Vq^T, an exact int32 accumulator in TMEM
-//              (4 accumulators of 128 columns, so the MMA runs ahead);
+//              second operand (128 x 128 bf16) into a 2-6 stage ring; per token
+//              block the projection L (128 x r float32) and the outlier values;
+//   MMA warp   per token block splits L into its three exact bf16 pieces (three
+//              swizzled operand tiles); per tile tcgen05.mma kind::f16 (M=128,
+//              N=128, K=16 steps over the three pieces) gives the low-rank term
+//              P = L . V^T in float32 in TMEM (4 accumulators of 128 columns, so
+//              the MMA runs ahead);
 //   epilogue   (16 warps: 4 row quarters x 4 column quarters, one token row
 //              and 32 channels per thread; the rotation exchanges quarters
-//              through shared memory) reads I with tcgen05.ld, forms
-//              xhat = bf16((u - 2^(b-1)) * s + I * sL) exactly as the oracle,
-//              puts the outlier channels back, applies the consumer op, writes
-//              the tile to a 128B-swizzled staging buffer and stores it by TMA.
+//              through shared memory) reads P with tcgen05.ld, forms
+//              xhat = bf16(P + (u - 2^(b-1)) * s) as the oracle does,
+//              puts the outlier channels back and applies the consumer op.  The
+//              decode writes the tile to a 64B-swizzled staging buffer and
+//              stores it by TMA; the consumers store each thread's 64 bytes
+//              straight from registers (no staging, so the ring stays deep).
 // The kernel is persistent: one CTA per SM walks the tiles with a fixed stride.
 #include <cudaTypedefs.h>
 
@@ -37,7 +41,7 @@ struct DecParams {
     int64_t T, H;
     int rank, k, group, batch;
     const float *scales;
-    const float *lr_scale;
+    const float *lr;           // projection L, T x rank float32 per slice
     const uint16_t *outliers;
     const int32_t *idx;
     int ntb, ncc;
@@ -52,19 +56,23 @@ struct DecParams {
     const float *rowsum;
     int causal;
     int tri;                   // walk only the tiles on or below the diagonal (causal softmax passes)
-    const int8_t *vqs;         // basis_qs tile operand (layout in include/actcomp.h), or null
+    const uint16_t *vtile;     // basis tile operand (layout in include/actcomp.h)
+    uint16_t *out;             // consumer output (direct stores), row stride ldo
+    int64_t ldo;
 };
 
-template <int BITS, int OP, bool WHT, int RB>
+template <int BITS, int OP, bool WHT, int RK>
 struct DecLayout {
-    static constexpr int LQ = RB ? ROWS * RB : 0;  // low-rank codes of a token block (2 slots, outside the ring)
-    static constexpr int VQ = RB ? CH * RB : 0;
+    static constexpr int LB = 2 * RK;              // bytes of one bf16 operand row
+    static constexpr int LQ = RK ? ROWS * RK * 4 : 0;  // float32 L of a token block (2 slots, outside the ring)
+    static constexpr int PT = RK ? 3 * ROWS * LB : 0;  // its three bf16 piece tiles (1 slot)
+    static constexpr int VQ = RK ? CH * LB : 0;        // basis tile
     static constexpr int CODES = ROWS * CH * BITS / 8;
     static constexpr int Y = OP == ACT_OP_DECODE ? 0 : ROWS * CH * 2;
     static constexpr int STAGE = VQ + CODES + Y;
-    static constexpr int OUT = ROWS * CH * 2;
+    static constexpr int OUT = OP == ACT_OP_DECODE ? ROWS * CH * 2 : 0;  // decode output staging
     static constexpr int WX = WHT ? 4 * ROWS * 32 * 4 : 0;  // rotation exchange: 32 floats per thread
-    static constexpr int FIXED = 2 * OUT + WX + 2 * LQ + 1024;  // + barriers
+    static constexpr int FIXED = 2 * OUT + WX + 2 * LQ + PT + 1024;  // + barriers
     static constexpr int S = (6 * STAGE + FIXED <= 200 * 1024) ? 6 : (4 * STAGE + FIXED <= 200 * 1024) ? 4
                                                                   : ((3 * STAGE + FIXED <= 214 * 1024) ? 3 : 2);
     static constexpr int EW = 16;  // epilogue warps: 4 row quarters x 4 column quarters
@@ -72,7 +80,8 @@ struct DecLayout {
     static constexpr int OUT_OFF = S * STAGE;
     static constexpr int WX_OFF = OUT_OFF + 2 * OUT;
     static constexpr int LQ_OFF = WX_OFF + WX;
-    static constexpr int BAR_OFF = LQ_OFF + 2 * LQ;
+    static constexpr int PT_OFF = LQ_OFF + 2 * LQ;
+    static constexpr int BAR_OFF = PT_OFF + PT;
     static constexpr int OT_OFF = BAR_OFF + 1024;
     static int ost_off(int n32) { return OT_OFF + ((n32 * 8 + 15) & ~15); }
     static int total(int n32, int k) { return ost_off(n32) + 2 * ((ROWS * k * 2 + 15) & ~15) + 1024; }
@@ -152,12 +161,12 @@ __device__ __forceinline__ float hi_bf(uint32_t w) { return __uint_as_float(w & 
 // h = (w - 2) / 4, one token row per thread: per tile a thread owns 32
 // consecutive channels of one row, i.e. one int4 group of 32, half of a group
 // of 64, a quarter of a group of 128 or of a rotation block.
-template <int BITS, int OP, bool WHT, int RB>
-__global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
-    cg_decode_tc_kernel(const __grid_constant__ CUtensorMap tm_lq, const __grid_constant__ CUtensorMap tm_vq,
-                        const __grid_constant__ CUtensorMap tm_codes, const __grid_constant__ CUtensorMap tm_y,
+template <int BITS, int OP, bool WHT, int RK>
+__global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RK>::THREADS, 1)
+    cg_decode_tc_kernel(const __grid_constant__ CUtensorMap tm_codes, const __grid_constant__ CUtensorMap tm_y,
                         const __grid_constant__ CUtensorMap tm_out, DecParams p) {
-    using L = DecLayout<BITS, OP, WHT, RB>;
+    using L = DecLayout<BITS, OP, WHT, RK>;
+    constexpr int LB = L::LB;
     constexpr int off = 1 << (BITS - 1);
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -165,13 +174,15 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
     uint64_t *empty = full + L::S;
     uint64_t *tfull = empty + L::S;
     uint64_t *tempty = tfull + NT;
-    uint64_t *lqfull = tempty + NT;   // [2] token-block slots (low-rank codes, outlier values) loaded
+    uint64_t *lqfull = tempty + NT;   // [2] token-block slots (projection, outlier values) loaded
     uint64_t *lqempty = lqfull + 2;  // [2] ... and no longer read
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(lqempty + 2);
+    uint64_t *ptfree = lqempty + 2;  // the MMAs of a token block have read its piece tiles
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(ptfree + 1);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
     uint8_t *lqbuf = smem + L::LQ_OFF;
+    uint8_t *ptile = smem + L::PT_OFF;
     uint8_t *ostbuf = smem + p.off_ost;
-    const bool blockbuf = RB > 0 || p.k > 0;  // per-token-block slots in use
+    const bool blockbuf = RK > 0 || p.k > 0;  // per-token-block slots in use
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int64_t t_lo, t_hi;
     tile_range(p, t_lo, t_hi);
@@ -179,7 +190,7 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
     if (threadIdx.x == 0) {
         for (int s = 0; s < L::S; ++s) {
             tc::mbar_init(&full[s], 1);
-            tc::mbar_init(&empty[s], L::EW + (RB ? 1 : 0));
+            tc::mbar_init(&empty[s], L::EW + (RK ? 1 : 0));
         }
         for (int b = 0; b < NT; ++b) {
             tc::mbar_init(&tfull[b], 1);
@@ -187,27 +198,24 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
         }
         for (int b = 0; b < 2; ++b) {
             tc::mbar_init(&lqfull[b], 1);
-            tc::mbar_init(&lqempty[b], (RB ? 1 : 0) + (p.k ? L::EW : 0));
+            tc::mbar_init(&lqempty[b], (RK ? 1 : 0) + (p.k ? L::EW : 0));
         }
+        tc::mbar_init(ptfree, 1);
         *abort = 0;
         tc::fence_mbar_init();
     }
-    if (RB && warp == 1) {
+    if (RK && warp == 1) {
         tc::tmem_alloc(tmem_slot, NT * CH);
         tc::tmem_relinquish();
     }
     tc::tc_fence_before();
     __syncthreads();
     tc::tc_fence_after();
-    const uint32_t tmem = RB ? *tmem_slot : 0;
+    const uint32_t tmem = RK ? *tmem_slot : 0;
 
     if (warp == 0) {
         // ------------------------------------------------------------ TMA producer
         if (lane == 0) {
-            if (RB) {
-                tc::prefetch_tmap(&tm_lq);
-                if (!p.vqs) tc::prefetch_tmap(&tm_vq);
-            }
             tc::prefetch_tmap(&tm_codes);
             int i = 0, nlq = 0;
             TileWalk tw(t_lo, p.ncc, p.ntb, p.tri != 0);
@@ -216,25 +224,25 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
                 const uint32_t ph = (i / L::S) & 1;
                 const int cc = tw.cc, tb = tw.tb, b = tw.b;
                 if (blockbuf && (tile == t_lo || cc == 0)) {
-                    // a new token block: its low-rank codes and outlier values into the free slot
+                    // a new token block: its projection and outlier values into the free slot
                     const int ls = nlq & 1;
                     if (!tc::mbar_wait(&lqempty[ls], ((nlq >> 1) & 1) ^ 1, abort)) break;
                     const uint16_t *osrc = nullptr;
                     const uint32_t obytes = ost_bytes(p, tb, b, osrc);
-                    tc::mbar_arrive_expect_tx(&lqfull[ls], (RB ? L::LQ : 0) + obytes);
-                    if (RB) tc::tma_load_3d(lqbuf + ls * L::LQ, &tm_lq, &lqfull[ls], 0, tb * ROWS, b);
+                    const int64_t rows = (p.T - (int64_t)tb * ROWS) < ROWS ? (p.T - (int64_t)tb * ROWS) : ROWS;
+                    const uint32_t lbytes = RK ? (uint32_t)(rows * p.rank * 4) : 0;
+                    tc::mbar_arrive_expect_tx(&lqfull[ls], lbytes + obytes);
+                    if (RK)
+                        tc::bulk_load(lqbuf + ls * L::LQ, p.lr + ((int64_t)b * p.T + (int64_t)tb * ROWS) * p.rank, lbytes,
+                                      &lqfull[ls]);
                     if (obytes) tc::bulk_load(ostbuf + ls * p.ostb, osrc, obytes, &lqfull[ls]);
                     ++nlq;
                 }
                 if (!tc::mbar_wait(&empty[s], ph ^ 1, abort)) break;
                 uint8_t *st = smem + s * L::STAGE;
                 tc::mbar_arrive_expect_tx(&full[s], L::STAGE);
-                if constexpr (RB > 0) {
-                    if (p.vqs)  // one contiguous tile of the prepared operand
-                        tc::bulk_load(st, p.vqs + ((int64_t)b * p.ncc + cc) * L::VQ, L::VQ, &full[s]);
-                    else
-                        tc::tma_load_3d(st, &tm_vq, &full[s], 0, cc * CH, b);
-                }
+                if constexpr (RK > 0)  // one contiguous tile of the prepared operand
+                    tc::bulk_load(st, p.vtile + ((int64_t)b * p.ncc + cc) * (L::VQ / 2), L::VQ, &full[s]);
                 tc::tma_load_3d(st + L::VQ, &tm_codes, &full[s], cc * L::CODE_ROW, tb * ROWS, b);
                 if constexpr (OP != ACT_OP_DECODE) {
                     uint8_t *y = st + L::VQ + L::CODES;
@@ -245,36 +253,78 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
         }
     } else if (warp == 1) {
         // ------------------------------------------------------------ MMA issuer
-        if constexpr (RB > 0) {
-            if (lane == 0) {
-                constexpr uint32_t idesc = tc::idesc_i8(ROWS, CH);
-                constexpr tc::Swizzle SW = RB == 32 ? tc::SW_32B : tc::SW_64B;
-                int i = 0, mlq = 0;
-                TileWalk tw(t_lo, p.ncc, p.ntb, p.tri != 0);
-                for (int64_t tile = t_lo; tile < t_hi; ++tile, ++i, tw.next()) {
-                    const int s = i % L::S, b = i % NT;
-                    const uint32_t ph = (i / L::S) & 1, bph = (i / NT) & 1;
-                    if (tile == t_lo || tw.cc == 0) {  // a new token block: its low-rank codes have landed
-                        if (!tc::mbar_wait(&lqfull[mlq & 1], (mlq >> 1) & 1, abort)) break;
-                        ++mlq;
+        if constexpr (RK > 0) {
+            constexpr uint32_t idesc = tc::idesc_f16(ROWS, CH, true, false, false);
+            constexpr tc::Swizzle SW = LB == 32 ? tc::SW_32B : (LB == 64 ? tc::SW_64B : tc::SW_128B);
+            const int nkq = (p.rank + 15) / 16;
+            int i = 0, mlq = 0;
+            bool ok = true;
+            TileWalk tw(t_lo, p.ncc, p.ntb, p.tri != 0);
+            for (int64_t tile = t_lo; tile < t_hi && ok; ++tile, ++i, tw.next()) {
+                const int s = i % L::S, b = i % NT;
+                const uint32_t ph = (i / L::S) & 1, bph = (i / NT) & 1;
+                if (tile == t_lo || tw.cc == 0) {
+                    // a new token block: once its projection has landed and the previous
+                    // block's MMAs have read the piece tiles, split L into them
+                    const int ls = mlq & 1;
+                    int okw = 1;
+                    if (lane == 0) {
+                        okw = tc::mbar_wait(&lqfull[ls], (mlq >> 1) & 1, abort);
+                        if (okw && mlq > 0) okw = tc::mbar_wait(ptfree, (mlq - 1) & 1, abort);
                     }
-                    const int lslot = (mlq - 1) & 1;
-                    if (!tc::mbar_wait(&full[s], ph, abort)) break;
-                    if (!tc::mbar_wait(&tempty[b], bph ^ 1, abort)) break;
+                    if (!(ok = __shfl_sync(0xffffffffu, okw, 0) != 0)) break;
                     tc::tc_fence_after();
-                    uint8_t *st = smem + s * L::STAGE;
-                    const uint8_t *lq = lqbuf + lslot * L::LQ;
+                    const float *src = reinterpret_cast<const float *>(lqbuf + ls * L::LQ);
+                    const int cpr = LB / 16;  // 16-byte chunks per operand row
+                    const int64_t rows_here = p.T - (int64_t)tw.tb * ROWS;
+                    for (int e = lane; e < ROWS * cpr; e += 32) {
+                        const int row = e / cpr, c16 = e - row * cpr;
+                        uint32_t hp[4] = {0u, 0u, 0u, 0u}, mp[4] = {0u, 0u, 0u, 0u}, lp[4] = {0u, 0u, 0u, 0u};
+                        if (8 * c16 < p.rank && row < rows_here) {
+                            const float4 v0 = *reinterpret_cast<const float4 *>(src + row * p.rank + 8 * c16);
+                            const float4 v1 = *reinterpret_cast<const float4 *>(src + row * p.rank + 8 * c16 + 4);
+                            const float in[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
 #pragma unroll
-                    for (int kk = 0; kk < RB / 32; ++kk) {
-                        const uint64_t ad = tc::smem_desc(lq + kk * 32, 16, 8 * RB, SW);
-                        const uint64_t bd = tc::smem_desc(st + kk * 32, 16, 8 * RB, SW);
-                        tc::mma_i8(tmem + b * CH, ad, bd, idesc, kk > 0);
+                            for (int hh = 0; hh < 4; ++hh) {
+                                float h0, m0, l0, h1, m1, l1;
+                                split3_bf16(in[2 * hh], h0, m0, l0);
+                                split3_bf16(in[2 * hh + 1], h1, m1, l1);
+                                hp[hh] = pack_bf16x2(h0, h1);
+                                mp[hh] = pack_bf16x2(m0, m1);
+                                lp[hh] = pack_bf16x2(l0, l1);
+                            }
+                        }
+                        const int o = swz<LB>(row, c16);
+                        *reinterpret_cast<uint4 *>(ptile + o) = make_uint4(hp[0], hp[1], hp[2], hp[3]);
+                        *reinterpret_cast<uint4 *>(ptile + ROWS * LB + o) = make_uint4(mp[0], mp[1], mp[2], mp[3]);
+                        *reinterpret_cast<uint4 *>(ptile + 2 * ROWS * LB + o) = make_uint4(lp[0], lp[1], lp[2], lp[3]);
                     }
-                    tc::mma_commit(&tfull[b]);
-                    tc::mma_commit(&empty[s]);
-                    // last tile of this token block in my range: the slot frees once these MMAs complete
-                    if (tw.cc == tw.last_cc() || tile == t_hi - 1) tc::mma_commit(&lqempty[lslot]);
+                    tc::fence_proxy_async();
+                    __syncwarp();
+                    // the projection slot has been read (the outlier values in it may still be)
+                    if (lane == 0) tc::mbar_arrive(&lqempty[ls]);
+                    ++mlq;
                 }
+                int okw = 1;
+                if (lane == 0) {
+                    okw = tc::mbar_wait(&full[s], ph, abort) && tc::mbar_wait(&tempty[b], bph ^ 1, abort);
+                    if (okw) {
+                        tc::tc_fence_after();
+                        uint8_t *st = smem + s * L::STAGE;
+                        // P = hi . V^T + mid . V^T + lo . V^T
+                        for (int pc = 0; pc < 3; ++pc)
+                            for (int kk = 0; kk < nkq; ++kk) {
+                                const uint64_t ad = tc::smem_desc(ptile + pc * ROWS * LB + kk * 32, 16, 8 * LB, SW);
+                                const uint64_t bd = tc::smem_desc(st + kk * 32, 16, 8 * LB, SW);
+                                tc::mma_f16(tmem + b * CH, ad, bd, idesc, (pc | kk) > 0);
+                            }
+                        tc::mma_commit(&tfull[b]);
+                        tc::mma_commit(&empty[s]);
+                        // last tile of this token block in my range: the piece tiles free once these MMAs complete
+                        if (tw.cc == tw.last_cc() || tile == t_hi - 1) tc::mma_commit(ptfree);
+                    }
+                }
+                ok = __shfl_sync(0xffffffffu, okw, 0) != 0;
             }
         }
     } else {
@@ -291,16 +341,15 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
         float *wx = reinterpret_cast<float *>(smem + L::WX_OFF);
         int cur_slice = -1;
 
-        // per-row scalars of a tile (group scale, low-rank scale), loaded PD tiles
+        // per-row scalars of a tile (group scale, softmax row sum), loaded PD tiles
         // ahead into a register queue so the global-load latency (~1-2 us under
         // load) hides behind PD tiles of work
         constexpr int PD = 4;
-        float qsc[PD], qsl[PD], qrs[PD];
+        float qsc[PD], qrs[PD];
         TileWalk tw(t_lo, p.ncc, p.ntb, p.tri != 0), nw = tw;  // this tile, the one PD ahead
         const int gshift = 31 - __clz(p.group);
-        auto load_scalars = [&](int64_t tile, const TileWalk &at, float &vsc, float &vsl, float &vrs) {
+        auto load_scalars = [&](int64_t tile, const TileWalk &at, float &vsc, float &vrs) {
             vsc = 0.f;
-            vsl = 0.f;
             vrs = 0.f;
             if (tile >= t_hi) return;
             const int64_t t = (int64_t)at.tb * ROWS + r;
@@ -308,12 +357,11 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
             const int64_t trow = (int64_t)at.b * p.T + t;
             const int64_t c = (int64_t)at.cc * CH + 32 * h;
             if (c < p.H) vsc = __ldg(p.scales + trow * ngr + (c >> gshift));
-            if (RB) vsl = __ldg(p.lr_scale + trow);
             if constexpr (OP == OP_SMAX_BWD) vrs = __ldg(p.rowsum + trow);
         };
 #pragma unroll
         for (int d = 0; d < PD; ++d) {
-            load_scalars(t_lo + d, nw, qsc[d], qsl[d], qrs[d]);
+            load_scalars(t_lo + d, nw, qsc[d], qrs[d]);
             nw.next();
         }
 
@@ -323,14 +371,13 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
             const int s = i % L::S, b = i % NT, ob = i & 1;
             const uint32_t ph = (i / L::S) & 1, bph = (i / NT) & 1;
             const int cc = tw.cc, tb = tw.tb, sl_b = tw.b;
-            const float sc = qsc[0], sl = qsl[0], rsum = qrs[0];
+            const float sc = qsc[0], rsum = qrs[0];
 #pragma unroll
             for (int d = 0; d + 1 < PD; ++d) {
                 qsc[d] = qsc[d + 1];
-                qsl[d] = qsl[d + 1];
                 qrs[d] = qrs[d + 1];
             }
-            load_scalars(tile + PD, nw, qsc[PD - 1], qsl[PD - 1], qrs[PD - 1]);
+            load_scalars(tile + PD, nw, qsc[PD - 1], qrs[PD - 1]);
             nw.next();
 
             // outlier table of the slice: per 32-channel group a mask and the
@@ -360,7 +407,7 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
                 ++elq;
             }
             bool ok = tc::mbar_wait(&full[s], ph, abort);
-            if (RB) ok = ok && tc::mbar_wait(&tfull[b], bph, abort);
+            if (RK) ok = ok && tc::mbar_wait(&tfull[b], bph, abort);
             if (!ok) break;
             tc::tc_fence_after();
             const int64_t t = (int64_t)tb * ROWS + r;
@@ -368,9 +415,9 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
             const int64_t trow = (int64_t)sl_b * p.T + t;
             const int64_t c_first = (int64_t)cc * CH + 32 * h;
 
-            // low-rank term I (int32) for my 32 channels: issued first, waited for late
+            // low-rank term P (float32) for my 32 channels: issued first, waited for late
             uint32_t I[32];
-            if constexpr (RB > 0) tc::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + b * CH + 32 * h, I);
+            if constexpr (RK > 0) tc::tmem_ld32(tmem + ((uint32_t)(q * 32) << 16) + b * CH + 32 * h, I);
 
             // residual: w = (u - 2^(b-1)) * s, exact conversion of the code
             const uint8_t *ct = smem + s * L::STAGE + L::VQ;
@@ -457,18 +504,12 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
                     }
                 }
             }
-            // xhat = fma(I, sL, w), I converted exactly (magic-number add)
-            if constexpr (RB > 0) {
+            // xhat = P + w
+            if constexpr (RK > 0) {
                 tc::tmem_ld_wait();
-                const float2 sl2 = make_float2(sl, sl);
-                const float2 m2 = make_float2(12582912.0f, 12582912.0f);
 #pragma unroll
-                for (int e = 0; e < 16; ++e) {
-                    const float2 iv = sub2(make_float2(__int_as_float((int)I[2 * e] + 0x4B400000),
-                                                       __int_as_float((int)I[2 * e + 1] + 0x4B400000)),
-                                           m2);
-                    w[e] = fma2(iv, sl2, w[e]);
-                }
+                for (int e = 0; e < 16; ++e)
+                    w[e] = add2(make_float2(__uint_as_float(I[2 * e]), __uint_as_float(I[2 * e + 1])), w[e]);
                 tc::tc_fence_before();
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(&tempty[b]);
@@ -547,8 +588,20 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
                 continue;
             }
 
-            // each warp stores its own 32 x 32 sub-tile: staging buffer ob of the
-            // warp is free once the warp's store issued two tiles ago has read it
+            if constexpr (OP != ACT_OP_DECODE) {  // 64 bytes of my row straight from registers
+                if (rv && c_first < p.H) {
+                    uint4 *dst = reinterpret_cast<uint4 *>(p.out + trow * p.ldo + c_first);
+#pragma unroll
+                    for (int c16 = 0; c16 < 4; ++c16) {
+                        const int e = 4 * c16;
+                        dst[c16] = make_uint4(pack_bf16x2(w[e].x, w[e].y), pack_bf16x2(w[e + 1].x, w[e + 1].y),
+                                              pack_bf16x2(w[e + 2].x, w[e + 2].y), pack_bf16x2(w[e + 3].x, w[e + 3].y));
+                    }
+                }
+                continue;
+            }
+            // decode: each warp stores its own 32 x 32 sub-tile; staging buffer ob of
+            // the warp is free once the warp's store issued two tiles ago has read it
             uint8_t *stg = smem + L::OUT_OFF + ew * (2 * WST) + ob * WST;
             if (lane == 0) tc::bulk_wait_read<1>();
             __syncwarp();
@@ -573,7 +626,7 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RB>::THREADS, 1)
     }
     tc::tc_fence_before();
     __syncthreads();
-    if (RB && warp == 1) {
+    if (RK && warp == 1) {
         tc::tc_fence_after();
         tc::tmem_dealloc(tmem, NT * CH);
     }
@@ -586,21 +639,15 @@ struct SmaxArgs {
     int causal = 0;
 };
 
-template <int BITS, int OP, bool WHT, int RB>
+template <int BITS, int OP, bool WHT, int RK>
 int launch_decode(const actcomp_cg_desc *d, const uint16_t *y, int64_t ldy, uint16_t *out, int64_t ldo,
                   cudaStream_t stream, const SmaxArgs &sx = SmaxArgs()) {
-    using L = DecLayout<BITS, OP, WHT, RB>;
+    using L = DecLayout<BITS, OP, WHT, RK>;
     const int64_t T = d->tokens, H = d->channels, B = d->batch;
-    const int r = d->rank;
-    CUtensorMap m_lq{}, m_vq{}, m_codes{}, m_y{}, m_out{};
+    CUtensorMap m_codes{}, m_y{}, m_out{};
     int st;
     const auto U8 = CU_TENSOR_MAP_DATA_TYPE_UINT8;
     const auto BF = CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
-    if (RB) {
-        const auto sw = RB == 32 ? CU_TENSOR_MAP_SWIZZLE_32B : CU_TENSOR_MAP_SWIZZLE_64B;
-        if ((st = make_map_3d(&m_lq, d->lr_codes, U8, 1, r, T, B, r, T * r, RB, ROWS, sw))) return st;
-        if ((st = make_map_3d(&m_vq, d->basis_q, U8, 1, r, H, B, r, H * r, RB, CH, sw))) return st;
-    }
     const int64_t rowb = H * BITS / 8;
     if ((st = make_map_3d(&m_codes, d->codes, U8, 1, rowb, T, B, rowb, T * rowb, L::CODE_ROW, ROWS,
                           BITS == 4 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_128B)))
@@ -608,17 +655,17 @@ int launch_decode(const actcomp_cg_desc *d, const uint16_t *y, int64_t ldy, uint
     if (OP != ACT_OP_DECODE &&
         (st = make_map_3d(&m_y, y, BF, 2, H, T, B, ldy, T * ldy, 64, ROWS, CU_TENSOR_MAP_SWIZZLE_128B)))
         return st;
-    // per-warp output boxes: 32 tokens x 32 channels (64-byte rows)
+    // per-warp output boxes of the decode: 32 tokens x 32 channels (64-byte rows)
     if ((st = make_map_3d(&m_out, out, BF, 2, H, T, B, ldo, T * ldo, 32, 32, CU_TENSOR_MAP_SWIZZLE_64B))) return st;
     DecParams p{};
     p.T = T;
     p.H = H;
-    p.rank = r;
+    p.rank = d->rank;
     p.k = d->n_outlier;
     p.group = d->group;
     p.batch = d->batch;
     p.scales = d->scales;
-    p.lr_scale = d->lr_scale;
+    p.lr = d->lowrank;
     p.outliers = d->outliers;
     p.idx = d->outlier_idx;
     p.ntb = (int)((T + ROWS - 1) / ROWS);
@@ -627,7 +674,9 @@ int launch_decode(const actcomp_cg_desc *d, const uint16_t *y, int64_t ldy, uint
     p.ntiles = p.tri ? (int64_t)p.ntb * (p.ntb + 1) / 2 * B : (int64_t)p.ntb * p.ncc * B;
     p.n32 = (int)((H + 31) / 32);
     p.off_ot = L::OT_OFF;
-    p.vqs = d->basis_qs;
+    p.vtile = d->basis_tile;
+    p.out = out;
+    p.ldo = ldo;
     p.partials = sx.partials;
     p.rowsum = sx.rowsum;
     p.causal = sx.causal;
@@ -635,27 +684,33 @@ int launch_decode(const actcomp_cg_desc *d, const uint16_t *y, int64_t ldy, uint
     p.ostb = (ROWS * p.k * 2 + 15) & ~15;
     const int smem = L::total(p.n32, p.k);
     if (smem > 227 * 1024) return ACT_E_UNSUPPORTED;
-    auto kern = cg_decode_tc_kernel<BITS, OP, WHT, RB>;
+    auto kern = cg_decode_tc_kernel<BITS, OP, WHT, RK>;
     ACT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
     const int grid = (int)(p.ntiles < num_sms() ? p.ntiles : num_sms());
     p.tq = (int)(p.ntiles / grid);
     p.trem = (int)(p.ntiles % grid);
-    kern<<<grid, L::THREADS, smem, stream>>>(m_lq, m_vq, m_codes, m_y, m_out, p);
+    kern<<<grid, L::THREADS, smem, stream>>>(m_codes, m_y, m_out, p);
     return launch_status();
 }
 
 template <int BITS, int OP>
 int dispatch_rb(const actcomp_cg_desc *d, const uint16_t *y, int64_t ldy, uint16_t *out, int64_t ldo,
                 cudaStream_t s, const SmaxArgs &sx = SmaxArgs()) {
-    const int rb = d->rank == 0 ? 0 : (d->rank <= 32 ? 32 : 64);
-    if (d->wht) {
-        if (rb == 0) return launch_decode<BITS, OP, true, 0>(d, y, ldy, out, ldo, s, sx);
-        if (rb == 32) return launch_decode<BITS, OP, true, 32>(d, y, ldy, out, ldo, s, sx);
-        return launch_decode<BITS, OP, true, 64>(d, y, ldy, out, ldo, s, sx);
-    }
-    if (rb == 0) return launch_decode<BITS, OP, false, 0>(d, y, ldy, out, ldo, s, sx);
-    if (rb == 32) return launch_decode<BITS, OP, false, 32>(d, y, ldy, out, ldo, s, sx);
-    return launch_decode<BITS, OP, false, 64>(d, y, ldy, out, ldo, s, sx);
+    if (d->rank && (!d->basis_tile || !act::aligned(d->basis_tile, 16) || !act::aligned(d->lowrank, 16)))
+        return ACT_E_UNSUPPORTED;
+    const int rk = d->rank == 0 ? 0 : (d->rank <= 16 ? 16 : (d->rank <= 32 ? 32 : 64));
+#define ACT_DTC(W)                                                                 \
+    do {                                                                           \
+        switch (rk) {                                                              \
+            case 0: return launch_decode<BITS, OP, W, 0>(d, y, ldy, out, ldo, s, sx);   \
+            case 16: return launch_decode<BITS, OP, W, 16>(d, y, ldy, out, ldo, s, sx); \
+            case 32: return launch_decode<BITS, OP, W, 32>(d, y, ldy, out, ldo, s, sx); \
+            default: return launch_decode<BITS, OP, W, 64>(d, y, ldy, out, ldo, s, sx); \
+        }                                                                          \
+    } while (0)
+    if (d->wht) ACT_DTC(true);
+    ACT_DTC(false);
+#undef ACT_DTC
 }
 
 // row sums of the softmax partials, in a fixed order (deterministic)

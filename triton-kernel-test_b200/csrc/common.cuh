@@ -82,6 +82,16 @@ __device__ __forceinline__ uint32_t pack_bf16x2(float lo, float hi) {
     __nv_bfloat162 v = __floats2bfloat162_rn(lo, hi);
     return *reinterpret_cast<uint32_t *>(&v);
 }
+// v = hi + mid + lo exactly, each a bf16 value: hi = bf16(v), mid = bf16(v - hi),
+// lo = v - hi - mid (both differences are exact in binary32, and the last one
+// has at most 8 significant bits).  The tensor cores multiply the three pieces
+// by a bf16 operand exactly, so a float32 factor enters an MMA at full precision.
+__device__ __forceinline__ void split3_bf16(float v, float &hi, float &mid, float &lo) {
+    hi = rne_bf(v);
+    const float r1 = __fsub_rn(v, hi);
+    mid = rne_bf(r1);
+    lo = rne_bf(__fsub_rn(r1, mid));
+}
 
 // ---------------------------------------------------------------- consumer ops
 // The derivative formulas of the reference twins, evaluated in binary32 in the
