@@ -49,9 +49,16 @@ const char *actcomp_strerror(int status);
 int actcomp_abi_version(void);
 /* Device-side error word of the current device: 0 when no bounded wait has
  * timed out since the last call to actcomp_clear_device_error.  Synchronises
- * the given stream. */
+ * the given stream; returns ACT_E_TIMEOUT when the word records a timed-out
+ * wait, else ACT_OK (or a CUDA error). */
 int actcomp_last_device_error(void *stream, uint32_t *word);
 int actcomp_clear_device_error(void *stream);
+/* Failure-detection self-test (no reference counterpart): one CTA waits on an
+ * mbarrier with the kernels' bounded wait cut to `polls` (1..2^24) polls.
+ * With arrive == 0 nothing completes the barrier: the wait gives up, records
+ * the timeout in the device error word and the kernel returns (no trap, no
+ * hang); with arrive != 0 the wait completes and the word is untouched. */
+int actcomp_selftest_bounded_wait(uint32_t polls, int32_t arrive, void *stream);
 
 /* ========================================================= channel-group format
  * One compressed activation: `batch` independent slices, each a T x H bf16

@@ -136,3 +136,12 @@ def test_dw_workspace_size():
     lib = _lib.load()
     d = _desc(tokens=16384, channels=4096)
     assert lib.actcomp_cg_dw_workspace(ctypes.byref(d), 11008) >= 16384 * 4096 * 2
+
+
+def test_selftest_rejects_bad_poll_counts():
+    """Host-side validation of the failure-detection self-test (no launch)."""
+    from actcomp import _lib
+
+    lib = _lib.load()
+    assert lib.actcomp_selftest_bounded_wait(0, 0, None) == _lib.ACT_E_INVALID
+    assert lib.actcomp_selftest_bounded_wait((1 << 24) + 1, 0, None) == _lib.ACT_E_INVALID

@@ -11,7 +11,8 @@ import os
 import threading
 
 _HERE = os.path.dirname(os.path.abspath(__file__))
-LIB_PATH = os.path.join(_HERE, "libactcomp.so")
+#: the in-tree build; ACTCOMP_LIBRARY names another build of the same sources instead
+LIB_PATH = os.environ.get("ACTCOMP_LIBRARY") or os.path.join(_HERE, "libactcomp.so")
 
 c_i64 = ctypes.c_int64
 c_i32 = ctypes.c_int32
@@ -85,6 +86,7 @@ SIGNATURES = {
     "actcomp_abi_version": (ctypes.c_int, []),
     "actcomp_last_device_error": (ctypes.c_int, [c_vp, ctypes.POINTER(ctypes.c_uint32)]),
     "actcomp_clear_device_error": (ctypes.c_int, [c_vp]),
+    "actcomp_selftest_bounded_wait": (ctypes.c_int, [ctypes.c_uint32, c_i32, c_vp]),
     "actcomp_cg_basis_prepare": (ctypes.c_int, [c_vp, c_i64, c_i32, c_i32, c_vp, c_vp, c_vp, c_vp]),
     "actcomp_cg_encode": (ctypes.c_int, [ctypes.POINTER(CgDesc), c_vp, c_i64, c_vp]),
     "actcomp_cg_decode": (ctypes.c_int, [ctypes.POINTER(CgDesc), c_vp, c_i64, c_vp]),

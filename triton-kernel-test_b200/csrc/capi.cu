@@ -2,7 +2,7 @@
 // plus status strings and the device error word.
 #include <mutex>
 
-#include "common.cuh"
+#include "tc_ptx.cuh"
 
 namespace act {
 __device__ uint32_t g_device_error = 0;
@@ -29,6 +29,7 @@ int act_cg_consume_simt(const actcomp_cg_desc *d, int op, const uint16_t *y, int
 int act_cg_consume_tc(const actcomp_cg_desc *d, int op, const uint16_t *y, int64_t ldy, uint16_t *out, int64_t ldo,
                       cudaStream_t s);
 int act_cg_encode_rows(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cudaStream_t s);
+int act_cg_encode_split(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cudaStream_t s);
 int act_cg_softmax_simt(const actcomp_cg_desc *d, const uint16_t *dp, uint16_t *ds, int64_t ld, int causal,
                         cudaStream_t s);
 size_t act_cg_softmax_tc_workspace(const actcomp_cg_desc *d);
@@ -58,7 +59,34 @@ extern "C" int actcomp_last_device_error(void *stream, uint32_t *word) {
     ACT_CHECK(word, ACT_E_INVALID);
     ACT_CUDA_TRY(cudaStreamSynchronize(as_stream(stream)));
     ACT_CUDA_TRY(cudaMemcpyFromSymbol(word, g_device_error, sizeof(uint32_t)));
-    return ACT_OK;
+    return (*word & DEV_ERR_MBAR_TIMEOUT) ? ACT_E_TIMEOUT : ACT_OK;
+}
+
+namespace act {
+// One CTA waits on an mbarrier with the library's bounded wait cut to `polls`
+// polls.  Without an arrival nothing completes the barrier, the wait gives up,
+// sets the device error word and the kernel returns; with one, the wait ends
+// at once and the word is left alone.
+__global__ void selftest_wait_kernel(uint32_t polls, int arrive) {
+    __shared__ uint64_t bar;
+    __shared__ int abort_word;
+    if (threadIdx.x == 0) {
+        tc::mbar_init(&bar, 1);
+        abort_word = 0;
+        tc::fence_mbar_init();
+    }
+    __syncthreads();
+    if (threadIdx.x == 0) {
+        if (arrive) tc::mbar_arrive(&bar);
+        (void)tc::mbar_wait(&bar, 0, &abort_word, polls);
+    }
+}
+}  // namespace act
+
+extern "C" int actcomp_selftest_bounded_wait(uint32_t polls, int32_t arrive, void *stream) {
+    ACT_CHECK(polls >= 1 && polls <= (1u << 24), ACT_E_INVALID);
+    act::selftest_wait_kernel<<<1, 32, 0, as_stream(stream)>>>(polls, arrive);
+    return launch_status();
 }
 
 extern "C" int actcomp_clear_device_error(void *stream) {
@@ -92,9 +120,13 @@ extern "C" int actcomp_cg_encode(const actcomp_cg_desc *d, const uint16_t *x, in
     if (st) return st;
     if ((st = check_rows(x, ldx, d->channels))) return st;
     if (d->rank) ACT_CHECK(d->basis_t && aligned(d->basis_t, 16), ACT_E_ALIGN);
-    // the tensor-core row encode, else (rank 0, H outside 1024..16384 or not a
-    // multiple of 128, no basis tile) the CUDA-core encode; the row encode
-    // declines (ACT_E_UNSUPPORTED, before launching) what it does not cover
+    // the two-kernel encode (projection, then quantisation: rank 16 or 32, groups
+    // of 32 or 64, no rotation, one slice, H a multiple of 128), else the
+    // two-pass row encode (1024 <= H <= 16384, a multiple of 128), else the
+    // CUDA-core encode; each tensor-core encode declines (ACT_E_UNSUPPORTED,
+    // before launching) what it does not cover
+    st = act_cg_encode_split(d, x, ldx, as_stream(stream));
+    if (st != ACT_E_UNSUPPORTED) return st;
     st = act_cg_encode_rows(d, x, ldx, as_stream(stream));
     if (st != ACT_E_UNSUPPORTED) return st;
     return act_cg_encode_simt(d, x, ldx, as_stream(stream));

@@ -6,11 +6,13 @@
 //   warp 0      producer: per tile one bulk copy of the prepared bf16 basis
 //               tile (128 channels x r) and one TMA load of the residual codes
 //               into an S-stage ring; per token block one bulk copy of its
-//               projection L (128 x r float32) and of its outlier values;
-//   warp 1      MMA: per token block splits L into its three exact bf16 pieces
-//               (three swizzled operand tiles); per tile tcgen05.mma kind::f16
-//               (M=128, N=128, K=16 steps, three pieces) gives the low-rank term
-//               P = L . V^T in float32 in TMEM, one accumulator per epilogue group;
+//               outlier values;
+//   last warp   per token block, ahead of the MMAs, splits L (read from global
+//               memory) into its three exact bf16 pieces: three swizzled operand
+//               tiles in one of two slots;
+//   warp 1      MMA: per tile tcgen05.mma kind::f16 (M=128, N=128, K=16 steps,
+//               three pieces) gives the low-rank term P = L . V^T in float32 in
+//               TMEM, one accumulator per epilogue group;
 //   warps 2-17  epilogue: four groups of four warps, group g takes the tiles
 //               g, g+4, g+8, ... of the range; a thread owns one token row of
 //               the tile and all 128 channels, processed as four 32-channel
@@ -44,7 +46,7 @@ template <bool WHT>
 struct Geo {
     static constexpr int NG = WHT ? 2 : 4;
     static constexpr int EW = 4 * NG;
-    static constexpr int THREADS = 64 + 32 * EW;
+    static constexpr int THREADS = 64 + 32 * EW + 32;  // + the warp that prepares the piece tiles
 };
 // TMEM columns a block allocates: the accumulators, plus 128 scratch columns per
 // group for the rotated formats
@@ -71,7 +73,7 @@ struct RowParams {
     const uint16_t *outliers;
     const int32_t *idx;
     const uint16_t *vtile; // basis tile operand
-    int off_stg, off_lqb, off_lqi, off_ost, off_bar, off_ot;
+    int off_stg, off_lqb, off_ost, off_bar, off_ot;
 };
 
 template <int BITS, int RK>
@@ -84,8 +86,7 @@ struct RowLayout {
     static constexpr int LQB = RK ? 3 * ROWS * LB : 0;  // the three bf16 pieces of a token block's L
     // returns the shared-memory bytes, or 0 if S < 3 stages would fit
     static int plan(RowParams &p, int nsl, int EW) {
-        const int lqi = p.rank ? ROWS * p.rank * 4 : 0;  // float32 L of a token block
-        const int fixed_no_ost = EW * WSTG + 2 * LQB + 2 * ((lqi + 1023) & ~1023) + 1024 /*bars*/ +
+        const int fixed_no_ost = EW * WSTG + 2 * LQB + 1024 /*bars*/ +
                                  ((nsl * p.n32 * 8 + 15) & ~15) + 1024 /*align*/;
         const int ostb = (ROWS * p.k * 2 + 15) & ~15;
         for (int ost = p.k ? 1 : 0; ost >= 0; --ost) {
@@ -97,8 +98,7 @@ struct RowLayout {
                     p.ostb = ostb;
                     p.off_stg = S * STAGE;
                     p.off_lqb = p.off_stg + EW * WSTG;
-                    p.off_lqi = p.off_lqb + 2 * LQB;
-                    p.off_ost = p.off_lqi + 2 * ((lqi + 1023) & ~1023);
+                    p.off_ost = p.off_lqb + 2 * LQB;
                     p.off_bar = p.off_ost + (ost ? 2 * ostb : 0);
                     p.off_ot = p.off_bar + 1024;
                     return p.off_ot + ((nsl * p.n32 * 8 + 15) & ~15) + 1024;
@@ -229,16 +229,16 @@ __global__ void __launch_bounds__(Geo<WHT>::THREADS, 1)
     uint64_t *empty = full + 6;
     uint64_t *tfull = empty + 6;
     uint64_t *tempty = tfull + NG;
-    uint64_t *lqfull = tempty + NG;  // [2] token-block slots loaded
+    uint64_t *lqfull = tempty + NG;  // [2] token-block outlier slots loaded
     uint64_t *lqempty = lqfull + 2;  // [2] ... and no longer read
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(lqempty + 2);
+    uint64_t *pready = lqempty + 2;  // [2] piece tiles of a token block written
+    uint64_t *pfree = pready + 2;    // [2] ... and read by the MMAs
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(pfree + 2);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
     uint8_t *lqb = smem + p.off_lqb;
-    uint8_t *lqi = smem + p.off_lqi;
     uint8_t *ostbuf = smem + p.off_ost;
-    const int lqi_slot = ((p.rank * ROWS * 4) + 1023) & ~1023;
     const bool use_ost = p.k > 0 && p.ostage;
-    const bool blockbuf = RK > 0 || use_ost;
+    const bool blockbuf = use_ost;
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     const int i_blk = blockIdx.x;
     const int64_t t_lo = (int64_t)i_blk * p.tq + (i_blk < p.trem ? i_blk : p.trem);
@@ -257,9 +257,10 @@ __global__ void __launch_bounds__(Geo<WHT>::THREADS, 1)
         }
         for (int b = 0; b < 2; ++b) {
             tc::mbar_init(&lqfull[b], 1);
-            // the MMA warp's commit, plus 4 arrivals per tile of the block (the
-            // warps of the group that decodes it) when outliers are staged
-            tc::mbar_init(&lqempty[b], (RK ? 1 : 0) + (use_ost ? 4 * p.ncc : 0));
+            // 4 arrivals per tile of the block (the warps of the group that decodes it)
+            if (use_ost) tc::mbar_init(&lqempty[b], 4 * p.ncc);
+            tc::mbar_init(&pready[b], 1);
+            tc::mbar_init(&pfree[b], 1);
         }
         *abort = 0;
         tc::fence_mbar_init();
@@ -288,13 +289,7 @@ __global__ void __launch_bounds__(Geo<WHT>::THREADS, 1)
                     if (!tc::mbar_wait(&lqempty[ls], ((nlq >> 1) & 1) ^ 1, abort)) break;
                     const uint16_t *osrc = nullptr;
                     const uint32_t obytes = p.k ? ost_bytes(p, tw.tb, tw.b, osrc) : 0;
-                    const int64_t rows =
-                        (p.T - (int64_t)tw.tb * ROWS) < ROWS ? (p.T - (int64_t)tw.tb * ROWS) : ROWS;
-                    const uint32_t lbytes = RK ? (uint32_t)(rows * p.rank * 4) : 0;
-                    tc::mbar_arrive_expect_tx(&lqfull[ls], lbytes + obytes);
-                    if (RK)
-                        tc::bulk_load(lqi + ls * lqi_slot, p.lr + ((int64_t)tw.b * p.T + (int64_t)tw.tb * ROWS) * p.rank,
-                                      lbytes, &lqfull[ls]);
+                    tc::mbar_arrive_expect_tx(&lqfull[ls], obytes);
                     if (obytes) tc::bulk_load(ostbuf + ls * p.ostb, osrc, obytes, &lqfull[ls]);
                     ++nlq;
                 }
@@ -319,41 +314,11 @@ __global__ void __launch_bounds__(Geo<WHT>::THREADS, 1)
                 const int s = i % S, acc = i & (NG - 1);
                 const uint32_t ph = (i / S) & 1, aph = (i / NG) & 1;
                 if (tile == t_lo || tw.cc == 0) {
-                    // a new token block: its projection as three bf16 operand tiles
+                    // a new token block: its piece tiles (prepared by the last warp)
                     const int ls = mlq & 1;
                     int okw = 1;
-                    if (lane == 0) okw = tc::mbar_wait(&lqfull[ls], (mlq >> 1) & 1, abort);
+                    if (lane == 0) okw = tc::mbar_wait(&pready[ls], (mlq >> 1) & 1, abort);
                     if (!(ok = __shfl_sync(0xffffffffu, okw, 0) != 0)) break;
-                    const float *src = reinterpret_cast<const float *>(lqi + ls * lqi_slot);
-                    uint8_t *dst = lqb + ls * L::LQB;
-                    // 8 coefficients (two 16-byte loads) per 16-byte chunk of each
-                    // piece tile; chunks past the rank and rows past T are zero
-                    const int cpr = LB / 16;  // chunks per row
-                    const int64_t rows_here = p.T - (int64_t)tw.tb * ROWS;
-                    for (int e = lane; e < ROWS * cpr; e += 32) {
-                        const int row = e / cpr, c16 = e - row * cpr;
-                        uint32_t ph[4] = {0u, 0u, 0u, 0u}, pm[4] = {0u, 0u, 0u, 0u}, pl[4] = {0u, 0u, 0u, 0u};
-                        if (8 * c16 < p.rank && row < rows_here) {
-                            const float4 v0 = *reinterpret_cast<const float4 *>(src + row * p.rank + 8 * c16);
-                            const float4 v1 = *reinterpret_cast<const float4 *>(src + row * p.rank + 8 * c16 + 4);
-                            const float in[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-#pragma unroll
-                            for (int h = 0; h < 4; ++h) {
-                                float h0, m0, l0, h1, m1, l1;
-                                split3_bf16(in[2 * h], h0, m0, l0);
-                                split3_bf16(in[2 * h + 1], h1, m1, l1);
-                                ph[h] = pack_bf16x2(h0, h1);
-                                pm[h] = pack_bf16x2(m0, m1);
-                                pl[h] = pack_bf16x2(l0, l1);
-                            }
-                        }
-                        const int o = swz<LB>(row, c16);
-                        *reinterpret_cast<uint4 *>(dst + o) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
-                        *reinterpret_cast<uint4 *>(dst + ROWS * LB + o) = make_uint4(pm[0], pm[1], pm[2], pm[3]);
-                        *reinterpret_cast<uint4 *>(dst + 2 * ROWS * LB + o) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
-                    }
-                    tc::fence_proxy_async();
-                    __syncwarp();
                     ++mlq;
                 }
                 const int ls = (mlq - 1) & 1;
@@ -374,10 +339,55 @@ __global__ void __launch_bounds__(Geo<WHT>::THREADS, 1)
                         tc::mma_commit(&tfull[acc]);
                         tc::mma_commit(&empty[s]);
                         // last tile of this token block in the range: the slot frees when these MMAs complete
-                        if (tw.cc == p.ncc - 1 || tile == t_hi - 1) tc::mma_commit(&lqempty[ls]);
+                        if (tw.cc == p.ncc - 1 || tile == t_hi - 1) tc::mma_commit(&pfree[ls]);
                     }
                 }
                 ok = __shfl_sync(0xffffffffu, okw, 0) != 0;
+            }
+        }
+    } else if (warp == 2 + EW) {
+        // ------------------------------------------------------------ L -> piece tiles, per token block
+        if constexpr (RK > 0) {
+            Walk tw(t_lo, p.ncc, p.ntb);
+            int m = 0;
+            bool ok = true;
+            for (int64_t tile = t_lo; tile < t_hi && ok; ++tile, tw.next()) {
+                if (tile != t_lo && tw.cc != 0) continue;  // not the first tile of a token block
+                const int ls = m & 1;
+                if (!(ok = tc::mbar_wait(&pfree[ls], ((m >> 1) & 1) ^ 1, abort))) break;
+                uint8_t *dst = lqb + ls * L::LQB;
+                const int64_t t0 = (int64_t)tw.b * p.T + (int64_t)tw.tb * ROWS;  // first row of the block
+                const int64_t rows_here = p.T - (int64_t)tw.tb * ROWS;
+                // 8 coefficients (two 16-byte loads) per 16-byte chunk of each piece
+                // tile; chunks past the rank and rows past T are zero
+                constexpr int CPR = LB / 16;
+#pragma unroll 2
+                for (int e = lane; e < ROWS * CPR; e += 32) {
+                    const int row = e / CPR, c16 = e - row * CPR;
+                    uint32_t ph[4] = {0u, 0u, 0u, 0u}, pm[4] = {0u, 0u, 0u, 0u}, pl[4] = {0u, 0u, 0u, 0u};
+                    if (8 * c16 < p.rank && row < rows_here) {
+                        const float4 *src = reinterpret_cast<const float4 *>(p.lr + (t0 + row) * p.rank + 8 * c16);
+                        const float4 v0 = __ldg(src), v1 = __ldg(src + 1);
+                        const float in[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+                        for (int h = 0; h < 4; ++h) {
+                            float h0, m0, l0, h1, m1, l1;
+                            split3_bf16(in[2 * h], h0, m0, l0);
+                            split3_bf16(in[2 * h + 1], h1, m1, l1);
+                            ph[h] = pack_bf16x2(h0, h1);
+                            pm[h] = pack_bf16x2(m0, m1);
+                            pl[h] = pack_bf16x2(l0, l1);
+                        }
+                    }
+                    const int o = swz<LB>(row, c16);
+                    *reinterpret_cast<uint4 *>(dst + o) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
+                    *reinterpret_cast<uint4 *>(dst + ROWS * LB + o) = make_uint4(pm[0], pm[1], pm[2], pm[3]);
+                    *reinterpret_cast<uint4 *>(dst + 2 * ROWS * LB + o) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+                }
+                tc::fence_proxy_async();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&pready[ls]);
+                ++m;
             }
         }
     } else {

@@ -5,12 +5,13 @@
 //   TMA warp   loads the prepared bf16 basis tile of the 128 channels, the
 //              residual codes (128 x 64 B for int4) and, for a consumer, the
 //              second operand (128 x 128 bf16) into a 2-6 stage ring; per token
-//              block the projection L (128 x r float32) and the outlier values;
-//   MMA warp   per token block splits L into its three exact bf16 pieces (three
-//              swizzled operand tiles); per tile tcgen05.mma kind::f16 (M=128,
-//              N=128, K=16 steps over the three pieces) gives the low-rank term
-//              P = L . V^T in float32 in TMEM (4 accumulators of 128 columns, so
-//              the MMA runs ahead);
+//              block the outlier values;
+//   last warp  per token block, ahead of the MMAs, splits L (read from global
+//              memory) into its three exact bf16 pieces: three swizzled operand
+//              tiles in one of two slots;
+//   MMA warp   per tile tcgen05.mma kind::f16 (M=128, N=128, K=16 steps over
+//              the three pieces) gives the low-rank term P = L . V^T in float32
+//              in TMEM (4 accumulators of 128 columns, so the MMA runs ahead);
 //   epilogue   (16 warps: 4 row quarters x 4 column quarters, one token row
 //              and 32 channels per thread; the rotation exchanges quarters
 //              through shared memory) reads P with tcgen05.ld, forms
@@ -64,24 +65,22 @@ struct DecParams {
 template <int BITS, int OP, bool WHT, int RK>
 struct DecLayout {
     static constexpr int LB = 2 * RK;              // bytes of one bf16 operand row
-    static constexpr int LQ = RK ? ROWS * RK * 4 : 0;  // float32 L of a token block (2 slots, outside the ring)
-    static constexpr int PT = RK ? 3 * ROWS * LB : 0;  // its three bf16 piece tiles (1 slot)
+    static constexpr int PT = RK ? 3 * ROWS * LB : 0;  // the three bf16 piece tiles of a token block (2 slots)
     static constexpr int VQ = RK ? CH * LB : 0;        // basis tile
     static constexpr int CODES = ROWS * CH * BITS / 8;
     static constexpr int Y = OP == ACT_OP_DECODE ? 0 : ROWS * CH * 2;
     static constexpr int STAGE = VQ + CODES + Y;
     static constexpr int OUT = OP == ACT_OP_DECODE ? ROWS * CH * 2 : 0;  // decode output staging
     static constexpr int WX = WHT ? 4 * ROWS * 32 * 4 : 0;  // rotation exchange: 32 floats per thread
-    static constexpr int FIXED = 2 * OUT + WX + 2 * LQ + PT + 1024;  // + barriers
+    static constexpr int FIXED = 2 * OUT + WX + 2 * PT + 1024;  // + barriers
     static constexpr int S = (6 * STAGE + FIXED <= 200 * 1024) ? 6 : (4 * STAGE + FIXED <= 200 * 1024) ? 4
                                                                   : ((3 * STAGE + FIXED <= 214 * 1024) ? 3 : 2);
     static constexpr int EW = 16;  // epilogue warps: 4 row quarters x 4 column quarters
-    static constexpr int THREADS = 64 + 32 * EW;
+    static constexpr int THREADS = 64 + 32 * EW + 32;  // + the warp that prepares the piece tiles
     static constexpr int OUT_OFF = S * STAGE;
     static constexpr int WX_OFF = OUT_OFF + 2 * OUT;
-    static constexpr int LQ_OFF = WX_OFF + WX;
-    static constexpr int PT_OFF = LQ_OFF + 2 * LQ;
-    static constexpr int BAR_OFF = PT_OFF + PT;
+    static constexpr int PT_OFF = WX_OFF + WX;
+    static constexpr int BAR_OFF = PT_OFF + 2 * PT;
     static constexpr int OT_OFF = BAR_OFF + 1024;
     static int ost_off(int n32) { return OT_OFF + ((n32 * 8 + 15) & ~15); }
     static int total(int n32, int k) { return ost_off(n32) + 2 * ((ROWS * k * 2 + 15) & ~15) + 1024; }
@@ -174,15 +173,15 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RK>::THREADS, 1)
     uint64_t *empty = full + L::S;
     uint64_t *tfull = empty + L::S;
     uint64_t *tempty = tfull + NT;
-    uint64_t *lqfull = tempty + NT;   // [2] token-block slots (projection, outlier values) loaded
+    uint64_t *lqfull = tempty + NT;   // [2] token-block outlier slots loaded
     uint64_t *lqempty = lqfull + 2;  // [2] ... and no longer read
-    uint64_t *ptfree = lqempty + 2;  // the MMAs of a token block have read its piece tiles
-    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(ptfree + 1);
+    uint64_t *pready = lqempty + 2;  // [2] piece tiles of a token block written
+    uint64_t *pfree = pready + 2;    // [2] ... and read by the MMAs
+    uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(pfree + 2);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
-    uint8_t *lqbuf = smem + L::LQ_OFF;
     uint8_t *ptile = smem + L::PT_OFF;
     uint8_t *ostbuf = smem + p.off_ost;
-    const bool blockbuf = RK > 0 || p.k > 0;  // per-token-block slots in use
+    const bool blockbuf = p.k > 0;  // per-token-block outlier slots in use
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
     int64_t t_lo, t_hi;
     tile_range(p, t_lo, t_hi);
@@ -198,9 +197,10 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RK>::THREADS, 1)
         }
         for (int b = 0; b < 2; ++b) {
             tc::mbar_init(&lqfull[b], 1);
-            tc::mbar_init(&lqempty[b], (RK ? 1 : 0) + (p.k ? L::EW : 0));
+            if (p.k) tc::mbar_init(&lqempty[b], L::EW);
+            tc::mbar_init(&pready[b], 1);
+            tc::mbar_init(&pfree[b], 1);
         }
-        tc::mbar_init(ptfree, 1);
         *abort = 0;
         tc::fence_mbar_init();
     }
@@ -224,17 +224,12 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RK>::THREADS, 1)
                 const uint32_t ph = (i / L::S) & 1;
                 const int cc = tw.cc, tb = tw.tb, b = tw.b;
                 if (blockbuf && (tile == t_lo || cc == 0)) {
-                    // a new token block: its projection and outlier values into the free slot
+                    // a new token block: its outlier values into the free slot
                     const int ls = nlq & 1;
                     if (!tc::mbar_wait(&lqempty[ls], ((nlq >> 1) & 1) ^ 1, abort)) break;
                     const uint16_t *osrc = nullptr;
                     const uint32_t obytes = ost_bytes(p, tb, b, osrc);
-                    const int64_t rows = (p.T - (int64_t)tb * ROWS) < ROWS ? (p.T - (int64_t)tb * ROWS) : ROWS;
-                    const uint32_t lbytes = RK ? (uint32_t)(rows * p.rank * 4) : 0;
-                    tc::mbar_arrive_expect_tx(&lqfull[ls], lbytes + obytes);
-                    if (RK)
-                        tc::bulk_load(lqbuf + ls * L::LQ, p.lr + ((int64_t)b * p.T + (int64_t)tb * ROWS) * p.rank, lbytes,
-                                      &lqfull[ls]);
+                    tc::mbar_arrive_expect_tx(&lqfull[ls], obytes);
                     if (obytes) tc::bulk_load(ostbuf + ls * p.ostb, osrc, obytes, &lqfull[ls]);
                     ++nlq;
                 }
@@ -264,47 +259,13 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RK>::THREADS, 1)
                 const int s = i % L::S, b = i % NT;
                 const uint32_t ph = (i / L::S) & 1, bph = (i / NT) & 1;
                 if (tile == t_lo || tw.cc == 0) {
-                    // a new token block: once its projection has landed and the previous
-                    // block's MMAs have read the piece tiles, split L into them
-                    const int ls = mlq & 1;
+                    // a new token block: its piece tiles (prepared by the last warp)
                     int okw = 1;
-                    if (lane == 0) {
-                        okw = tc::mbar_wait(&lqfull[ls], (mlq >> 1) & 1, abort);
-                        if (okw && mlq > 0) okw = tc::mbar_wait(ptfree, (mlq - 1) & 1, abort);
-                    }
+                    if (lane == 0) okw = tc::mbar_wait(&pready[mlq & 1], (mlq >> 1) & 1, abort);
                     if (!(ok = __shfl_sync(0xffffffffu, okw, 0) != 0)) break;
-                    tc::tc_fence_after();
-                    const float *src = reinterpret_cast<const float *>(lqbuf + ls * L::LQ);
-                    const int cpr = LB / 16;  // 16-byte chunks per operand row
-                    const int64_t rows_here = p.T - (int64_t)tw.tb * ROWS;
-                    for (int e = lane; e < ROWS * cpr; e += 32) {
-                        const int row = e / cpr, c16 = e - row * cpr;
-                        uint32_t hp[4] = {0u, 0u, 0u, 0u}, mp[4] = {0u, 0u, 0u, 0u}, lp[4] = {0u, 0u, 0u, 0u};
-                        if (8 * c16 < p.rank && row < rows_here) {
-                            const float4 v0 = *reinterpret_cast<const float4 *>(src + row * p.rank + 8 * c16);
-                            const float4 v1 = *reinterpret_cast<const float4 *>(src + row * p.rank + 8 * c16 + 4);
-                            const float in[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-#pragma unroll
-                            for (int hh = 0; hh < 4; ++hh) {
-                                float h0, m0, l0, h1, m1, l1;
-                                split3_bf16(in[2 * hh], h0, m0, l0);
-                                split3_bf16(in[2 * hh + 1], h1, m1, l1);
-                                hp[hh] = pack_bf16x2(h0, h1);
-                                mp[hh] = pack_bf16x2(m0, m1);
-                                lp[hh] = pack_bf16x2(l0, l1);
-                            }
-                        }
-                        const int o = swz<LB>(row, c16);
-                        *reinterpret_cast<uint4 *>(ptile + o) = make_uint4(hp[0], hp[1], hp[2], hp[3]);
-                        *reinterpret_cast<uint4 *>(ptile + ROWS * LB + o) = make_uint4(mp[0], mp[1], mp[2], mp[3]);
-                        *reinterpret_cast<uint4 *>(ptile + 2 * ROWS * LB + o) = make_uint4(lp[0], lp[1], lp[2], lp[3]);
-                    }
-                    tc::fence_proxy_async();
-                    __syncwarp();
-                    // the projection slot has been read (the outlier values in it may still be)
-                    if (lane == 0) tc::mbar_arrive(&lqempty[ls]);
                     ++mlq;
                 }
+                const uint8_t *pts = ptile + ((mlq - 1) & 1) * L::PT;
                 int okw = 1;
                 if (lane == 0) {
                     okw = tc::mbar_wait(&full[s], ph, abort) && tc::mbar_wait(&tempty[b], bph ^ 1, abort);
@@ -314,17 +275,60 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RK>::THREADS, 1)
                         // P = hi . V^T + mid . V^T + lo . V^T
                         for (int pc = 0; pc < 3; ++pc)
                             for (int kk = 0; kk < nkq; ++kk) {
-                                const uint64_t ad = tc::smem_desc(ptile + pc * ROWS * LB + kk * 32, 16, 8 * LB, SW);
+                                const uint64_t ad = tc::smem_desc(pts + pc * ROWS * LB + kk * 32, 16, 8 * LB, SW);
                                 const uint64_t bd = tc::smem_desc(st + kk * 32, 16, 8 * LB, SW);
                                 tc::mma_f16(tmem + b * CH, ad, bd, idesc, (pc | kk) > 0);
                             }
                         tc::mma_commit(&tfull[b]);
                         tc::mma_commit(&empty[s]);
                         // last tile of this token block in my range: the piece tiles free once these MMAs complete
-                        if (tw.cc == tw.last_cc() || tile == t_hi - 1) tc::mma_commit(ptfree);
+                        if (tw.cc == tw.last_cc() || tile == t_hi - 1) tc::mma_commit(&pfree[(mlq - 1) & 1]);
                     }
                 }
                 ok = __shfl_sync(0xffffffffu, okw, 0) != 0;
+            }
+        }
+    } else if (warp == 2 + L::EW) {
+        // ------------------------------------------------------------ L -> piece tiles, per token block
+        if constexpr (RK > 0) {
+            TileWalk tw(t_lo, p.ncc, p.ntb, p.tri != 0);
+            int m = 0;
+            bool ok = true;
+            for (int64_t tile = t_lo; tile < t_hi && ok; ++tile, tw.next()) {
+                if (tile != t_lo && tw.cc != 0) continue;  // not the first tile of a token block
+                const int ls = m & 1;
+                if (!(ok = tc::mbar_wait(&pfree[ls], ((m >> 1) & 1) ^ 1, abort))) break;
+                uint8_t *dst = ptile + ls * L::PT;
+                const int64_t t0 = (int64_t)tw.b * p.T + (int64_t)tw.tb * ROWS;  // first row of the block
+                const int64_t rows_here = p.T - (int64_t)tw.tb * ROWS;
+                constexpr int CPR = LB / 16;  // 16-byte chunks per operand row (8 coefficients each)
+#pragma unroll 2
+                for (int e = lane; e < ROWS * CPR; e += 32) {
+                    const int row = e / CPR, c16 = e - row * CPR;
+                    uint32_t hp[4] = {0u, 0u, 0u, 0u}, mp[4] = {0u, 0u, 0u, 0u}, lp[4] = {0u, 0u, 0u, 0u};
+                    if (8 * c16 < p.rank && row < rows_here) {
+                        const float4 *src = reinterpret_cast<const float4 *>(p.lr + (t0 + row) * p.rank + 8 * c16);
+                        const float4 v0 = __ldg(src), v1 = __ldg(src + 1);
+                        const float in[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
+#pragma unroll
+                        for (int hh = 0; hh < 4; ++hh) {
+                            float h0, m0, l0, h1, m1, l1;
+                            split3_bf16(in[2 * hh], h0, m0, l0);
+                            split3_bf16(in[2 * hh + 1], h1, m1, l1);
+                            hp[hh] = pack_bf16x2(h0, h1);
+                            mp[hh] = pack_bf16x2(m0, m1);
+                            lp[hh] = pack_bf16x2(l0, l1);
+                        }
+                    }
+                    const int o = swz<LB>(row, c16);
+                    *reinterpret_cast<uint4 *>(dst + o) = make_uint4(hp[0], hp[1], hp[2], hp[3]);
+                    *reinterpret_cast<uint4 *>(dst + ROWS * LB + o) = make_uint4(mp[0], mp[1], mp[2], mp[3]);
+                    *reinterpret_cast<uint4 *>(dst + 2 * ROWS * LB + o) = make_uint4(lp[0], lp[1], lp[2], lp[3]);
+                }
+                tc::fence_proxy_async();
+                __syncwarp();
+                if (lane == 0) tc::mbar_arrive(&pready[ls]);
+                ++m;
             }
         }
     } else {

@@ -47,14 +47,16 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t *bar, uint32_t parity) {
         : "memory");
     return ok != 0;
 }
-// Bounded wait: gives up after ~2^24 polls (well over a second), records the
-// timeout in the device error word and in *abort (shared), and returns false.
-// Once *abort is set every later wait returns false at once, so a kernel that
-// lost a producer drains and exits instead of hanging.
-__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort) {
+// Bounded wait: gives up after `polls` polls (2^24 by default, well over a
+// second), records the timeout in the device error word and in *abort
+// (shared), and returns false.  Once *abort is set every later wait returns
+// false at once, so a kernel that lost a producer drains and exits instead of
+// hanging.
+__device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volatile int *abort,
+                                          uint32_t polls = 1u << 24) {
     // the abort word is read every 64th poll: a waiting warp issues little
     // more than the try_wait itself, leaving issue slots to working warps
-    for (uint32_t i = 0; i < (1u << 24); ++i) {
+    for (uint32_t i = 0; i < polls; ++i) {
         if (mbar_try_wait(bar, parity)) return true;
         if ((i & 63u) == 63u && *abort) return false;
     }
@@ -77,6 +79,21 @@ __device__ __forceinline__ void tma_load_3d(void *dst, const CUtensorMap *map, u
             smem_u32(dst)),
         "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z)
         : "memory");
+}
+// The same with an L2 cache policy (createpolicy) for the loaded lines.
+__device__ __forceinline__ void tma_load_3d_hint(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y, int z,
+                                                 uint64_t policy) {
+    asm volatile(
+        "cp.async.bulk.tensor.3d.shared::cluster.global.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%3, "
+        "%4, %5}], [%2], %6;" ::"r"(smem_u32(dst)),
+        "l"(map), "r"(smem_u32(bar)), "r"(x), "r"(y), "r"(z), "l"(policy)
+        : "memory");
+}
+// L2 policy: lines loaded under it are the first to be evicted.
+__device__ __forceinline__ uint64_t l2_policy_evict_first() {
+    uint64_t pol;
+    asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(pol));
+    return pol;
 }
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap *map) {
     asm volatile("prefetch.tensormap [%0];" ::"l"(map) : "memory");
@@ -155,6 +172,20 @@ __device__ __forceinline__ bool mbar_wait_cluster(uint64_t *bar, uint32_t parity
     return false;
 }
 __device__ __forceinline__ void fence_acq_rel_cluster() { asm volatile("fence.acq_rel.cluster;" ::: "memory"); }
+// Stores into another CTA's shared memory (cluster address from map_cluster).
+__device__ __forceinline__ void st_cluster_v4(uint32_t addr, uint4 v) {
+    asm volatile("st.shared::cluster.v4.b32 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(v.x), "r"(v.y), "r"(v.z),
+                 "r"(v.w)
+                 : "memory");
+}
+__device__ __forceinline__ void st_cluster_v2(uint32_t addr, uint2 v) {
+    asm volatile("st.shared::cluster.v2.b32 [%0], {%1, %2};" ::"r"(addr), "r"(v.x), "r"(v.y) : "memory");
+}
+// Order this thread's generic-proxy shared::cluster writes before later
+// async-proxy reads of them (tensor-core operands written by peer CTAs).
+__device__ __forceinline__ void fence_proxy_async_cluster() {
+    asm volatile("fence.proxy.async.shared::cluster;" ::: "memory");
+}
 
 // Bulk copy of `bytes` (multiple of 16) from this CTA's shared memory into
 // another CTA's shared memory (both cluster addresses from map_cluster),
