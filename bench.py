@@ -168,6 +168,20 @@ def barrier(world):
         dist.barrier()
 
 
+def gather_all(x, world):
+    """x from every rank, in rank order (a list)."""
+    import torch
+
+    if world == 1:
+        return [x]
+    import torch.distributed as dist
+
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [float(v.item()) for v in out]
+
+
 def allreduce_max(x, world):
     import torch
 
@@ -180,11 +194,36 @@ def allreduce_max(x, world):
     return t.item()
 
 
+class _Done:
+    """A finished handle (wait() returns at once) for time_copy."""
+
+    def wait(self):
+        pass
+
+
 # ---------------------------------------------------------------- timing
-def time_steps(fn, steps, warmup, flush, world, clk=None):
+class L2Flush:
+    """Between timed steps: a 256 MB write, then a 256 MB read of another
+    buffer.  The write evicts every line of the step's inputs; the read then
+    evicts the write's dirty lines, so that their write-back to HBM happens
+    here and not inside the next timed step."""
+
+    def __init__(self, dev):
+        import torch
+
+        self.w = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+        self.r = torch.ones(64 * 1024 * 1024, dtype=torch.int32, device=dev)
+
+    def __call__(self):
+        self.w.zero_()
+        self.r.max()
+
+
+def time_steps(fn, steps, warmup, flush, world, clk=None, detail=None):
     """Warm up, then time exactly `steps` calls of fn, each bracketed by CUDA
-    events on the current stream, with an L2 flush (a 256 MB write) between
-    calls outside the events.  Returns per-step ms (mean) as max over ranks."""
+    events on the current stream, with an L2 flush (L2Flush: a 256 MB write,
+    then a 256 MB read) between calls outside the events.  Returns per-step ms
+    (mean) as max over ranks."""
     import torch
 
     for _ in range(warmup):
@@ -195,7 +234,7 @@ def time_steps(fn, steps, warmup, flush, world, clk=None):
     evs = []
     with (clk.timed() if clk is not None else contextlib.nullcontext()):
         for _ in range(steps):
-            flush.zero_()
+            flush()
             a = torch.cuda.Event(enable_timing=True)
             b = torch.cuda.Event(enable_timing=True)
             a.record()
@@ -206,7 +245,10 @@ def time_steps(fn, steps, warmup, flush, world, clk=None):
     barrier(world)
     torch.cuda.synchronize()
     ms = sum(a.elapsed_time(b) for a, b in evs) / steps
-    return allreduce_max(ms, world)
+    ranks = gather_all(ms, world)
+    if detail is not None:
+        detail["per_rank_ms"] = ranks
+    return max(ranks)
 
 
 # ---------------------------------------------------------------- CPU baseline (oracle port)
@@ -322,7 +364,7 @@ def run_gpu(args):
     idx = actcomp.select_outlier_channels(xcal, k)
     x, _ = synthetic.lowrank_activation(T, H, n_outlier=k, seed=rank, device=dev, outlier_seed=0)
     del xcal
-    flush = torch.empty(256 * 1024 * 1024, dtype=torch.uint8, device=dev)
+    flush = L2Flush(dev)
 
     state = {}
 
@@ -341,7 +383,8 @@ def run_gpu(args):
         actcomp.decode(c0, out=state["xh"].view(1, T, H))
 
     clk = ClockSampler(torch.cuda.current_device()).__enter__()
-    ms_step = time_steps(step, args.steps, args.warmup, flush, world, clk)
+    step_detail = {}
+    ms_step = time_steps(step, args.steps, args.warmup, flush, world, clk, step_detail)
     ms_enc = time_steps(enc_only, args.steps, 1, flush, world, clk)
     ms_dec = time_steps(dec_only, args.steps, 1, flush, world, clk)
 
@@ -382,9 +425,16 @@ def run_gpu(args):
                            flush, world, clk)
         flops = 2.0 * H * N * T
         tf = flops / (ms_dw * 1e-3) / 1e12
+        # error of dW = Xhat^T dY against the bf16 GEMM of the uncompressed X, and
+        # against the float32 GEMM of Xhat (the fused path's own arithmetic)
+        dw = actcomp.weight_grad(c0, dy, torch.float32, ws)
+        dw_x = actcomp.gemm(x.mT, dy, torch.float32)
+        dw_xh = actcomp.gemm(actcomp.decode(c0).mT, dy, torch.float32)
         components["dw_gemm_fused_4096x11008_k16384"] = {
-            "ms": ms_dw, "TFLOP/s": tf, "frac_of_bf16_peak": tf / pk.get("bf16_tflops", 1590.0), "flops": flops}
-        del dy, ws
+            "ms": ms_dw, "TFLOP/s": tf, "frac_of_bf16_peak": tf / pk.get("bf16_tflops", 1590.0), "flops": flops,
+            "rel_err_vs_bf16_gemm_of_x": float((dw - dw_x).norm() / dw_x.norm()),
+            "rel_err_vs_gemm_of_xhat": float((dw - dw_xh).norm() / dw_xh.norm())}
+        del dy, ws, dw, dw_x, dw_xh
         # config 5: GELU backward on a compressed 65536 x 5120 activation
         T5, H5 = 4 * T, 5120
         x5, _ = synthetic.lowrank_activation(T5, H5, n_outlier=k, seed=200 + rank, device=dev, outlier_seed=200)
@@ -411,7 +461,13 @@ def run_gpu(args):
         for name, ms3 in ((f"encode_wht_{T3}x{H3}", ms_e3), (f"decode_wht_{T3}x{H3}", ms_d3)):
             components[name] = {"ms": ms3, "GB/s": wb / (ms3 * 1e-3) / 1e9,
                                 "frac_of_hbm": wb / (ms3 * 1e-3) / 1e9 / hbm, "bytes": wb}
-        del x3, b3, c3
+        # reconstruction error of the heavy-tailed activation with and without the rotation
+        e_rot = actcomp.error_stats(actcomp.decode(c3), x3).cpu().tolist()
+        c3p = actcomp.encode(x3, b3, None, bits=4, group=128, wht=False)
+        e_plain = actcomp.error_stats(actcomp.decode(c3p), x3).cpu().tolist()
+        components[f"encode_wht_{T3}x{H3}"]["rel_err_rotated"] = (e_rot[0] / e_rot[1]) ** 0.5
+        components[f"encode_wht_{T3}x{H3}"]["rel_err_without_rotation"] = (e_plain[0] / e_plain[1]) ** 0.5
+        del x3, b3, c3, c3p
         # config 5: softmax backward on compressed causal probabilities P (8, 32, 2048, 2048), one basis for all heads
         Bh, NH, S = 8, 32, 2048
         P = torch.empty((Bh * NH, S, S), dtype=torch.bfloat16, device=dev)
@@ -431,6 +487,41 @@ def run_gpu(args):
             "ms": ms_smax, "GB/s": sbytes / (ms_smax * 1e-3) / 1e9, "frac_of_hbm": sbytes / (ms_smax * 1e-3) / 1e9 / hbm,
             "bytes": sbytes}
         del cP, dP, bP
+
+        # the reference-named API (compat / reference_api) on its own speed-test
+        # shapes: x (B=4, M, M), rank R=16, 1-bit encode with a dense outlier
+        # matrix, 2-bit decode (low_rank_kernel_encode_speed_test.py:28-33,
+        # low_rank_kernel_decode_speed_test.py:28-38).  The harness reports
+        # 2 B M R M / t as TFLOPS; the kernels are HBM-bound, so GB/s is beside it.
+        from actcomp import ops as AOPS
+        from actcomp import reference_api as RA
+
+        for Mrc in (4096, 16384):
+            g = torch.Generator(device=dev).manual_seed(21)
+            xr = torch.randn((4, Mrc, Mrc), device=dev, dtype=torch.bfloat16, generator=g)
+            lr_ = torch.randn((Mrc, 16), device=dev, dtype=torch.bfloat16, generator=g)
+            rr_ = torch.randn((16, Mrc), device=dev, dtype=torch.bfloat16, generator=g)
+            sr_ = torch.randn((4, Mrc), device=dev, dtype=torch.bfloat16, generator=g) + 2
+            # the kernel (dense o), and the named call (which converts o to COO, as the reference does)
+            ms_e = time_steps(lambda: AOPS.rc_encode(lr_, rr_, xr, sr_, 1, 12.0, 0), max(3, args.steps // 4), 1,
+                              flush, world, clk)
+            ms_api = time_steps(lambda: RA.low_rank_addition_fuse_compression_quantization(lr_, rr_, xr, sr_, 1, 12.0),
+                                3, 1, flush, world, clk)
+            el = 4 * Mrc * Mrc
+            eb = el * 2 + el * 2 + el // 8  # x in, dense o out, 1-bit codes out
+            components[f"rc_encode_1bit_B4_M{Mrc}"] = {
+                "ms": ms_e, "GB/s": eb / (ms_e * 1e-3) / 1e9, "frac_of_hbm": eb / (ms_e * 1e-3) / 1e9 / hbm,
+                "harness_TFLOPS": 2 * 4 * Mrc * 16 * Mrc / (ms_e * 1e-3) / 1e12, "bytes": eb,
+                "named_call_ms": ms_api}
+            o_, q_ = AOPS.rc_encode(lr_, rr_, xr, sr_, 2, 12.0, 0)
+            del xr
+            ms_d = time_steps(lambda: RA.low_rank_addition_fuse_decompression_dequantization(lr_, rr_, q_, o_, sr_, 2),
+                              max(3, args.steps // 4), 1, flush, world, clk)
+            db = el // 4 + el * 2 + el * 2  # 2-bit codes and dense o in, x out
+            components[f"rc_decode_2bit_B4_M{Mrc}"] = {
+                "ms": ms_d, "GB/s": db / (ms_d * 1e-3) / 1e9, "frac_of_hbm": db / (ms_d * 1e-3) / 1e9 / hbm,
+                "harness_TFLOPS": 2 * 4 * Mrc * 16 * Mrc / (ms_d * 1e-3) / 1e12, "bytes": db}
+            del o_, q_, lr_, rr_, sr_
 
     # offload of the packed activation to pinned host memory and back (side stream, events)
     off = actcomp.Offloader(dev)
@@ -462,9 +553,47 @@ def run_gpu(args):
     ms_rel = time_copy(reload_once, max(3, args.steps // 2), False)
     torch.cuda.synchronize()
     assert torch.equal(state["back"].codes, c0.codes)
-    components["offload_d2h"] = {"ms": ms_off, "GB/s": nb_packed / (ms_off * 1e-3) / 1e9, "bytes": nb_packed}
-    components["reload_h2d"] = {"ms": ms_rel, "GB/s": nb_packed / (ms_rel * 1e-3) / 1e9, "bytes": nb_packed}
+    # the host link's measured peak: one pinned 1 GiB copy each way
+    big_d = torch.empty(1 << 30, dtype=torch.uint8, device=dev)
+    big_h = torch.empty(1 << 30, dtype=torch.uint8, pin_memory=True)
+
+    def link(copy):
+        ts = []
+        for _ in range(3):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record()
+            copy()
+            e1.record()
+            torch.cuda.synchronize()
+            ts.append(e0.elapsed_time(e1))
+        return (1 << 30) / (statistics.median(ts) * 1e-3) / 1e9
+
+    d2h_peak = link(lambda: big_h.copy_(big_d, non_blocking=True))
+    h2d_peak = link(lambda: big_d.copy_(big_h, non_blocking=True))
+    del big_d, big_h
+    components["offload_d2h"] = {"ms": ms_off, "GB/s": nb_packed / (ms_off * 1e-3) / 1e9, "bytes": nb_packed,
+                                 "link_peak_GB/s": d2h_peak}
+    components["reload_h2d"] = {"ms": ms_rel, "GB/s": nb_packed / (ms_rel * 1e-3) / 1e9, "bytes": nb_packed,
+                                "link_peak_GB/s": h2d_peak}
     del state["back"]
+    # offload overlapped with compute: the packed activation leaves on the side
+    # stream while a GEMM of about the copy's length runs on the compute stream;
+    # overlap = (t_copy + t_gemm - t_both) / min(t_copy, t_gemm)
+    ga = torch.randn(8192, 8192, device=dev).to(torch.bfloat16)
+    gb_ = torch.randn(8192, 8192, device=dev).to(torch.bfloat16)
+
+    def both():
+        h = off.offload(c0)
+        actcomp.gemm(ga, gb_, torch.bfloat16)
+        h.wait()
+        return h
+
+    ms_gemm = time_copy(lambda: (actcomp.gemm(ga, gb_, torch.bfloat16), _Done())[1], 3, False)
+    ms_both = time_copy(both, 3, True)
+    components["offload_overlap_with_gemm"] = {
+        "copy_ms": ms_off, "gemm_ms": ms_gemm, "both_ms": ms_both,
+        "overlap": (ms_off + ms_gemm - ms_both) / min(ms_off, ms_gemm)}
+    del ga, gb_
 
     # end to end through the public API with host buffers: pinned X -> H2D -> encode -> decode -> D2H,
     # streamed in token chunks (every token row is encoded on its own, so chunking changes no bit):
@@ -520,7 +649,7 @@ def run_gpu(args):
             "config": {"workload": "config-2 encode+decode, 16384 x 4096 bf16 per rank, r=32 k=16 int4 g64",
                        "tokens_per_rank": T, "channels": H, "rank": r, "n_outlier": k, "bits": bits,
                        "group": group, "global_batch": T * world, "parallelism": f"token-shard x{world}",
-                       "l2": "256 MB write between timed steps (outside the events)"},
+                       "l2": "256 MB write, then 256 MB read of another buffer, between timed steps (outside the events)"},
             "roofline": {"bound": "hbm", "kernel": dom[0], "achieved": achieved, "peak": hbm, "unit": "GB/s",
                          "frac": achieved / hbm, "traffic": traffic, "peak_kind": peak_kind,
                          "algorithmic_bytes_per_launch": dom[2]},
@@ -529,6 +658,7 @@ def run_gpu(args):
                     "d2h_bytes_per_step": T * H * 2,
                     "pipeline": f"{E2E_CHUNKS} token chunks: H2D, encode + decode, D2H on three streams"},
             "gpu_launches": args.steps * launches_per_step(),
+            "per_rank_ms_per_step": step_detail.get("per_rank_ms"),
             "components": components,
             "error": {"rel_fro": (st[0] / st[1]) ** 0.5 if st[1] else None, "max_abs": st[2],
                       "changed_values": st[3]},
@@ -544,7 +674,7 @@ def run_gpu(args):
 
 def launches_per_step():
     """Kernels of this library launched by one encode + decode."""
-    return 2  # tensor-core encode (one cluster kernel) and decode
+    return 3  # the encode's projection and quantisation kernels, and the row decode
 
 
 def main():

@@ -40,7 +40,8 @@ enum actcomp_status {
     ACT_E_CUDA = -4,        /* a CUDA runtime call or launch failed */
     ACT_E_NODEVICE = -5,    /* no usable sm_100 device */
     ACT_E_WORKSPACE = -6,   /* workspace missing or too small */
-    ACT_E_TIMEOUT = -7      /* a bounded device-side wait gave up (see actcomp_last_device_error) */
+    ACT_E_TIMEOUT = -7,     /* a bounded device-side wait gave up (see actcomp_last_device_error) */
+    ACT_E_BOUNDS = -8       /* bounds-checked build: a device-side index check failed */
 };
 
 /* Human-readable name of a status code (static storage). */
@@ -48,9 +49,11 @@ const char *actcomp_strerror(int status);
 /* ACTCOMP_ABI_VERSION of the loaded library. */
 int actcomp_abi_version(void);
 /* Device-side error word of the current device: 0 when no bounded wait has
- * timed out since the last call to actcomp_clear_device_error.  Synchronises
- * the given stream; returns ACT_E_TIMEOUT when the word records a timed-out
- * wait, else ACT_OK (or a CUDA error). */
+ * timed out (bit 0) and, in the bounds-checked build, no index check has failed
+ * (bit 2) since the last call to actcomp_clear_device_error.  Synchronises the
+ * given stream; returns ACT_E_TIMEOUT when the word records a timed-out wait,
+ * ACT_E_BOUNDS when it records a failed index check, else ACT_OK (or a CUDA
+ * error). */
 int actcomp_last_device_error(void *stream, uint32_t *word);
 int actcomp_clear_device_error(void *stream);
 /* Failure-detection self-test (no reference counterpart): one CTA waits on an
@@ -286,6 +289,16 @@ typedef struct actcomp_gemm_args {
     int64_t ldb, sb_batch;
     void *C;
     int64_t ldc, sc_batch;
+    /* Optional second K segment: C = A * B + A2 * B2, A2 (M x K2) and B2
+     * (K2 x N) stored like A and B (same major-ness, row strides lda2, ldb2),
+     * batch 1 only; K2 = 0 for none.  One accumulator in TMEM over K + K2:
+     * compute_lora_gradient's dx = dy (w^T + b^T a^T) as dy w^T + (dy b^T) a^T
+     * without forming w^T + b^T a^T (low_rank_system_profile_backward.py:15). */
+    int64_t K2;
+    const void *A2;
+    int64_t lda2;
+    const void *B2;
+    int64_t ldb2;
 } actcomp_gemm_args;
 int actcomp_gemm(const actcomp_gemm_args *g, void *stream);
 

@@ -110,14 +110,83 @@ def test_gemm_batched_and_reference_names():
     torch.testing.assert_close(c, (a2.float() @ b2.float()).half(), atol=1e-2, rtol=1e-2)  # triton_matmul.py:232
 
 
+def _lora_formula(dy, x, w, a, b):
+    """low_rank_system_profile_backward.py:14-18 in float64."""
+    dy, x, w, a, b = (t.double() for t in (dy, x, w, a, b))
+    return dy @ (w.mT + b.mT @ a.mT), x.mT @ (dy @ b.mT), (x @ a).mT @ dy
+
+
+def _bf(t):
+    return t.to(torch.bfloat16).float()
+
+
+def _check_lora(got, ref):
+    """dx (bf16) against the float64 value rounded to bf16: equal but at
+    rounding ties; da, db (float32) within float32 accumulation."""
+    dx, da, db = got
+    rdx, rda, rdb = ref
+    e = (dx.double() - rdx.to(torch.bfloat16).double()).norm() / rdx.norm()
+    assert e < 2e-4, f"dx {float(e):.2e}"
+    for g_, r_, n in ((da, rda, "da"), (db, rdb, "db")):
+        e = (g_.double() - r_).norm() / r_.norm()
+        assert e < 1e-5, f"{n} {float(e):.2e}"
+
+
 def test_lora_gradient_matches_reference(golden):
+    """The reference's own outputs (fixture) pin the formula; the GPU result
+    on the bf16 operands matches the formula on those operands."""
     from actcomp import reference_api as R
 
-    t = {k: torch.from_numpy(golden["lora_" + k]).cuda() for k in ("x", "dy", "w", "a", "b")}
-    dx, da, db = R.compute_lora_gradient(t["dy"], t["x"], t["w"], t["a"], t["b"])
-    for got, name in ((dx, "dx"), (da, "da"), (db, "db")):
-        ref = torch.from_numpy(golden["lora_" + name]).cuda()
-        assert (got.float() - ref).norm() / ref.norm() < 2e-2, name  # bf16 operands vs the fp32 reference
+    t = {k: torch.from_numpy(golden["lora_" + k]) for k in ("x", "dy", "w", "a", "b")}
+    ref = _lora_formula(t["dy"], t["x"], t["w"], t["a"], t["b"])
+    for r_, name in zip(ref, ("dx", "da", "db")):
+        g_ = torch.from_numpy(golden["lora_" + name]).double()
+        assert (r_ - g_).norm() / g_.norm() < 1e-5, name  # the fixture is the reference's float32 run
+    tb = {k: _bf(v) for k, v in t.items()}
+    got = R.compute_lora_gradient(*(tb[k].cuda() for k in ("dy", "x", "w", "a", "b")))
+    _check_lora([g_.cpu() for g_ in got], _lora_formula(tb["dy"], tb["x"], tb["w"], tb["a"], tb["b"]))
+
+
+def test_lora_gradient_on_a_compressed_activation():
+    """x saved compressed (the reference decompresses it before the backward,
+    low_rank_system_profile_backward.py:60-62): da through the fused
+    dequant-GEMM, x a from the reconstruction, against the formula on the
+    decoded activation."""
+    import actcomp
+    from actcomp import reference_api as R
+    from actcomp import synthetic
+
+    S, d_in, d_out, r = 1024, 512, 768, 16
+    x, _ = synthetic.lowrank_activation(S, d_in, n_outlier=8, seed=5, device="cuda")
+    basis = actcomp.Basis.fit(x, 32)
+    c = actcomp.encode(x, basis, actcomp.select_outlier_channels(x, 8), bits=4, group=64)
+    g = torch.Generator().manual_seed(6)
+    dy = _bf(torch.randn(S, d_out, generator=g))
+    w = _bf(torch.randn(d_in, d_out, generator=g) * 0.05)
+    a = _bf(torch.randn(d_in, r, generator=g) * 0.1)
+    b = _bf(torch.randn(r, d_out, generator=g) * 0.1)
+    got = R.compute_lora_gradient(dy.cuda(), c, w.cuda(), a.cuda(), b.cuda())
+    xh = actcomp.decode(c).float().cpu()
+    _check_lora([g_.cpu() for g_ in got], _lora_formula(dy, xh, w, a, b))
+
+
+def test_gemm_second_segment():
+    """C = A B + A2 B2 in one accumulator, both layouts of each operand."""
+    import actcomp
+
+    g = torch.Generator().manual_seed(8)
+    M, N, K, K2 = 200, 136, 264, 48
+    A, B = _bf(torch.randn(M, K, generator=g)), _bf(torch.randn(K, N, generator=g))
+    A2, B2 = _bf(torch.randn(M, K2, generator=g)), _bf(torch.randn(K2, N, generator=g))
+    ref = A.double() @ B.double() + A2.double() @ B2.double()
+    bf = torch.bfloat16
+    for a_t in (False, True):
+        for b_t in (False, True):
+            a_ = A.cuda().to(bf) if not a_t else A.cuda().to(bf).mT.contiguous().mT
+            b_ = B.cuda().to(bf) if not b_t else B.cuda().to(bf).mT.contiguous().mT
+            c = actcomp.gemm(a_, b_, torch.float32, "", A2.cuda().to(bf), B2.cuda().to(bf))
+            e = (c.double().cpu() - ref).norm() / ref.norm()
+            assert e < 1e-6, (a_t, b_t, float(e))
 
 
 def test_error_stats():

@@ -151,3 +151,16 @@ def test_fp32_activation_config1_shape(O):
                   8, 128, False, x_f32=True)
     assert np.array_equal(xh[:, ch], x[:, ch])
     assert O.rel_fro(xh, x) < 5e-3
+
+
+def test_lora_formula_pinned_by_the_reference_fixture(golden):
+    """The float64 statement of low_rank_system_profile_backward.py:14-18 used
+    by the GPU LoRA tests reproduces the reference's own outputs (fixture made
+    by running the reference's compute_lora_gradient)."""
+    import torch
+
+    t = {k: torch.from_numpy(golden["lora_" + k]).double() for k in ("x", "dy", "w", "a", "b", "dx", "da", "db")}
+    dy, x, w, a, b = t["dy"], t["x"], t["w"], t["a"], t["b"]
+    ref = (dy @ (w.mT + b.mT @ a.mT), x.mT @ (dy @ b.mT), (x @ a).mT @ dy)
+    for r_, name in zip(ref, ("dx", "da", "db")):
+        assert (r_ - t[name]).norm() / t[name].norm() < 1e-5, name

@@ -47,7 +47,10 @@ def test_encode_codes_match_reference_twin(O, golden, qb):
 
 
 @pytest.mark.parametrize("qb", [1, 2, 4, 8])
-@pytest.mark.parametrize("B,M,N,K", [(2, 33, 64, 16), (1, 16, 96, 32), (3, 8, 32, 5)])
+@pytest.mark.parametrize("B,M,N,K", [(2, 33, 64, 16), (1, 16, 96, 32), (3, 8, 32, 5),
+                                     # the tiled kernels (whole 256-column tiles): ragged row tiles,
+                                     # several column tiles, the largest rank
+                                     (2, 70, 256, 16), (1, 131, 512, 32), (2, 9, 768, 64)])
 def test_kernel_semantics_match_oracle(O, qb, B, M, N, K):
     """Default (Triton-kernel) semantics on non-dyadic data: batch-0 scale,
     half-away rounding, 32-column block packing -- bit for bit."""
@@ -67,6 +70,31 @@ def test_kernel_semantics_match_oracle(O, qb, B, M, N, K):
     xh = R.low_rank_addition_fuse_decompression_dequantization(to_bf16(l), to_bf16(r), q, o_sp, to_bf16(s),
                                                                quantize_bit=qb)
     assert np.array_equal(bits(xh), O.rc_decode(l, r, q_ref, o_ref, s, qb, flags=0))
+
+
+@pytest.mark.parametrize("flags", [1, 2, 4, 16, 1 | 2 | 4 | 16])
+@pytest.mark.parametrize("qb", [1, 2, 4, 8])
+def test_tiled_kernels_honour_every_flag(O, qb, flags):
+    """The twin-semantics flags on the tiled path (N a multiple of 256), bit for
+    bit against the oracle; decode also through the fused consumers."""
+    from actcomp import _lib, refcompat
+
+    rng = np.random.default_rng(qb * 1000 + flags)
+    B, M, N, K = 2, 37, 256, 16
+    l = O.f32_to_bf16(rng.standard_normal((M, K)).astype(np.float32) * 0.3)
+    r = O.f32_to_bf16(rng.standard_normal((K, N)).astype(np.float32) * 0.3)
+    x = O.f32_to_bf16(rng.standard_normal((B, M, N)).astype(np.float32) * 2)
+    s = O.f32_to_bf16((rng.random((B, N)) * 0.3 + 0.05).astype(np.float32))
+    o_ref, q_ref, _ = O.rc_encode(l, r, x, s, qb, 2.5, flags=flags)
+    o, q = refcompat.encode(to_bf16(l), to_bf16(r), to_bf16(x), to_bf16(s), qb, 2.5, flags)
+    assert np.array_equal(q.cpu().numpy(), q_ref)
+    assert np.array_equal(bits(o), o_ref)
+    xh = refcompat.decode(to_bf16(l), to_bf16(r), q, o, to_bf16(s), qb, flags)
+    ref = O.rc_decode(l, r, q_ref, o_ref, s, qb, flags=flags)
+    assert np.array_equal(bits(xh), ref)
+    y = O.f32_to_bf16(rng.standard_normal((B, M, N)).astype(np.float32))
+    got = refcompat.decode(to_bf16(l), to_bf16(r), q, o, to_bf16(s), qb, flags, op=_lib.ACT_OP_MUL, y=to_bf16(y))
+    assert np.array_equal(bits(got), bits(to_bf16(ref) * to_bf16(y)))
 
 
 def test_fused_consumers_match_unfused(O):

@@ -28,6 +28,7 @@ ACT_E_CUDA = -4
 ACT_E_NODEVICE = -5
 ACT_E_WORKSPACE = -6
 ACT_E_TIMEOUT = -7
+ACT_E_BOUNDS = -8
 
 ACT_OP_DECODE = 0
 ACT_OP_MUL = 1
@@ -77,6 +78,7 @@ class GemmArgs(ctypes.Structure):
         ("A", c_vp), ("lda", c_i64), ("sa_batch", c_i64),
         ("B", c_vp), ("ldb", c_i64), ("sb_batch", c_i64),
         ("C", c_vp), ("ldc", c_i64), ("sc_batch", c_i64),
+        ("K2", c_i64), ("A2", c_vp), ("lda2", c_i64), ("B2", c_vp), ("ldb2", c_i64),
     ]
 
 

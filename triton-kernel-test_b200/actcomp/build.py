@@ -20,6 +20,9 @@ PKG = os.path.dirname(os.path.abspath(__file__))
 ROOT = os.path.dirname(PKG)
 CSRC = os.path.join(ROOT, "csrc")
 LIB = os.path.join(PKG, "libactcomp.so")
+# the bounds-checked build (-DACT_BOUNDS_CHECK): device-side index checks that
+# record a bit in the device error word instead of trapping; tests only
+LIB_BC = os.path.join(PKG, "libactcomp_bc.so")
 
 NVCC_FLAGS = [
     "-gencode", "arch=compute_100a,code=sm_100a",
@@ -48,25 +51,28 @@ def _deps() -> list[str]:
     return sources() + hdr + ([inc] if os.path.exists(inc) else [])
 
 
-def stale() -> bool:
-    if not os.path.exists(LIB):
+def stale(lib: str = LIB) -> bool:
+    if not os.path.exists(lib):
         return True
-    t = os.path.getmtime(LIB)
+    t = os.path.getmtime(lib)
     return any(os.path.getmtime(p) > t for p in _deps())
 
 
-def build(force: bool = False, verbose: bool = False, jobs: int | None = None) -> str:
-    """Compile (if stale) and return the path of libactcomp.so."""
-    if not force and not stale():
-        return LIB
+def build(force: bool = False, verbose: bool = False, jobs: int | None = None, bounds_check: bool = False) -> str:
+    """Compile (if stale) and return the path of libactcomp.so (libactcomp_bc.so
+    with bounds_check)."""
+    lib = LIB_BC if bounds_check else LIB
+    if not force and not stale(lib):
+        return lib
     exe = nvcc()
+    flags = NVCC_FLAGS + (["-DACT_BOUNDS_CHECK"] if bounds_check else [])
     tmp = tempfile.mkdtemp(prefix="actcomp_build_")
     try:
         objs = []
         procs = []
         for src in sources():
             obj = os.path.join(tmp, os.path.basename(src) + ".o")
-            cmd = [exe, *NVCC_FLAGS, "-c", src, "-o", obj]
+            cmd = [exe, *flags, "-c", src, "-o", obj]
             if verbose:
                 print(" ".join(cmd), flush=True)
             procs.append((src, subprocess.Popen(cmd, stdout=subprocess.PIPE, stderr=subprocess.STDOUT, text=True)))
@@ -80,15 +86,15 @@ def build(force: bool = False, verbose: bool = False, jobs: int | None = None) -
                 failed.append(src)
         if failed:
             raise RuntimeError(f"nvcc failed for {failed}")
-        out_tmp = LIB + ".tmp"
+        out_tmp = lib + ".tmp"
         cmd = [exe, "-gencode", "arch=compute_100a,code=sm_100a", "-shared", "-Xcompiler", "-fPIC", "-o", out_tmp,
                *objs, "-cudart", "static"]
         subprocess.run(cmd, check=True)
-        os.replace(out_tmp, LIB)
+        os.replace(out_tmp, lib)
     finally:
         shutil.rmtree(tmp, ignore_errors=True)
-    return LIB
+    return lib
 
 
 if __name__ == "__main__":
-    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv))
+    print(build(force="--force" in sys.argv, verbose="-v" in sys.argv, bounds_check="--bounds-check" in sys.argv))

@@ -387,11 +387,15 @@ _IN = {torch.bfloat16: 0, torch.float16: 1}
 _OUT = {torch.float32: 0, torch.bfloat16: 1, torch.float16: 2}
 
 
-def gemm(a: torch.Tensor, b: torch.Tensor, out_dtype: torch.dtype = torch.float32, activation: str = "") -> torch.Tensor:
-    """C = a @ b on tcgen05 for 2-D or batched 3-D bf16/fp16 operands.
+def gemm(a: torch.Tensor, b: torch.Tensor, out_dtype: torch.dtype = torch.float32, activation: str = "",
+         a2: Optional[torch.Tensor] = None, b2: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """C = a @ b (+ a2 @ b2) on tcgen05 for 2-D or batched 3-D bf16/fp16 operands.
 
     Each operand may be row-major or a transposed view of a row-major tensor
-    (K-major or MN-major); other layouts are copied."""
+    (K-major or MN-major); other layouts are copied.  The optional second
+    product (2-D only) is accumulated with the first in one float32 TMEM
+    accumulator: a2 (M x K2) and b2 (K2 x N) are brought to the layouts of a
+    and b."""
     _need_cuda(a, b)
     if a.dtype not in _IN or b.dtype != a.dtype:
         raise TypeError("gemm operands must both be bf16 or both fp16")
@@ -424,6 +428,19 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out_dtype: torch.dtype = torch.float3
         a3, a_rowmajor, lda, sa = layout(a3, M, K)
         b3, b_rowmajor, ldb, sb = layout(b3, K, N)
         a_kmajor, b_kmajor = a_rowmajor, 0 if b_rowmajor else 1
+    if (a2 is None) != (b2 is None):
+        raise ValueError("a2 and b2 come together")
+    if a2 is not None:
+        if batched or a2.dim() != 2 or b2.dim() != 2:
+            raise ValueError("the second product is 2-D only")
+        if a2.dtype != a.dtype or b2.dtype != a.dtype:
+            raise TypeError("the second product's operands have the first's dtype")
+        K2 = a2.shape[1]
+        if a2.shape[0] != M or b2.shape != (K2, N):
+            raise ValueError(f"second product shapes {tuple(a2.shape)} x {tuple(b2.shape)} do not give {M} x {N}")
+        # same major-ness as the first product's operands
+        a2 = a2.contiguous() if a_kmajor else a2.mT.contiguous().mT
+        b2 = b2.mT.contiguous().mT if b_kmajor else b2.contiguous()
     c = torch.empty((batch, M, N), dtype=out_dtype, device=a.device)
     g = GemmArgs()
     g.M, g.N, g.K, g.batch = M, N, K, batch
@@ -432,6 +449,10 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out_dtype: torch.dtype = torch.float3
     g.A, g.lda, g.sa_batch = a3.data_ptr(), lda, sa
     g.B, g.ldb, g.sb_batch = b3.data_ptr(), ldb, sb
     g.C, g.ldc, g.sc_batch = c.data_ptr(), N, M * N if batch > 1 else 0
+    if a2 is not None:
+        g.K2 = a2.shape[1]
+        g.A2, g.lda2 = a2.data_ptr(), a2.stride(0) if a_kmajor else a2.stride(1)
+        g.B2, g.ldb2 = b2.data_ptr(), b2.stride(1) if b_kmajor else b2.stride(0)
     call("actcomp_gemm", ctypes.byref(g), _stream(c))
     return c if batched else c.squeeze(0)
 

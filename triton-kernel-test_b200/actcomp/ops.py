@@ -111,6 +111,17 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out_dtype: torch.dtype, activation: s
     return core.gemm(a, b, out_dtype, activation)
 
 
+@torch.library.custom_op("actcomp::gemm_two", mutates_args=())
+def gemm_two(a: torch.Tensor, b: torch.Tensor, a2: torch.Tensor, b2: torch.Tensor, out_dtype: torch.dtype) -> torch.Tensor:
+    """a @ b + a2 @ b2 (2-D) in one float32 accumulator."""
+    return core.gemm(a, b, out_dtype, "", a2, b2)
+
+
+@gemm_two.register_fake
+def _(a, b, a2, b2, out_dtype):
+    return a.new_empty((a.shape[0], b.shape[1]), dtype=out_dtype)
+
+
 @gemm.register_fake
 def _(a, b, out_dtype, activation):
     if a.dim() == 3 or b.dim() == 3:

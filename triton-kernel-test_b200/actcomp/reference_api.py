@@ -207,22 +207,55 @@ def _mm(x, w):
     return out.reshape(*lead, w.shape[-1])
 
 
+def _pieces3(v):
+    """float32 (..., r) -> bf16 (..., 3r): [hi | mid | lo] with hi + mid + lo == v
+    exactly (three 8-bit significands hold float32's 24), so that a bf16 tensor
+    core product with the pieces accumulates v's exact products in float32."""
+    hi = v.to(_BF)
+    r1 = v - hi.float()
+    mid = r1.to(_BF)
+    lo = (r1 - mid.float()).to(_BF)
+    return torch.cat([hi, mid, lo], dim=-1)
+
+
+def _sum3(v, r, dim):
+    """(hi + mid) + lo of a product with _pieces3 operands, split along `dim`."""
+    h, m, l = v.split(r, dim=dim)
+    return (h + m) + l
+
+
 def compute_lora_gradient(dy, x, w, a, b):
-    """low_rank_system_profile_forward.py:14 / ..._backward.py:14:
+    """low_rank_system_profile_backward.py:14:
     dx = dy (w^T + b^T a^T), da = x^T (dy b^T), db = (x a)^T dy.
-    x may be a dense (B, S, d_in) tensor or a :class:`actcomp.core.Compressed`
-    activation of B*S tokens, in which case da is the fused dequant-GEMM and
-    x a is computed from the reconstruction."""
+
+    dx is one tensor-core GEMM with two K segments, dy w^T + (dy b^T) a^T, so
+    w^T + b^T a^T is never formed; dy b^T and x a are float32 and enter the
+    bf16 tensor cores as three exact bf16 pieces, so every product is the
+    float32-accumulated value of the formula on the bf16 operands.  x may be a
+    dense (B, S, d_in) tensor (da, db per batch, as the reference's batched
+    matmuls) or a :class:`actcomp.core.Compressed` activation of B*S tokens
+    (da from the fused dequant-GEMM, x a from the reconstruction; da, db over
+    all tokens)."""
     B = dy.shape[0] if dy.dim() == 3 else 1
+    r = a.shape[-1]
     dy2 = dy.reshape(-1, dy.shape[-1]).to(_BF).contiguous()
-    wt = w.mT.to(_BF) + _mm(b.mT.contiguous(), a.mT.contiguous()).to(_BF)
-    dx = _mm(dy2, wt)
-    dyb = _mm(dy2, b.mT.contiguous())  # (BS, r)
+    a_bf, b_bf, w_bf = a.to(_BF).contiguous(), b.to(_BF).contiguous(), w.to(_BF).contiguous()
+    dyb = ops.gemm(dy2, b_bf.mT, torch.float32, "")          # (BS, r) = dy b^T
+    P = _pieces3(dyb)                                         # (BS, 3r)
+    a3 = torch.cat([a_bf, a_bf, a_bf], dim=1)                # (d_in, 3r)
+    dx = ops.gemm_two(dy2, w_bf.mT, P, a3.mT, _BF)           # dy w^T + (dy b^T) a^T
+    dx = dx.reshape(dy.shape[:-1] + (dx.shape[-1],))
     if isinstance(x, core.Compressed):
-        da = core.weight_grad(x, dyb, torch.float32)
-        xa = _mm(core.decode(x), a)
-        db = ops.gemm(xa.mT.contiguous(), dy2, torch.float32, "")
-        return dx.reshape(dy.shape[:-1] + (dx.shape[-1],)), da, db
+        da = _sum3(core.weight_grad(x, P, torch.float32), r, 1)
+        xa = ops.gemm(core.decode(x).reshape(-1, x.channels), a_bf, torch.float32, "")
+        db = _sum3(ops.gemm(_pieces3(xa).mT, dy2, torch.float32, ""), r, 0)
+        return dx, da, db
+    x3 = x.reshape(B, -1, x.shape[-1]).to(_BF)
+    P3 = P.reshape(B, -1, 3 * r)
+    da = _sum3(ops.gemm(x3.mT, P3, torch.float32, ""), r, -1)
+    xa = ops.gemm(x3, a_bf, torch.float32, "")               # (B, S, r)
+    db = _sum3(ops.gemm(_pieces3(xa).mT, dy2.reshape(B, -1, dy2.shape[-1]), torch.float32, ""), r, -2)
+    return dx, da, db
     x3 = x.reshape(B, -1, x.shape[-1]).to(_BF)
     dyb3 = dyb.reshape(B, -1, dyb.shape[-1])
     da = ops.gemm(x3.mT, dyb3, torch.float32, "")

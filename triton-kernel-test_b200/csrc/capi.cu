@@ -49,6 +49,7 @@ extern "C" const char *actcomp_strerror(int status) {
         case ACT_E_NODEVICE: return "no usable sm_100 device";
         case ACT_E_WORKSPACE: return "workspace missing or too small";
         case ACT_E_TIMEOUT: return "device-side wait timed out";
+        case ACT_E_BOUNDS: return "device-side index check failed (bounds-checked build)";
         default: return "unknown status";
     }
 }
@@ -59,7 +60,8 @@ extern "C" int actcomp_last_device_error(void *stream, uint32_t *word) {
     ACT_CHECK(word, ACT_E_INVALID);
     ACT_CUDA_TRY(cudaStreamSynchronize(as_stream(stream)));
     ACT_CUDA_TRY(cudaMemcpyFromSymbol(word, g_device_error, sizeof(uint32_t)));
-    return (*word & DEV_ERR_MBAR_TIMEOUT) ? ACT_E_TIMEOUT : ACT_OK;
+    if (*word & DEV_ERR_MBAR_TIMEOUT) return ACT_E_TIMEOUT;
+    return (*word & DEV_ERR_BOUNDS) ? ACT_E_BOUNDS : ACT_OK;
 }
 
 namespace act {
@@ -120,9 +122,9 @@ extern "C" int actcomp_cg_encode(const actcomp_cg_desc *d, const uint16_t *x, in
     if (st) return st;
     if ((st = check_rows(x, ldx, d->channels))) return st;
     if (d->rank) ACT_CHECK(d->basis_t && aligned(d->basis_t, 16), ACT_E_ALIGN);
-    // the two-kernel encode (projection, then quantisation: rank 16 or 32, groups
-    // of 32 or 64, no rotation, one slice, H a multiple of 128), else the
-    // two-pass row encode (1024 <= H <= 16384, a multiple of 128), else the
+    // the two-kernel encode (projection, then quantisation: rank 16 or 32,
+    // groups of 32 or 64, no rotation, one slice, H a multiple of 128), else
+    // the two-pass row encode (1024 <= H <= 16384, a multiple of 128), else the
     // CUDA-core encode; each tensor-core encode declines (ACT_E_UNSUPPORTED,
     // before launching) what it does not cover
     st = act_cg_encode_split(d, x, ldx, as_stream(stream));

@@ -643,7 +643,7 @@ __global__ void __launch_bounds__(Geo<WHT>::THREADS, 1)
                 if (k & 1) {
                     tc::fence_proxy_async();
                     __syncwarp();
-                    if (lane == 0) {
+                    if (lane == 0 && ACT_DCHECK(cc * CH + 64 * (k >> 1) < p.H)) {
                         tc::tma_store_3d(&tm_out, buf, cc * CH + 64 * (k >> 1), tb * ROWS + 32 * q, b);
                         tc::bulk_commit();
                     }

@@ -8,11 +8,12 @@
 // (float32, one token row per thread).
 //
 // Kernel 2, quantisation (cg_quant_kernel): 128-token x 128-channel tiles,
-// persistent, each CTA a contiguous range of the tiles walked from the last
-// one down, so that the channels the projection read last -- still in L2 --
-// come first.  Warp 0 streams each tile's X[128 x 128] by TMA (marked
-// evict-first in L2, so that these loads' misses do not push out the lines
-// the projection left behind) and its prepared basis tile into a 3-stage
+// persistent, each CTA a contiguous range of the tiles in the order the
+// projection read them (least recently read first: under L2's LRU eviction
+// the lines this kernel has used up go before the ones it still needs).
+// Warp 0 streams each tile's X[128 x 128] by TMA (marked evict-first in L2,
+// so that these loads do not push out the lines the projection left behind)
+// and its prepared basis tile into a 3-stage
 // ring; warp 2 splits each token block's L into three exact bf16 pieces (two
 // buffered slots); warp 1 issues P = L . V^T (kind::f16, three pieces,
 // float32 accumulation) into one of three TMEM accumulators; twelve epilogue
@@ -142,7 +143,7 @@ __global__ void __launch_bounds__(P_THREADS, 1)
                 float4 *dst = reinterpret_cast<float4 *>(p.lr + t * r);
 #pragma unroll
                 for (int e = 0; e < RK / 4; ++e)
-                    if (4 * e < r) dst[e] = make_float4(__uint_as_float(v[4 * e]), __uint_as_float(v[4 * e + 1]),
+                    if (4 * e < r && ACT_DCHECK(4 * e + 4 <= r)) dst[e] = make_float4(__uint_as_float(v[4 * e]), __uint_as_float(v[4 * e + 1]),
                                                         __uint_as_float(v[4 * e + 2]), __uint_as_float(v[4 * e + 3]));
             }
         }
@@ -207,18 +208,18 @@ __device__ __forceinline__ uint32_t pack_codes(float2 t0, float2 t1, float2 t2, 
     }
 }
 
-// Tile u of the walk (u = 0 is the last tile of the activation).
+// Tile v of the walk: token block v / ncc, channel tile v % ncc (first channels first).
 struct Walk {
     int tb, cc, ncc;
     __device__ Walk(int64_t v, int64_t ntiles, int ncc_) : ncc(ncc_) {
-        const int64_t u = ntiles - 1 - v;
-        tb = (int)(u / ncc);
-        cc = (int)(u - (int64_t)tb * ncc);
+        (void)ntiles;
+        tb = (int)(v / ncc);
+        cc = (int)(v - (int64_t)tb * ncc);
     }
     __device__ __forceinline__ void next() {
-        if (--cc < 0) {
-            cc = ncc - 1;
-            --tb;
+        if (++cc == ncc) {
+            cc = 0;
+            ++tb;
         }
     }
 };
@@ -325,7 +326,7 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
         int m = 0;
         bool ok = true;
         for (int64_t v = v_lo; v < v_hi && ok; ++v, w.next()) {
-            if (v != v_lo && w.cc != p.ncc - 1) continue;  // not the first tile of a token block
+            if (v != v_lo && w.cc != 0) continue;  // not the first tile of a token block
             const int slot = m & 1;
             if (!(ok = tc::mbar_wait(&pfree[slot], ((m >> 1) & 1) ^ 1, abort))) break;
             uint8_t *dst = smem + L::OFF_PT + slot * L::PT;
@@ -369,7 +370,7 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
             Walk w(v_lo, p.ntiles, p.ncc);
             for (int64_t v = v_lo; v < v_hi && ok; ++v, ++i, w.next()) {
                 const int s = i % Q_STAGES, acc = i % NG;
-                if (v == v_lo || w.cc == p.ncc - 1) {  // a new token block: its piece tiles
+                if (v == v_lo || w.cc == 0) {  // a new token block: its piece tiles
                     ++m;
                     if (!(ok = tc::mbar_wait(&pready[m & 1], (m >> 1) & 1, abort))) break;
                 }
@@ -387,7 +388,7 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
                 tc::mma_commit(&tfull[acc]);
                 tc::mma_commit(&empty[s]);
                 // the last tile of this token block in the range: the piece slot frees with these MMAs
-                if (w.cc == 0 || v == v_hi - 1) tc::mma_commit(&pfree[m & 1]);
+                if (w.cc == p.ncc - 1 || v == v_hi - 1) tc::mma_commit(&pfree[m & 1]);
             }
         }
     } else {
@@ -460,7 +461,7 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
                                 const uint32_t word =
                                     wi == 0 ? xv[c16].x : (wi == 1 ? xv[c16].y : (wi == 2 ? xv[c16].z : xv[c16].w));
                                 const uint16_t xb = (uint16_t)(e & 1 ? (word >> 16) : (word & 0xffffu));
-                                if (rv) p.outl[t * p.k + slot] = xb;
+                                if (rv && ACT_DCHECK(slot < p.k)) p.outl[t * p.k + slot] = xb;
                                 if (e & 1) w2[h][e >> 1].y = 0.f;
                                 else w2[h][e >> 1].x = 0.f;
                             }
@@ -520,14 +521,14 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
                 tc::mbar_arrive(&tempty[g]);
                 tc::mbar_arrive(&empty[s]);
             }
-            if (rv) {
+            if (rv && ACT_DCHECK((c0 >> gshift) + (G == 32 ? 4 : 2) <= ngr)) {
                 float *sp = p.scales + t * ngr + (c0 >> gshift);
                 if (G == 32) *reinterpret_cast<float4 *>(sp) = make_float4(scv[0], scv[1], scv[2], scv[3]);
                 else *reinterpret_cast<float2 *>(sp) = make_float2(scv[0], scv[2]);
             }
             tc::fence_proxy_async();
             __syncwarp();
-            if (lane == 0) {
+            if (lane == 0 && ACT_DCHECK(c0 + CH <= p.H)) {
                 tc::tma_store_3d(&tm_c, buf, (int)(c0 * BITS / 8), tb * ROWS + 32 * q, 0);
                 tc::bulk_commit();
             }

@@ -588,12 +588,12 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RK>::THREADS, 1)
                 if (p.k && (tw.cc == tw.last_cc() || tile == t_hi - 1)) tc::mbar_arrive(&lqempty[(elq - 1) & 1]);
             }
             if constexpr (OP == OP_SMAX_DOT) {  // the partial goes out, no tile
-                if (rv) p.partials[trow * (4 * p.ncc) + 4 * cc + h] = __fadd_rn(dot2.x, dot2.y);
+                if (rv && ACT_DCHECK(cc < p.ncc && h < 4)) p.partials[trow * (4 * p.ncc) + 4 * cc + h] = __fadd_rn(dot2.x, dot2.y);
                 continue;
             }
 
             if constexpr (OP != ACT_OP_DECODE) {  // 64 bytes of my row straight from registers
-                if (rv && c_first < p.H) {
+                if (rv && c_first < p.H && ACT_DCHECK(c_first + 32 <= p.ldo)) {
                     uint4 *dst = reinterpret_cast<uint4 *>(p.out + trow * p.ldo + c_first);
 #pragma unroll
                     for (int c16 = 0; c16 < 4; ++c16) {
@@ -621,7 +621,7 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RK>::THREADS, 1)
             }
             tc::fence_proxy_async();
             __syncwarp();
-            if (lane == 0) {
+            if (lane == 0 && ACT_DCHECK(cc * CH + 32 * h < p.H)) {
                 tc::tma_store_3d(&tm_out, stg, cc * CH + 32 * h, tb * ROWS + 32 * q, sl_b);
                 tc::bulk_commit();
             }

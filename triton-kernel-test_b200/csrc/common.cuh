@@ -25,9 +25,23 @@
 
 namespace act {
 
-// Error word set by device-side bounded waits that give up (never by a trap).
+// Error word set by device-side bounded waits that give up and, in the
+// bounds-checked build, by an index check that fails (never by a trap).
 extern __device__ uint32_t g_device_error;
-enum : uint32_t { DEV_ERR_MBAR_TIMEOUT = 1u, DEV_ERR_BAD_ARG = 2u };
+enum : uint32_t { DEV_ERR_MBAR_TIMEOUT = 1u, DEV_ERR_BAD_ARG = 2u, DEV_ERR_BOUNDS = 4u };
+
+// ACT_DCHECK(cond): in the build with -DACT_BOUNDS_CHECK (libactcomp_bc.so), a
+// false cond records DEV_ERR_BOUNDS and the guarded access is skipped; in the
+// product build it is `true` and costs nothing.
+#ifdef ACT_BOUNDS_CHECK
+__device__ __forceinline__ bool act_dcheck(bool ok) {
+    if (!ok) atomicOr(&g_device_error, DEV_ERR_BOUNDS);
+    return ok;
+}
+#define ACT_DCHECK(cond) ::act::act_dcheck((cond))
+#else
+#define ACT_DCHECK(cond) true
+#endif
 
 static inline cudaStream_t as_stream(void *s) { return reinterpret_cast<cudaStream_t>(s); }
 static inline int launch_status() { return cudaGetLastError() == cudaSuccess ? ACT_OK : ACT_E_CUDA; }

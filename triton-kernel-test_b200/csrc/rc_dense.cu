@@ -106,6 +106,232 @@ __global__ void rc_lowrank_add_kernel(actcomp_rc_args a) {
     }
 }
 
+// ---------------------------------------------------------------- tiled rc kernels
+// A CTA takes a tile of RCT = 256 columns (8 packing blocks) of one batch and
+// RCR rows of it, in passes of RPP rows.  Dynamic shared memory holds r[:, tile]
+// reordered so that the epp values one packed byte needs for each k are
+// contiguous (one vector load per k), the pass's rows of l, and the pass's
+// coalesced tile: x in and o out of the encode (in place), o in and the output
+// out of the decode (in place), plus y for the fused consumers.  A thread owns
+// one packed byte in each of NRW rows of the pass: the epp elements of its
+// block that share the byte.  Per element the arithmetic (sequential binary32
+// FMAs over k from 0, the roundings) is the per-element kernels' above, bit
+// for bit.
+constexpr int RCT = 256, RCR = 128, NRW = 4;
+
+template <int BITS>
+struct RcTile {
+    static constexpr int EPP = 8 / BITS;     // elements per packed byte
+    static constexpr int BPB = 32 / EPP;     // bytes per 32-column block
+    static constexpr int TPR = RCT / EPP;    // threads (bytes) per row of the tile
+    static constexpr int RP = 256 / TPR;     // rows one sweep of the CTA covers
+    static constexpr int RPP = RP * NRW;     // rows per pass
+    // column of element i of tile byte w
+    __device__ static int col(int w, int i) { return (w / BPB) * 32 + (w % BPB) + i * BPB; }
+    // dynamic shared memory: r_s [K][RCT] floats, l_s [RPP][K] bf16, t_s [RPP][RCT] bf16, y_s [RPP][RCT] bf16,
+    // s_s [RCT] floats
+    __host__ __device__ static int off_l(int K) { return K * RCT * 4; }
+    __host__ __device__ static int off_t(int K) { return (off_l(K) + RPP * K * 2 + 15) & ~15; }
+    __host__ __device__ static int off_y(int K) { return off_t(K) + RPP * RCT * 2; }
+    __host__ __device__ static int off_s(int K, bool y) { return off_y(K) + (y ? RPP * RCT * 2 : 0); }
+    __host__ __device__ static int bytes(int K, bool y) { return off_s(K, y) + RCT * 4; }
+};
+
+// the EPP values (float, from bf16) one thread needs for one k, in vector loads
+template <int EPP>
+__device__ __forceinline__ void load_epp(const float *p, float (&v)[EPP]) {
+    if constexpr (EPP == 8) {
+        const float4 a = reinterpret_cast<const float4 *>(p)[0], b = reinterpret_cast<const float4 *>(p)[1];
+        v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w, v[4] = b.x, v[5] = b.y, v[6] = b.z, v[7] = b.w;
+    } else if constexpr (EPP == 4) {
+        const float4 a = *reinterpret_cast<const float4 *>(p);
+        v[0] = a.x, v[1] = a.y, v[2] = a.z, v[3] = a.w;
+    } else if constexpr (EPP == 2) {
+        const float2 a = *reinterpret_cast<const float2 *>(p);
+        v[0] = a.x, v[1] = a.y;
+    } else {
+        v[0] = *p;
+    }
+}
+
+// d[j][i] = sum_k l[row j][k] r[k][col(w, i)] for the thread's NRW rows, each
+// a sequential binary32 FMA chain from k = 0 (the r values of one k serve all
+// NRW rows)
+template <int EPP, int RP>
+__device__ __forceinline__ void rc_dots(const float *r_s, const uint16_t *l_s, int K, int rp0, int w,
+                                        float (&d)[NRW][EPP]) {
+#pragma unroll
+    for (int j = 0; j < NRW; ++j)
+#pragma unroll
+        for (int i = 0; i < EPP; ++i) d[j][i] = 0.f;
+    for (int k = 0; k < K; ++k) {
+        float rv[EPP];
+        load_epp<EPP>(r_s + k * RCT + w * EPP, rv);
+#pragma unroll
+        for (int j = 0; j < NRW; ++j) {
+            const float lv = bf2f(l_s[(rp0 + j * RP) * K + k]);
+#pragma unroll
+            for (int i = 0; i < EPP; ++i) d[j][i] = __fmaf_rn(lv, rv[i], d[j][i]);
+        }
+    }
+}
+
+// r_s[k][w * EPP + i] = r[k][n0 + col(w, i)]; the scale row of the tile
+template <int BITS>
+__device__ __forceinline__ void rc_stage_tile(const actcomp_rc_args &a, float *r_s, float *s_s, int64_t n0,
+                                              int64_t srow) {
+    using R = RcTile<BITS>;
+    for (int e = threadIdx.x; e < a.K * RCT; e += 256) {
+        const int k = e / RCT, c = e - k * RCT, w = c / R::EPP, i = c - w * R::EPP;
+        r_s[e] = bf2f(a.r[(int64_t)k * a.N + n0 + R::col(w, i)]);
+    }
+    for (int c = threadIdx.x; c < RCT; c += 256) s_s[c] = bf2f(a.s[srow * a.N + n0 + c]);
+}
+
+// rows [m0, m0 + RPP) of a (rows x ld) bf16 matrix, columns n0 .. n0 + RCT, into t (16-byte chunks)
+__device__ __forceinline__ void rc_load_rows(uint16_t *t, const uint16_t *src, int64_t ld, int64_t m0, int64_t m_hi,
+                                             int rpp, int64_t n0) {
+    for (int e = threadIdx.x; e < rpp * (RCT / 8); e += 256) {
+        const int r = e / (RCT / 8), c8 = e - r * (RCT / 8);
+        uint4 v = make_uint4(0u, 0u, 0u, 0u);
+        if (src && m0 + r < m_hi) v = *reinterpret_cast<const uint4 *>(src + (m0 + r) * ld + n0 + 8 * c8);
+        *reinterpret_cast<uint4 *>(t + r * RCT + 8 * c8) = v;
+    }
+}
+__device__ __forceinline__ void rc_store_rows(uint16_t *dst, const uint16_t *t, int64_t ld, int64_t N, int64_t m0,
+                                              int64_t m_hi, int rpp, int64_t n0) {
+    for (int e = threadIdx.x; e < rpp * (RCT / 8); e += 256) {
+        const int r = e / (RCT / 8), c8 = e - r * (RCT / 8);
+        if (m0 + r < m_hi && ACT_DCHECK(n0 + 8 * c8 + 8 <= N))
+            *reinterpret_cast<uint4 *>(dst + (m0 + r) * ld + n0 + 8 * c8) = *reinterpret_cast<const uint4 *>(t + r * RCT + 8 * c8);
+    }
+}
+
+template <int BITS>
+__global__ void __launch_bounds__(256, 4) rc_encode_tiled(actcomp_rc_args a) {
+    using R = RcTile<BITS>;
+    constexpr int EPP = R::EPP;
+    extern __shared__ __align__(16) uint8_t rc_smem[];
+    const int K = a.K, tid = threadIdx.x;
+    float *r_s = reinterpret_cast<float *>(rc_smem);
+    uint16_t *l_s = reinterpret_cast<uint16_t *>(rc_smem + R::off_l(K));
+    uint16_t *t_s = reinterpret_cast<uint16_t *>(rc_smem + R::off_t(K));
+    float *s_s = reinterpret_cast<float *>(rc_smem + R::off_s(K, false));
+    const int64_t n0 = (int64_t)blockIdx.x * RCT, b = blockIdx.z;
+    const int64_t m_lo = (int64_t)blockIdx.y * RCR;
+    const int64_t m_hi = m_lo + RCR < a.M ? m_lo + RCR : a.M;
+    const int lo = -(1 << (BITS - 1)), hi = (1 << (BITS - 1)) - 1, off = 1 << (BITS - 1);
+    const float thr = (a.flags & ACT_RC_OUTLIER_BF16) ? rne_bf(a.outlier) : a.outlier;
+    const int64_t srow = (a.flags & ACT_RC_SCALE_BATCH) ? (a.s_rows > 1 ? b : 0) : 0;
+    const int64_t W = a.N * BITS / 8;
+    rc_stage_tile<BITS>(a, r_s, s_s, n0, srow);
+    const int rp0 = tid / R::TPR, w = tid - rp0 * R::TPR;
+    for (int64_t m0 = m_lo; m0 < m_hi; m0 += R::RPP) {
+        __syncthreads();  // the previous pass's o tile has gone out
+        rc_load_rows(t_s, a.x + b * a.sxb, a.sxm, m0, m_hi, R::RPP, n0);
+        for (int e = tid; e < R::RPP * K; e += 256) {
+            const int r = e / K, k = e - r * K;
+            l_s[e] = m0 + r < m_hi ? a.l[(m0 + r) * K + k] : (uint16_t)0;
+        }
+        __syncthreads();
+        float dd[NRW][EPP];
+        rc_dots<EPP, R::RP>(r_s, l_s, K, rp0, w, dd);
+#pragma unroll
+        for (int j = 0; j < NRW; ++j) {
+            const int rp = rp0 + j * R::RP;
+            const int64_t m = m0 + rp;
+            if (m >= m_hi) break;
+            const float (&d)[EPP] = dd[j];
+            uint32_t byte = 0;
+#pragma unroll
+            for (int i = 0; i < EPP; ++i) {
+                const int c = R::col(w, i);
+                const float xv = bf2f(t_s[rp * RCT + c]);
+                const float res = (a.flags & ACT_RC_TWIN_LOWRANK) ? rne_bf(__fsub_rn(xv, rne_bf(d[i])))
+                                                                  : rne_bf(__fsub_rn(xv, d[i]));
+                const float ov = fabsf(res) > thr ? res : 0.f;
+                t_s[rp * RCT + c] = f2bf(ov);  // o over x, the same element of the same thread
+                const float xr = __fsub_rn(res, ov);
+                const float t = rne_bf(__fdiv_rn(xr, s_s[c]));
+                float rq = (a.flags & ACT_RC_HALF_EVEN) ? rintf(t) : roundf(t);
+                rq = fminf(fmaxf(rq, (float)lo), (float)hi);
+                byte |= (uint32_t)((int)rq + off) << (i * BITS);
+            }
+            if (ACT_DCHECK(n0 * BITS / 8 + w < W)) a.q[(b * a.M + m) * W + n0 * BITS / 8 + w] = (uint8_t)byte;
+        }
+        __syncthreads();
+        rc_store_rows(a.o + b * a.M * a.N, t_s, a.N, a.N, m0, m_hi, R::RPP, n0);
+    }
+}
+
+template <int BITS, int OP>
+__global__ void __launch_bounds__(256, 4) rc_decode_tiled(actcomp_rc_args a) {
+    using R = RcTile<BITS>;
+    constexpr int EPP = R::EPP;
+    constexpr bool Y = OP != ACT_OP_DECODE;
+    extern __shared__ __align__(16) uint8_t rc_smem[];
+    const int K = a.K, tid = threadIdx.x;
+    float *r_s = reinterpret_cast<float *>(rc_smem);
+    uint16_t *l_s = reinterpret_cast<uint16_t *>(rc_smem + R::off_l(K));
+    uint16_t *t_s = reinterpret_cast<uint16_t *>(rc_smem + R::off_t(K));
+    uint16_t *y_s = reinterpret_cast<uint16_t *>(rc_smem + R::off_y(K));
+    float *s_s = reinterpret_cast<float *>(rc_smem + R::off_s(K, Y));
+    const int64_t n0 = (int64_t)blockIdx.x * RCT, b = blockIdx.z;
+    const int64_t m_lo = (int64_t)blockIdx.y * RCR;
+    const int64_t m_hi = m_lo + RCR < a.M ? m_lo + RCR : a.M;
+    const int off = 1 << (BITS - 1);
+    const uint32_t mask = (1u << BITS) - 1u;
+    const int64_t srow = (a.flags & ACT_RC_SCALE_BATCH) ? (a.s_rows > 1 ? b : 0) : 0;
+    const int64_t W = a.N * BITS / 8;
+    rc_stage_tile<BITS>(a, r_s, s_s, n0, srow);
+    const int rp0 = tid / R::TPR, w = tid - rp0 * R::TPR;
+    for (int64_t m0 = m_lo; m0 < m_hi; m0 += R::RPP) {
+        __syncthreads();  // the previous pass's output tile has gone out
+        rc_load_rows(t_s, a.o ? a.o + b * a.M * a.N : nullptr, a.N, m0, m_hi, R::RPP, n0);
+        if constexpr (Y) rc_load_rows(y_s, a.x + b * a.sxb, a.sxm, m0, m_hi, R::RPP, n0);
+        for (int e = tid; e < R::RPP * K; e += 256) {
+            const int r = e / K, k = e - r * K;
+            l_s[e] = m0 + r < m_hi ? a.l[(m0 + r) * K + k] : (uint16_t)0;
+        }
+        __syncthreads();
+        float dd[NRW][EPP];
+        rc_dots<EPP, R::RP>(r_s, l_s, K, rp0, w, dd);
+#pragma unroll
+        for (int j = 0; j < NRW; ++j) {
+            const int rp = rp0 + j * R::RP;
+            const int64_t m = m0 + rp;
+            if (m >= m_hi) break;
+            const float (&d)[EPP] = dd[j];
+            const uint32_t byte = a.q[(b * a.M + m) * W + n0 * BITS / 8 + w];
+#pragma unroll
+            for (int i = 0; i < EPP; ++i) {
+                const int c = R::col(w, i);
+                const uint32_t u = (byte >> (i * BITS)) & mask;
+                const float wv = rne_bf(__fmul_rn(__int2float_rn((int)u - off), s_s[c]));
+                const float av = a.o ? rne_bf(__fadd_rn(wv, bf2f(t_s[rp * RCT + c]))) : wv;
+                float x = (a.flags & ACT_RC_TWIN_LOWRANK) ? rne_bf(__fadd_rn(av, rne_bf(d[i])))
+                                                          : rne_bf(__fadd_rn(av, d[i]));
+                if constexpr (Y) x = apply_op<OP>(x, bf2f(y_s[rp * RCT + c]));
+                t_s[rp * RCT + c] = f2bf(x);  // the output over o, the same element of the same thread
+            }
+        }
+        __syncthreads();
+        rc_store_rows(a.out + b * a.M * a.N, t_s, a.N, a.N, m0, m_hi, R::RPP, n0);
+    }
+}
+
+// The tiled kernels cover the 32-column block packing with whole 256-column
+// tiles and 16-byte aligned rows; anything else takes the per-element kernels.
+static bool rc_tiled_ok(const actcomp_rc_args *a, bool needs_x, bool needs_o) {
+    if ((a->flags & ACT_RC_ROW_PACK) || a->N % RCT) return false;
+    if (needs_x && (!aligned(a->x, 16) || a->sxb % 8 || a->sxm % 8)) return false;
+    if (needs_o && a->o && !aligned(a->o, 16)) return false;
+    return a->B <= 65535 && (a->M + RCR - 1) / RCR <= 65535;
+}
+static dim3 rc_tiled_grid(const actcomp_rc_args *a) {
+    return dim3((unsigned)(a->N / RCT), (unsigned)((a->M + RCR - 1) / RCR), (unsigned)a->B);
+}
+
 // ---------------------------------------------------------------- dense helpers
 template <int OP>
 __global__ void elementwise_kernel(actcomp_ew_args a) {
@@ -209,7 +435,22 @@ extern "C" int actcomp_rc_encode(const actcomp_rc_args *a, void *stream) {
     ACT_CHECK(a->x && a->o, ACT_E_INVALID);
     const int64_t bytes = a->B * a->M * (a->N * a->bits / 8);
     if (bytes == 0) return ACT_OK;
-    rc_encode_kernel<<<blocks_for(bytes), 256, 0, as_stream(stream)>>>(*a);
+    cudaStream_t s = as_stream(stream);
+    if (rc_tiled_ok(a, true, true)) {
+        const dim3 g = rc_tiled_grid(a);
+        auto go = [&](auto kern, int smem) -> int {
+            ACT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+            kern<<<g, 256, smem, s>>>(*a);
+            return launch_status();
+        };
+        switch (a->bits) {
+            case 1: return go(rc_encode_tiled<1>, RcTile<1>::bytes(a->K, false));
+            case 2: return go(rc_encode_tiled<2>, RcTile<2>::bytes(a->K, false));
+            case 4: return go(rc_encode_tiled<4>, RcTile<4>::bytes(a->K, false));
+            default: return go(rc_encode_tiled<8>, RcTile<8>::bytes(a->K, false));
+        }
+    }
+    rc_encode_kernel<<<blocks_for(bytes), 256, 0, s>>>(*a);
     return launch_status();
 }
 
@@ -222,6 +463,41 @@ extern "C" int actcomp_rc_decode(const actcomp_rc_args *a, int32_t op, void *str
     const int64_t n = a->B * a->M * a->N;
     if (n == 0) return ACT_OK;
     cudaStream_t s = as_stream(stream);
+    if (rc_tiled_ok(a, op != ACT_OP_DECODE, true)) {
+        const dim3 g = rc_tiled_grid(a);
+        const bool y = op != ACT_OP_DECODE;
+        auto one = [&](auto kern, int smem) {
+            if (cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem) != cudaSuccess) return;
+            kern<<<g, 256, smem, s>>>(*a);
+        };
+        auto go = [&](auto k1, auto k2, auto k4, auto k8) {
+            switch (a->bits) {
+                case 1: one(k1, RcTile<1>::bytes(a->K, y)); break;
+                case 2: one(k2, RcTile<2>::bytes(a->K, y)); break;
+                case 4: one(k4, RcTile<4>::bytes(a->K, y)); break;
+                default: one(k8, RcTile<8>::bytes(a->K, y)); break;
+            }
+        };
+        switch (op) {
+            case ACT_OP_DECODE:
+                go(rc_decode_tiled<1, ACT_OP_DECODE>, rc_decode_tiled<2, ACT_OP_DECODE>, rc_decode_tiled<4, ACT_OP_DECODE>,
+                   rc_decode_tiled<8, ACT_OP_DECODE>);
+                break;
+            case ACT_OP_MUL:
+                go(rc_decode_tiled<1, ACT_OP_MUL>, rc_decode_tiled<2, ACT_OP_MUL>, rc_decode_tiled<4, ACT_OP_MUL>,
+                   rc_decode_tiled<8, ACT_OP_MUL>);
+                break;
+            case ACT_OP_SILU_BWD:
+                go(rc_decode_tiled<1, ACT_OP_SILU_BWD>, rc_decode_tiled<2, ACT_OP_SILU_BWD>,
+                   rc_decode_tiled<4, ACT_OP_SILU_BWD>, rc_decode_tiled<8, ACT_OP_SILU_BWD>);
+                break;
+            default:
+                go(rc_decode_tiled<1, ACT_OP_GELU_BWD>, rc_decode_tiled<2, ACT_OP_GELU_BWD>,
+                   rc_decode_tiled<4, ACT_OP_GELU_BWD>, rc_decode_tiled<8, ACT_OP_GELU_BWD>);
+                break;
+        }
+        return launch_status();
+    }
     switch (op) {
         case ACT_OP_DECODE: rc_decode_kernel<ACT_OP_DECODE><<<blocks_for(n), 256, 0, s>>>(*a); break;
         case ACT_OP_MUL: rc_decode_kernel<ACT_OP_MUL><<<blocks_for(n), 256, 0, s>>>(*a); break;

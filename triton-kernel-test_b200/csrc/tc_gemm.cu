@@ -50,6 +50,23 @@ int make_map_3d(CUtensorMap *map, const void *base, CUtensorMapDataType dt, int 
     return r == CUDA_SUCCESS ? ACT_OK : ACT_E_CUDA;
 }
 
+// The same with a box of {box0, box1, box2}: with dim2 a channel-chunk axis
+// (stride 128 bytes) a single copy lands as box2 stacked 128-byte-swizzled
+// atom columns of box1 rows.
+int make_map_3d_box(CUtensorMap *map, const void *base, CUtensorMapDataType dt, int elem_bytes, uint64_t dim0,
+                    uint64_t dim1, uint64_t dim2, uint64_t stride1, uint64_t stride2, uint32_t box0, uint32_t box1,
+                    uint32_t box2, CUtensorMapSwizzle sw) {
+    auto fn = encode_fn();
+    if (!fn) return ACT_E_CUDA;
+    cuuint64_t dims[3] = {dim0, dim1, dim2};
+    cuuint64_t strides[2] = {stride1 * elem_bytes, stride2 * elem_bytes};
+    cuuint32_t box[3] = {box0, box1, box2};
+    cuuint32_t estr[3] = {1, 1, 1};
+    CUresult r = fn(map, dt, 3, const_cast<void *>(base), dims, strides, box, estr, CU_TENSOR_MAP_INTERLEAVE_NONE, sw,
+                    CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+    return r == CUDA_SUCCESS ? ACT_OK : ACT_E_CUDA;
+}
+
 namespace gemm {
 
 constexpr int BM = 128, BK = 64, THREADS = 192;
@@ -70,6 +87,8 @@ struct Smem {
 
 struct Params {
     int64_t M, N, K;
+    int kb2;  // k-blocks of the second segment (0: none)
+    int m_tiles, n_tiles;
     int a_mn, b_mn;
     void *C;
     int64_t ldc, sc_batch;
@@ -113,8 +132,8 @@ __device__ __forceinline__ void store_row32(T *dst, const float (&v)[32], int va
 
 template <int BN, int MA, typename TOut>
 __global__ void __launch_bounds__(THREADS, 1)
-    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, Params p,
-                int bf16) {
+    gemm_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                const __grid_constant__ CUtensorMap tmA2, const __grid_constant__ CUtensorMap tmB2, Params p, int bf16) {
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
     using S = Smem<BN, MA>;
@@ -126,8 +145,24 @@ __global__ void __launch_bounds__(THREADS, 1)
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
 
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-    const int n0 = blockIdx.x * BN, m0 = blockIdx.y * (BM * MA), bz = blockIdx.z;
-    const int kblocks = (int)((p.K + BK - 1) / BK);
+    // Grouped raster: the tiles of a batch are numbered in groups of up to 16
+    // M-tiles, M fastest inside a group, so that the CTAs resident at one time
+    // cover a compact block of C and share their A rows and B columns in L2
+    // (with N fastest every wave would stream all of B).
+    int m_t, n_t;
+    {
+        const int nm = p.m_tiles, nn = p.n_tiles;
+        const int id = blockIdx.x;
+        const int gsz = 16 * nn;
+        const int grp = id / gsz, first = grp * 16;
+        const int gm = nm - first < 16 ? nm - first : 16;
+        const int in = id - grp * gsz;
+        m_t = first + in % gm;
+        n_t = in / gm;
+    }
+    const int n0 = n_t * BN, m0 = m_t * (BM * MA), bz = blockIdx.z;
+    const int kb1 = (int)((p.K + BK - 1) / BK);
+    const int kblocks = kb1 + p.kb2;  // the second segment's k-blocks follow the first's
 
     if (threadIdx.x == 0) {
         for (int s = 0; s < STAGES; ++s) {
@@ -157,23 +192,25 @@ __global__ void __launch_bounds__(THREADS, 1)
             uint8_t *a = smem + s * S::STAGE;
             uint8_t *b = a + MA * S::A_BYTES;
             tc::mbar_arrive_expect_tx(&full[s], S::STAGE);
-            const int k0 = kb * BK;
+            const bool second = kb >= kb1;
+            const CUtensorMap *ma = second ? &tmA2 : &tmA, *mb = second ? &tmB2 : &tmB;
+            const int k0 = (second ? kb - kb1 : kb) * BK;
 #pragma unroll
             for (int h = 0; h < MA; ++h) {
                 uint8_t *ah = a + h * S::A_BYTES;
                 const int mh = m0 + BM * h;
                 if (!p.a_mn) {
-                    tc::tma_load_3d(ah, &tmA, &full[s], k0, mh, bz);
+                    tc::tma_load_3d(ah, ma, &full[s], k0, mh, bz);
                 } else {
-                    tc::tma_load_3d(ah, &tmA, &full[s], mh, k0, bz);
-                    tc::tma_load_3d(ah + 8192, &tmA, &full[s], mh + 64, k0, bz);
+                    tc::tma_load_3d(ah, ma, &full[s], mh, k0, bz);
+                    tc::tma_load_3d(ah + 8192, ma, &full[s], mh + 64, k0, bz);
                 }
             }
             if (!p.b_mn) {
-                tc::tma_load_3d(b, &tmB, &full[s], k0, n0, bz);
+                tc::tma_load_3d(b, mb, &full[s], k0, n0, bz);
             } else {
 #pragma unroll
-                for (int j = 0; j < BN / 64; ++j) tc::tma_load_3d(b + j * 8192, &tmB, &full[s], n0 + 64 * j, k0, bz);
+                for (int j = 0; j < BN / 64; ++j) tc::tma_load_3d(b + j * 8192, mb, &full[s], n0 + 64 * j, k0, bz);
             }
         }
     } else if (warp == 1 && lane == 0) {
@@ -268,12 +305,29 @@ int gemm_launch(const actcomp_gemm_args *g, cudaStream_t stream) {
         st = make_map_3d(&tmB, g->B, dt, 2, g->N, g->K, g->sb_batch ? batch : 1, g->ldb, g->sb_batch, 64, 64,
                          CU_TENSOR_MAP_SWIZZLE_128B);
     if (st) return st;
-    Params p{g->M, g->N, g->K, a_mn, b_mn, g->C, g->ldc, g->sc_batch, g->c_dtype, g->activation};
-    dim3 grid((unsigned)((g->N + BN - 1) / BN), (unsigned)((g->M + BM * (two ? 2 : 1) - 1) / (BM * (two ? 2 : 1))),
-              (unsigned)g->batch);
+    // the second K segment (or, without one, copies of the first maps that are never read)
+    CUtensorMap tmA2 = tmA, tmB2 = tmB;
+    if (g->K2 > 0) {
+        if (!a_mn)
+            st = make_map_3d(&tmA2, g->A2, dt, 2, g->K2, g->M, 1, g->lda2, 0, 64, 128, CU_TENSOR_MAP_SWIZZLE_128B);
+        else
+            st = make_map_3d(&tmA2, g->A2, dt, 2, g->M, g->K2, 1, g->lda2, 0, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (st) return st;
+        if (!b_mn)
+            st = make_map_3d(&tmB2, g->B2, dt, 2, g->K2, g->N, 1, g->ldb2, 0, 64, BN, CU_TENSOR_MAP_SWIZZLE_128B);
+        else
+            st = make_map_3d(&tmB2, g->B2, dt, 2, g->N, g->K2, 1, g->ldb2, 0, 64, 64, CU_TENSOR_MAP_SWIZZLE_128B);
+        if (st) return st;
+    }
+    const int kb2 = g->K2 > 0 ? (int)((g->K2 + 63) / 64) : 0;
+    const int m_tiles = (int)((g->M + BM * (two ? 2 : 1) - 1) / (BM * (two ? 2 : 1)));
+    const int n_tiles = (int)((g->N + BN - 1) / BN);
+    Params p{g->M, g->N, g->K, kb2, m_tiles, n_tiles, a_mn, b_mn, g->C, g->ldc, g->sc_batch, g->c_dtype, g->activation};
+    if ((int64_t)m_tiles * n_tiles > INT32_MAX) return ACT_E_UNSUPPORTED;
+    dim3 grid((unsigned)(m_tiles * n_tiles), 1, (unsigned)g->batch);
     auto launch = [&](auto kern, int smem) -> int {
         ACT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
-        kern<<<grid, THREADS, smem, stream>>>(tmA, tmB, p, bf16 ? 1 : 0);
+        kern<<<grid, THREADS, smem, stream>>>(tmA, tmB, tmA2, tmB2, p, bf16 ? 1 : 0);
         return launch_status();
     };
     if (BN == 128) {
@@ -311,5 +365,12 @@ extern "C" int actcomp_gemm(const actcomp_gemm_args *g, void *stream) {
     // a broadcast (stride 0) operand is only supported for batch == 1 maps;
     // otherwise every batched operand needs its own slice
     if (g->batch > 1) ACT_CHECK(g->sa_batch != 0 && g->sb_batch != 0 && g->sc_batch != 0, ACT_E_UNSUPPORTED);
+    ACT_CHECK(g->K2 >= 0 && g->K2 <= INT32_MAX, ACT_E_INVALID);
+    if (g->K2 > 0) {
+        ACT_CHECK(g->batch == 1, ACT_E_UNSUPPORTED);
+        ACT_CHECK(g->A2 && g->B2, ACT_E_INVALID);
+        ACT_CHECK(aligned(g->A2, 16) && aligned(g->B2, 16) && g->lda2 % 8 == 0 && g->ldb2 % 8 == 0, ACT_E_ALIGN);
+        ACT_CHECK(g->lda2 >= (g->a_kmajor ? g->K2 : g->M) && g->ldb2 >= (g->b_kmajor ? g->K2 : g->N), ACT_E_INVALID);
+    }
     return gemm_launch(g, as_stream(stream));
 }

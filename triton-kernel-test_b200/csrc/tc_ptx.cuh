@@ -65,6 +65,21 @@ __device__ __forceinline__ bool mbar_wait(uint64_t *bar, uint32_t parity, volati
     return false;
 }
 
+// Bounded wait for warps off the critical path: sleeps `ns` between polls so
+// that the spin leaves issue slots to working warps; gives up (as mbar_wait)
+// after `polls` polls.
+__device__ __forceinline__ bool mbar_wait_sleep(uint64_t *bar, uint32_t parity, volatile int *abort,
+                                                uint32_t ns = 256, uint32_t polls = 1u << 22) {
+    for (uint32_t i = 0; i < polls; ++i) {
+        if (mbar_try_wait(bar, parity)) return true;
+        if (*abort) return false;
+        __nanosleep(ns);
+    }
+    *abort = 1;
+    atomicOr(&g_device_error, DEV_ERR_MBAR_TIMEOUT);
+    return false;
+}
+
 // ------------------------------------------------------------------ TMA
 __device__ __forceinline__ void tma_load_2d(void *dst, const CUtensorMap *map, uint64_t *bar, int x, int y) {
     asm volatile(
@@ -326,4 +341,7 @@ __host__ __device__ constexpr uint32_t idesc_i8(int M, int N) {
 int make_map_3d(CUtensorMap *map, const void *base, CUtensorMapDataType dt, int elem_bytes, uint64_t dim0,
                 uint64_t dim1, uint64_t dim2, uint64_t stride1, uint64_t stride2, uint32_t box0, uint32_t box1,
                 CUtensorMapSwizzle sw);
+int make_map_3d_box(CUtensorMap *map, const void *base, CUtensorMapDataType dt, int elem_bytes, uint64_t dim0,
+                    uint64_t dim1, uint64_t dim2, uint64_t stride1, uint64_t stride2, uint32_t box0, uint32_t box1,
+                    uint32_t box2, CUtensorMapSwizzle sw);
 }  // namespace act
