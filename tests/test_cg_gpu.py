@@ -78,6 +78,9 @@ CASES = [
     # more token blocks than SMs: some CTAs of the row encode take two blocks
     # (separate projection / residual rings, double-buffered low-rank tiles)
     (19277, 1024, 32, 8, 4, 64, False),
+    # int8 codes through the two-kernel encode (projection, quantisation)
+    (160, 1024, 32, 8, 8, 64, False),
+    (90, 768, 16, 4, 8, 32, False),
 ]
 
 

@@ -19,8 +19,8 @@
 // float32 accumulation) into one of three TMEM accumulators; twelve epilogue
 // warps in three groups of four take the tiles round-robin, a thread one
 // token row x 128 channels: residual x - P with x from the ring, outlier
-// channels copied out and zeroed, group absmax and scale, codes staged in
-// shared memory and stored by one TMA store per warp.  X reaches the SMs
+// channels copied out and zeroed, group absmax and scale, codes stored from
+// registers (a thread's 64 bytes of its row per tile).  X reaches the SMs
 // twice (once from HBM, once mostly from L2) and the two kernels split the
 // work over every SM.
 // Arithmetic is that of oracle/actcomp_oracle.c (cg_encode_given_lr) given the
@@ -159,7 +159,7 @@ __global__ void __launch_bounds__(P_THREADS, 1)
 // ======================================================================== quantisation
 constexpr int NG = 3;                 // epilogue groups = TMEM accumulators
 constexpr int Q_THREADS = (3 + 4 * NG) * 32;
-constexpr int Q_STAGES = 3;           // tiles in flight (X tile + basis tile each)
+constexpr int Q_STAGES = 4;           // tiles in flight (X tile + basis tile each)
 
 struct QuantParams {
     int64_t T, H;
@@ -172,6 +172,7 @@ struct QuantParams {
     uint16_t *outl;
     const int32_t *idx;
     const uint16_t *vtile;
+    uint8_t *codes;
 };
 
 template <int PITCH>
@@ -232,20 +233,19 @@ struct QLayout {
     static constexpr int STAGE = XT + VT;
     static constexpr int PT = 3 * ROWS * LB;         // piece tiles of a token block
     static constexpr int CROW = CH * BITS / 8;       // code bytes of one token row of a tile
-    static constexpr int WSTG = 32 * CROW;           // one warp's code staging (32 rows)
     static constexpr int OFF_ST = 0;
     static constexpr int OFF_PT = OFF_ST + Q_STAGES * STAGE;
     static constexpr int OFF_STG = OFF_PT + 2 * PT;
-    static constexpr int OFF_OT = OFF_STG + 4 * NG * 2 * WSTG;  // outlier table: per 32 channels (mask, below)
+    static constexpr int OFF_OT = OFF_STG;  // outlier table: per 32 channels (mask, below)
     __host__ __device__ static int bar_off(int n32) { return (OFF_OT + n32 * 8 + 1023) & ~1023; }
     __host__ __device__ static int total(int n32) { return bar_off(n32) + 1024 + 1024; }
 };
 
 template <int BITS, int RK>
 __global__ void __launch_bounds__(Q_THREADS, 1)
-    cg_quant_kernel(const __grid_constant__ CUtensorMap tm_x, const __grid_constant__ CUtensorMap tm_c, QuantParams p) {
+    cg_quant_kernel(const __grid_constant__ CUtensorMap tm_x, QuantParams p) {
     using L = QLayout<BITS, RK>;
-    constexpr int LB = L::LB, CROW = L::CROW;
+    constexpr int LB = L::LB;
     constexpr int qmax = (1 << (BITS - 1)) - 1, off = 1 << (BITS - 1);
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -400,7 +400,7 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
         const int G = p.group;
         const int gshift = 31 - __clz(G);
         const int ngr = (int)(p.H / G);
-        uint8_t *stg = smem + L::OFF_STG + ew * 2 * L::WSTG;
+        const int64_t crow = p.H * BITS / 8;  // code bytes per token row
         int j = 0;
         bool ok = true;
         Walk w(v_lo, p.ntiles, p.ncc);
@@ -419,10 +419,9 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
             const uint32_t acc = tmem + g * CH + ((uint32_t)(q * 32) << 16);
             const uint8_t *xt = smem + L::OFF_ST + s * L::STAGE;
             const uint32_t *ot = otab + 2 * (c0 >> 5);
-            uint8_t *buf = stg + (j & 1) * L::WSTG;
+            uint8_t *cdst = p.codes + t * crow + c0 * BITS / 8;  // this row's codes of the tile
             // this warp's code staging (two buffers) is free once the store issued
             // two tiles ago has read it
-            if (lane == 0) tc::bulk_wait_read<1>();
             __syncwarp();
             float scv[4];
             // groups of G channels: G / 32 pieces of 32 held as residuals in registers
@@ -500,7 +499,7 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
                             pk[wd] = pack_codes<4>(fma2(w2[h][4 * wd], rs2, magic2), fma2(w2[h][4 * wd + 1], rs2, magic2),
                                                    fma2(w2[h][4 * wd + 2], rs2, magic2),
                                                    fma2(w2[h][4 * wd + 3], rs2, magic2));
-                        *reinterpret_cast<uint4 *>(buf + swz<CROW>(lane, pc)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                        if (rv) *reinterpret_cast<uint4 *>(cdst + 16 * pc) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
                     } else {
                         const float2 z = make_float2(0.f, 0.f);
                         uint32_t pk[8];
@@ -508,9 +507,10 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
                         for (int wd = 0; wd < 8; ++wd)
                             pk[wd] = pack_codes<8>(fma2(w2[h][2 * wd], rs2, magic2), fma2(w2[h][2 * wd + 1], rs2, magic2),
                                                    z, z);
-                        *reinterpret_cast<uint4 *>(buf + swz<CROW>(lane, 2 * pc)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
-                        *reinterpret_cast<uint4 *>(buf + swz<CROW>(lane, 2 * pc + 1)) =
-                            make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                        if (rv) {
+                            *reinterpret_cast<uint4 *>(cdst + 32 * pc) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+                            *reinterpret_cast<uint4 *>(cdst + 32 * pc + 16) = make_uint4(pk[4], pk[5], pk[6], pk[7]);
+                        }
                     }
                 }
             }
@@ -526,14 +526,7 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
                 if (G == 32) *reinterpret_cast<float4 *>(sp) = make_float4(scv[0], scv[1], scv[2], scv[3]);
                 else *reinterpret_cast<float2 *>(sp) = make_float2(scv[0], scv[2]);
             }
-            tc::fence_proxy_async();
-            __syncwarp();
-            if (lane == 0 && ACT_DCHECK(c0 + CH <= p.H)) {
-                tc::tma_store_3d(&tm_c, buf, (int)(c0 * BITS / 8), tb * ROWS + 32 * q, 0);
-                tc::bulk_commit();
-            }
         }
-        if (lane == 0) tc::bulk_wait<0>();
     }
     tc::tc_fence_before();
     __syncthreads();
@@ -573,15 +566,10 @@ template <int BITS, int RK>
 int launch_quant(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cudaStream_t stream) {
     using L = QLayout<BITS, RK>;
     const int64_t T = d->tokens, H = d->channels;
-    const int64_t rowb = H * BITS / 8;
-    CUtensorMap m_x{}, m_c{};
+    CUtensorMap m_x{};
     int st;
     if ((st = make_map_3d(&m_x, x, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, H, T, 1, ldx, T * ldx, 64, ROWS,
                           CU_TENSOR_MAP_SWIZZLE_128B)))
-        return st;
-    // codes leave per warp: 32 token rows x one tile's code bytes
-    if ((st = make_map_3d(&m_c, d->codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, rowb, T, 1, rowb, T * rowb, L::CROW, 32,
-                          tma_swz<L::CROW>())))
         return st;
     QuantParams p{};
     p.T = T;
@@ -597,6 +585,7 @@ int launch_quant(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cudaS
     p.outl = d->outliers;
     p.idx = d->outlier_idx;
     p.vtile = d->basis_tile;
+    p.codes = d->codes;
     const int smem = L::total((int)(H / 32));
     if (smem > 227 * 1024) return ACT_E_UNSUPPORTED;
     auto kern = cg_quant_kernel<BITS, RK>;
@@ -604,7 +593,7 @@ int launch_quant(const actcomp_cg_desc *d, const uint16_t *x, int64_t ldx, cudaS
     const int grid = (int)(p.ntiles < num_sms() ? p.ntiles : num_sms());
     p.tq = (int)(p.ntiles / grid);
     p.trem = (int)(p.ntiles % grid);
-    kern<<<grid, Q_THREADS, smem, stream>>>(m_x, m_c, p);
+    kern<<<grid, Q_THREADS, smem, stream>>>(m_x, p);
     return launch_status();
 }
 
