@@ -358,32 +358,7 @@ __global__ void __launch_bounds__(Geo<WHT>::THREADS, 1)
                 uint8_t *dst = lqb + ls * L::LQB;
                 const int64_t t0 = (int64_t)tw.b * p.T + (int64_t)tw.tb * ROWS;  // first row of the block
                 const int64_t rows_here = p.T - (int64_t)tw.tb * ROWS;
-                // 8 coefficients (two 16-byte loads) per 16-byte chunk of each piece
-                // tile; chunks past the rank and rows past T are zero
-                constexpr int CPR = LB / 16;
-#pragma unroll 2
-                for (int e = lane; e < ROWS * CPR; e += 32) {
-                    const int row = e / CPR, c16 = e - row * CPR;
-                    uint32_t ph[4] = {0u, 0u, 0u, 0u}, pm[4] = {0u, 0u, 0u, 0u}, pl[4] = {0u, 0u, 0u, 0u};
-                    if (8 * c16 < p.rank && row < rows_here) {
-                        const float4 *src = reinterpret_cast<const float4 *>(p.lr + (t0 + row) * p.rank + 8 * c16);
-                        const float4 v0 = __ldg(src), v1 = __ldg(src + 1);
-                        const float in[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-#pragma unroll
-                        for (int h = 0; h < 4; ++h) {
-                            float h0, m0, l0, h1, m1, l1;
-                            split3_bf16(in[2 * h], h0, m0, l0);
-                            split3_bf16(in[2 * h + 1], h1, m1, l1);
-                            ph[h] = pack_bf16x2(h0, h1);
-                            pm[h] = pack_bf16x2(m0, m1);
-                            pl[h] = pack_bf16x2(l0, l1);
-                        }
-                    }
-                    const int o = swz<LB>(row, c16);
-                    *reinterpret_cast<uint4 *>(dst + o) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
-                    *reinterpret_cast<uint4 *>(dst + ROWS * LB + o) = make_uint4(pm[0], pm[1], pm[2], pm[3]);
-                    *reinterpret_cast<uint4 *>(dst + 2 * ROWS * LB + o) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
-                }
+                build_piece_tiles<ROWS, LB>(p.lr, t0, rows_here, p.rank, dst, lane);
                 tc::fence_proxy_async();
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(&pready[ls]);

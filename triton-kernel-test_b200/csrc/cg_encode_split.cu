@@ -331,29 +331,7 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
             if (!(ok = tc::mbar_wait(&pfree[slot], ((m >> 1) & 1) ^ 1, abort))) break;
             uint8_t *dst = smem + L::OFF_PT + slot * L::PT;
             const int64_t t0 = (int64_t)w.tb * ROWS;
-            constexpr int CPR = LB / 16;  // 16-byte chunks per operand row (8 coefficients each)
-            for (int e = lane; e < ROWS * CPR; e += 32) {
-                const int row = e / CPR, c16 = e - row * CPR;
-                uint32_t hp[4] = {0u, 0u, 0u, 0u}, mp[4] = {0u, 0u, 0u, 0u}, lp[4] = {0u, 0u, 0u, 0u};
-                if (8 * c16 < r && t0 + row < p.T) {
-                    const float4 *src = reinterpret_cast<const float4 *>(p.lr + (t0 + row) * r + 8 * c16);
-                    const float4 v0 = __ldg(src), v1 = __ldg(src + 1);
-                    const float in[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-#pragma unroll
-                    for (int h = 0; h < 4; ++h) {
-                        float h0, m0, l0, h1, m1, l1;
-                        split3_bf16(in[2 * h], h0, m0, l0);
-                        split3_bf16(in[2 * h + 1], h1, m1, l1);
-                        hp[h] = pack_bf16x2(h0, h1);
-                        mp[h] = pack_bf16x2(m0, m1);
-                        lp[h] = pack_bf16x2(l0, l1);
-                    }
-                }
-                const int o = swz<LB>(row, c16);
-                *reinterpret_cast<uint4 *>(dst + o) = make_uint4(hp[0], hp[1], hp[2], hp[3]);
-                *reinterpret_cast<uint4 *>(dst + ROWS * LB + o) = make_uint4(mp[0], mp[1], mp[2], mp[3]);
-                *reinterpret_cast<uint4 *>(dst + 2 * ROWS * LB + o) = make_uint4(lp[0], lp[1], lp[2], lp[3]);
-            }
+            build_piece_tiles<ROWS, LB>(p.lr, t0, p.T - t0, r, dst, lane);
             tc::fence_proxy_async();
             __syncwarp();
             if (lane == 0) tc::mbar_arrive(&pready[slot]);

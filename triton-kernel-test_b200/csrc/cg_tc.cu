@@ -301,30 +301,7 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RK>::THREADS, 1)
                 uint8_t *dst = ptile + ls * L::PT;
                 const int64_t t0 = (int64_t)tw.b * p.T + (int64_t)tw.tb * ROWS;  // first row of the block
                 const int64_t rows_here = p.T - (int64_t)tw.tb * ROWS;
-                constexpr int CPR = LB / 16;  // 16-byte chunks per operand row (8 coefficients each)
-#pragma unroll 2
-                for (int e = lane; e < ROWS * CPR; e += 32) {
-                    const int row = e / CPR, c16 = e - row * CPR;
-                    uint32_t hp[4] = {0u, 0u, 0u, 0u}, mp[4] = {0u, 0u, 0u, 0u}, lp[4] = {0u, 0u, 0u, 0u};
-                    if (8 * c16 < p.rank && row < rows_here) {
-                        const float4 *src = reinterpret_cast<const float4 *>(p.lr + (t0 + row) * p.rank + 8 * c16);
-                        const float4 v0 = __ldg(src), v1 = __ldg(src + 1);
-                        const float in[8] = {v0.x, v0.y, v0.z, v0.w, v1.x, v1.y, v1.z, v1.w};
-#pragma unroll
-                        for (int hh = 0; hh < 4; ++hh) {
-                            float h0, m0, l0, h1, m1, l1;
-                            split3_bf16(in[2 * hh], h0, m0, l0);
-                            split3_bf16(in[2 * hh + 1], h1, m1, l1);
-                            hp[hh] = pack_bf16x2(h0, h1);
-                            mp[hh] = pack_bf16x2(m0, m1);
-                            lp[hh] = pack_bf16x2(l0, l1);
-                        }
-                    }
-                    const int o = swz<LB>(row, c16);
-                    *reinterpret_cast<uint4 *>(dst + o) = make_uint4(hp[0], hp[1], hp[2], hp[3]);
-                    *reinterpret_cast<uint4 *>(dst + ROWS * LB + o) = make_uint4(mp[0], mp[1], mp[2], mp[3]);
-                    *reinterpret_cast<uint4 *>(dst + 2 * ROWS * LB + o) = make_uint4(lp[0], lp[1], lp[2], lp[3]);
-                }
+                build_piece_tiles<ROWS, LB>(p.lr, t0, rows_here, p.rank, dst, lane);
                 tc::fence_proxy_async();
                 __syncwarp();
                 if (lane == 0) tc::mbar_arrive(&pready[ls]);

@@ -211,4 +211,63 @@ __device__ __forceinline__ float2 apply_op2(float2 xhat, float2 y) {
     else return xhat;
 }
 
+// Row-swizzled K-major operand layout (PITCH bytes a row, 16-byte chunks
+// XORed with the row as the 128/64/32-byte tcgen05 swizzles expect).
+template <int PITCH>
+__device__ __forceinline__ int kmajor_swz(int r, int c) {
+    if constexpr (PITCH == 128) return r * 128 + ((c ^ (r & 7)) << 4);
+    else if constexpr (PITCH == 64) return r * 64 + ((c ^ ((r >> 1) & 3)) << 4);
+    else return r * 32 + ((c ^ ((r >> 2) & 1)) << 4);
+}
+
+// One warp splits ROWS rows of the float32 projection (rows t0 .., row
+// stride `rank`; rows from `rows_here` on and coefficients from `rank` on are
+// zero) into its three exact bf16 pieces (split3_bf16), written as three
+// K-major operand tiles of LB bytes a row at dst, dst + ROWS*LB and
+// dst + 2*ROWS*LB.  Each lane issues the loads of up to eight 8-coefficient
+// chunks before converting any, so the warp waits for memory once per batch.
+template <int ROWS, int LB>
+__device__ __forceinline__ void build_piece_tiles(const float *lr, int64_t t0, int64_t rows_here, int rank,
+                                                  uint8_t *dst, int lane) {
+    constexpr int CPR = LB / 16;          // 16-byte chunks per operand row (8 coefficients)
+    constexpr int N = ROWS * CPR / 32;    // chunks per lane
+    constexpr int BATCH = N < 8 ? N : 8;
+    static_assert((ROWS * CPR) % 32 == 0 && N % BATCH == 0, "whole chunks per lane");
+#pragma unroll 1
+    for (int j0 = 0; j0 < N; j0 += BATCH) {
+        float4 v[BATCH][2];
+#pragma unroll
+        for (int j = 0; j < BATCH; ++j) {
+            const int e = lane + 32 * (j0 + j), row = e / CPR, c16 = e - row * CPR;
+            if (8 * c16 < rank && row < rows_here) {
+                const float4 *src = reinterpret_cast<const float4 *>(lr + (t0 + row) * rank + 8 * c16);
+                v[j][0] = __ldg(src);
+                v[j][1] = __ldg(src + 1);
+            } else {
+                v[j][0] = v[j][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+            }
+        }
+#pragma unroll
+        for (int j = 0; j < BATCH; ++j) {
+            const int e = lane + 32 * (j0 + j), row = e / CPR, c16 = e - row * CPR;
+            const float in[8] = {v[j][0].x, v[j][0].y, v[j][0].z, v[j][0].w,
+                                 v[j][1].x, v[j][1].y, v[j][1].z, v[j][1].w};
+            uint32_t ph[4], pm[4], pl[4];
+#pragma unroll
+            for (int h = 0; h < 4; ++h) {
+                float h0, m0, l0, h1, m1, l1;
+                split3_bf16(in[2 * h], h0, m0, l0);
+                split3_bf16(in[2 * h + 1], h1, m1, l1);
+                ph[h] = pack_bf16x2(h0, h1);
+                pm[h] = pack_bf16x2(m0, m1);
+                pl[h] = pack_bf16x2(l0, l1);
+            }
+            const int o = kmajor_swz<LB>(row, c16);
+            *reinterpret_cast<uint4 *>(dst + o) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
+            *reinterpret_cast<uint4 *>(dst + ROWS * LB + o) = make_uint4(pm[0], pm[1], pm[2], pm[3]);
+            *reinterpret_cast<uint4 *>(dst + 2 * ROWS * LB + o) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+        }
+    }
+}
+
 }  // namespace act
