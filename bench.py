@@ -487,6 +487,29 @@ def run_gpu(args):
             "ms": ms_smax, "GB/s": sbytes / (ms_smax * 1e-3) / 1e9, "frac_of_hbm": sbytes / (ms_smax * 1e-3) / 1e9 / hbm,
             "bytes": sbytes}
         del cP, dP, bP
+        # NF4 base weight of the reference's backward driver (d1 = 4096 in,
+        # d2 = 14336 out, low_rank_system_profile_backward.py:21-22,31,58):
+        # blocksize 64 with nested statistics (LinearNF4's default), dequantised
+        # to bf16 every step; HBM-bound: n/2 + n/64 bytes in, 2n bytes out
+        from actcomp import nf4 as NF4
+
+        d1n, d2n = 4096, 14336
+        nn4 = d1n * d2n
+        gq = torch.Generator(device=dev).manual_seed(31)
+        wq = torch.randint(0, 256, ((nn4 + 1) // 2, 1), dtype=torch.uint8, device=dev, generator=gq)
+        st2 = NF4.QuantState(absmax=torch.rand(-(-nn4 // (64 * 256)), device=dev, generator=gq) * 0.1,
+                             shape=torch.Size([-(-nn4 // (64 * 256))]),
+                             code=torch.linspace(-1, 1, 256, device=dev), blocksize=256)
+        stq = NF4.QuantState(absmax=torch.randint(0, 256, (nn4 // 64,), dtype=torch.uint8, device=dev, generator=gq),
+                             shape=torch.Size([d2n, d1n]), code=NF4.nf4_code(dev), blocksize=64,
+                             offset=torch.tensor(0.05, device=dev), state2=st2)
+        wout = torch.empty((d2n, d1n), dtype=torch.bfloat16, device=dev)
+        ms_nf4 = time_steps(lambda: NF4.dequantize_4bit(wq.t(), stq, out=wout), max(3, args.steps // 2), 1, flush,
+                            world, clk)
+        nb4 = (nn4 + 1) // 2 + nn4 // 64 + 2 * nn4
+        components[f"nf4_dequant_{d2n}x{d1n}"] = {"ms": ms_nf4, "GB/s": nb4 / (ms_nf4 * 1e-3) / 1e9,
+                                                  "frac_of_hbm": nb4 / (ms_nf4 * 1e-3) / 1e9 / hbm, "bytes": nb4}
+        del wq, st2, stq, wout
 
         # the reference-named API (compat / reference_api) on its own speed-test
         # shapes: x (B=4, M, M), rank R=16, 1-bit encode with a dense outlier

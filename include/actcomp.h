@@ -302,6 +302,26 @@ typedef struct actcomp_gemm_args {
 } actcomp_gemm_args;
 int actcomp_gemm(const actcomp_gemm_args *g, void *stream);
 
+/* ========================================================= NF4 base weight
+ * F.dequantize_4bit(w.t(), quant_state, quant_type='nf4') of bitsandbytes as
+ * low_rank_system_profile_backward.py:58 calls it on the frozen LinearNF4 base
+ * weight (:31) before compute_lora_gradient.  n values (the weight flattened
+ * row-major), blocks of `blocksize` consecutive values (a power of two >= 8);
+ * packed: ceil(n/2) bytes, value 2j in the high nibble of byte j, 2j+1 in the
+ * low; code: 16 floats (the data type's values, quant_state.code).  Block
+ * statistics, exactly one of:
+ *   absmax (float per block), or
+ *   absmax_q (uint8 per block) with absmax2 (float per blocksize2 blocks),
+ *   code2 (256 floats) and offset (one float; device memory, like every
+ *   pointer here): absmax_b = code2[absmax_q[b]] * absmax2[b / blocksize2] +
+ *   *offset (float32, product then sum; the nested statistics of
+ *   compress_statistics=True).
+ * out[i] = bf16(code[q_i] * absmax_{i / blocksize}) (float32 product, round to
+ * nearest even).  packed 4-byte aligned, out 16-byte aligned (ACT_E_ALIGN). */
+int actcomp_nf4_dequant(const uint8_t *packed, int64_t n, int64_t blocksize, const float *code,
+                        const float *absmax, const uint8_t *absmax_q, const float *absmax2,
+                        const float *code2, int64_t blocksize2, const float *offset, uint16_t *out, void *stream);
+
 /* Error statistics of a reconstruction against its original (n bf16 values):
  * out[0] += sum (a-b)^2, out[1] += sum b^2, out[2] = max(out[2], max|a-b|),
  * out[3] += count(a != b); out: 4 doubles of device memory (accumulated into,

@@ -404,3 +404,90 @@ def compare_bf16(a, b, max_frac=1e-4):
     ulp = np.abs(fb) * 2.0 ** -7  # one bf16 step (7 explicit mantissa bits), upper bound
     step_ok = bool(np.all(np.abs(fa - fb) <= ulp + 1e-38))
     return {"values": int(a.size), "differing": n, "ok": step_ok and n <= max_frac * a.size}
+
+
+# ------------------------------------------------------------------ NF4 base weight
+# bitsandbytes (a third-party dependency of the reference's driver scripts, not
+# vendored under the reference and not installed here; no version pinned by the
+# reference) quantises the frozen LoRA base weight to NF4
+# (low_rank_system_profile_backward.py:31) and dequantises it with
+# F.dequantize_4bit(..., quant_type='nf4') (:58).  What follows restates the
+# published algorithm (the QLoRA paper's NormalFloat data type and blockwise
+# absmax quantisation with optional nested statistics).  No reference test or
+# fixture holds NF4 values, so this part of the oracle is "parity unpinned":
+# it pins the kernel to this restatement, not to bitsandbytes.
+
+#: quantile offset of the NF4 construction: 1 - (1/32 + 1/30) / 2
+NF4_OFFSET = 1.0 - 0.5 * (1.0 / 32.0 + 1.0 / 30.0)
+
+
+def nf4_code() -> np.ndarray:
+    """The 16 NF4 values (float32, ascending): 8 quantiles of N(0, 1) at
+    probabilities evenly spaced from NF4_OFFSET down to (not including) 1/2 for
+    the positive half, 7 such quantiles for the negative half, and an exact
+    zero; normalised so that the extremes are -1 and +1."""
+    from statistics import NormalDist
+
+    nd = NormalDist()
+    pos = [nd.inv_cdf(p) for p in np.linspace(NF4_OFFSET, 0.5, 9)[:-1]]
+    neg = [-nd.inv_cdf(p) for p in np.linspace(NF4_OFFSET, 0.5, 8)[:-1]]
+    v = np.array(sorted(pos + [0.0] + neg), dtype=np.float64)
+    return (v / np.abs(v).max()).astype(np.float32)
+
+
+def nf4_quantize(w: np.ndarray, blocksize: int, code: np.ndarray) -> tuple[np.ndarray, np.ndarray]:
+    """Blockwise absmax quantisation of w (flattened row-major) to 4-bit indices
+    of the nearest code value: returns (packed bytes, value 2j in the high
+    nibble of byte j; float32 absmax per block).  Test data only."""
+    x = np.ascontiguousarray(w, dtype=np.float32).ravel()
+    n = x.size
+    nb = -(-n // blocksize)
+    pad = np.zeros(nb * blocksize, np.float32)
+    pad[:n] = x
+    absmax = np.abs(pad.reshape(nb, blocksize)).max(axis=1).astype(np.float32)
+    scale = np.where(absmax > 0, absmax, 1.0).astype(np.float32)
+    t = (pad.reshape(nb, blocksize) / scale[:, None]).ravel()[:n]
+    idx = np.abs(t[:, None] - code[None, :].astype(np.float32)).argmin(axis=1).astype(np.uint8)
+    if n % 2:
+        idx = np.concatenate([idx, np.zeros(1, np.uint8)])
+    packed = ((idx[0::2] << 4) | idx[1::2]).astype(np.uint8)
+    return packed, absmax
+
+
+def nested_stats(absmax: np.ndarray, blocksize2: int, code2: np.ndarray):
+    """Nested (double) quantisation of float32 block statistics: offset = mean,
+    then blockwise absmax quantisation of (absmax - offset) to the nearest of
+    the 256 code2 values.  Returns (absmax_q uint8, absmax2 float32, offset
+    float32).  Test data only."""
+    a = np.asarray(absmax, np.float32)
+    offset = np.float32(a.astype(np.float64).mean())
+    d = (a - offset).astype(np.float32)
+    nb2 = -(-d.size // blocksize2)
+    pad = np.zeros(nb2 * blocksize2, np.float32)
+    pad[: d.size] = d
+    a2 = np.abs(pad.reshape(nb2, blocksize2)).max(axis=1).astype(np.float32)
+    s2 = np.where(a2 > 0, a2, 1.0).astype(np.float32)
+    t = (pad.reshape(nb2, blocksize2) / s2[:, None]).ravel()[: d.size]
+    q = np.abs(t[:, None] - np.asarray(code2, np.float32)[None, :]).argmin(axis=1).astype(np.uint8)
+    return q, a2, offset
+
+
+def nf4_dequant(packed, n, blocksize, code, absmax=None, absmax_q=None, absmax2=None, code2=None,
+                blocksize2=256, offset=0.0) -> np.ndarray:
+    """bf16 bits of the n dequantised values, with the rounding points of
+    F.dequantize_4bit followed by .to(bfloat16): block statistic in float32
+    (nested: code2[q] * absmax2, rounded, plus the offset, rounded), the value
+    code[index] * statistic rounded to float32, then to bf16 (nearest even)."""
+    packed = np.asarray(packed, np.uint8)
+    idx = np.empty(2 * packed.size, np.uint8)
+    idx[0::2] = packed >> 4
+    idx[1::2] = packed & 15
+    idx = idx[:n]
+    if absmax_q is not None:
+        prod = (np.asarray(code2, np.float32)[np.asarray(absmax_q)] * np.asarray(absmax2, np.float32)[
+            np.arange(len(absmax_q)) // blocksize2]).astype(np.float32)
+        am = (prod + np.float32(offset)).astype(np.float32)
+    else:
+        am = np.asarray(absmax, np.float32)
+    v = (np.asarray(code, np.float32)[idx] * am[np.arange(n) // blocksize]).astype(np.float32)
+    return f32_to_bf16(v)

@@ -111,6 +111,8 @@ SIGNATURES = {
     "actcomp_extract_channel": (ctypes.c_int, [c_vp, c_i64, c_i64, c_i64, c_vp, c_i32, c_vp, c_vp]),
     "actcomp_gemm": (ctypes.c_int, [ctypes.POINTER(GemmArgs), c_vp]),
     "actcomp_error_stats": (ctypes.c_int, [c_vp, c_vp, c_i64, c_vp, c_vp]),
+    "actcomp_nf4_dequant": (ctypes.c_int, [c_vp, c_i64, c_i64, c_vp, c_vp, c_vp, c_vp, c_vp, c_i64,
+                                           c_vp, c_vp, c_vp]),
 }
 
 _lock = threading.Lock()

@@ -13,6 +13,7 @@ from __future__ import annotations
 import torch
 
 from . import core, ops, refcompat
+from .nf4 import dequantize_4bit  # F.dequantize_4bit, low_rank_system_profile_backward.py:58  # noqa: F401
 from ._lib import ACT_OP_DECODE, ACT_OP_MUL, ACT_OP_SILU_BWD
 
 _BF = torch.bfloat16
@@ -239,7 +240,9 @@ def compute_lora_gradient(dy, x, w, a, b):
     B = dy.shape[0] if dy.dim() == 3 else 1
     r = a.shape[-1]
     dy2 = dy.reshape(-1, dy.shape[-1]).to(_BF).contiguous()
-    a_bf, b_bf, w_bf = a.to(_BF).contiguous(), b.to(_BF).contiguous(), w.to(_BF).contiguous()
+    # w is read in place: the GEMM takes either major-ness, so the transposed
+    # view dequantize_4bit returns for the frozen base weight is not copied
+    a_bf, b_bf, w_bf = a.to(_BF).contiguous(), b.to(_BF).contiguous(), w.to(_BF)
     dyb = ops.gemm(dy2, b_bf.mT, torch.float32, "")          # (BS, r) = dy b^T
     P = _pieces3(dyb)                                         # (BS, 3r)
     a3 = torch.cat([a_bf, a_bf, a_bf], dim=1)                # (d_in, 3r)
@@ -256,9 +259,3 @@ def compute_lora_gradient(dy, x, w, a, b):
     xa = ops.gemm(x3, a_bf, torch.float32, "")               # (B, S, r)
     db = _sum3(ops.gemm(_pieces3(xa).mT, dy2.reshape(B, -1, dy2.shape[-1]), torch.float32, ""), r, -2)
     return dx, da, db
-    x3 = x.reshape(B, -1, x.shape[-1]).to(_BF)
-    dyb3 = dyb.reshape(B, -1, dyb.shape[-1])
-    da = ops.gemm(x3.mT, dyb3, torch.float32, "")
-    xa = _mm(x3, a)
-    db = ops.gemm(xa.mT, dy2.reshape(B, -1, dy2.shape[-1]), torch.float32, "")
-    return dx.reshape(dy.shape[:-1] + (dx.shape[-1],)), da, db
