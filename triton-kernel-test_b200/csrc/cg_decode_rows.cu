@@ -353,6 +353,10 @@ __global__ void __launch_bounds__(Geo<WHT>::THREADS, 1)
             bool ok = true;
             for (int64_t tile = t_lo; tile < t_hi && ok; ++tile, tw.next()) {
                 if (tile != t_lo && tw.cc != 0) continue;  // not the first tile of a token block
+                if (m == 0) {  // the range's first block: built by the epilogue warps
+                    ++m;
+                    continue;
+                }
                 const int ls = m & 1;
                 if (!(ok = tc::mbar_wait(&pfree[ls], ((m >> 1) & 1) ^ 1, abort))) break;
                 uint8_t *dst = lqb + ls * L::LQB;
@@ -375,6 +379,18 @@ __global__ void __launch_bounds__(Geo<WHT>::THREADS, 1)
         const int gshift = 31 - __clz(p.group);
         const uint32_t *otab = reinterpret_cast<const uint32_t *>(smem + p.off_ot);
         uint8_t *stg = smem + p.off_stg + ew * WSTG;
+        // the piece tiles of the range's first token block, by all epilogue warps
+        // (idle until its P exists): one memory round trip instead of the
+        // builder warp's several
+        if constexpr (RK > 0) {
+            if (t_lo < t_hi) {
+                const Walk fw(t_lo, p.ncc, p.ntb);
+                const int64_t t0 = (int64_t)fw.b * p.T + (int64_t)fw.tb * ROWS;
+                build_piece_tiles_team<ROWS, LB, 32 * EW>(p.lr, t0, p.T - (int64_t)fw.tb * ROWS, p.rank, lqb,
+                                                          (int)threadIdx.x - 64);
+                tc::fence_proxy_async();
+            }
+        }
         // outlier table of every slice this range touches: per 32-channel group a
         // mask of its outlier channels and the number of outliers below it (built
         // here, after the producer has started its loads)
@@ -395,7 +411,10 @@ __global__ void __launch_bounds__(Geo<WHT>::THREADS, 1)
                 omask[2 * e] = m;
                 omask[2 * e + 1] = (uint32_t)below;
             }
-            tc::named_bar(1, 32 * EW);  // complete before any epilogue warp reads it
+        }
+        if (p.k || (RK > 0 && t_lo < t_hi)) {
+            tc::named_bar(1, 32 * EW);  // the table and the first piece tiles complete
+            if (RK > 0 && t_lo < t_hi && threadIdx.x == 64) tc::mbar_arrive(&pready[0]);
         }
 
         // per-row scalars of a tile: the group scales of its 128 channels,

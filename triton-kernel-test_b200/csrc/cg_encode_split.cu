@@ -327,6 +327,10 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
         bool ok = true;
         for (int64_t v = v_lo; v < v_hi && ok; ++v, w.next()) {
             if (v != v_lo && w.cc != 0) continue;  // not the first tile of a token block
+            if (m == 0) {  // the range's first block: built by the epilogue warps
+                ++m;
+                continue;
+            }
             const int slot = m & 1;
             if (!(ok = tc::mbar_wait(&pfree[slot], ((m >> 1) & 1) ^ 1, abort))) break;
             uint8_t *dst = smem + L::OFF_PT + slot * L::PT;
@@ -379,6 +383,17 @@ __global__ void __launch_bounds__(Q_THREADS, 1)
         const int gshift = 31 - __clz(G);
         const int ngr = (int)(p.H / G);
         const int64_t crow = p.H * BITS / 8;  // code bytes per token row
+        // the piece tiles of the range's first token block, by all epilogue
+        // warps (idle until its P exists): one memory round trip instead of the
+        // builder warp's several
+        if (v_lo < v_hi) {
+            const int64_t t0 = (v_lo / p.ncc) * ROWS;
+            build_piece_tiles_team<ROWS, LB, 32 * 4 * NG>(p.lr, t0, p.T - t0, r, smem + L::OFF_PT,
+                                                          (int)threadIdx.x - 96);
+            tc::fence_proxy_async();
+            tc::named_bar(1, 32 * 4 * NG);
+            if (threadIdx.x == 96) tc::mbar_arrive(&pready[0]);
+        }
         int j = 0;
         bool ok = true;
         Walk w(v_lo, p.ntiles, p.ncc);

@@ -270,4 +270,50 @@ __device__ __forceinline__ void build_piece_tiles(const float *lr, int64_t t0, i
     }
 }
 
+// The same piece tiles built by a team of TEAM threads (tid 0 .. TEAM-1, whole
+// warps): each thread loads all of its chunks (at most a few) before converting
+// any, so a kernel's idle warps turn its first token block around in one
+// memory round trip instead of the one builder warp's several.  The caller
+// fences the async proxy and synchronises the team before the tiles are used.
+template <int ROWS, int LB, int TEAM>
+__device__ __forceinline__ void build_piece_tiles_team(const float *lr, int64_t t0, int64_t rows_here, int rank,
+                                                       uint8_t *dst, int tid) {
+    constexpr int CPR = LB / 16;
+    constexpr int TOTAL = ROWS * CPR;
+    constexpr int N = (TOTAL + TEAM - 1) / TEAM;
+    float4 v[N][2];
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+        const int e = tid + TEAM * j, row = e / CPR, c16 = e - row * CPR;
+        if (e < TOTAL && 8 * c16 < rank && row < rows_here) {
+            const float4 *src = reinterpret_cast<const float4 *>(lr + (t0 + row) * rank + 8 * c16);
+            v[j][0] = __ldg(src);
+            v[j][1] = __ldg(src + 1);
+        } else {
+            v[j][0] = v[j][1] = make_float4(0.f, 0.f, 0.f, 0.f);
+        }
+    }
+#pragma unroll
+    for (int j = 0; j < N; ++j) {
+        const int e = tid + TEAM * j, row = e / CPR, c16 = e - row * CPR;
+        if (e >= TOTAL) continue;
+        const float in[8] = {v[j][0].x, v[j][0].y, v[j][0].z, v[j][0].w,
+                             v[j][1].x, v[j][1].y, v[j][1].z, v[j][1].w};
+        uint32_t ph[4], pm[4], pl[4];
+#pragma unroll
+        for (int h = 0; h < 4; ++h) {
+            float h0, m0, l0, h1, m1, l1;
+            split3_bf16(in[2 * h], h0, m0, l0);
+            split3_bf16(in[2 * h + 1], h1, m1, l1);
+            ph[h] = pack_bf16x2(h0, h1);
+            pm[h] = pack_bf16x2(m0, m1);
+            pl[h] = pack_bf16x2(l0, l1);
+        }
+        const int o = kmajor_swz<LB>(row, c16);
+        *reinterpret_cast<uint4 *>(dst + o) = make_uint4(ph[0], ph[1], ph[2], ph[3]);
+        *reinterpret_cast<uint4 *>(dst + ROWS * LB + o) = make_uint4(pm[0], pm[1], pm[2], pm[3]);
+        *reinterpret_cast<uint4 *>(dst + 2 * ROWS * LB + o) = make_uint4(pl[0], pl[1], pl[2], pl[3]);
+    }
+}
+
 }  // namespace act
