@@ -296,6 +296,10 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RK>::THREADS, 1)
             bool ok = true;
             for (int64_t tile = t_lo; tile < t_hi && ok; ++tile, tw.next()) {
                 if (tile != t_lo && tw.cc != 0) continue;  // not the first tile of a token block
+                if (m == 0) {  // the range's first block: built by the epilogue warps
+                    ++m;
+                    continue;
+                }
                 const int ls = m & 1;
                 if (!(ok = tc::mbar_wait(&pfree[ls], ((m >> 1) & 1) ^ 1, abort))) break;
                 uint8_t *dst = ptile + ls * L::PT;
@@ -328,6 +332,18 @@ __global__ void __launch_bounds__(DecLayout<BITS, OP, WHT, RK>::THREADS, 1)
         constexpr int PD = 4;
         float qsc[PD], qrs[PD];
         TileWalk tw(t_lo, p.ncc, p.ntb, p.tri != 0), nw = tw;  // this tile, the one PD ahead
+        // the piece tiles of the range's first token block, by all epilogue warps
+        // (idle until its P exists): one memory round trip instead of the
+        // builder warp's several
+        if constexpr (RK > 0) {
+            if (t_lo < t_hi) {
+                const int64_t t0 = (int64_t)tw.b * p.T + (int64_t)tw.tb * ROWS;
+                build_piece_tiles_team<ROWS, LB, ETH>(p.lr, t0, p.T - (int64_t)tw.tb * ROWS, p.rank, ptile, etid);
+                tc::fence_proxy_async();
+                tc::named_bar(3, ETH);
+                if (etid == 0) tc::mbar_arrive(&pready[0]);
+            }
+        }
         const int gshift = 31 - __clz(p.group);
         auto load_scalars = [&](int64_t tile, const TileWalk &at, float &vsc, float &vrs) {
             vsc = 0.f;
