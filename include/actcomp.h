@@ -189,6 +189,25 @@ int actcomp_cg_dw(const actcomp_cg_desc *d, const uint16_t *dy, int64_t N, int64
 int actcomp_cg_dw_static(const actcomp_cg_desc *d, const uint16_t *dy, int64_t N, int64_t lddy, void *dw,
                          int32_t dw_dtype, int64_t lddw, void *stream);
 
+/* dW = xhat^T * dy with the dequantisation inside the GEMM's producer, as
+ * triton_matmul_decompress (extraction_fuse_matmul.py:224) reconstructs its
+ * tiles while loading them (:151-221).  The GEMM follows the format instead of
+ * rebuilding xhat: dW = Q^T dy + V (L^T dy), Q = bf16((u - 2^(b-1)) * s) made
+ * from the codes in shared memory by dequantising warps (zero in the outlier
+ * channels), V (L^T dy) a second K segment of the same accumulator (exact
+ * bf16 pieces of the float32 L^T dy), and the outlier channels' rows
+ * overwritten by outliers^T dy.  No T x H reconstruction is written.  The
+ * result differs from actcomp_cg_dw (the GEMM of the bf16 reconstruction) by
+ * the bf16 rounding of the residual instead of that of L V^T + R: about 5e-4
+ * relative, both equally far (about 4e-3) from the GEMM of the uncompressed x.
+ * Same arguments as actcomp_cg_dw; ACT_E_UNSUPPORTED for batch > 1, the
+ * rotated format, H % 64 != 0 or n_outlier % 8 != 0.  workspace:
+ * actcomp_cg_dw_fused_workspace() bytes (the low-rank and outlier terms:
+ * (T + 2 H) * 3r * 2 + 3r * N * 6 + n_outlier * N * 4 bytes, rounded). */
+size_t actcomp_cg_dw_fused_workspace(const actcomp_cg_desc *d, int64_t N);
+int actcomp_cg_dw_fused(const actcomp_cg_desc *d, const uint16_t *dy, int64_t N, int64_t lddy, void *dw,
+                        int32_t dw_dtype, int64_t lddw, void *workspace, size_t workspace_bytes, void *stream);
+
 /* Column absmax of x (T x H, row stride ldx) and the k largest channels
  * (score descending, ties to the lower index), returned ascending in idx.
  * score_ws: H floats of device scratch.  Selection rule for the outlier

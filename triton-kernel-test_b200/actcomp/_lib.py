@@ -99,6 +99,9 @@ SIGNATURES = {
     "actcomp_cg_dw_workspace": (ctypes.c_size_t, [ctypes.POINTER(CgDesc), c_i64]),
     "actcomp_cg_dw": (ctypes.c_int, [ctypes.POINTER(CgDesc), c_vp, c_i64, c_i64, c_vp, c_i32, c_i64, c_vp,
                                      ctypes.c_size_t, c_vp]),
+    "actcomp_cg_dw_fused_workspace": (ctypes.c_size_t, [ctypes.POINTER(CgDesc), c_i64]),
+    "actcomp_cg_dw_fused": (ctypes.c_int, [ctypes.POINTER(CgDesc), c_vp, c_i64, c_i64, c_vp, c_i32, c_i64, c_vp,
+                                           ctypes.c_size_t, c_vp]),
     "actcomp_cg_dw_static": (ctypes.c_int, [ctypes.POINTER(CgDesc), c_vp, c_i64, c_i64, c_vp, c_i32, c_i64, c_vp]),
     "actcomp_cg_channel_topk": (ctypes.c_int, [c_vp, c_i64, c_i64, c_i64, c_i32, c_vp, c_vp, c_vp]),
     "actcomp_cg_copy": (ctypes.c_int, [ctypes.POINTER(CgDesc), ctypes.POINTER(CgDesc), c_vp]),

@@ -269,9 +269,15 @@ def softmax_backward(c: Compressed, dp: torch.Tensor, causal: bool = False,
 
 
 def weight_grad(c: Compressed, dy: torch.Tensor, out_dtype: torch.dtype = torch.float32,
-                workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+                workspace: Optional[torch.Tensor] = None, fused: bool = False) -> torch.Tensor:
     """dW = xhat^T dy (H x N) with xhat reconstructed from c, fp32 accumulation
-    on the tcgen05 tensor cores (extraction_fuse_matmul.py:224)."""
+    on the tcgen05 tensor cores (extraction_fuse_matmul.py:224).
+
+    fused=False: the reconstruction into a workspace, then the GEMM
+    (actcomp_cg_dw; bit-for-bit the GEMM of decode(c)).  fused=True: the
+    dequantisation inside the GEMM's producer and the low-rank and outlier
+    terms as their own skinny products (actcomp_cg_dw_fused; about 5e-4
+    relative from the former, no T x H workspace)."""
     _need_cuda(dy)
     if c.batch != 1:
         raise ValueError("weight_grad takes a single-slice activation")
@@ -283,10 +289,11 @@ def weight_grad(c: Compressed, dy: torch.Tensor, out_dtype: torch.dtype = torch.
         raise ValueError("dy rows must equal the activation's tokens")
     dw = torch.empty((c.channels, N), dtype=out_dtype, device=dy.device)
     d = c.desc()
-    need = _lib.load().actcomp_cg_dw_workspace(ctypes.byref(d), N)
+    name = "actcomp_cg_dw_fused" if fused else "actcomp_cg_dw"
+    need = getattr(_lib.load(), name + "_workspace")(ctypes.byref(d), N)
     if workspace is None or workspace.numel() < need:
-        workspace = torch.empty((need,), dtype=torch.uint8, device=dy.device)
-    call("actcomp_cg_dw", ctypes.byref(d), dy.data_ptr(), N, dy.stride(0), dw.data_ptr(),
+        workspace = torch.empty((max(need, 1),), dtype=torch.uint8, device=dy.device)
+    call(name, ctypes.byref(d), dy.data_ptr(), N, dy.stride(0), dw.data_ptr(),
          0 if out_dtype == torch.float32 else 1, dw.stride(0), workspace.data_ptr(), workspace.numel(),
          _stream(dy))
     return dw
