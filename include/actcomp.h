@@ -201,7 +201,7 @@ int actcomp_cg_dw_static(const actcomp_cg_desc *d, const uint16_t *dy, int64_t N
  * the bf16 rounding of the residual instead of that of L V^T + R: about 5e-4
  * relative, both equally far (about 4e-3) from the GEMM of the uncompressed x.
  * Same arguments as actcomp_cg_dw; ACT_E_UNSUPPORTED for batch > 1, the
- * rotated format, H % 64 != 0 or n_outlier % 8 != 0.  workspace:
+ * rotated format, H % 64 != 0, H < 256, T < 64 or n_outlier % 8 != 0.  workspace:
  * actcomp_cg_dw_fused_workspace() bytes (the low-rank and outlier terms:
  * (T + 2 H) * 3r * 2 + 3r * N * 6 + n_outlier * N * 4 bytes, rounded). */
 size_t actcomp_cg_dw_fused_workspace(const actcomp_cg_desc *d, int64_t N);

@@ -24,9 +24,11 @@
 //   warps 2-5   epilogue (TMEM -> dW rows);
 //   warps 6-13  dequantisation: per 64-token k-block each thread turns one
 //               token's 64 channels of codes (and their group scales) into
-//               one 128-byte row of the MN-major, 128-byte-swizzled A tile,
-//               loading the next k-block's codes while it waits for a free
-//               stage.  The codes of a 256-channel slab (2 MB at 16384
+//               one 128-byte row of the MN-major, 128-byte-swizzled A tile.
+//               int4 codes come by TMA into a 3-slot ring of their own (one
+//               64 x 128-byte swizzled box a k-block, with its own arrival
+//               barrier); int8 codes and the scales are loaded by the
+//               threads one k-block ahead.  The codes of a 256-channel slab (2 MB at 16384
 //               tokens, int4) are read by every CTA of that M tile, mostly
 //               from L2.
 #include <cudaTypedefs.h>
@@ -46,7 +48,10 @@ constexpr int STAGE = MA * A_BYTES + B_BYTES;  // 64 KB
 constexpr int STAGES = 3;
 constexpr int DQ_WARPS = 8;
 constexpr int THREADS = (6 + DQ_WARPS) * 32;
-constexpr int SMEM = STAGES * STAGE + 1024 /*align*/ + 256 /*barriers*/;
+constexpr int CODE_BYTES = BK * 128;            // int4 codes of a k-block: 64 tokens x 256 channels
+// int4: the codes come by TMA into their own 3-slot ring (128-byte swizzle)
+template <int BITS>
+constexpr int smem_bytes() { return STAGES * STAGE + (BITS == 4 ? STAGES * CODE_BYTES : 0) + 1024 + 256; }
 
 struct Params {
     int64_t T, H, N;
@@ -70,9 +75,11 @@ struct Row {
 template <int BITS>
 __device__ __forceinline__ void load_row(const Params &p, int64_t t, int64_t c0, Row<BITS> &q) {
     if (t < p.T && c0 < p.H) {
-        const uint4 *src = reinterpret_cast<const uint4 *>(p.codes + t * (p.H * BITS / 8) + c0 * BITS / 8);
+        if constexpr (BITS == 8) {  // int4 codes arrive by TMA instead
+            const uint4 *src = reinterpret_cast<const uint4 *>(p.codes + t * (p.H * BITS / 8) + c0 * BITS / 8);
 #pragma unroll
-        for (int i = 0; i < BITS / 2; ++i) q.v[i] = __ldg(src + i);
+            for (int i = 0; i < BITS / 2; ++i) q.v[i] = __ldg(src + i);
+        }
         const int ngr = (int)(p.H / p.group);
         const int gshift = 31 - __clz(p.group);
         const float *sp = p.scales + t * ngr;
@@ -85,15 +92,6 @@ __device__ __forceinline__ void load_row(const Params &p, int64_t t, int64_t c0,
     }
 }
 
-// w = (u - 2^(b-1)) * s: the code's exact float, one rounded product (as the
-// oracle's dequantisation), zero in the outlier channels
-template <int BITS>
-__device__ __forceinline__ float dq(uint32_t u, float s, bool outlier) {
-    constexpr float UOFF = 8388608.0f + (float)(1 << (BITS - 1));
-    const float w = __fmul_rn(__fsub_rn(__uint_as_float(0x4B000000u | u), UOFF), s);
-    return outlier ? 0.f : w;
-}
-
 template <typename T>
 __device__ __forceinline__ T cvt_out(float v);
 template <>
@@ -104,12 +102,15 @@ __device__ __forceinline__ __nv_bfloat16 cvt_out<__nv_bfloat16>(float v) { retur
 template <int BITS, typename TOut>
 __global__ void __launch_bounds__(THREADS, 1)
     dq_gemm_kernel(const __grid_constant__ CUtensorMap tmB, const __grid_constant__ CUtensorMap tmA2,
-                   const __grid_constant__ CUtensorMap tmB2, Params p) {
+                   const __grid_constant__ CUtensorMap tmB2, const __grid_constant__ CUtensorMap tmQ, Params p) {
+    constexpr bool TMAC = BITS == 4;  // codes staged by TMA
     extern __shared__ uint8_t smem_raw[];
     uint8_t *smem = reinterpret_cast<uint8_t *>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-    uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE);
+    uint8_t *cring = smem + STAGES * STAGE;  // int4 codes, one slot a stage
+    uint64_t *full = reinterpret_cast<uint64_t *>(smem + STAGES * STAGE + (TMAC ? STAGES * CODE_BYTES : 0));
     uint64_t *empty = full + STAGES;
-    uint64_t *acc_full = empty + STAGES;
+    uint64_t *cfull = empty + STAGES;        // [STAGES] a k-block's codes arrived
+    uint64_t *acc_full = cfull + STAGES;
     uint32_t *tmem_slot = reinterpret_cast<uint32_t *>(acc_full + 1);
     volatile int *abort = reinterpret_cast<volatile int *>(tmem_slot + 1);
     const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -130,6 +131,7 @@ __global__ void __launch_bounds__(THREADS, 1)
         for (int s = 0; s < STAGES; ++s) {
             tc::mbar_init(&full[s], 1 + DQ_WARPS);  // the TMA producer and every dequantising warp
             tc::mbar_init(&empty[s], 1);
+            tc::mbar_init(&cfull[s], 1);
         }
         tc::mbar_init(acc_full, 1);
         *abort = 0;
@@ -154,6 +156,10 @@ __global__ void __launch_bounds__(THREADS, 1)
                 uint8_t *a = smem + s * STAGE;
                 uint8_t *b = a + MA * A_BYTES;
                 if (kb < p.kb1) {
+                    if constexpr (TMAC) {
+                        tc::mbar_arrive_expect_tx(&cfull[s], CODE_BYTES);
+                        tc::tma_load_3d(cring + s * CODE_BYTES, &tmQ, &cfull[s], m0 / 2, kb * BK, 0);
+                    }
                     tc::mbar_arrive_expect_tx(&full[s], B_BYTES);
 #pragma unroll
                     for (int j = 0; j < BN / 64; ++j) tc::tma_load_3d(b + j * 8192, &tmB, &full[s], n0 + 64 * j, kb * BK, 0);
@@ -257,8 +263,14 @@ __global__ void __launch_bounds__(THREADS, 1)
             const int s = kb % STAGES;
             if (kb + 1 < p.kb1) load_row<BITS>(p, (int64_t)(kb + 1) * BK + kk, c0, nxt);
             if (!tc::mbar_wait(&empty[s], ((kb / STAGES) & 1) ^ 1, abort)) break;
+            if (TMAC && kb < p.kb1 && !tc::mbar_wait(&cfull[s], (kb / STAGES) & 1, abort)) break;
             if (kb < p.kb1) {
                 uint8_t *row = smem + s * STAGE + dst_off;
+                if constexpr (TMAC) {  // this row's 32 code bytes: chunks 2 at, 2 at + 1 of the swizzled slot
+                    const uint8_t *cr = cring + s * CODE_BYTES + kk * 128;
+                    cur.v[0] = *reinterpret_cast<const uint4 *>(cr + (((2 * at) ^ (kk & 7)) << 4));
+                    cur.v[1] = *reinterpret_cast<const uint4 *>(cr + (((2 * at + 1) ^ (kk & 7)) << 4));
+                }
                 uint32_t wd[BITS * 2];  // the row's code words, by constant index (no local copy)
 #pragma unroll
                 for (int i = 0; i < BITS / 2; ++i) {
@@ -267,24 +279,43 @@ __global__ void __launch_bounds__(THREADS, 1)
                     wd[4 * i + 2] = cur.v[i].z;
                     wd[4 * i + 3] = cur.v[i].w;
                 }
+                // code u -> the float 2^23 + u by one byte permute against 0x4B000000,
+                // then (u - 2^(b-1)) exactly and one rounded product with the scale,
+                // two channels at a time
+                constexpr uint32_t K4B = 0x4B000000u;
+                constexpr float UOFF = 8388608.0f + (float)(1 << (BITS - 1));
+                const float2 uoff2 = make_float2(UOFF, UOFF);
 #pragma unroll
                 for (int j = 0; j < 8; ++j) {  // channels 8j .. 8j+7
-                    const float s8 = j < 4 ? cur.s0 : cur.s1;
+                    const float sj = j < 4 ? cur.s0 : cur.s1;
+                    const float2 s2 = make_float2(sj, sj);
                     uint32_t o[4];
+                    if constexpr (BITS == 4) {  // channel 2i in the low nibble of byte i
+                        const uint32_t ev = wd[j] & 0x0F0F0F0Fu, od = (wd[j] >> 4) & 0x0F0F0F0Fu;
 #pragma unroll
-                    for (int e = 0; e < 4; ++e) {
-                        const int c = 8 * j + 2 * e;
-                        uint32_t u0, u1;
-                        if constexpr (BITS == 4) {  // channel 2i in the low nibble of byte i
-                            const uint32_t byte = (wd[j] >> (8 * e)) & 0xffu;
-                            u0 = byte & 15u;
-                            u1 = byte >> 4;
-                        } else {
-                            const uint32_t w2 = wd[2 * j + (e >> 1)];
-                            u0 = (w2 >> (16 * (e & 1))) & 0xffu;
-                            u1 = (w2 >> (16 * (e & 1) + 8)) & 0xffu;
+                        for (int e = 0; e < 4; ++e) {
+                            const float2 f = make_float2(__uint_as_float(__byte_perm(ev, K4B, 0x7540u | e)),
+                                                         __uint_as_float(__byte_perm(od, K4B, 0x7540u | e)));
+                            const float2 w = mul2(sub2(f, uoff2), s2);
+                            o[e] = pack_bf16x2(w.x, w.y);
                         }
-                        o[e] = pack_bf16x2(dq<BITS>(u0, s8, (om >> c) & 1ull), dq<BITS>(u1, s8, (om >> (c + 1)) & 1ull));
+                    } else {
+#pragma unroll
+                        for (int e = 0; e < 4; ++e) {
+                            const uint32_t w2 = wd[2 * j + (e >> 1)];
+                            const uint32_t b0 = 2 * (e & 1);
+                            const float2 f = make_float2(__uint_as_float(__byte_perm(w2, K4B, 0x7540u | b0)),
+                                                         __uint_as_float(__byte_perm(w2, K4B, 0x7540u | (b0 + 1))));
+                            const float2 w = mul2(sub2(f, uoff2), s2);
+                            o[e] = pack_bf16x2(w.x, w.y);
+                        }
+                    }
+                    const uint32_t m8 = (uint32_t)(om >> (8 * j)) & 0xffu;
+                    if (m8) {  // outlier channels among these eight: zero
+#pragma unroll
+                        for (int e = 0; e < 4; ++e)
+                            o[e] &= ((m8 >> (2 * e)) & 1u ? 0xffff0000u : 0xffffffffu) &
+                                    ((m8 >> (2 * e + 1)) & 1u ? 0x0000ffffu : 0xffffffffu);
                     }
                     *reinterpret_cast<uint4 *>(row + ((j ^ (kk & 7)) << 4)) = make_uint4(o[0], o[1], o[2], o[3]);
                 }
@@ -395,7 +426,8 @@ extern "C" int actcomp_cg_dw_fused(const actcomp_cg_desc *d, const uint16_t *dy,
     const int64_t T = d->tokens, H = d->channels;
     const int r = d->rank, k = d->n_outlier;
     if (T == 0) return ACT_OK;
-    ACT_CHECK(H % 64 == 0 && T <= INT32_MAX && H <= INT32_MAX && N <= INT32_MAX, ACT_E_UNSUPPORTED);
+    ACT_CHECK(H % 64 == 0 && H >= 256 && T >= BK && T <= INT32_MAX && H <= INT32_MAX && N <= INT32_MAX,
+              ACT_E_UNSUPPORTED);  // at least one whole TMA box of codes
     ACT_CHECK(N % 8 == 0 && lddy % 8 == 0 && aligned(dy, 16) && aligned(d->codes, 16), ACT_E_ALIGN);
     if (k) {  // the outliers enter a GEMM as a T x k operand: 16-byte rows
         ACT_CHECK(d->outliers && d->outlier_idx, ACT_E_INVALID);
@@ -439,6 +471,10 @@ extern "C" int actcomp_cg_dw_fused(const actcomp_cg_desc *d, const uint16_t *dy,
                           CU_TENSOR_MAP_SWIZZLE_128B)))
         return st;
     tmA2 = tmB2 = tmB;  // copies never read without a low-rank segment
+    CUtensorMap tmQ = tmB;  // int4 codes: T rows of H/2 bytes, 128 x 64 boxes
+    if (d->bits == 4 && (st = make_map_3d(&tmQ, d->codes, CU_TENSOR_MAP_DATA_TYPE_UINT8, 1, H / 2, T, 1, H / 2, 0,
+                                          128, 64, CU_TENSOR_MAP_SWIZZLE_128B)))
+        return st;
     if (r) {
         if ((st = make_map_3d(&tmA2, V3, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, 3 * r, H, 1, 3 * r, 0, 64, 128,
                               CU_TENSOR_MAP_SWIZZLE_128B)))
@@ -457,13 +493,17 @@ extern "C" int actcomp_cg_dw_fused(const actcomp_cg_desc *d, const uint16_t *dy,
     p.codes = d->codes; p.scales = d->scales; p.idx = d->outlier_idx;
     p.C = dw; p.ldc = lddw;
     const dim3 grid((unsigned)(p.m_tiles * p.n_tiles));
-    auto launch = [&](auto kern) -> int {
-        ACT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM));
-        kern<<<grid, THREADS, SMEM, s>>>(tmB, tmA2, tmB2, p);
+    auto launch = [&](auto kern, int smem) -> int {
+        ACT_CUDA_TRY(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem));
+        kern<<<grid, THREADS, smem, s>>>(tmB, tmA2, tmB2, tmQ, p);
         return launch_status();
     };
-    if (d->bits == 4) st = dw_dtype == 0 ? launch(dq_gemm_kernel<4, float>) : launch(dq_gemm_kernel<4, __nv_bfloat16>);
-    else st = dw_dtype == 0 ? launch(dq_gemm_kernel<8, float>) : launch(dq_gemm_kernel<8, __nv_bfloat16>);
+    if (d->bits == 4)
+        st = dw_dtype == 0 ? launch(dq_gemm_kernel<4, float>, smem_bytes<4>())
+                           : launch(dq_gemm_kernel<4, __nv_bfloat16>, smem_bytes<4>());
+    else
+        st = dw_dtype == 0 ? launch(dq_gemm_kernel<8, float>, smem_bytes<8>())
+                           : launch(dq_gemm_kernel<8, __nv_bfloat16>, smem_bytes<8>());
     if (st) return st;
     if (k) {
         if (dw_dtype == 0)
