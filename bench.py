@@ -434,7 +434,20 @@ def run_gpu(args):
             "ms": ms_dw, "TFLOP/s": tf, "frac_of_bf16_peak": tf / pk.get("bf16_tflops", 1590.0), "flops": flops,
             "rel_err_vs_bf16_gemm_of_x": float((dw - dw_x).norm() / dw_x.norm()),
             "rel_err_vs_gemm_of_xhat": float((dw - dw_xh).norm() / dw_xh.norm())}
-        del dy, ws, dw, dw_x, dw_xh
+        # the same product with the dequantisation inside the GEMM's producer
+        # (actcomp_cg_dw_fused: dW = Q^T dY + V (L^T dY), outlier rows O^T dY;
+        # no T x H workspace), beside the decode-then-GEMM path above
+        ms_dwf = time_steps(lambda: actcomp.weight_grad(c0, dy, torch.float32, fused=True), max(3, args.steps // 2),
+                            1, flush, world, clk)
+        dwf = actcomp.weight_grad(c0, dy, torch.float32, fused=True)
+        tff = flops / (ms_dwf * 1e-3) / 1e12
+        components["dw_gemm_dequant_in_producer_4096x11008_k16384"] = {
+            "ms": ms_dwf, "TFLOP/s": tff, "frac_of_bf16_peak": tff / pk.get("bf16_tflops", 1590.0), "flops": flops,
+            "rel_err_vs_bf16_gemm_of_x": float((dwf - dw_x).norm() / dw_x.norm()),
+            "rel_err_vs_gemm_of_xhat": float((dwf - dw_xh).norm() / dw_xh.norm()),
+            "workspace_MB": actcomp._lib.load().actcomp_cg_dw_fused_workspace(
+                __import__("ctypes").byref(c0.desc()), N) / 1e6}
+        del dy, ws, dw, dw_x, dw_xh, dwf
         # config 5: GELU backward on a compressed 65536 x 5120 activation
         T5, H5 = 4 * T, 5120
         x5, _ = synthetic.lowrank_activation(T5, H5, n_outlier=k, seed=200 + rank, device=dev, outlier_seed=200)
