@@ -431,6 +431,7 @@ def run_gpu(args):
         dw_x = actcomp.gemm(x.mT, dy, torch.float32)
         dw_xh = actcomp.gemm(actcomp.decode(c0).mT, dy, torch.float32)
         components["dw_gemm_fused_4096x11008_k16384"] = {
+            "path": "one C call: decode into a workspace, then the tcgen05 GEMM (actcomp_cg_dw)",
             "ms": ms_dw, "TFLOP/s": tf, "frac_of_bf16_peak": tf / pk.get("bf16_tflops", 1590.0), "flops": flops,
             "rel_err_vs_bf16_gemm_of_x": float((dw - dw_x).norm() / dw_x.norm()),
             "rel_err_vs_gemm_of_xhat": float((dw - dw_xh).norm() / dw_xh.norm())}
@@ -442,6 +443,7 @@ def run_gpu(args):
         dwf = actcomp.weight_grad(c0, dy, torch.float32, fused=True)
         tff = flops / (ms_dwf * 1e-3) / 1e12
         components["dw_gemm_dequant_in_producer_4096x11008_k16384"] = {
+            "path": "dequantisation inside the GEMM's producer (actcomp_cg_dw_fused)",
             "ms": ms_dwf, "TFLOP/s": tff, "frac_of_bf16_peak": tff / pk.get("bf16_tflops", 1590.0), "flops": flops,
             "rel_err_vs_bf16_gemm_of_x": float((dwf - dw_x).norm() / dw_x.norm()),
             "rel_err_vs_gemm_of_xhat": float((dwf - dw_xh).norm() / dw_xh.norm()),
