@@ -145,3 +145,28 @@ def test_selftest_rejects_bad_poll_counts():
     lib = _lib.load()
     assert lib.actcomp_selftest_bounded_wait(0, 0, None) == _lib.ACT_E_INVALID
     assert lib.actcomp_selftest_bounded_wait((1 << 24) + 1, 0, None) == _lib.ACT_E_INVALID
+
+
+def test_fused_dw_validation_and_workspace_without_gpu():
+    """actcomp_cg_dw_fused refuses what it does not cover before launching
+    anything, and its workspace holds only the low-rank and outlier terms."""
+    from actcomp import _lib
+
+    lib = _lib.load()
+    T, H, N, r, k = 16384, 4096, 11008, 32, 16
+    d = _desc(tokens=T, channels=H, rank=r, n_outlier=k, lowrank=0x4000, basis=0x5000, outliers=0x6000,
+              outlier_idx=0x7000, basis_t=0x8000)
+    need = lib.actcomp_cg_dw_fused_workspace(ctypes.byref(d), N)
+    up = lambda b: (b + 255) // 256 * 256  # noqa: E731
+    assert need == up(T * 3 * r * 2) + up(3 * r * N * 4) + up(3 * r * N * 2) + up(H * 3 * r * 2) + up(k * N * 4)
+    assert need < T * H * 2 // 10  # against the reconstruction's 134 MB
+    call = lambda dd, ws, wsb: lib.actcomp_cg_dw_fused(  # noqa: E731
+        ctypes.byref(dd), 0x9000, N, N, 0xA000, 0, N, ws, wsb, None)
+    assert call(d, None, 0) == _lib.ACT_E_WORKSPACE                     # no workspace
+    assert call(d, 0x10000, need - 1) == _lib.ACT_E_WORKSPACE           # too small
+    assert call(_desc(tokens=T, channels=H, wht=1), None, 0) == _lib.ACT_E_UNSUPPORTED   # rotated
+    assert call(_desc(tokens=T, channels=H, n_outlier=4, outliers=0x6000, outlier_idx=0x7000), None, 0) == \
+        _lib.ACT_E_UNSUPPORTED                                          # outliers not a multiple of 8
+    assert call(_desc(tokens=32, channels=H), None, 0) == _lib.ACT_E_UNSUPPORTED         # fewer than 64 tokens
+    assert lib.actcomp_cg_dw_fused(ctypes.byref(d), 0x9000, N, N, 0xA000, 2, N, 0x10000, need, None) == \
+        _lib.ACT_E_INVALID                                              # output dtype
